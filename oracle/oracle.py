@@ -1,0 +1,262 @@
+"""CPU restatements of the reference's hot-path algorithms (test infrastructure).
+
+Every function cites the reference file:line it restates.  Floating-point
+paths are numpy in float64 (inputs are the exact fp32 / bf16 values the kernels
+see); the quantisation codes come from the plain-C restatement in
+``quant_ref.c`` (bit-exact byte work), loaded through ctypes.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+_LIB_PATH = _HERE / "_build" / "liboracle.so"
+_lib = None
+
+
+def build_c_oracle(force: bool = False) -> Path:
+    """Compile quant_ref.c into oracle/_build/liboracle.so (gcc, IEEE fp32)."""
+    src = _HERE / "quant_ref.c"
+    if force or not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        _LIB_PATH.parent.mkdir(parents=True, exist_ok=True)
+        tmp = _LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
+        subprocess.check_call(["gcc", "-O2", "-fPIC", "-shared", "-std=c11",
+                               "-fno-fast-math", "-ffp-contract=off", str(src), "-o", str(tmp), "-lm"])
+        os.replace(tmp, _LIB_PATH)
+    return _LIB_PATH
+
+
+def _c():
+    global _lib
+    if _lib is None:
+        lib = ctypes.CDLL(str(build_c_oracle()))
+        P, L, I = ctypes.c_void_p, ctypes.c_long, ctypes.c_int
+        lib.oracle_quant_int_rows.argtypes = [P, L, I, I, I, I, P, P]
+        lib.oracle_quant_int_rows.restype = I
+        lib.oracle_quant_e4m3_rows.argtypes = [P, L, I, I, P, P]
+        lib.oracle_quant_e4m3_rows.restype = I
+        lib.oracle_dequant_gemv.argtypes = [P, P, P, I, I, I, I, P]
+        lib.oracle_gemv_bf16.argtypes = [P, L, P, I, I, I, P]
+        lib.oracle_f32_to_e4m3.argtypes = [ctypes.c_float]
+        lib.oracle_f32_to_e4m3.restype = ctypes.c_uint8
+        lib.oracle_e4m3_to_f32.argtypes = [ctypes.c_uint8]
+        lib.oracle_e4m3_to_f32.restype = ctypes.c_float
+        lib.oracle_f32_to_bf16.argtypes = [ctypes.c_float]
+        lib.oracle_f32_to_bf16.restype = ctypes.c_uint16
+        _lib = lib
+    return _lib
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# --------------------------------------------------------------------------
+# bf16 helpers (bit patterns carried as uint16)
+# --------------------------------------------------------------------------
+
+def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    return (np.asarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(f: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 (torch's ``.to(torch.bfloat16)``)."""
+    u = np.ascontiguousarray(f, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = np.isnan(np.asarray(f, dtype=np.float32))
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+# --------------------------------------------------------------------------
+# GEMV (kernels/gemv.py, kernels/bench_gemv.py:48-55, validation_harness.py:356)
+# --------------------------------------------------------------------------
+
+def gemv_ref(x_bits: np.ndarray, w_bits: np.ndarray) -> np.ndarray:
+    """y[M, N] = x[M, K] . W[N, K]^T accumulated in float64.
+
+    Restates the fp32 ground truth ``x.float() @ W.float().t()`` of
+    kernels/bench_gemv.py:49 and scripts/validation_harness.py:356, which every
+    reference GEMV candidate (kernels/gemv.py:215-219) is gated against.
+    """
+    x = bf16_bits_to_f32(x_bits).astype(np.float64)
+    w = bf16_bits_to_f32(w_bits).astype(np.float64)
+    return x @ w.T
+
+
+def rel_err_inf(out: np.ndarray, truth: np.ndarray) -> float:
+    """max|out - truth| / max|truth| (kernels/bench_gemv.py:48-55)."""
+    truth = np.asarray(truth, dtype=np.float64)
+    return float(np.abs(np.asarray(out, np.float64) - truth).max() / max(np.abs(truth).max(), 1e-12))
+
+
+def rel_rms(out: np.ndarray, truth: np.ndarray) -> float:
+    """rel-RMS error of scripts/validation_harness.py:351,357."""
+    truth = np.asarray(truth, dtype=np.float64)
+    d = np.asarray(out, np.float64) - truth
+    return float(np.sqrt((d ** 2).mean()) / np.sqrt((truth ** 2).mean()))
+
+
+# --------------------------------------------------------------------------
+# Weight-only quantisation (scripts/fake_quant.py:16-42)
+# --------------------------------------------------------------------------
+
+def quant_int_rows(w_bits: np.ndarray, bits: int = 8, group_size: int | None = None):
+    """Codes and scales of ``fake_quantize_weights(w, bits, group_size)``.
+
+    Returns (q int8 [N, K], scale fp32 [N, K // group]).  The dequantised
+    weight of scripts/fake_quant.py:41 is ``q * scale`` in fp32 (see
+    ``dequant_int``).
+    """
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    N, K = w.shape
+    g = K if group_size is None else int(group_size)
+    q = np.empty((N, K), dtype=np.int8)
+    s = np.empty((N, K // g), dtype=np.float32)
+    rc = _c().oracle_quant_int_rows(_ptr(w), K, N, K, g, bits, _ptr(q), _ptr(s))
+    if rc != 0:
+        raise ValueError("group_size must divide K and bits must be in [2, 8]")
+    return q, s
+
+
+def dequant_int(q: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """fp32 ``q * scale`` (scripts/fake_quant.py:41), before the dtype cast."""
+    N, K = q.shape
+    G = scale.shape[1]
+    return (q.astype(np.float32).reshape(N, G, K // G) * scale[:, :, None]).reshape(N, K)
+
+
+def quant_e4m3_rows(w_bits: np.ndarray):
+    """Per-row e4m3 codes + fp32 scales (scale = amax/448)."""
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    N, K = w.shape
+    q = np.empty((N, K), dtype=np.uint8)
+    s = np.empty((N,), dtype=np.float32)
+    _c().oracle_quant_e4m3_rows(_ptr(w), K, N, K, _ptr(q), _ptr(s))
+    return q, s
+
+
+_E4M3_TABLE = None
+
+
+def e4m3_decode(q: np.ndarray) -> np.ndarray:
+    global _E4M3_TABLE
+    if _E4M3_TABLE is None:
+        _E4M3_TABLE = np.array([_c().oracle_e4m3_to_f32(i) for i in range(256)], dtype=np.float32)
+    return _E4M3_TABLE[np.asarray(q, dtype=np.uint8)]
+
+
+def f32_to_e4m3(v: np.ndarray) -> np.ndarray:
+    f = _c().oracle_f32_to_e4m3
+    flat = np.asarray(v, dtype=np.float32).ravel()
+    return np.array([f(float(a)) for a in flat], dtype=np.uint8).reshape(np.shape(v))
+
+
+def dequant_gemv_ref(x_bits: np.ndarray, q: np.ndarray, scale: np.ndarray, kind: str) -> np.ndarray:
+    """Dequantise to fp32 then matmul (float64 accumulation): BASELINE config 3's oracle."""
+    if kind == "int8":
+        wdq = dequant_int(q, scale.reshape(q.shape[0], -1))
+    elif kind == "e4m3":
+        wdq = e4m3_decode(q) * scale.reshape(-1, 1).astype(np.float32)
+    else:
+        raise ValueError(kind)
+    x = bf16_bits_to_f32(x_bits).astype(np.float64)
+    return x @ wdq.astype(np.float64).T
+
+
+# --------------------------------------------------------------------------
+# BMM (kernels/bmm.py)
+# --------------------------------------------------------------------------
+
+def ssd_chunk_bmm_ref(C_bits: np.ndarray, B_bits: np.ndarray, seqlen: int, chunk: int) -> np.ndarray:
+    """CB[b, c, g, i, j] = sum_d C[b, c*CH+i, g, d] * B[b, c*CH+j, g, d].
+
+    Restates kernels/bmm.py:134-136 (einsum "bcigd,bcjgd->bcgij") with the
+    masked semantics of kernels/bmm.py:205-212: rows at positions >= seqlen
+    (the padded tail of a ragged last chunk) contribute zeros.  C, B are bf16
+    bit patterns [BATCH, L, NGROUPS, DSTATE] with L >= seqlen.
+    """
+    BATCH, L, G, D = C_bits.shape
+    nchunks = -(-seqlen // chunk)
+    Cf = np.zeros((BATCH, nchunks * chunk, G, D), np.float64)
+    Bf = np.zeros_like(Cf)
+    Cf[:, :seqlen] = bf16_bits_to_f32(C_bits[:, :seqlen])
+    Bf[:, :seqlen] = bf16_bits_to_f32(B_bits[:, :seqlen])
+    Cc = Cf.reshape(BATCH, nchunks, chunk, G, D)
+    Bc = Bf.reshape(BATCH, nchunks, chunk, G, D)
+    return np.einsum("bcigd,bcjgd->bcgij", Cc, Bc)
+
+
+def codebook_head_ref(hidden_bits: np.ndarray, w_bits: np.ndarray) -> np.ndarray:
+    """logits[cb, b, n] = sum_k hidden[cb, b, k] * W[cb, k, n]  (float64).
+
+    The multi-codebook logit head of BASELINE config 4 (no reference kernel;
+    it is the per-codebook ``torch.bmm`` the survey's CPU probe times).
+    hidden: [NCB, B, K] bf16 bits, W: [NCB, K, N] bf16 bits.
+    """
+    h = bf16_bits_to_f32(hidden_bits).astype(np.float64)
+    w = bf16_bits_to_f32(w_bits).astype(np.float64)
+    return np.matmul(h, w)
+
+
+# --------------------------------------------------------------------------
+# Snake + Conv1d (kernels/fused_snake_conv.py)
+# --------------------------------------------------------------------------
+
+def conv1d_output_length(input_length: int, kernel_size: int, stride: int, padding: int,
+                         dilation: int) -> int:
+    """kernels/fused_snake_conv.py:13-26 (PyTorch Conv1d output length)."""
+    return (input_length + 2 * padding - dilation * (kernel_size - 1) - 1) // stride + 1
+
+
+def snake_ref(x: np.ndarray, alpha: np.ndarray, eps: float = 1e-9) -> np.ndarray:
+    """snake(v) = v + sin(alpha v)^2 / (alpha + eps), per input channel, float64.
+
+    kernels/fused_snake_conv.py:275-277 (reference_snake_conv1d's activation).
+    x: [B, C, T]; alpha: [C].
+    """
+    x = np.asarray(x, np.float64)
+    a = np.asarray(alpha, np.float64).reshape(1, -1, 1)
+    return x + np.sin(a * x) ** 2 / (a + eps)
+
+
+def snake_conv1d_ref(x: np.ndarray, alpha: np.ndarray, weight: np.ndarray, bias: np.ndarray | None,
+                     stride: int = 1, padding: int = 0, dilation: int = 1,
+                     eps: float = 1e-9) -> np.ndarray:
+    """Snake then Conv1d in float64 (kernels/fused_snake_conv.py:264-286).
+
+    Zero padding is applied to the *activated* signal (F.conv1d's padding),
+    which equals padding x because snake(0) == 0 (fused_snake_conv.py:240).
+    weight: [Cout, Cin, K]; returns [B, Cout, Tout].
+    """
+    act = snake_ref(x, alpha, eps)
+    Bn, Cin, T = act.shape
+    Cout, Cw, K = weight.shape
+    if Cw != Cin:
+        raise ValueError("Only groups=1 is supported.")
+    Tout = conv1d_output_length(T, K, stride, padding, dilation)
+    padded = np.zeros((Bn, Cin, T + 2 * padding), np.float64)
+    padded[:, :, padding:padding + T] = act
+    w = np.asarray(weight, np.float64)
+    y = np.zeros((Bn, Cout, Tout), np.float64)
+    span = (Tout - 1) * stride + 1
+    for k in range(K):
+        seg = padded[:, :, k * dilation:k * dilation + span:stride]  # [B, Cin, Tout]
+        y += np.einsum("oi,bit->bot", w[:, :, k], seg, optimize=True)
+    if bias is not None:
+        y += np.asarray(bias, np.float64).reshape(1, -1, 1)
+    return y
+
+
+def cosine(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-300))
+
+
+__all__ = [n for n in dir() if not n.startswith("_")]

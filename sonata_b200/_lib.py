@@ -1,0 +1,77 @@
+"""ctypes binding of libsonata_b200.so (the C ABI declared in include/sonata_b200.h).
+
+The library is built in-tree by ``sonata_b200.build``; there is no CPU or
+eager fallback: if the library cannot be loaded, every kernel entry point
+raises ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libsonata_b200.so"
+HEADER = _PKG.parent / "include" / "sonata_b200.h"
+
+SN_OK = 0
+SN_DTYPE_BF16 = 0
+SN_DTYPE_F32 = 1
+SN_FLAG_PDL = 1
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_U = ctypes.c_uint
+
+# argtypes of every exported symbol; must match include/sonata_b200.h
+SIGNATURES: dict[str, tuple[list, object]] = {
+    "sn_version": ([], _I),
+    "sn_status_string": ([_I], ctypes.c_char_p),
+    "sn_gemv_bf16": ([_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
+    "sn_gemv_int8": ([_P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
+    "sn_gemv_fp8e4m3": ([_P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
+    "sn_quantize_rows_int8": ([_P, _I64, _I, _I, _P, _I64, _P, _P], _I),
+    "sn_quantize_rows_fp8e4m3": ([_P, _I64, _I, _I, _P, _I64, _P, _P], _I),
+}
+
+_lib = None
+
+
+class SonataError(RuntimeError):
+    def __init__(self, fn: str, status: int):
+        msg = lib().sn_status_string(status).decode() if _lib is not None else str(status)
+        super().__init__(f"{fn} failed with status {status}: {msg}")
+        self.status = status
+
+
+def header_symbols() -> list[str]:
+    """Every sn_* function declared in include/sonata_b200.h."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(sn_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the CUDA library; raise if it is missing."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m sonata_b200.build` "
+                "(sonata_b200 has no CPU fallback)")
+        l = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in SIGNATURES.items():
+            f = getattr(l, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = l
+    return _lib
+
+
+def check(fn: str, status: int) -> None:
+    if status != SN_OK:
+        raise SonataError(fn, status)
+
+
+def call(fn: str, *args) -> None:
+    check(fn, getattr(lib(), fn)(*args))

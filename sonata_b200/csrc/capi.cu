@@ -1,0 +1,21 @@
+// Library-level C entry points (version, status strings).
+#include "common.cuh"
+
+extern "C" {
+
+int sn_version(void) { return 100; }  // 0.1.0
+
+const char* sn_status_string(int status) {
+  switch (status) {
+    case SN_OK: return "ok";
+    case SN_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer or inconsistent shape)";
+    case SN_ERR_MISALIGNED: return "pointer or stride not aligned as the kernel requires";
+    case SN_ERR_UNSUPPORTED: return "shape outside what the kernels implement";
+    case SN_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case SN_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case SN_ERR_TIMEOUT: return "a bounded device-side wait ran out";
+    default: return "unknown status";
+  }
+}
+
+}  // extern "C"

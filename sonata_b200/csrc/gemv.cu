@@ -1,0 +1,444 @@
+// Decode (batch 1-4) GEMV for B200: y[m, n] = scale[n] * sum_k x[m, k] * W[n, k].
+//
+// Replaces the CuTe-DSL skinny GEMVs of kernels/gemv.py (12-193) and adds the
+// fused-dequant weight-only int8 / e4m3 variants that scripts/fake_quant.py
+// only simulates.  The path is HBM-bound (the weight is streamed once, x and y
+// are a few KB), so the design is about keeping enough weight bytes in flight:
+//
+//  * one warp owns R whole rows; each lane issues R*CPL independent 16-byte
+//    ld.global.nc.L1::no_allocate loads (a full 4 KB row per warp instruction
+//    batch) before it consumes any of them;
+//  * the weight loads are issued BEFORE griddepcontrol.wait, so under
+//    programmatic dependent launch a GEMV streams its weights while the
+//    previous kernel of the decode step is still finishing;
+//  * x (M <= 4 rows) is converted to fp32 once per CTA into shared memory;
+//  * fp32 accumulation with packed f32x2 FMAs (FFMA2), warp-shuffle reduction,
+//    per-row scale applied once after the reduction, bf16 (RNE) or fp32 store.
+//
+// Grid: ceil(N / (8 * R)) CTAs of 256 threads; with R * CPL <= 16 chunks per
+// lane the whole matrix of a decode-sized projection is requested in the first
+// wave (e.g. 34.9 MB for in_proj over 148 SMs).
+#include "common.cuh"
+
+#include <utility>
+
+namespace sn {
+namespace {
+
+enum WKind : int { W_BF16 = 0, W_INT8 = 1, W_E4M3 = 2 };
+
+template <int WK>
+struct WT {
+  static constexpr int EPC = (WK == W_BF16) ? 8 : 16;  // elements per 16-byte chunk
+  static constexpr int ESZ = (WK == W_BF16) ? 2 : 1;   // bytes per element
+};
+
+struct GemvParams {
+  const uint8_t* W;  // weight base (bytes)
+  int64_t ldw;       // row stride, elements
+  int64_t sW;        // batch stride, elements
+  const float* scale;
+  int64_t sS;
+  const __nv_bfloat16* x;
+  int64_t ldx, sx;
+  void* y;
+  int64_t ldy, sy;
+  int M, N, K;
+  int Kp;     // padded fp32 row stride of x in shared memory
+  int y_f32;
+  int x_vec;  // x rows are 16-byte aligned and K % 8 == 0
+};
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+
+// Stage x[0:M, 0:K] (bf16, global) as fp32 rows of stride Kp in shared memory;
+// rows M..MT-1 are zero.
+template <int MT>
+__device__ __forceinline__ void stage_x(const GemvParams& p, const __nv_bfloat16* xb, float* xs) {
+  if (p.x_vec) {
+    const int cpr = p.K >> 3;  // 8-element chunks per row
+    for (int i = threadIdx.x; i < MT * cpr; i += kThreads) {
+      const int m = i / cpr, c = i - m * cpr;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      if (m < p.M) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xb + m * p.ldx + c * 8);
+        a = make_float4(bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y));
+        b = make_float4(bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w));
+      }
+      float4* dst = reinterpret_cast<float4*>(xs + m * p.Kp + c * 8);
+      dst[0] = a;
+      dst[1] = b;
+    }
+  } else {
+    for (int i = threadIdx.x; i < MT * p.K; i += kThreads) {
+      const int m = i / p.K, k = i - m * p.K;
+      xs[m * p.Kp + k] = (m < p.M) ? __bfloat162float(xb[m * p.ldx + k]) : 0.f;
+    }
+  }
+}
+
+// acc[m] += dot(16-byte weight chunk, x[m, k0 : k0 + EPC])
+template <int WK, int MT>
+__device__ __forceinline__ void chunk_fma(const uint4& w, const float* __restrict__ xs, int Kp, int k0,
+                                          float2 (&acc)[MT]) {
+  if constexpr (WK == W_BF16) {
+    const float2 w0 = make_float2(bf16lo(w.x), bf16hi(w.x));
+    const float2 w1 = make_float2(bf16lo(w.y), bf16hi(w.y));
+    const float2 w2 = make_float2(bf16lo(w.z), bf16hi(w.z));
+    const float2 w3 = make_float2(bf16lo(w.w), bf16hi(w.w));
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float4 xa = *reinterpret_cast<const float4*>(xs + m * Kp + k0);
+      const float4 xb = *reinterpret_cast<const float4*>(xs + m * Kp + k0 + 4);
+      acc[m] = __ffma2_rn(w0, make_float2(xa.x, xa.y), acc[m]);
+      acc[m] = __ffma2_rn(w1, make_float2(xa.z, xa.w), acc[m]);
+      acc[m] = __ffma2_rn(w2, make_float2(xb.x, xb.y), acc[m]);
+      acc[m] = __ffma2_rn(w3, make_float2(xb.z, xb.w), acc[m]);
+    }
+  } else {
+    float2 v[8];
+    if constexpr (WK == W_INT8) {
+      // Signed byte q -> fp32 exactly: bias to u = q + 128, splice u into the
+      // mantissa of 2^23 (0x4B0000uu == 2^23 + u), subtract 2^23 + 128.
+      const float2 off = make_float2(-8388736.0f, -8388736.0f);
+      const uint32_t words[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u,
+                                 w.w ^ 0x80808080u};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float f0 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7440));
+        const float f1 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7441));
+        const float f2 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7442));
+        const float f3 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7443));
+        v[2 * j] = __fadd2_rn(make_float2(f0, f1), off);
+        v[2 * j + 1] = __fadd2_rn(make_float2(f2, f3), off);
+      }
+    } else {
+      // e4m3 pairs -> f16x2 (hardware cvt, exact) -> fp32 pairs (exact).
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half2_raw h01 = __nv_cvt_fp8x2_to_halfraw2(
+            static_cast<__nv_fp8x2_storage_t>(words[j] & 0xFFFFu), __NV_E4M3);
+        const __half2_raw h23 =
+            __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(words[j] >> 16), __NV_E4M3);
+        v[2 * j] = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+        v[2 * j + 1] = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float4* xr = reinterpret_cast<const float4*>(xs + m * Kp + k0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 xv = xr[q];
+        acc[m] = __ffma2_rn(v[2 * q], make_float2(xv.x, xv.y), acc[m]);
+        acc[m] = __ffma2_rn(v[2 * q + 1], make_float2(xv.z, xv.w), acc[m]);
+      }
+    }
+  }
+}
+
+template <int WK>
+__device__ __forceinline__ float load_weight_scalar(const uint8_t* row, int k) {
+  if constexpr (WK == W_BF16) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[k]);
+  } else if constexpr (WK == W_INT8) {
+    return static_cast<float>(reinterpret_cast<const int8_t*>(row)[k]);
+  } else {
+    const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(row[k]), __NV_E4M3);
+    return __half2float(*reinterpret_cast<const __half*>(&h));
+  }
+}
+
+template <int MT>
+__device__ __forceinline__ void store_row(const GemvParams& p, void* yb, int n, int m, float v) {
+  if (m >= p.M) return;
+  if (p.y_f32)
+    reinterpret_cast<float*>(yb)[m * p.ldy + n] = v;
+  else
+    reinterpret_cast<__nv_bfloat16*>(yb)[m * p.ldy + n] = __float2bfloat16_rn(v);
+}
+
+// Vectorised kernel: weight rows are 16-byte aligned.
+template <int WK, int MT, int R, int CPL>
+__global__ void __launch_bounds__(kThreads) gemv_vec_kernel(const GemvParams p) {
+  constexpr int EPC = WT<WK>::EPC;
+  constexpr int ESZ = WT<WK>::ESZ;
+  extern __shared__ __align__(16) float xs[];
+  pdl_launch_dependents();
+
+  const int b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = (blockIdx.x * kWarps + warp) * R;
+  const int nck = p.K / EPC;  // whole 16-byte chunks per row
+  const uint8_t* Wb = p.W + (int64_t)b * p.sW * ESZ;
+
+  const uint4* rowp[R];
+  bool live[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    live[r] = (row0 + r) < p.N;
+    rowp[r] = reinterpret_cast<const uint4*>(Wb + (int64_t)(live[r] ? row0 + r : 0) * p.ldw * ESZ);
+  }
+
+  uint4 wv[R][CPL];
+  auto issue = [&](int base) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        const int idx = base + c * 32 + lane;
+        wv[r][c] = (live[r] && idx < nck) ? ld_stream_v4(rowp[r] + idx) : make_uint4(0, 0, 0, 0);
+      }
+  };
+
+  issue(0);           // weights are independent of the previous kernel
+  pdl_wait();         // x (and y) may be produced / consumed by it
+  stage_x<MT>(p, p.x + (int64_t)b * p.sx, xs);
+  __syncthreads();
+
+  float2 acc[R][MT];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[r][m] = make_float2(0.f, 0.f);
+
+  for (int base = 0; base < nck; base += CPL * 32) {
+    if (base) issue(base);
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      const int idx = base + c * 32 + lane;
+      if (idx < nck) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) chunk_fma<WK, MT>(wv[r][c], xs, p.Kp, idx * EPC, acc[r]);
+      }
+    }
+  }
+
+  // K tail that does not fill a 16-byte chunk
+  const int k_tail = nck * EPC;
+  if (k_tail < p.K) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (!live[r]) continue;
+      const uint8_t* row = reinterpret_cast<const uint8_t*>(rowp[r]);
+      for (int k = k_tail + lane; k < p.K; k += 32) {
+        const float wk = load_weight_scalar<WK>(row, k);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[r][m].x = fmaf(wk, xs[m * p.Kp + k], acc[r][m].x);
+      }
+    }
+  }
+
+  void* yb = reinterpret_cast<uint8_t*>(p.y) + (int64_t)b * p.sy * (p.y_f32 ? 4 : 2);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float s = warp_sum(acc[r][m].x + acc[r][m].y);
+      if (lane == 0 && live[r]) {
+        float v = s;
+        if constexpr (WK != W_BF16) v *= p.scale[(int64_t)b * p.sS + row0 + r];
+        store_row<MT>(p, yb, row0 + r, m, v);
+      }
+    }
+  }
+}
+
+// Fallback for weight rows that are not 16-byte aligned: one warp per row,
+// element loads.  Correct for any stride; not the fast path.
+template <int WK, int MT>
+__global__ void __launch_bounds__(kThreads) gemv_scalar_kernel(const GemvParams p) {
+  constexpr int ESZ = WT<WK>::ESZ;
+  extern __shared__ __align__(16) float xs[];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.y;
+  stage_x<MT>(p, p.x + (int64_t)b * p.sx, xs);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kWarps + warp;
+  if (n >= p.N) return;
+  const uint8_t* row = p.W + ((int64_t)b * p.sW + (int64_t)n * p.ldw) * ESZ;
+  float acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+  for (int k = lane; k < p.K; k += 32) {
+    const float wk = load_weight_scalar<WK>(row, k);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = fmaf(wk, xs[m * p.Kp + k], acc[m]);
+  }
+  void* yb = reinterpret_cast<uint8_t*>(p.y) + (int64_t)b * p.sy * (p.y_f32 ? 4 : 2);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const float s = warp_sum(acc[m]);
+    if (lane == 0) {
+      float v = s;
+      if constexpr (WK != W_BF16) v *= p.scale[(int64_t)b * p.sS + n];
+      store_row<MT>(p, yb, n, m, v);
+    }
+  }
+}
+
+template <typename Kern>
+int launch_gemv(Kern kern, const GemvParams& p, int rows_per_cta, int batch, size_t smem, cudaStream_t st,
+                bool pdl) {
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+      cudaGetLastError();
+      return SN_ERR_UNSUPPORTED;
+    }
+  }
+  dim3 grid((p.N + rows_per_cta - 1) / rows_per_cta, batch);
+  return launch(kern, grid, dim3(kThreads), smem, st, pdl, p);
+}
+
+template <int WK, int MT>
+int dispatch_mt(const GemvParams& p, int batch, size_t smem, cudaStream_t st, bool pdl, bool wvec) {
+  constexpr int EPC = WT<WK>::EPC;
+  if (!wvec) return launch_gemv(gemv_scalar_kernel<WK, MT>, p, kWarps, batch, smem, st, pdl);
+  const int nck = p.K / EPC;
+  const int per_lane = (nck + 31) / 32;
+  // Two rows per warp only when there are plenty of rows to fill 148 SMs.
+  const bool many_rows = (int64_t)p.N * batch >= 4736;
+  if (per_lane <= 4) {
+    if (many_rows) return launch_gemv(gemv_vec_kernel<WK, MT, 2, 4>, p, kWarps * 2, batch, smem, st, pdl);
+    return launch_gemv(gemv_vec_kernel<WK, MT, 1, 4>, p, kWarps, batch, smem, st, pdl);
+  }
+  if (per_lane <= 8) {
+    if (many_rows) return launch_gemv(gemv_vec_kernel<WK, MT, 2, 8>, p, kWarps * 2, batch, smem, st, pdl);
+    return launch_gemv(gemv_vec_kernel<WK, MT, 1, 8>, p, kWarps, batch, smem, st, pdl);
+  }
+  return launch_gemv(gemv_vec_kernel<WK, MT, 1, 16>, p, kWarps, batch, smem, st, pdl);
+}
+
+}  // namespace
+
+// Shared by the C entry points and the codebook-head BMM (batch > 1).
+int gemv_any(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS,
+             const void* x, int64_t ldx, int64_t sx, void* y, int64_t ldy, int64_t sy, int M, int N, int K,
+             int batch, int y_dtype, unsigned flags, cudaStream_t st) {
+  if (!W || !x || !y) return SN_ERR_INVALID_ARGUMENT;
+  if (wk != W_BF16 && !scale) return SN_ERR_INVALID_ARGUMENT;
+  if (M < 1 || M > 4 || N < 1 || K < 1 || batch < 1 || batch > 65535) return SN_ERR_INVALID_ARGUMENT;
+  if (ldw < K || ldx < K || ldy < N) return SN_ERR_INVALID_ARGUMENT;
+  if (y_dtype != SN_DTYPE_BF16 && y_dtype != SN_DTYPE_F32) return SN_ERR_INVALID_ARGUMENT;
+  GemvParams p;
+  p.W = static_cast<const uint8_t*>(W);
+  p.ldw = ldw;
+  p.sW = sW;
+  p.scale = scale;
+  p.sS = sS;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.sx = sx;
+  p.y = y;
+  p.ldy = ldy;
+  p.sy = sy;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.Kp = (K + 15) & ~15;
+  p.y_f32 = y_dtype == SN_DTYPE_F32;
+  p.x_vec = aligned16(x) && (K % 8 == 0) && (ldx % 8 == 0) && (batch == 1 || sx % 8 == 0);
+  const int esz = (wk == W_BF16) ? 2 : 1;
+  const bool wvec = aligned16(W) && ((ldw * esz) % 16 == 0) && (batch == 1 || (sW * esz) % 16 == 0);
+  const int MT = M == 1 ? 1 : (M == 2 ? 2 : 4);
+  const size_t smem = (size_t)MT * p.Kp * sizeof(float);
+  if (smem > 200 * 1024) return SN_ERR_UNSUPPORTED;  // x must fit in shared memory
+  const bool pdl = (flags & SN_FLAG_PDL) != 0;
+#define SN_DISPATCH(WKV)                                                   \
+  switch (MT) {                                                            \
+    case 1: return dispatch_mt<WKV, 1>(p, batch, smem, st, pdl, wvec);     \
+    case 2: return dispatch_mt<WKV, 2>(p, batch, smem, st, pdl, wvec);     \
+    default: return dispatch_mt<WKV, 4>(p, batch, smem, st, pdl, wvec);    \
+  }
+  switch (wk) {
+    case W_BF16: SN_DISPATCH(W_BF16)
+    case W_INT8: SN_DISPATCH(W_INT8)
+    case W_E4M3: SN_DISPATCH(W_E4M3)
+    default: return SN_ERR_INVALID_ARGUMENT;
+  }
+#undef SN_DISPATCH
+}
+
+// ---------------------------------------------------------------------------
+// Device-side per-row quantisation (bit-identical to scripts/fake_quant.py:37-40
+// for int8; BASELINE's e4m3 rule with torch's RNE float8_e4m3fn conversion).
+// One warp per row: max|w| by warp reduction, then q = rne(w / scale).
+// ---------------------------------------------------------------------------
+namespace {
+template <bool E4M3>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16* W, int64_t ldw, int N, int K,
+                                                            uint8_t* q, int64_t ldq, float* scale) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  if (n >= N) return;
+  const __nv_bfloat16* row = W + (int64_t)n * ldw;
+  float amax = 0.f;
+  for (int k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(__bfloat162float(row[k])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = fmaxf(amax, 1e-8f);
+  const float s = amax / (E4M3 ? 448.0f : 127.0f);  // IEEE division (no fast-math)
+  if (lane == 0) scale[n] = s;
+  uint8_t* qrow = q + (int64_t)n * ldq;
+  for (int k = lane; k < K; k += 32) {
+    const float v = __bfloat162float(row[k]) / s;
+    if (E4M3) {
+      // |v| <= 448 * (1 + 2^-23) here, so satfinite and torch's
+      // NaN-on-overflow rule give the same code.
+      qrow[k] = static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+    } else {
+      float r = rintf(v);
+      r = fminf(fmaxf(r, -127.f), 127.f);
+      qrow[k] = static_cast<uint8_t>(static_cast<int8_t>(r));
+    }
+  }
+}
+}  // namespace
+
+}  // namespace sn
+
+extern "C" {
+
+int sn_gemv_bf16(const void* W, int64_t ldw, const void* x, int64_t ldx, void* y, int64_t ldy, int M, int N,
+                 int K, int y_dtype, unsigned flags, void* stream) {
+  return sn::gemv_any(sn::W_BF16, W, ldw, 0, nullptr, 0, x, ldx, 0, y, ldy, 0, M, N, K, 1, y_dtype, flags,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int sn_gemv_int8(const int8_t* q, int64_t ldq, const float* scale, const void* x, int64_t ldx, void* y,
+                 int64_t ldy, int M, int N, int K, int y_dtype, unsigned flags, void* stream) {
+  return sn::gemv_any(sn::W_INT8, q, ldq, 0, scale, 0, x, ldx, 0, y, ldy, 0, M, N, K, 1, y_dtype, flags,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int sn_gemv_fp8e4m3(const uint8_t* q, int64_t ldq, const float* scale, const void* x, int64_t ldx, void* y,
+                    int64_t ldy, int M, int N, int K, int y_dtype, unsigned flags, void* stream) {
+  return sn::gemv_any(sn::W_E4M3, q, ldq, 0, scale, 0, x, ldx, 0, y, ldy, 0, M, N, K, 1, y_dtype, flags,
+                      static_cast<cudaStream_t>(stream));
+}
+
+static int quantize_rows(bool e4m3, const void* W, int64_t ldw, int N, int K, void* q, int64_t ldq, float* scale,
+                         void* stream) {
+  if (!W || !q || !scale) return SN_ERR_INVALID_ARGUMENT;
+  if (N < 1 || K < 1 || ldw < K || ldq < K) return SN_ERR_INVALID_ARGUMENT;
+  dim3 grid((N + 7) / 8);
+  auto k = e4m3 ? sn::quantize_rows_kernel<true> : sn::quantize_rows_kernel<false>;
+  return sn::launch(k, grid, dim3(256), 0, static_cast<cudaStream_t>(stream), false,
+                    static_cast<const __nv_bfloat16*>(W), ldw, N, K, static_cast<uint8_t*>(q), ldq, scale);
+}
+
+int sn_quantize_rows_int8(const void* W, int64_t ldw, int N, int K, int8_t* q, int64_t ldq, float* scale,
+                          void* stream) {
+  return quantize_rows(false, W, ldw, N, K, q, ldq, scale, stream);
+}
+
+int sn_quantize_rows_fp8e4m3(const void* W, int64_t ldw, int N, int K, uint8_t* q, int64_t ldq, float* scale,
+                             void* stream) {
+  return quantize_rows(true, W, ldw, N, K, q, ldq, scale, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,188 @@
+"""Decode GEMV: y[M, N] = x[M, K] . W[N, K]^T, bf16 in, fp32 accumulate.
+
+Drop-in for the reference's kernels/gemv.py:
+
+* ``candidate_cute``, ``candidate_cute_coalesced``, ``candidate_cute_splitk``
+  (gemv.py:215-219): functional ``(x[M, K], W[N, K]) -> y[M, N]`` bf16 on x's
+  device, allocating ``y`` on every call like ``_run`` (gemv.py:199-212).
+* ``skinny_gemv``, ``skinny_gemv_coalesced``, ``skinny_gemv_splitk_m1``,
+  ``skinny_gemv_splitk_m2`` (gemv.py:38-54, 169-193): launchers with the
+  reference's ``(y, x, W, M, N, K, stream)`` argument order that write into a
+  caller-owned ``y`` on ``stream`` without allocating, so they can be captured
+  in a CUDA graph.
+
+The reference's four launchers are four kernel *variants* of one contract; on
+B200 they all run the same tuned sm_100a kernel (``sn_gemv_bf16``), which
+streams W once with 16-byte non-allocating loads, accumulates in fp32 and
+rounds to bf16 once in the epilogue.  Unlike ``_skinny_gemv_splitk_m2_kernel``
+(gemv.py:135), K need not be a multiple of 8: the tail is summed, not dropped.
+
+Additions: ``gemv`` (fp32 or bf16 output, optional programmatic dependent
+launch), and the fused-dequant weight-only GEMVs ``gemv_int8`` /
+``gemv_fp8e4m3`` with ``quantize_weight`` (the real kernels behind
+scripts/fake_quant.py's simulation).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _lib
+from ._common import call, require_cuda, row_major, stream_handle
+
+_BF16 = torch.bfloat16
+MAX_M = 4
+
+
+def _check_gemv(x: torch.Tensor, W: torch.Tensor):
+    require_cuda("x", x, _BF16, 2)
+    require_cuda("W", W, _BF16, 2)
+    M, K = x.shape
+    N, K2 = W.shape
+    if K2 != K:
+        raise ValueError(f"x has K={K} but W has K={K2}")
+    if not 1 <= M <= MAX_M:
+        raise ValueError(f"M={M}: the decode GEMV supports 1 <= M <= {MAX_M}")
+    if x.device != W.device:
+        raise ValueError("x and W must be on the same device")
+    return M, N, K
+
+
+def gemv(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor | None = None, out_dtype=_BF16,
+         pdl: bool = False, stream=None) -> torch.Tensor:
+    """y = x @ W.T with fp32 accumulation; y is bf16 (RNE) or fp32.
+
+    ``pdl=True`` lets the kernel overlap the previous kernel on the stream;
+    only use it when that kernel does not write W.
+    """
+    M, N, K = _check_gemv(x, W)
+    if out is None:
+        out = torch.empty(M, N, device=x.device, dtype=out_dtype)
+    require_cuda("out", out, None, 2)
+    if out.shape != (M, N) or out.dtype not in (_BF16, torch.float32):
+        raise ValueError(f"out must be [{M}, {N}] bf16 or fp32")
+    call("sn_gemv_bf16", W.data_ptr(), row_major("W", W), x.data_ptr(), row_major("x", x), out.data_ptr(),
+         row_major("out", out), M, N, K, _lib.SN_DTYPE_F32 if out.dtype == torch.float32 else _lib.SN_DTYPE_BF16,
+         _lib.SN_FLAG_PDL if pdl else 0, stream_handle(stream))
+    return out
+
+
+def _launcher(y, x, W, M, N, K, stream):
+    if tuple(x.shape) != (M, K) or tuple(W.shape) != (N, K) or tuple(y.shape) != (M, N):
+        raise ValueError("shapes of y, x, W disagree with M, N, K")
+    gemv(x, W, out=y, stream=stream)
+
+
+def skinny_gemv(y, x, W, M, N, K, stream=None):
+    """Launcher with the signature of kernels/gemv.py:38-54."""
+    _launcher(y, x, W, M, N, K, stream)
+
+
+def skinny_gemv_coalesced(y, x, W, M, N, K, stream=None):
+    """Launcher with the signature of kernels/gemv.py:169-175."""
+    _launcher(y, x, W, M, N, K, stream)
+
+
+def skinny_gemv_splitk_m1(y, x, W, M, N, K, stream=None):
+    """Launcher with the signature of kernels/gemv.py:179-185 (M == 1)."""
+    _launcher(y, x, W, M, N, K, stream)
+
+
+def skinny_gemv_splitk_m2(y, x, W, M, N, K, stream=None):
+    """Launcher with the signature of kernels/gemv.py:187-193 (M == 2)."""
+    _launcher(y, x, W, M, N, K, stream)
+
+
+def candidate_cute(x, W):
+    return gemv(x, W)
+
+
+def candidate_cute_coalesced(x, W):
+    return gemv(x, W)
+
+
+def candidate_cute_splitk(x, W):
+    return gemv(x, W)
+
+
+# ---------------------------------------------------------------------------
+# weight-only quantised GEMV
+# ---------------------------------------------------------------------------
+
+@dataclass
+class QuantizedWeight:
+    """Per-output-channel quantised weight: codes [N, K] + fp32 scale [N]."""
+    q: torch.Tensor       # int8 (kind "int8") or uint8 e4m3 bit patterns (kind "e4m3")
+    scale: torch.Tensor   # fp32 [N]
+    kind: str
+
+    @property
+    def shape(self):
+        return tuple(self.q.shape)
+
+    def dequantize(self) -> torch.Tensor:
+        """fp32 ``q * scale`` (scripts/fake_quant.py:41 before its dtype cast)."""
+        if self.kind == "int8":
+            c = self.q.float()
+        else:
+            c = self.q.view(torch.float8_e4m3fn).float()
+        return c * self.scale[:, None]
+
+
+def quantize_weight(W: torch.Tensor, kind: str = "int8", stream=None) -> QuantizedWeight:
+    """Quantise a bf16 [N, K] weight per output channel on the device.
+
+    int8: scale = max(amax_row, 1e-8) / 127, q = round-half-even(w / scale),
+    identical to scripts/fake_quant.py:16-42 (bits=8, group_size=None).
+    e4m3: scale = max(amax_row, 1e-8) / 448, q = e4m3_rn(w / scale).
+    """
+    require_cuda("W", W, _BF16, 2)
+    N, K = W.shape
+    if kind == "int8":
+        q = torch.empty(N, K, device=W.device, dtype=torch.int8)
+        fn = "sn_quantize_rows_int8"
+    elif kind == "e4m3":
+        q = torch.empty(N, K, device=W.device, dtype=torch.uint8)
+        fn = "sn_quantize_rows_fp8e4m3"
+    else:
+        raise ValueError(f"unknown quantisation kind {kind!r} (int8 | e4m3)")
+    scale = torch.empty(N, device=W.device, dtype=torch.float32)
+    call(fn, W.data_ptr(), row_major("W", W), N, K, q.data_ptr(), K, scale.data_ptr(), stream_handle(stream))
+    return QuantizedWeight(q, scale, kind)
+
+
+def gemv_quantized(x: torch.Tensor, qw: QuantizedWeight, out: torch.Tensor | None = None,
+                   out_dtype=torch.float32, pdl: bool = False, stream=None) -> torch.Tensor:
+    """y[m, n] = scale[n] * sum_k x[m, k] * q[n, k] with the dequant fused in-kernel."""
+    require_cuda("x", x, _BF16, 2)
+    q, scale = qw.q, qw.scale
+    require_cuda("q", q, None, 2)
+    require_cuda("scale", scale, torch.float32, 1)
+    M, K = x.shape
+    N = q.shape[0]
+    if q.shape[1] != K or scale.numel() != N or not scale.is_contiguous():
+        raise ValueError("x, q and scale shapes disagree")
+    if not 1 <= M <= MAX_M:
+        raise ValueError(f"M={M}: the decode GEMV supports 1 <= M <= {MAX_M}")
+    if out is None:
+        out = torch.empty(M, N, device=x.device, dtype=out_dtype)
+    if out.shape != (M, N) or out.dtype not in (_BF16, torch.float32):
+        raise ValueError(f"out must be [{M}, {N}] bf16 or fp32")
+    fn = {"int8": "sn_gemv_int8", "e4m3": "sn_gemv_fp8e4m3"}[qw.kind]
+    call(fn, q.data_ptr(), row_major("q", q), scale.data_ptr(), x.data_ptr(), row_major("x", x), out.data_ptr(),
+         row_major("out", out), M, N, K, _lib.SN_DTYPE_F32 if out.dtype == torch.float32 else _lib.SN_DTYPE_BF16,
+         _lib.SN_FLAG_PDL if pdl else 0, stream_handle(stream))
+    return out
+
+
+def gemv_int8(x, qw: QuantizedWeight, **kw):
+    if qw.kind != "int8":
+        raise ValueError("gemv_int8 needs an int8 QuantizedWeight")
+    return gemv_quantized(x, qw, **kw)
+
+
+def gemv_fp8e4m3(x, qw: QuantizedWeight, **kw):
+    if qw.kind != "e4m3":
+        raise ValueError("gemv_fp8e4m3 needs an e4m3 QuantizedWeight")
+    return gemv_quantized(x, qw, **kw)

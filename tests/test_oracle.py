@@ -1,0 +1,152 @@
+"""The CPU oracle against the reference's own frozen outputs (no GPU)."""
+import numpy as np
+import pytest
+
+import oracle as O
+
+
+# ---------------- quantisation: bit-exact codes ----------------
+
+def _bits32(a):
+    """fp32 bit patterns with -0.0 folded into +0.0.
+
+    torch.round keeps the sign of a negative value that rounds to zero, so
+    fake_quantize_weights can emit -0.0; an int8 code cannot carry that sign,
+    and the two zeros are equal values.
+    """
+    a = np.asarray(a, np.float32)
+    return np.where(a == 0, np.float32(0), a).view(np.uint32)
+
+
+def test_int8_rows_match_fake_quant(golden):
+    fq = golden("fake_quant")
+    q, s = O.quant_int_rows(fq["w"], bits=8)
+    wdq = O.dequant_int(q, s)
+    # fp32 dequantised weight is bit-identical to fake_quantize_weights(w.float())
+    assert np.array_equal(_bits32(wdq), _bits32(fq["int8_rows_f32"]))
+    # and casting it to bf16 reproduces the reference's bf16 output bit for bit
+    ref_bf16 = fq["int8_rows_bf16"]
+    ref_bf16 = np.where(ref_bf16 == 0x8000, np.uint16(0), ref_bf16)
+    assert np.array_equal(O.f32_to_bf16_bits(wdq), ref_bf16)
+    assert q.min() >= -127 and q.max() <= 127
+    assert np.all(s[5] == np.float32(1e-8) / np.float32(127))  # dead row clamp
+
+
+@pytest.mark.parametrize("bits,group,key", [(8, 64, "int8_g64_f32"), (4, None, "int4_rows_f32"),
+                                            (4, 64, "int4_g64_f32")])
+def test_int_group_and_bits_variants(golden, bits, group, key):
+    fq = golden("fake_quant")
+    q, s = O.quant_int_rows(fq["w"], bits=bits, group_size=group)
+    assert np.array_equal(_bits32(O.dequant_int(q, s)), _bits32(fq[key]))
+
+
+def test_int_quant_rejects_bad_group(golden):
+    fq = golden("fake_quant")
+    with pytest.raises(ValueError):
+        O.quant_int_rows(fq["w"], bits=8, group_size=100)
+
+
+def test_e4m3_conversion_matches_torch_sweep(golden):
+    fq = golden("fake_quant")
+    codes = O.f32_to_e4m3(fq["e4m3_sweep_in"])
+    ref = fq["e4m3_sweep_codes"]
+    # NaN codes: torch emits 0x7F/0xFF; compare exactly
+    assert np.array_equal(codes, ref), np.nonzero(codes != ref)
+
+
+def test_e4m3_rows_match(golden):
+    fq = golden("fake_quant")
+    q, s = O.quant_e4m3_rows(fq["w"])
+    assert np.array_equal(q, fq["e4m3_codes"])
+    assert np.array_equal(s.view(np.uint32), fq["e4m3_scale"].view(np.uint32))
+    deq = O.e4m3_decode(q) * s[:, None]
+    assert np.array_equal(deq.view(np.uint32), fq["e4m3_dequant_f32"].view(np.uint32))
+
+
+def test_e4m3_decode_roundtrip_all_codes():
+    codes = np.arange(256, dtype=np.uint8)
+    vals = O.e4m3_decode(codes)
+    finite = ~np.isnan(vals)
+    assert finite.sum() == 254
+    back = O.f32_to_e4m3(vals[finite])
+    # +0 and -0 keep their sign bit
+    assert np.array_equal(back, codes[finite])
+
+
+# ---------------- GEMV ----------------
+
+def test_gemv_oracle_matches_linear(golden):
+    g = golden("gemv")
+    y = O.gemv_ref(g["x"], g["w"])
+    np.testing.assert_allclose(y, g["y_truth_f32"], rtol=0, atol=1e-5)
+    # torch's bf16 F.linear output is within bf16 rounding of the float64 truth
+    yl = O.bf16_bits_to_f32(g["y_linear_bf16"])
+    assert O.rel_err_inf(yl, y) < 1e-2
+
+
+def test_dequant_gemv_oracle(golden):
+    fq = golden("fake_quant")
+    rng = np.random.default_rng(0)
+    x = O.f32_to_bf16_bits(rng.standard_normal((2, 256)).astype(np.float32))
+    q, s = O.quant_int_rows(fq["w"], 8)
+    y = O.dequant_gemv_ref(x, q, s, "int8")
+    ref = O.bf16_bits_to_f32(x).astype(np.float64) @ fq["int8_rows_f32"].astype(np.float64).T
+    np.testing.assert_allclose(y, ref, rtol=1e-12, atol=1e-12)
+    q8, s8 = O.quant_e4m3_rows(fq["w"])
+    y8 = O.dequant_gemv_ref(x, q8, s8, "e4m3")
+    ref8 = O.bf16_bits_to_f32(x).astype(np.float64) @ fq["e4m3_dequant_f32"].astype(np.float64).T
+    np.testing.assert_allclose(y8, ref8, rtol=1e-12, atol=1e-12)
+
+
+# ---------------- BMM ----------------
+
+def test_ssd_chunk_bmm_oracle(golden):
+    b = golden("bmm")
+    BATCH, SEQLEN, NG, DS, CH, SEQ_R = b["dims"].tolist()
+    cb = O.ssd_chunk_bmm_ref(b["C"], b["B"], SEQLEN, CH)
+    np.testing.assert_allclose(cb, b["CB"], rtol=1e-6, atol=1e-5)
+    cbr = O.ssd_chunk_bmm_ref(b["C_ragged"], b["B_ragged"], SEQ_R, CH)
+    np.testing.assert_allclose(cbr, b["CB_ragged"], rtol=1e-6, atol=1e-5)
+    # masked region is exactly zero (kernels/bmm.py:205-212 semantics)
+    last = cbr[:, -1]
+    valid = SEQ_R - (cbr.shape[1] - 1) * CH
+    assert np.all(last[:, :, valid:, :] == 0) and np.all(last[:, :, :, valid:] == 0)
+    # hand-computed diagonal/off-diagonal (kernels/bmm.py:143-152)
+    C = O.bf16_bits_to_f32(b["C"]).astype(np.float64)
+    B = O.bf16_bits_to_f32(b["B"]).astype(np.float64)
+    assert abs((C[0, 0, 0] * B[0, 0, 0]).sum() - cb[0, 0, 0, 0, 0]) < 1e-9
+    assert abs((C[0, 3, 0] * B[0, 7, 0]).sum() - cb[0, 0, 0, 3, 7]) < 1e-9
+
+
+def test_codebook_head_oracle():
+    rng = np.random.default_rng(0)
+    h = O.f32_to_bf16_bits(rng.standard_normal((3, 4, 64)).astype(np.float32))
+    w = O.f32_to_bf16_bits((rng.standard_normal((3, 64, 33)) * 0.02).astype(np.float32))
+    y = O.codebook_head_ref(h, w)
+    hf, wf = O.bf16_bits_to_f32(h).astype(np.float64), O.bf16_bits_to_f32(w).astype(np.float64)
+    for cb in range(3):
+        np.testing.assert_allclose(y[cb], hf[cb] @ wf[cb], rtol=1e-12)
+
+
+# ---------------- Snake + Conv1d ----------------
+
+CASES = ["selftest", "same_d1", "same_d3", "same_d9", "stride2_pad1_d2", "large_x"]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_snake_conv_oracle_matches_reference(golden, case):
+    sc = golden("snake_conv")
+    s, p, d = sc[f"{case}__spd"].tolist()
+    y = O.snake_conv1d_ref(sc[f"{case}__x"], sc[f"{case}__alpha"], sc[f"{case}__w"],
+                           sc[f"{case}__b"], stride=s, padding=p, dilation=d)
+    yr = sc[f"{case}__y_reference"]
+    assert y.shape == yr.shape
+    # the reference runs in fp32; the oracle in float64
+    np.testing.assert_allclose(y, yr, rtol=0, atol=2e-5 * max(1.0, np.abs(yr).max()))
+    np.testing.assert_allclose(sc[f"{case}__y_explicit"], yr, rtol=0, atol=1e-4 * max(1.0, np.abs(yr).max()))
+
+
+def test_conv1d_output_length(golden):
+    sc = golden("snake_conv")
+    for L, K, s, p, d, out in sc["output_length_cases"].tolist():
+        assert O.conv1d_output_length(L, K, s, p, d) == out
