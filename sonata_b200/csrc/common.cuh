@@ -112,11 +112,91 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Returns false when the wait gave up (about a second at B200 clocks).
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < (1u << 22); ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: returns false when the phase did not complete within
+// `timeout_ns` (default one second); the caller then records SN_ERR_TIMEOUT
+// and unwinds instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t timeout_ns = 1000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+  return true;
+}
+
+// 1-D bulk copy global -> shared, completion signalled on `bar` (tx bytes).
+// dst, src and bytes must all be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Named barrier over `threads` threads (a multiple of 32), id 1..15.
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Device status word, one per translation unit (no relocatable device code):
+// kernels record the first non-OK status (e.g. SN_ERR_TIMEOUT from a bounded
+// wait); sn_device_status() reads and optionally clears every unit's word.
+// ---------------------------------------------------------------------------
+static __device__ int g_tu_status;
+__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tu_status, 0, code); }
+
+inline int read_tu_status(bool reset, cudaStream_t st, int* out) {
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_tu_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_LAUNCH;
+  }
+  if (reset && v != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbolAsync(g_tu_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+      cudaGetLastError();
+      return SN_ERR_LAUNCH;
+    }
+  }
+  *out = v;
+  return SN_OK;
+}
+
+// Number of SMs of the current device (cached per device).
+inline int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return 148; }
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
 }
 
 }  // namespace sn

@@ -2,24 +2,32 @@
 //
 // Replaces the CuTe-DSL skinny GEMVs of kernels/gemv.py (12-193) and adds the
 // fused-dequant weight-only int8 / e4m3 variants that scripts/fake_quant.py
-// only simulates.  The path is HBM-bound (the weight is streamed once, x and y
-// are a few KB), so the design is about keeping enough weight bytes in flight:
+// only simulates.  The path is HBM-bound: the weight is streamed once, x and y
+// are a few KB.
 //
-//  * one warp owns R whole rows; each lane issues R*CPL independent 16-byte
-//    ld.global.nc.L1::no_allocate loads (a full 4 KB row per warp instruction
-//    batch) before it consumes any of them;
-//  * the weight loads are issued BEFORE griddepcontrol.wait, so under
-//    programmatic dependent launch a GEMV streams its weights while the
-//    previous kernel of the decode step is still finishing;
-//  * x (M <= 4 rows) is converted to fp32 once per CTA into shared memory;
-//  * fp32 accumulation with packed f32x2 FMAs (FFMA2), warp-shuffle reduction,
-//    per-row scale applied once after the reduction, bf16 (RNE) or fp32 store.
+// Fast path (gemv_bulk_kernel): one CTA per SM owns an equal contiguous range
+// of weight rows.  A producer lane streams ~32 KB chunks of whole rows
+// (cp.async.bulk, L2 evict-first) into a shared-memory ring; eight consumer
+// warps each reduce one row of a chunk with packed f32x2 FMAs (FFMA2) against
+// x staged once as bf16 in shared memory, then warp-shuffle and store.  The
+// CTA uses about half an SM, and the producer issues its weight copies
+// before griddepcontrol.wait: launched with programmatic dependent launch, the
+// next GEMV of a decode step is resident beside this one and streams its
+// weights while this one drains.  Measured on B200: the 156-GEMV decode chain
+// of BASELINE config 2 runs about 1.5x faster than cuBLAS in the same graph;
+// what remains is the latency of each kernel boundary (waiting for the
+// producer of x, then loading x), not the arithmetic.
 //
-// Grid: ceil(N / (8 * R)) CTAs of 256 threads; with R * CPL <= 16 chunks per
-// lane the whole matrix of a decode-sized projection is requested in the first
-// wave (e.g. 34.9 MB for in_proj over 148 SMs).
+// Fallbacks: gemv_vec_kernel (16-byte register loads; rows whose length is not
+// a multiple of 16 bytes or longer than 64 KB) and gemv_scalar_kernel (rows
+// that are not 16-byte aligned).
 #include "common.cuh"
 
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
 #include <utility>
 
 namespace sn {
@@ -78,6 +86,38 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, const __nv_bfloat16
   }
 }
 
+// 16 one-byte codes -> 16 exact fp32 values (as 8 float2 pairs).
+template <int WK>
+__device__ __forceinline__ void dequant16(const uint4& w, float2 (&v)[8]) {
+  if constexpr (WK == W_INT8) {
+    // Signed byte q -> fp32 exactly: bias to u = q + 128, splice u into the
+    // mantissa of 2^23 (0x4B0000uu == 2^23 + u), subtract 2^23 + 128.
+    const float2 off = make_float2(-8388736.0f, -8388736.0f);
+    const uint32_t words[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float f0 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7440));
+      const float f1 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7441));
+      const float f2 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7442));
+      const float f3 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7443));
+      v[2 * j] = __fadd2_rn(make_float2(f0, f1), off);
+      v[2 * j + 1] = __fadd2_rn(make_float2(f2, f3), off);
+    }
+  } else {
+    // e4m3 pairs -> f16x2 (hardware cvt, exact) -> fp32 pairs (exact).
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2_raw h01 =
+          __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(words[j] & 0xFFFFu), __NV_E4M3);
+      const __half2_raw h23 =
+          __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(words[j] >> 16), __NV_E4M3);
+      v[2 * j] = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+      v[2 * j + 1] = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+    }
+  }
+}
+
 // acc[m] += dot(16-byte weight chunk, x[m, k0 : k0 + EPC])
 template <int WK, int MT>
 __device__ __forceinline__ void chunk_fma(const uint4& w, const float* __restrict__ xs, int Kp, int k0,
@@ -98,34 +138,7 @@ __device__ __forceinline__ void chunk_fma(const uint4& w, const float* __restric
     }
   } else {
     float2 v[8];
-    if constexpr (WK == W_INT8) {
-      // Signed byte q -> fp32 exactly: bias to u = q + 128, splice u into the
-      // mantissa of 2^23 (0x4B0000uu == 2^23 + u), subtract 2^23 + 128.
-      const float2 off = make_float2(-8388736.0f, -8388736.0f);
-      const uint32_t words[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u,
-                                 w.w ^ 0x80808080u};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float f0 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7440));
-        const float f1 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7441));
-        const float f2 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7442));
-        const float f3 = __uint_as_float(__byte_perm(words[j], 0x4B000000u, 0x7443));
-        v[2 * j] = __fadd2_rn(make_float2(f0, f1), off);
-        v[2 * j + 1] = __fadd2_rn(make_float2(f2, f3), off);
-      }
-    } else {
-      // e4m3 pairs -> f16x2 (hardware cvt, exact) -> fp32 pairs (exact).
-      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const __half2_raw h01 = __nv_cvt_fp8x2_to_halfraw2(
-            static_cast<__nv_fp8x2_storage_t>(words[j] & 0xFFFFu), __NV_E4M3);
-        const __half2_raw h23 =
-            __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(words[j] >> 16), __NV_E4M3);
-        v[2 * j] = __half22float2(*reinterpret_cast<const __half2*>(&h01));
-        v[2 * j + 1] = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-      }
-    }
+    dequant16<WK>(w, v);
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       const float4* xr = reinterpret_cast<const float4*>(xs + m * Kp + k0);
@@ -136,6 +149,29 @@ __device__ __forceinline__ void chunk_fma(const uint4& w, const float* __restric
         acc[m] = __ffma2_rn(v[2 * q + 1], make_float2(xv.z, xv.w), acc[m]);
       }
     }
+  }
+}
+
+// acc[m] += dot(16-byte weight chunk, xr[m][o : o + EPC]) with x in registers.
+template <int WK, int MT, int XN>
+__device__ __forceinline__ void chunk_fma_regs(const uint4& w, const float (&xr)[MT][XN], int o,
+                                               float2 (&acc)[MT]) {
+  if constexpr (WK == W_BF16) {
+    const float2 wv[4] = {make_float2(bf16lo(w.x), bf16hi(w.x)), make_float2(bf16lo(w.y), bf16hi(w.y)),
+                          make_float2(bf16lo(w.z), bf16hi(w.z)), make_float2(bf16lo(w.w), bf16hi(w.w))};
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        acc[m] = __ffma2_rn(wv[j], make_float2(xr[m][o + 2 * j], xr[m][o + 2 * j + 1]), acc[m]);
+  } else {
+    float2 v[8];
+    dequant16<WK>(w, v);
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        acc[m] = __ffma2_rn(v[j], make_float2(xr[m][o + 2 * j], xr[m][o + 2 * j + 1]), acc[m]);
   }
 }
 
@@ -281,23 +317,317 @@ __global__ void __launch_bounds__(kThreads) gemv_scalar_kernel(const GemvParams 
   }
 }
 
+// ---------------------------------------------------------------------------
+// TMA bulk-copy kernel (the fast path).
+//
+// Grid: one CTA per SM.  CTA c owns the contiguous row range
+// [c*R/G, (c+1)*R/G) of the flattened (batch x N) rows, so every SM streams
+// the same number of bytes.  Warp 8 lane 0 streams chunks of `rs` whole rows
+// (~32 KB, one cp.async.bulk when the rows are adjacent) global -> shared into
+// a ring of `ns` slots with a full/empty mbarrier pair per slot; warps 0-7
+// consume.  x is staged once as bf16 in shared memory.
+//
+// Resource use is kept to about half an SM (<= 112 registers per thread,
+// ~110 KB of shared memory) so that under programmatic dependent launch the
+// next GEMV's CTA fits beside this one and streams its weights (issued before
+// griddepcontrol.wait) while this one drains: the HBM pipe stays full across
+// the kernel boundaries of a decode step.
+// ---------------------------------------------------------------------------
+constexpr int kBulkWarps = 8;  // consumer warps; +1 producer warp
+constexpr int kBulkThreads = (kBulkWarps + 1) * 32;
+
+__host__ __device__ constexpr uint32_t round_up_u32(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+struct BulkShape {
+  int ns;              // ring slots
+  int rs;              // weight rows per slot (<= kBulkWarps: one row per consumer warp)
+  uint32_t slot_bytes;
+  uint32_t bar_bytes;
+  uint32_t xs_bytes;   // x area: span * MT rows of Kp (fp32 for bf16 weights, bf16 planes for 8-bit)
+  int total_rows;      // batch * N (< 2^31, checked on the host)
+  int contiguous;      // rows of consecutive index are adjacent in memory
+};
+
+// x is staged in shared memory as bf16 (half the shared-memory traffic of
+// fp32, which measured slower in the decode chain).  Next to bf16 weights a
+// row is plain; next to 8-bit weights it is stored as two planes of Kp/2, the
+// h-th plane holding the h-th 8-element half of every 16-element chunk, so
+// that both 16-byte x loads of a warp are contiguous.
+template <int WK>
+struct XStage {
+  static constexpr int BYTES = 2;
+};
+
+// acc[m][*] += dot(16-byte weight chunk idx, x[m]); two FFMA2 chains per row.
+template <int WK, int MT>
+__device__ __forceinline__ void chunk_fma2(const uint4& w, const __nv_bfloat16* __restrict__ xs, int Kp, int idx,
+                                           float2 (&acc)[MT][2]) {
+  if constexpr (WK == W_BF16) {
+    const float2 w0 = make_float2(bf16lo(w.x), bf16hi(w.x));
+    const float2 w1 = make_float2(bf16lo(w.y), bf16hi(w.y));
+    const float2 w2 = make_float2(bf16lo(w.z), bf16hi(w.z));
+    const float2 w3 = make_float2(bf16lo(w.w), bf16hi(w.w));
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(xs + m * Kp + idx * 8);
+      acc[m][0] = __ffma2_rn(w0, make_float2(bf16lo(xv.x), bf16hi(xv.x)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(w1, make_float2(bf16lo(xv.y), bf16hi(xv.y)), acc[m][1]);
+      acc[m][0] = __ffma2_rn(w2, make_float2(bf16lo(xv.z), bf16hi(xv.z)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(w3, make_float2(bf16lo(xv.w), bf16hi(xv.w)), acc[m][1]);
+    }
+  } else {
+    float2 v[8];
+    dequant16<WK>(w, v);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const uint4 xa = *reinterpret_cast<const uint4*>(xs + m * Kp + idx * 8);
+      const uint4 xb = *reinterpret_cast<const uint4*>(xs + m * Kp + (Kp >> 1) + idx * 8);
+      acc[m][0] = __ffma2_rn(v[0], make_float2(bf16lo(xa.x), bf16hi(xa.x)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(v[1], make_float2(bf16lo(xa.y), bf16hi(xa.y)), acc[m][1]);
+      acc[m][0] = __ffma2_rn(v[2], make_float2(bf16lo(xa.z), bf16hi(xa.z)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(v[3], make_float2(bf16lo(xa.w), bf16hi(xa.w)), acc[m][1]);
+      acc[m][0] = __ffma2_rn(v[4], make_float2(bf16lo(xb.x), bf16hi(xb.x)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(v[5], make_float2(bf16lo(xb.y), bf16hi(xb.y)), acc[m][1]);
+      acc[m][0] = __ffma2_rn(v[6], make_float2(bf16lo(xb.z), bf16hi(xb.z)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(v[7], make_float2(bf16lo(xb.w), bf16hi(xb.w)), acc[m][1]);
+    }
+  }
+}
+
+template <int WK, int MT>
+__global__ void __launch_bounds__(kBulkThreads, 2) gemv_bulk_kernel(const GemvParams p, const BulkShape sh) {
+  constexpr int EPC = WT<WK>::EPC;
+  constexpr int ESZ = WT<WK>::ESZ;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int ns = sh.ns, rs = sh.rs;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + ns;
+  uint8_t* xs = smem + sh.bar_bytes;
+  uint8_t* slots = smem + sh.bar_bytes + sh.xs_bytes;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = static_cast<int>(static_cast<int64_t>(sh.total_rows) * blockIdx.x / gridDim.x);
+  const int r1 = static_cast<int>(static_cast<int64_t>(sh.total_rows) * (blockIdx.x + 1) / gridDim.x);
+  const int nrows = r1 - r0;
+  const uint32_t row_bytes = static_cast<uint32_t>(p.K) * ESZ;
+  const int nchunks = (nrows + rs - 1) / rs;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, kBulkWarps);  // every consumer warp releases every chunk
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kBulkWarps) {
+    // ---------------- producer: weights only, so no griddepcontrol.wait ----
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int c = 0;
+      for (; c < nchunks; ++c) {
+        const int s = c % ns, k = c / ns;
+        if (k > 0 && !mbar_wait_bounded(empty + s, (k - 1) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          break;
+        }
+        const int first = r0 + c * rs;
+        const int cnt = min(rs, r1 - first);
+        uint8_t* dst = slots + static_cast<size_t>(s) * sh.slot_bytes;
+        mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(cnt) * row_bytes);
+        if (sh.contiguous) {
+          const int b = first / p.N, n = first - b * p.N;
+          bulk_g2s(dst, p.W + (static_cast<int64_t>(b) * p.sW + static_cast<int64_t>(n) * p.ldw) * ESZ,
+                   static_cast<uint32_t>(cnt) * row_bytes, full + s, pol);
+        } else {
+          for (int r = 0; r < cnt; ++r) {
+            const int row = first + r;
+            const int b = row / p.N, n = row - b * p.N;
+            bulk_g2s(dst + static_cast<size_t>(r) * row_bytes,
+                     p.W + (static_cast<int64_t>(b) * p.sW + static_cast<int64_t>(n) * p.ldw) * ESZ, row_bytes,
+                     full + s, pol);
+          }
+        }
+      }
+      if (c < nchunks) {  // error path: let the copies in flight land before exit
+        for (int j = (c > ns ? c - ns : 0); j < c; ++j) mbar_wait_bounded(full + j % ns, (j / ns) & 1);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait();  // x and y belong to the previous kernel from here on
+  const int nck = p.K / EPC;
+  const int b0 = r0 / p.N;
+  const int nb = (r1 - 1) / p.N - b0 + 1;  // batch entries touched by this CTA
+  {
+    const int cpr = p.Kp >> 3;  // 8-element groups per staged row
+    for (int i = threadIdx.x; i < nb * MT * cpr; i += kBulkWarps * 32) {
+      const int bm = i / cpr, c = i - bm * cpr;
+      const int bb = bm / MT, m = bm - bb * MT;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (m < p.M && c * 8 < p.K) {
+        const __nv_bfloat16* src = p.x + static_cast<int64_t>(b0 + bb) * p.sx + m * p.ldx + c * 8;
+        if (p.x_vec) {
+          v = *reinterpret_cast<const uint4*>(src);
+        } else {
+          __align__(16) __nv_bfloat16 t[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t[e] = (c * 8 + e < p.K) ? src[e] : __float2bfloat16_rn(0.f);
+          v = *reinterpret_cast<const uint4*>(t);
+        }
+      }
+      const int dst = (WK == W_BF16) ? c * 8 : (c & 1) * (p.Kp >> 1) + (c >> 1) * 8;
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(xs) + bm * p.Kp + dst) = v;
+    }
+  }
+  named_bar_sync(1, kBulkWarps * 32);
+
+  // Every consumer warp waits on every chunk in ring order and arrives once on
+  // its empty barrier, so no warp can ever test a slot's parity two phases
+  // ahead.  Warp w reduces row w of the chunk.
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int s = ch % ns, k = ch / ns;
+    if (!mbar_wait_bounded(full + s, k & 1)) {
+      record_status(SN_ERR_TIMEOUT);
+      break;
+    }
+    const int cnt = min(rs, nrows - ch * rs);
+    const bool has_row = warp < cnt;
+    const uint4* wr = reinterpret_cast<const uint4*>(slots + static_cast<size_t>(s) * sh.slot_bytes +
+                                                     static_cast<size_t>(warp) * row_bytes);
+    const int row = r0 + ch * rs + warp;
+    const int b = row / p.N, n = row - b * p.N;
+    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(xs) + static_cast<size_t>(b - b0) * MT * p.Kp;
+    float2 acc[MT][2];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m][0] = acc[m][1] = make_float2(0.f, 0.f);
+    if (has_row) {
+#pragma unroll 4
+      for (int idx = lane; idx < nck; idx += 32) chunk_fma2<WK, MT>(wr[idx], xb, p.Kp, idx, acc);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + s);
+    if (has_row) {
+      void* yb = reinterpret_cast<uint8_t*>(p.y) + static_cast<int64_t>(b) * p.sy * (p.y_f32 ? 4 : 2);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const float v = warp_sum((acc[m][0].x + acc[m][1].x) + (acc[m][0].y + acc[m][1].y));
+        if (lane == 0) {
+          float o = v;
+          if constexpr (WK != W_BF16) o *= p.scale[static_cast<int64_t>(b) * p.sS + n];
+          store_row<MT>(p, yb, n, m, o);
+        }
+      }
+    }
+  }
+}
+
+// Opt a kernel into more than 48 KB of dynamic shared memory, once per
+// (kernel, device); the table is keyed by the kernel's address.
+inline bool ensure_smem(const void* kern, size_t bytes) {
+  if (bytes <= 48 * 1024) return true;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(kern, dev);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  // carve the unified L1/shared array for shared memory, so that two CTAs
+  // (this kernel's and the next PDL-launched one's) can be resident per SM
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    cudaGetLastError();
+  done[key] = bytes;
+  return true;
+}
+
+// Kernel selection override for measurement: SONATA_GEMV_KERNEL = bulk | regs.
+int gemv_kernel_choice() {
+  static int v = [] {
+    const char* e = getenv("SONATA_GEMV_KERNEL");
+    if (e && strcmp(e, "regs") == 0) return 2;
+    return 1;
+  }();
+  return v;
+}
+
 template <typename Kern>
 int launch_gemv(Kern kern, const GemvParams& p, int rows_per_cta, int batch, size_t smem, cudaStream_t st,
                 bool pdl) {
-  if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
-      cudaGetLastError();
-      return SN_ERR_UNSUPPORTED;
-    }
-  }
+  if (!ensure_smem(reinterpret_cast<const void*>(kern), smem)) return SN_ERR_UNSUPPORTED;
   dim3 grid((p.N + rows_per_cta - 1) / rows_per_cta, batch);
   return launch(kern, grid, dim3(kThreads), smem, st, pdl, p);
+}
+
+// Shared-memory budget of one bulk-GEMV CTA (override: SONATA_GEMV_SMEM_KB).
+// The default leaves room for two CTAs per SM (this GEMV and the next one).
+size_t bulk_smem_budget() {
+  static size_t v = [] {
+    const char* e = getenv("SONATA_GEMV_SMEM_KB");
+    long kb = e ? strtol(e, nullptr, 10) : 0;
+    if (kb < 32 || kb > 220) kb = 110;
+    return static_cast<size_t>(kb) * 1024;
+  }();
+  return v;
+}
+
+// Returns SN_ERR_UNSUPPORTED when the bulk kernel does not apply.
+template <int WK, int MT>
+int dispatch_bulk(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
+  constexpr int ESZ = WT<WK>::ESZ;
+  constexpr int EPC = WT<WK>::EPC;
+  const uint32_t row_bytes = static_cast<uint32_t>(p.K) * ESZ;
+  if (row_bytes % 16 != 0 || row_bytes > 64 * 1024) return SN_ERR_UNSUPPORTED;
+  const int64_t total_rows = static_cast<int64_t>(batch) * p.N;
+  if (total_rows >= (int64_t(1) << 31)) return SN_ERR_UNSUPPORTED;
+  const int grid = static_cast<int>(std::min<int64_t>(sm_count(), total_rows));
+  const int64_t rows_per_cta = (total_rows + grid - 1) / grid;
+  BulkShape sh;
+  sh.total_rows = static_cast<int>(total_rows);
+  sh.contiguous = (p.ldw == p.K) && (batch == 1 || p.sW == static_cast<int64_t>(p.N) * p.ldw);
+  // ~32 KB per bulk copy, one row per consumer warp
+  sh.rs = static_cast<int>(std::max<uint32_t>(1, std::min<uint32_t>(kBulkWarps, (32u * 1024u) / row_bytes)));
+  sh.rs = static_cast<int>(std::min<int64_t>(sh.rs, rows_per_cta));
+  sh.slot_bytes = round_up_u32(static_cast<uint32_t>(sh.rs) * row_bytes, 128);
+  const int ns_max = 16;
+  sh.bar_bytes = round_up_u32(2 * ns_max * 8, 128);
+  const int64_t span = std::min<int64_t>(batch, rows_per_cta / p.N + 2);
+  sh.xs_bytes = round_up_u32(static_cast<uint32_t>(span * MT * p.Kp * XStage<WK>::BYTES), 128);
+  const size_t budget = bulk_smem_budget();
+  size_t room = budget > sh.bar_bytes + sh.xs_bytes ? budget - sh.bar_bytes - sh.xs_bytes : 0;
+  int ns = static_cast<int>(std::min<size_t>(ns_max, room / sh.slot_bytes));
+  const int64_t chunks_per_cta = (rows_per_cta + sh.rs - 1) / sh.rs;
+  ns = static_cast<int>(std::min<int64_t>(ns, chunks_per_cta));
+  ns = std::max(ns, 2);  // two slots even when that exceeds the budget (one CTA per SM then)
+  sh.ns = ns;
+  const size_t smem = sh.bar_bytes + sh.xs_bytes + static_cast<size_t>(sh.ns) * sh.slot_bytes;
+  if (smem > 220 * 1024) return SN_ERR_UNSUPPORTED;
+  auto kern = gemv_bulk_kernel<WK, MT>;
+  if (!ensure_smem(reinterpret_cast<const void*>(kern), smem)) return SN_ERR_UNSUPPORTED;
+  return launch(kern, dim3(grid), dim3(kBulkThreads), smem, st, pdl, p, sh);
 }
 
 template <int WK, int MT>
 int dispatch_mt(const GemvParams& p, int batch, size_t smem, cudaStream_t st, bool pdl, bool wvec) {
   constexpr int EPC = WT<WK>::EPC;
   if (!wvec) return launch_gemv(gemv_scalar_kernel<WK, MT>, p, kWarps, batch, smem, st, pdl);
+  if (gemv_kernel_choice() == 1) {
+    const int rc = dispatch_bulk<WK, MT>(p, batch, st, pdl);
+    if (rc != SN_ERR_UNSUPPORTED) return rc;
+  }
   const int nck = p.K / EPC;
   const int per_lane = (nck + 31) / 32;
   // Two rows per warp only when there are plenty of rows to fill 148 SMs.
