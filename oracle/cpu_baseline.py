@@ -1,0 +1,72 @@
+"""The reference's CPU path for each hot path, timed as the CPU baseline.
+
+TEST / BENCHMARK INFRASTRUCTURE ONLY: ``bench.py`` runs these on the GPU box's
+host cores for its ``cpu_baseline`` field and for ``--impl reference``; the
+product never calls them.
+
+The reference (Vishal-Padia/Sonata) is Python whose CPU-side oracle for every
+path is plain torch:
+
+* decode GEMV: ``torch.nn.functional.linear`` in bf16 (
+  kernels/bench_gemv.py:18-19 ``candidate_torch``);
+* codebook-head BMM: ``torch.bmm`` in bf16 (the survey's CPU probe);
+* Snake + Conv1d: ``reference_snake_conv1d`` (kernels/fused_snake_conv.py:
+  264-286): snake then ``F.conv1d`` in fp32.
+
+These are restated here (the reference modules import cutlass at top level
+and cannot travel to the GPU box).
+"""
+from __future__ import annotations
+
+import os
+import time
+
+import torch
+import torch.nn.functional as F
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def gemv_layer_set(shapes: dict, seed: int = 0, layers: int = 1):
+    """bf16 weights N(0, 0.02) and activations N(0, 1) for `layers` layers."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(layers):
+        out.append({n: ((torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16),
+                        torch.randn(1, K, generator=g).to(torch.bfloat16)) for n, (N, K) in shapes.items()})
+    return out
+
+
+def run_gemv_layers(layer_set) -> None:
+    for layer in layer_set:
+        for W, x in layer.values():
+            F.linear(x, W)
+
+
+def time_gemv(shapes: dict, threads: int, min_seconds: float = 10.0, layers: int = 2):
+    """Time the reference CPU GEMV path; returns (GB/s, seconds, iterations)."""
+    torch.set_num_threads(threads)
+    ls = gemv_layer_set(shapes, layers=layers)
+    per_pass = sum((N * K + K + N) * 2 for (N, K) in shapes.values()) * layers
+    run_gemv_layers(ls)  # warm-up
+    t0 = time.perf_counter()
+    it = 0
+    while True:
+        run_gemv_layers(ls)
+        it += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return per_pass * it / el / 1e9, el, it
+
+
+def reference_snake_conv1d(x, alpha, weight, bias=None, stride=1, padding=0, dilation=1, eps=1e-9):
+    """kernels/fused_snake_conv.py:264-286, restated."""
+    a = alpha.reshape(1, -1, 1)
+    activated = x + torch.sin(a * x).square() / (a + eps)
+    return F.conv1d(activated, weight, bias, stride=stride, padding=padding, dilation=dilation)
