@@ -90,6 +90,41 @@ int sn_quantize_rows_int8(const void *W, int64_t ldw, int N, int K, int8_t *q, i
 int sn_quantize_rows_fp8e4m3(const void *W, int64_t ldw, int N, int K, uint8_t *q, int64_t ldq,
                              float *scale, void *stream);
 
+/*
+ * Status recorded on the device by kernels whose bounded waits ran out
+ * (SN_ERR_TIMEOUT), SN_OK if none.  reset != 0 clears it.  Unlike every other
+ * entry point this one synchronises `stream` (it copies the status words back),
+ * so it must not be called while the stream is being captured.
+ * No counterpart in the reference (its kernels have no device-side waits).
+ */
+int sn_device_status(int reset, void *stream);
+
+/*
+ * Multi-codebook logit head, BASELINE config 4 (no kernel exists in the
+ * reference; it is the per-codebook bmm its decode step runs on the 9 heads):
+ *   logits[cb, b, n] = sum_k hidden[cb, b, k] * W[cb, k, n]
+ * sn_codebook_head_pack transposes W [ncb, K, N] (bf16) once into Wt
+ * [ncb, N, K]; sn_codebook_head_bmm reads hidden [ncb, B, K] (bf16,
+ * contiguous) and Wt, and writes fp32 logits [ncb, B, N].  B <= 4 runs the
+ * decode GEMV, B >= 5 the tcgen05 contraction (K a multiple of 64).
+ */
+int sn_codebook_head_pack(const void *W, int ncb, int K, int N, void *Wt, void *stream);
+int sn_codebook_head_bmm(const void *hidden, const void *Wt, float *logits, int ncb, int B, int K, int N,
+                         unsigned flags, void *stream);
+
+/*
+ * Mamba2 SSD chunk product, replaces launch_bmm (kernels/bmm.py:96-117):
+ *   CB[b, c, g, i, j] = sum_d C[b, c*CHUNK+i, g, d] * B[b, c*CHUNK+j, g, d]
+ * C, B: bf16 [BATCH, >= SEQLEN, NGROUPS, DSTATE] with element strides
+ * (s*b, s*t, s*g) and unit stride over d; CB_out: fp32 contiguous
+ * [BATCH, NCHUNKS, NGROUPS, CHUNK, CHUNK].  Positions >= SEQLEN count as zero
+ * (the masked semantics of kernels/bmm.py:205-212), so the ragged last chunk
+ * is exact.  NCHUNKS * CHUNK must cover SEQLEN.
+ */
+int sn_ssd_chunk_bmm(const void *C, const void *B, int64_t sCb, int64_t sCt, int64_t sCg, int64_t sBb,
+                     int64_t sBt, int64_t sBg, int batch, int seqlen, int ngroups, int dstate, int chunk,
+                     int nchunks, float *CB_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,6 +33,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_gemv_fp8e4m3": ([_P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
     "sn_quantize_rows_int8": ([_P, _I64, _I, _I, _P, _I64, _P, _P], _I),
     "sn_quantize_rows_fp8e4m3": ([_P, _I64, _I, _I, _P, _I64, _P, _P], _I),
+    "sn_device_status": ([_I, _P], _I),
+    "sn_codebook_head_pack": ([_P, _I, _I, _I, _P, _P], _I),
+    "sn_codebook_head_bmm": ([_P, _P, _P, _I, _I, _I, _I, _U, _P], _I),
+    "sn_ssd_chunk_bmm": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _I, _I, _I, _I, _I, _P, _P], _I),
 }
 
 _lib = None

@@ -1,0 +1,399 @@
+// Batched matrix products on B200 tensor cores (tcgen05 + TMA + TMEM).
+//
+// 1. Multi-codebook logit head:
+//      logits[cb, b, n] = sum_k hidden[cb, b, k] * W[cb, k, n]
+//    W is packed once to [cb, n, k] (K-major rows, sn_codebook_head_pack).
+//    B <= 4 streams: the decode GEMV (weights streamed once, CUDA cores).
+//    B >= 5: a tcgen05 contraction -- tile of 128 weight rows (UMMA M) x the
+//    stream batch (UMMA N <= 256) accumulated over K in TMEM; 3-D TMA maps
+//    make the rows past N = 1025 and the streams past B read as zero without
+//    touching memory.
+// 2. Mamba2 SSD chunk product of kernels/bmm.py (launch_bmm, bmm.py:96-117):
+//      CB[b, c, g, i, j] = sum_d C[b, c*CH+i, g, d] * B[b, c*CH+j, g, d]
+//    with the masked semantics of bmm.py:205-212 (positions >= SEQLEN are
+//    zero): the 4-D TMA maps give the sequence dimension the extent SEQLEN, so
+//    the ragged tail of the last chunk is filled with zeros by the copy engine.
+//
+// Roles in the tensor-core kernels: warp 0 lane 0 issues TMA, warp 1 owns TMEM
+// and lane 0 of it issues tcgen05.mma, warps 2-5 drain TMEM (32x32b loads, one
+// lane quarter each) and store fp32.  All mbarrier waits are bounded.
+#include "tc.cuh"
+
+#include <algorithm>
+
+namespace sn {
+int gemv_any(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS, const void* x,
+             int64_t ldx, int64_t sx, void* y, int64_t ldy, int64_t sy, int M, int N, int K, int batch,
+             int y_dtype, unsigned flags, cudaStream_t st);
+
+namespace {
+
+constexpr int kTcThreads = 192;  // 6 warps
+constexpr int kHeadStages = 4;
+
+// ---------------------------------------------------------------------------
+// codebook head
+// ---------------------------------------------------------------------------
+struct HeadParams {
+  float* out;  // [ncb, B, N]
+  int ncb, B, K, N;
+  int bt;      // streams per tile (UMMA N, multiple of 16, <= 256)
+  int nbt;     // stream tiles
+  int ntiles;  // 128-row weight tiles per codebook
+  uint32_t stage_bytes, a_bytes;
+};
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    head_mma_kernel(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapH,
+                    const HeadParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kHeadStages * p.stage_bytes);
+  uint64_t* empty = full + kHeadStages;
+  uint64_t* done = empty + kHeadStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int u = blockIdx.x;
+  const int bt = u % p.nbt;
+  u /= p.nbt;
+  const int nt = u % p.ntiles;
+  const int cb = u / p.ntiles;
+  const int n0 = nt * 128, b0 = bt * p.bt;
+  const int nkb = p.K / 64;
+  const uint32_t tcols = tc::tmem_cols_for(p.bt);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kHeadStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+    tc::prefetch_map(&mapW);
+    tc::prefetch_map(&mapH);
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, tcols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int kb = 0;
+    for (; kb < nkb; ++kb) {
+      const int s = kb % kHeadStages, k = kb / kHeadStages;
+      if (k > 0 && !mbar_wait_bounded(empty + s, (k - 1) & 1)) {
+        record_status(SN_ERR_TIMEOUT);
+        break;
+      }
+      uint8_t* a = smem + s * p.stage_bytes;
+      uint8_t* b = a + p.a_bytes;
+      mbar_arrive_expect_tx(full + s, p.stage_bytes);
+      tc::tma_load_3d(a, &mapW, kb * 64, n0, cb, full + s);
+      tc::tma_load_3d(b, &mapH, kb * 64, b0, cb, full + s);
+    }
+    if (kb < nkb) {  // error path: let issued copies land before the CTA exits
+      for (int j = (kb > kHeadStages ? kb - kHeadStages : 0); j < kb; ++j)
+        mbar_wait_bounded(full + j % kHeadStages, (j / kHeadStages) & 1);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = tc::idesc_bf16_f32(128, p.bt);
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % kHeadStages;
+      if (!mbar_wait_bounded(full + s, (kb / kHeadStages) & 1)) {
+        record_status(SN_ERR_TIMEOUT);
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      const uint8_t* a = smem + s * p.stage_bytes;
+      const uint64_t da = tc::smem_desc_sw128(a), db = tc::smem_desc_sw128(a + p.a_bytes);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)  // 16 bf16 = 32 bytes per step inside the 128-byte swizzle row
+        tc::mma_bf16(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+      tc::mma_commit(empty + s);
+    }
+    (void)ok;
+    tc::mma_commit(done);  // fires once every issued MMA has completed
+  } else if (warp >= 2) {
+    // ---------------- epilogue: TMEM -> fp32 logits ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // the TMEM loads below are warp-collective: take the wait's outcome as a warp
+    if (__all_sync(0xffffffffu, mbar_wait_bounded(done, 0))) {
+      tc::fence_after_sync();
+      const int n = n0 + q * 32 + lane;
+      for (int c = 0; c < p.bt; c += 16) {
+        float v[16];
+        tc::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c, v);
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int b = b0 + c + j;
+            if (b < p.B) p.out[(static_cast<int64_t>(cb) * p.B + b) * p.N + n] = v[j];
+          }
+        }
+      }
+    } else {
+      record_status(SN_ERR_TIMEOUT);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, tcols);
+}
+
+// W [ncb, K, N] -> Wt [ncb, N, K] (32 x 32 tiles through shared memory)
+__global__ void transpose_kn_kernel(const __nv_bfloat16* __restrict__ W, __nv_bfloat16* __restrict__ Wt, int K,
+                                    int N) {
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int cb = blockIdx.z;
+  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  const __nv_bfloat16* src = W + static_cast<int64_t>(cb) * K * N;
+  __nv_bfloat16* dst = Wt + static_cast<int64_t>(cb) * K * N;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int k = k0 + r, n = n0 + threadIdx.x;
+    if (k < K && n < N) tile[r][threadIdx.x] = src[static_cast<int64_t>(k) * N + n];
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int n = n0 + r, k = k0 + threadIdx.x;
+    if (k < K && n < N) dst[static_cast<int64_t>(n) * K + k] = tile[threadIdx.x][r];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SSD chunk product
+// ---------------------------------------------------------------------------
+struct SsdParams {
+  float* out;  // [BATCH, NCH, NG, CH, CH]
+  int batch, seqlen, ng, dstate, ch, nch;
+  int mtiles;  // CH / 128
+  uint32_t a_bytes, b_bytes;  // per 64-wide K block
+};
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    ssd_mma_kernel(const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapB,
+                   const SsdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nkb = p.dstate / 64;
+  const uint32_t kb_bytes = p.a_bytes + p.b_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nkb * kb_bytes);  // one barrier per K block
+  uint64_t* done = full + nkb;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int u = blockIdx.x;
+  const int mt = u % p.mtiles;
+  u /= p.mtiles;
+  const int g = u % p.ng;
+  u /= p.ng;
+  const int c = u % p.nch;
+  const int b = u / p.nch;
+  const int i0 = c * p.ch + mt * 128;  // first sequence row of the A tile
+  const int j0 = c * p.ch;             // first sequence row of the B tile
+  const uint32_t tcols = tc::tmem_cols_for(p.ch);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nkb; ++s) mbar_init(full + s, 1);
+    mbar_init(done, 1);
+    fence_barrier_init();
+    tc::prefetch_map(&mapC);
+    tc::prefetch_map(&mapB);
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, tcols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    for (int kb = 0; kb < nkb; ++kb) {
+      uint8_t* a = smem + kb * kb_bytes;
+      mbar_arrive_expect_tx(full + kb, kb_bytes);
+      tc::tma_load_4d(a, &mapC, kb * 64, g, i0, b, full + kb);
+      tc::tma_load_4d(a + p.a_bytes, &mapB, kb * 64, g, j0, b, full + kb);
+    }
+  } else if (warp == 1 && lane == 0) {
+    const uint32_t idesc = tc::idesc_bf16_f32(128, p.ch);
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (!mbar_wait_bounded(full + kb, 0)) {
+        record_status(SN_ERR_TIMEOUT);
+        break;
+      }
+      tc::fence_after_sync();
+      const uint8_t* a = smem + kb * kb_bytes;
+      const uint64_t da = tc::smem_desc_sw128(a), db = tc::smem_desc_sw128(a + p.a_bytes);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tc::mma_bf16(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+    }
+    tc::mma_commit(done);
+  } else if (warp >= 2) {
+    const int q = warp & 3;
+    if (__all_sync(0xffffffffu, mbar_wait_bounded(done, 0))) {
+      tc::fence_after_sync();
+      const int i = mt * 128 + q * 32 + lane;  // row within the chunk
+      float* row = p.out + ((((static_cast<int64_t>(b) * p.nch + c) * p.ng + g) * p.ch) + i) * p.ch;
+      for (int j = 0; j < p.ch; j += 16) {
+        float v[16];
+        tc::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + j, v);
+        float4* dst = reinterpret_cast<float4*>(row + j);
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        dst[2] = make_float4(v[8], v[9], v[10], v[11]);
+        dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+      }
+    } else {
+      record_status(SN_ERR_TIMEOUT);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, tcols);
+}
+
+// Any-shape fallback: one thread per output element, masked, fp32 accumulate.
+__global__ void ssd_simt_kernel(const __nv_bfloat16* __restrict__ C, const __nv_bfloat16* __restrict__ Bm,
+                                int64_t sCb, int64_t sCt, int64_t sCg, int64_t sBb, int64_t sBt, int64_t sBg,
+                                SsdParams p) {
+  const int64_t total = static_cast<int64_t>(p.batch) * p.nch * p.ng * p.ch * p.ch;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t r = e;
+    const int j = static_cast<int>(r % p.ch);
+    r /= p.ch;
+    const int i = static_cast<int>(r % p.ch);
+    r /= p.ch;
+    const int g = static_cast<int>(r % p.ng);
+    r /= p.ng;
+    const int c = static_cast<int>(r % p.nch);
+    const int b = static_cast<int>(r / p.nch);
+    const int ti = c * p.ch + i, tj = c * p.ch + j;
+    float acc = 0.f;
+    if (ti < p.seqlen && tj < p.seqlen) {
+      const __nv_bfloat16* ci = C + b * sCb + ti * sCt + g * sCg;
+      const __nv_bfloat16* bj = Bm + b * sBb + tj * sBt + g * sBg;
+      for (int d = 0; d < p.dstate; ++d) acc = fmaf(__bfloat162float(ci[d]), __bfloat162float(bj[d]), acc);
+    }
+    p.out[e] = acc;
+  }
+}
+
+}  // namespace
+
+int tu_status_bmm(bool reset, cudaStream_t st, int* out) { return read_tu_status(reset, st, out); }
+}  // namespace sn
+
+extern "C" {
+
+int sn_codebook_head_pack(const void* W, int ncb, int K, int N, void* Wt, void* stream) {
+  if (!W || !Wt || ncb < 1 || K < 1 || N < 1 || ncb > 65535) return SN_ERR_INVALID_ARGUMENT;
+  dim3 grid((N + 31) / 32, (K + 31) / 32, ncb);
+  return sn::launch(sn::transpose_kn_kernel, grid, dim3(32, 8), 0, static_cast<cudaStream_t>(stream), false,
+                    static_cast<const __nv_bfloat16*>(W), static_cast<__nv_bfloat16*>(Wt), K, N);
+}
+
+int sn_codebook_head_bmm(const void* hidden, const void* Wt, float* logits, int ncb, int B, int K, int N,
+                         unsigned flags, void* stream) {
+  if (!hidden || !Wt || !logits || ncb < 1 || B < 1 || K < 1 || N < 1) return SN_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool tc_ok = (K % 64 == 0) && sn::aligned16(hidden) && sn::aligned16(Wt);
+  if (B <= 4 || !tc_ok) {
+    // decode GEMV over the (codebook, row) pairs, up to 4 streams per launch
+    for (int b0 = 0; b0 < B; b0 += 4) {
+      const int m = std::min(4, B - b0);
+      const int rc = sn::gemv_any(0, Wt, K, static_cast<int64_t>(N) * K, nullptr, 0,
+                                  static_cast<const __nv_bfloat16*>(hidden) + static_cast<int64_t>(b0) * K, K,
+                                  static_cast<int64_t>(B) * K, logits + static_cast<int64_t>(b0) * N, N,
+                                  static_cast<int64_t>(B) * N, m, N, K, ncb, SN_DTYPE_F32, flags, st);
+      if (rc != SN_OK) return rc;
+    }
+    return SN_OK;
+  }
+  sn::HeadParams p;
+  p.out = logits;
+  p.ncb = ncb;
+  p.B = B;
+  p.K = K;
+  p.N = N;
+  p.bt = std::min(256, (B + 15) / 16 * 16);
+  p.nbt = (B + p.bt - 1) / p.bt;
+  p.ntiles = (N + 127) / 128;
+  p.a_bytes = 128 * 64 * 2;
+  p.stage_bytes = p.a_bytes + static_cast<uint32_t>(p.bt) * 64 * 2;
+  CUtensorMap mapW, mapH;
+  const uint64_t dW[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint64_t>(ncb)};
+  const uint64_t sW[2] = {static_cast<uint64_t>(K) * 2, static_cast<uint64_t>(N) * K * 2};
+  const uint32_t bW[3] = {64, 128, 1};
+  const uint64_t dH[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(B), static_cast<uint64_t>(ncb)};
+  const uint64_t sH[2] = {static_cast<uint64_t>(K) * 2, static_cast<uint64_t>(B) * K * 2};
+  const uint32_t bH[3] = {64, static_cast<uint32_t>(p.bt), 1};
+  if (!sn::tc::make_map_bf16_sw128(&mapW, Wt, 3, dW, sW, bW) ||
+      !sn::tc::make_map_bf16_sw128(&mapH, hidden, 3, dH, sH, bH))
+    return SN_ERR_UNSUPPORTED;
+  const size_t smem = 1024 + sn::kHeadStages * static_cast<size_t>(p.stage_bytes) + 256;
+  if (cudaFuncSetAttribute(sn::head_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_UNSUPPORTED;
+  }
+  const int units = ncb * p.ntiles * p.nbt;
+  return sn::launch(sn::head_mma_kernel, dim3(units), dim3(sn::kTcThreads), smem, st, false, mapW, mapH, p);
+}
+
+int sn_ssd_chunk_bmm(const void* C, const void* Bm, int64_t sCb, int64_t sCt, int64_t sCg, int64_t sBb,
+                     int64_t sBt, int64_t sBg, int batch, int seqlen, int ngroups, int dstate, int chunk,
+                     int nchunks, float* CB_out, void* stream) {
+  if (!C || !Bm || !CB_out || batch < 1 || seqlen < 0 || ngroups < 1 || dstate < 1 || chunk < 1 || nchunks < 0)
+    return SN_ERR_INVALID_ARGUMENT;
+  if (static_cast<int64_t>(nchunks) * chunk < seqlen) return SN_ERR_INVALID_ARGUMENT;
+  if (nchunks == 0) return SN_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  sn::SsdParams p;
+  p.out = CB_out;
+  p.batch = batch;
+  p.seqlen = seqlen;
+  p.ng = ngroups;
+  p.dstate = dstate;
+  p.ch = chunk;
+  p.nch = nchunks;
+  p.mtiles = chunk / 128;
+  p.a_bytes = 128 * 64 * 2;
+  p.b_bytes = static_cast<uint32_t>(chunk) * 64 * 2;
+  const bool tc_ok = (chunk == 128 || chunk == 256) && dstate % 64 == 0 && dstate <= 256 && seqlen > 0 &&
+                     sn::aligned16(C) && sn::aligned16(Bm) && ((sCg * 2) % 16 == 0) && ((sCt * 2) % 16 == 0) &&
+                     ((sCb * 2) % 16 == 0) && ((sBg * 2) % 16 == 0) && ((sBt * 2) % 16 == 0) &&
+                     ((sBb * 2) % 16 == 0);
+  const size_t smem = 1024 + static_cast<size_t>(dstate / 64) * (p.a_bytes + p.b_bytes) + 256;
+  if (tc_ok && smem <= 220 * 1024) {
+    CUtensorMap mapC, mapB;
+    const uint64_t dims[4] = {static_cast<uint64_t>(dstate), static_cast<uint64_t>(ngroups),
+                              static_cast<uint64_t>(seqlen), static_cast<uint64_t>(batch)};
+    const uint64_t stC[3] = {static_cast<uint64_t>(sCg) * 2, static_cast<uint64_t>(sCt) * 2,
+                             static_cast<uint64_t>(sCb) * 2};
+    const uint64_t stB[3] = {static_cast<uint64_t>(sBg) * 2, static_cast<uint64_t>(sBt) * 2,
+                             static_cast<uint64_t>(sBb) * 2};
+    const uint32_t boxC[4] = {64, 1, 128, 1};
+    const uint32_t boxB[4] = {64, 1, static_cast<uint32_t>(chunk), 1};
+    if (sn::tc::make_map_bf16_sw128(&mapC, C, 4, dims, stC, boxC) &&
+        sn::tc::make_map_bf16_sw128(&mapB, Bm, 4, dims, stB, boxB)) {
+      if (cudaFuncSetAttribute(sn::ssd_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+          cudaSuccess) {
+        const int units = batch * nchunks * ngroups * p.mtiles;
+        return sn::launch(sn::ssd_mma_kernel, dim3(units), dim3(sn::kTcThreads), smem, st, false, mapC, mapB, p);
+      }
+      cudaGetLastError();
+    }
+  }
+  const int64_t total = static_cast<int64_t>(batch) * nchunks * ngroups * chunk * chunk;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  return sn::launch(sn::ssd_simt_kernel, dim3(blocks), dim3(256), 0, st, false,
+                    static_cast<const __nv_bfloat16*>(C), static_cast<const __nv_bfloat16*>(Bm), sCb, sCt, sCg,
+                    sBb, sBt, sBg, p);
+}
+
+}  // extern "C"

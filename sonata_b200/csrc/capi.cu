@@ -1,7 +1,25 @@
 // Library-level C entry points (version, status strings).
 #include "common.cuh"
 
+namespace sn {
+int tu_status_gemv(bool reset, cudaStream_t st, int* out);
+int tu_status_bmm(bool reset, cudaStream_t st, int* out);
+}  // namespace sn
+
 extern "C" {
+
+int sn_device_status(int reset, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int (*units[])(bool, cudaStream_t, int*) = {sn::tu_status_gemv, sn::tu_status_bmm};
+  int first = SN_OK;
+  for (auto f : units) {
+    int v = SN_OK;
+    const int rc = f(reset != 0, st, &v);
+    if (rc != SN_OK) return rc;
+    if (first == SN_OK && v != SN_OK) first = v;
+  }
+  return first;
+}
 
 int sn_version(void) { return 100; }  // 0.1.0
 

@@ -645,6 +645,8 @@ int dispatch_mt(const GemvParams& p, int batch, size_t smem, cudaStream_t st, bo
 
 }  // namespace
 
+int tu_status_gemv(bool reset, cudaStream_t st, int* out) { return read_tu_status(reset, st, out); }
+
 // Shared by the C entry points and the codebook-head BMM (batch > 1).
 int gemv_any(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS,
              const void* x, int64_t ldx, int64_t sx, void* y, int64_t ldy, int64_t sy, int M, int N, int K,
