@@ -19,6 +19,7 @@
 #ifndef SONATA_B200_H_
 #define SONATA_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -124,6 +125,25 @@ int sn_codebook_head_bmm(const void *hidden, const void *Wt, float *logits, int 
 int sn_ssd_chunk_bmm(const void *C, const void *B, int64_t sCb, int64_t sCt, int64_t sCg, int64_t sBb,
                      int64_t sBt, int64_t sBg, int batch, int seqlen, int ngroups, int dstate, int chunk,
                      int nchunks, float *CB_out, void *stream);
+
+/*
+ * Fused Snake + Conv1d, replaces fused_snake_conv1d / _launch_fused_snake_conv1d
+ * (kernels/fused_snake_conv.py:89-199):
+ *   y[b, o, t] = bias[o] + sum_{i,k} W[o, i, k] * snake(x[b, i, t*stride - padding + k*dilation])
+ *   snake(v) = v + sin(alpha[i] * v)^2 / (alpha[i] + eps), zero outside [0, T)
+ * x: fp32 [B, Cin, T]; alpha: fp32 [Cin]; W: fp32 [Cout, Cin, K]; bias: fp32
+ * [Cout] or NULL; y: fp32 [B, Cout, Tout], Tout = sn_snake_conv1d_output_length
+ * (kernels/fused_snake_conv.py:13-26).  All contiguous.  With a workspace of
+ * at least sn_snake_conv1d_workspace_size(Cin, Cout, K) bytes (16-byte
+ * aligned; the packed bf16 hi/lo weights go there) shapes with stride 1,
+ * K <= 7, (K-1)*dilation <= 72 and Cin, Cout multiples of 16 run on the
+ * tensor cores; everything else runs the per-output fallback.
+ */
+int64_t sn_snake_conv1d_output_length(int64_t T, int K, int stride, int padding, int dilation);
+size_t sn_snake_conv1d_workspace_size(int Cin, int Cout, int K);
+int sn_snake_conv1d(const float *x, const float *alpha, const float *W, const float *bias, float *y, int B,
+                    int Cin, int Cout, int T, int K, int stride, int padding, int dilation, float eps,
+                    void *workspace, size_t workspace_bytes, void *stream);
 
 #ifdef __cplusplus
 }

@@ -37,6 +37,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_codebook_head_pack": ([_P, _I, _I, _I, _P, _P], _I),
     "sn_codebook_head_bmm": ([_P, _P, _P, _I, _I, _I, _I, _U, _P], _I),
     "sn_ssd_chunk_bmm": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _I, _I, _I, _I, _I, _P, _P], _I),
+    "sn_snake_conv1d_output_length": ([_I64, _I, _I, _I, _I], _I64),
+    "sn_snake_conv1d_workspace_size": ([_I, _I, _I], ctypes.c_size_t),
+    "sn_snake_conv1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P, ctypes.c_size_t,
+                         _P], _I),
 }
 
 _lib = None

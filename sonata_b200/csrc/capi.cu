@@ -4,13 +4,14 @@
 namespace sn {
 int tu_status_gemv(bool reset, cudaStream_t st, int* out);
 int tu_status_bmm(bool reset, cudaStream_t st, int* out);
+int tu_status_snake(bool reset, cudaStream_t st, int* out);
 }  // namespace sn
 
 extern "C" {
 
 int sn_device_status(int reset, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int (*units[])(bool, cudaStream_t, int*) = {sn::tu_status_gemv, sn::tu_status_bmm};
+  int (*units[])(bool, cudaStream_t, int*) = {sn::tu_status_gemv, sn::tu_status_bmm, sn::tu_status_snake};
   int first = SN_OK;
   for (auto f : units) {
     int v = SN_OK;

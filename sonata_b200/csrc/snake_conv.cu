@@ -1,0 +1,386 @@
+// Fused Snake + Conv1d on B200 tensor cores.
+//
+// Replaces _fused_snake_conv1d_kernel (kernels/fused_snake_conv.py:29-131):
+//   y[b, o, t] = bias[o] + sum_{i,k} W[o, i, k] * snake(x[b, i, t*s - p + k*d])
+//   snake(v)   = v + sin(alpha_i v)^2 / (alpha_i + eps),   zero outside [0, T)
+// The reference evaluates sin once per (output, input, tap); here every input
+// element is activated once per CTA tile and reused by all taps and output
+// channels of the tile.
+//
+// Fast path (stride 1, K <= 7, (K-1)*d <= 72, Cin and Cout multiples of 16):
+// an implicit GEMM per batch row,  Y[t, o] = sum_k sum_i S[t - p + k*d, i] W_k[o, i]
+//   * UMMA M = 128 output times, N = an output-channel tile (<= 256), K = input
+//     channels in chunks of 64;
+//   * 8 producer warps load x (coalesced along time), apply snake in fp32 and
+//     store the activation as K-major bf16 hi/lo pairs in the 128-byte-swizzled
+//     layout, (128 + (K-1)*d) rows per chunk; tap k reads the same buffer
+//     through a descriptor whose start is k*d rows further (the hardware
+//     applies the swizzle to the absolute shared-memory address, so any row
+//     offset addresses the rows TMA-style writes left there);
+//   * weights are packed once per call into bf16 hi/lo planes [K][2][Cout][Cin]
+//     and streamed per tap by TMA;
+//   * split-precision products hi*hi + lo*hi + hi*lo (three kind::f16 MMAs)
+//     accumulate in fp32 TMEM: about 2^-16 relative error per product, far
+//     inside the 2e-3 max-abs gate, at 1.5x the cost of a tf32 MMA;
+//   * epilogue: TMEM -> registers, + bias, stores coalesced along time.
+// Any other shape runs the fallback: one thread per output, the reference's
+// loop order (correct for every stride / padding / dilation / kernel size).
+#include "tc.cuh"
+
+#include <algorithm>
+
+namespace sn {
+namespace {
+
+constexpr int kScProducerWarps = 8;
+constexpr int kScThreads = (2 + kScProducerWarps) * 32;  // TMA, MMA, 8 producers
+constexpr int kScWStages = 2;
+constexpr int kMaxTaps = 7;
+
+struct ScParams {
+  const float* x;      // [B, Cin, T]
+  const float* alpha;  // [Cin]
+  const float* bias;   // [Cout] or nullptr
+  float* y;            // [B, Cout, Tout]
+  int B, Cin, Cout, T, Tout, K, pad, dil;
+  float eps;
+  int nt;              // output channels per tile (UMMA N)
+  int ntiles_o, ntiles_t;
+  int rows;            // activation rows per chunk (128 + (K-1)*d, rounded up to 8)
+  uint32_t a_bytes;    // one activation plane (rows * 128)
+  uint32_t w_bytes;    // one weight plane (nt * 128)
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return a | (b << 16);
+}
+
+__global__ void __launch_bounds__(kScThreads, 1)
+    snake_conv_mma_kernel(const __grid_constant__ CUtensorMap mapW, const ScParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // layout: [A buf0 hi][A buf0 lo][A buf1 hi][A buf1 lo][W stage0 hi][lo][W stage1 hi][lo][barriers]
+  uint8_t* abuf = smem;
+  uint8_t* wbuf = smem + 4 * p.a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wbuf + 2 * kScWStages * p.w_bytes);
+  uint64_t* a_full = bars;
+  uint64_t* a_empty = bars + 2;
+  uint64_t* w_full = bars + 4;
+  uint64_t* w_empty = w_full + kScWStages;
+  uint64_t* done = w_empty + kScWStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int u = blockIdx.x;
+  const int ot = u % p.ntiles_o;
+  u /= p.ntiles_o;
+  const int tt = u % p.ntiles_t;
+  const int b = u / p.ntiles_t;
+  const int o0 = ot * p.nt, t0 = tt * 128;
+  const int nchunks = (p.Cin + 63) / 64;
+  const uint32_t tcols = tc::tmem_cols_for(p.nt);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(a_full + i, kScProducerWarps);
+      mbar_init(a_empty + i, 1);
+    }
+    for (int i = 0; i < kScWStages; ++i) {
+      mbar_init(w_full + i, 1);
+      mbar_init(w_empty + i, 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+    tc::prefetch_map(&mapW);
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, tcols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- weight TMA: per (chunk, tap) the hi and lo planes ------
+    if (lane == 0) {
+      const int total = nchunks * p.K;
+      int q = 0;
+      for (; q < total; ++q) {
+        const int s = q % kScWStages, k = q / kScWStages;
+        if (k > 0 && !mbar_wait_bounded(w_empty + s, (k - 1) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          break;
+        }
+        const int c = q / p.K, tap = q - c * p.K;
+        uint8_t* dst = wbuf + static_cast<size_t>(s) * 2 * p.w_bytes;
+        mbar_arrive_expect_tx(w_full + s, 2 * p.w_bytes);
+        tc::tma_load_3d(dst, &mapW, c * 64, o0, tap * 2 + 0, w_full + s);
+        tc::tma_load_3d(dst + p.w_bytes, &mapW, c * 64, o0, tap * 2 + 1, w_full + s);
+      }
+      if (q < total) {
+        for (int j = (q > kScWStages ? q - kScWStages : 0); j < q; ++j)
+          mbar_wait_bounded(w_full + j % kScWStages, (j / kScWStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_bf16_f32(128, p.nt);
+      bool ok = true;
+      int q = 0;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int ab = c & 1;
+        if (!mbar_wait_bounded(a_full + ab, (c >> 1) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const int ksteps = min(4, (p.Cin - c * 64) / 16);  // 16-channel MMA steps in this chunk
+        const uint64_t a_hi = tc::smem_desc_sw128(abuf + (2 * ab + 0) * p.a_bytes);
+        const uint64_t a_lo = tc::smem_desc_sw128(abuf + (2 * ab + 1) * p.a_bytes);
+        for (int tap = 0; tap < p.K; ++tap, ++q) {
+          const int s = q % kScWStages;
+          if (!mbar_wait_bounded(w_full + s, (q / kScWStages) & 1)) {
+            record_status(SN_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint8_t* w = wbuf + static_cast<size_t>(s) * 2 * p.w_bytes;
+          const uint64_t w_hi = tc::smem_desc_sw128(w), w_lo = tc::smem_desc_sw128(w + p.w_bytes);
+          const uint64_t shift = static_cast<uint64_t>(tap * p.dil * 128) >> 4;  // tap rows further on
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const uint32_t acc0 = (c | tap | kk) != 0;
+            tc::mma_bf16(tmem, a_hi + shift + 2 * kk, w_hi + 2 * kk, idesc, acc0);
+            tc::mma_bf16(tmem, a_lo + shift + 2 * kk, w_hi + 2 * kk, idesc, 1);
+            tc::mma_bf16(tmem, a_hi + shift + 2 * kk, w_lo + 2 * kk, idesc, 1);
+          }
+          tc::mma_commit(w_empty + s);
+        }
+        tc::mma_commit(a_empty + ab);
+      }
+      tc::mma_commit(done);
+    }
+  } else {
+    // ---------------- snake producers, then the epilogue ----------------
+    const int pw = warp - 2;  // 0..7: the 8-channel group of every chunk this warp fills
+    const float* xb = p.x + static_cast<int64_t>(b) * p.Cin * p.T;
+    const int tin0 = t0 - p.pad;  // input time of activation row 0
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      const int ab = c & 1;
+      if (c >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(a_empty + ab, ((c >> 1) - 1) & 1))) {
+        record_status(SN_ERR_TIMEOUT);
+        ok = false;
+        break;
+      }
+      uint8_t* ahi = abuf + (2 * ab + 0) * p.a_bytes;
+      uint8_t* alo = abuf + (2 * ab + 1) * p.a_bytes;
+      const int i0 = c * 64 + pw * 8;  // first input channel of this warp's group
+      float al[8], inv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = i0 + e;
+        al[e] = i < p.Cin ? p.alpha[i] : 0.f;
+        inv[e] = 1.0f / (al[e] + p.eps);
+      }
+      for (int r = lane; r < p.rows; r += 32) {
+        const int tin = tin0 + r;
+        const bool in_t = tin >= 0 && tin < p.T;
+        float hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = i0 + e;
+          float v = 0.f;
+          if (in_t && i < p.Cin) v = xb[static_cast<int64_t>(i) * p.T + tin];
+          const float sv = __sinf(al[e] * v);
+          const float s = fmaf(sv * sv, inv[e], v);  // snake(v); snake(0) == 0
+          hi[e] = __bfloat162float(__float2bfloat16_rn(s));
+          lo[e] = s - hi[e];
+        }
+        // 16-byte chunk pw of row r, XOR-swizzled with the row's low 3 bits
+        const uint32_t off = static_cast<uint32_t>(r) * 128u + ((static_cast<uint32_t>(pw) ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(ahi + off) = make_uint4(pack_bf16x2(hi[0], hi[1]), pack_bf16x2(hi[2], hi[3]),
+                                                          pack_bf16x2(hi[4], hi[5]), pack_bf16x2(hi[6], hi[7]));
+        *reinterpret_cast<uint4*>(alo + off) = make_uint4(pack_bf16x2(lo[0], lo[1]), pack_bf16x2(lo[2], lo[3]),
+                                                          pack_bf16x2(lo[4], lo[5]), pack_bf16x2(lo[6], lo[7]));
+      }
+      fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(a_full + ab);
+    }
+    // epilogue: a warp may only read the TMEM lane quarter (warp id % 4); warps
+    // 2-5 drain the first half of the columns, warps 6-9 the second half
+    if (ok && __all_sync(0xffffffffu, mbar_wait_bounded(done, 0))) {
+      tc::fence_after_sync();
+      const int q4 = warp & 3, half = pw >> 2;
+      const int t = t0 + q4 * 32 + lane;
+      const int cols = p.nt / 2;  // nt is a multiple of 32 here
+      float* yb = p.y + static_cast<int64_t>(b) * p.Cout * p.Tout;
+      for (int cc = half * cols; cc < (half + 1) * cols; cc += 16) {
+        float v[16];
+        tc::tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + cc, v);
+        if (t < p.Tout) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int o = o0 + cc + j;
+            if (o < p.Cout) yb[static_cast<int64_t>(o) * p.Tout + t] = v[j] + (p.bias ? p.bias[o] : 0.f);
+          }
+        }
+      }
+    } else if (ok) {
+      record_status(SN_ERR_TIMEOUT);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, tcols);
+}
+
+// W fp32 [Cout, Cin, K] -> bf16 planes Wp[(k*2 + h)][o][i], h = 0 hi, 1 lo.
+__global__ void pack_weights_kernel(const float* __restrict__ W, __nv_bfloat16* __restrict__ Wp, int Cout,
+                                    int Cin, int K) {
+  const int64_t total = static_cast<int64_t>(Cout) * Cin * K;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(e % K);
+    const int64_t oi = e / K;
+    const int i = static_cast<int>(oi % Cin);
+    const int o = static_cast<int>(oi / Cin);
+    const float w = W[e];
+    const __nv_bfloat16 h = __float2bfloat16_rn(w);
+    const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
+    const int64_t plane = static_cast<int64_t>(Cout) * Cin;
+    Wp[(static_cast<int64_t>(k) * 2 + 0) * plane + static_cast<int64_t>(o) * Cin + i] = h;
+    Wp[(static_cast<int64_t>(k) * 2 + 1) * plane + static_cast<int64_t>(o) * Cin + i] = l;
+  }
+}
+
+// Fallback: one thread per output element, the reference's loop order.
+__global__ void snake_conv_simt_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
+                                       const float* __restrict__ W, const float* __restrict__ bias,
+                                       float* __restrict__ y, int B, int Cin, int Cout, int T, int Tout, int K,
+                                       int stride, int pad, int dil, float eps) {
+  const int64_t total = static_cast<int64_t>(B) * Cout * Tout;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(e % Tout);
+    const int64_t r = e / Tout;
+    const int o = static_cast<int>(r % Cout);
+    const int b = static_cast<int>(r / Cout);
+    float acc = bias ? bias[o] : 0.f;
+    for (int i = 0; i < Cin; ++i) {
+      const float a = alpha[i];
+      const float inv = 1.0f / (a + eps);
+      const float* xr = x + (static_cast<int64_t>(b) * Cin + i) * T;
+      const float* wr = W + (static_cast<int64_t>(o) * Cin + i) * K;
+      for (int k = 0; k < K; ++k) {
+        const int ti = t * stride - pad + k * dil;
+        if (ti < 0 || ti >= T) continue;
+        const float v = xr[ti];
+        const float sv = sinf(a * v);
+        acc = fmaf(fmaf(sv * sv, inv, v), wr[k], acc);
+      }
+    }
+    y[e] = acc;
+  }
+}
+
+bool fast_path_ok(int Cin, int Cout, int K, int stride, int dil, int Tout) {
+  return stride == 1 && K >= 1 && K <= kMaxTaps && dil >= 1 && (K - 1) * dil <= 72 && Cin % 16 == 0 &&
+         Cout % 16 == 0 && Tout >= 1;
+}
+
+int out_tile(int Cout) {
+  // output-channel tile: <= 256, a multiple of 32, splitting Cout evenly
+  const int tiles = (Cout + 255) / 256;
+  int nt = (Cout + tiles - 1) / tiles;
+  return (nt + 31) / 32 * 32;
+}
+
+}  // namespace
+
+int tu_status_snake(bool reset, cudaStream_t st, int* out) { return read_tu_status(reset, st, out); }
+
+}  // namespace sn
+
+extern "C" {
+
+int64_t sn_snake_conv1d_output_length(int64_t T, int K, int stride, int padding, int dilation) {
+  if (stride < 1 || K < 1 || dilation < 1 || padding < 0) return -1;
+  return (T + 2 * static_cast<int64_t>(padding) - static_cast<int64_t>(dilation) * (K - 1) - 1) / stride + 1;
+}
+
+size_t sn_snake_conv1d_workspace_size(int Cin, int Cout, int K) {
+  return static_cast<size_t>(Cin) * Cout * K * 2 * sizeof(__nv_bfloat16);
+}
+
+int sn_snake_conv1d(const float* x, const float* alpha, const float* W, const float* bias, float* y, int B, int Cin,
+                    int Cout, int T, int K, int stride, int padding, int dilation, float eps, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!x || !alpha || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0 ||
+      dilation < 1)
+    return SN_ERR_INVALID_ARGUMENT;
+  const int64_t tout64 = sn_snake_conv1d_output_length(T, K, stride, padding, dilation);
+  if (tout64 < 1 || tout64 > (int64_t(1) << 31) - 1) return SN_ERR_INVALID_ARGUMENT;
+  const int Tout = static_cast<int>(tout64);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool fast = sn::fast_path_ok(Cin, Cout, K, stride, dilation, Tout) && workspace &&
+                    workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && sn::aligned16(workspace);
+  if (fast) {
+    sn::ScParams p;
+    p.x = x;
+    p.alpha = alpha;
+    p.bias = bias;
+    p.y = y;
+    p.B = B;
+    p.Cin = Cin;
+    p.Cout = Cout;
+    p.T = T;
+    p.Tout = Tout;
+    p.K = K;
+    p.pad = padding;
+    p.dil = dilation;
+    p.eps = eps;
+    p.nt = sn::out_tile(Cout);
+    p.ntiles_o = (Cout + p.nt - 1) / p.nt;
+    p.ntiles_t = (Tout + 127) / 128;
+    p.rows = (128 + (K - 1) * dilation + 7) / 8 * 8;
+    p.a_bytes = static_cast<uint32_t>(p.rows) * 128;
+    p.w_bytes = static_cast<uint32_t>(p.nt) * 128;
+    const size_t smem = 1024 + 4 * static_cast<size_t>(p.a_bytes) +
+                        2 * sn::kScWStages * static_cast<size_t>(p.w_bytes) + 256;
+    if (smem <= 227 * 1024 && static_cast<int64_t>(B) * p.ntiles_t * p.ntiles_o < (int64_t(1) << 31)) {
+      __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
+      const int64_t tot = static_cast<int64_t>(Cout) * Cin * K;
+      const int blocks = static_cast<int>(std::min<int64_t>((tot + 255) / 256, 148 * 8));
+      int rc = sn::launch(sn::pack_weights_kernel, dim3(blocks), dim3(256), 0, st, false, W, Wp, Cout, Cin, K);
+      if (rc != SN_OK) return rc;
+      CUtensorMap mapW;
+      const uint64_t dims[3] = {static_cast<uint64_t>(Cin), static_cast<uint64_t>(Cout),
+                                static_cast<uint64_t>(2 * K)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(Cin) * 2, static_cast<uint64_t>(Cout) * Cin * 2};
+      const uint32_t box[3] = {64, static_cast<uint32_t>(p.nt), 1};
+      if (sn::tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box)) {
+        if (cudaFuncSetAttribute(sn::snake_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)) == cudaSuccess) {
+          const int units = B * p.ntiles_t * p.ntiles_o;
+          return sn::launch(sn::snake_conv_mma_kernel, dim3(units), dim3(sn::kScThreads), smem, st, false, mapW, p);
+        }
+        cudaGetLastError();
+      }
+    }
+  }
+  const int64_t total = static_cast<int64_t>(B) * Cout * Tout;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 32));
+  return sn::launch(sn::snake_conv_simt_kernel, dim3(blocks), dim3(256), 0, st, false, x, alpha, W, bias, y, B, Cin,
+                    Cout, T, Tout, K, stride, padding, dilation, eps);
+}
+
+}  // extern "C"

@@ -1,0 +1,127 @@
+"""GPU parity of the fused Snake + Conv1d against the CPU oracle.
+
+Gate (north star): cosine >= 0.9999 and max|err| <= 2e-3 against
+reference_snake_conv1d (the oracle restates it in float64).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999
+MAX_ABS = 2e-3
+
+
+@pytest.fixture(scope="module")
+def S(cuda_lib):
+    from sonata_b200.kernels import fused_snake_conv
+    return fused_snake_conv
+
+
+def check(y, truth):
+    y = np.asarray(y, np.float64)
+    assert y.shape == truth.shape
+    assert np.isfinite(y).all()
+    err = np.abs(y - truth).max()
+    cos = O.cosine(y, truth)
+    assert err <= MAX_ABS and cos >= COS_MIN, (err, cos)
+
+
+@pytest.mark.parametrize("case", ["selftest", "same_d1", "same_d3", "same_d9", "stride2_pad1_d2", "large_x"])
+def test_golden_cases(S, golden, case):
+    sc = golden("snake_conv")
+    s, p, d = sc[f"{case}__spd"].tolist()
+    t = {k: torch.from_numpy(sc[f"{case}__{k}"]).cuda() for k in ("x", "alpha", "w", "b")}
+    y = S.fused_snake_conv1d(t["x"], t["alpha"], t["w"], t["b"], stride=s, padding=p, dilation=d)
+    torch.cuda.synchronize()
+    yr = sc[f"{case}__y_reference"]
+    np.testing.assert_allclose(y.cpu().numpy(), yr, rtol=0, atol=MAX_ABS * max(1.0, np.abs(yr).max()))
+
+
+def test_reference_selftests(S):
+    S.test_snake_conv1d()
+    S.test_fused_kernel()
+
+
+def rand_case(B, Cin, Cout, T, seed, xscale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, Cin, T, generator=g) * xscale
+    alpha = torch.rand(Cin, generator=g) + 0.5
+    W = torch.randn(Cout, Cin, 7, generator=g) / math.sqrt(7 * Cin)
+    b = torch.randn(Cout, generator=g)
+    return x, alpha, W, b
+
+
+@pytest.mark.parametrize("C", [96, 192, 384, 768])
+@pytest.mark.parametrize("d", [1, 3, 9])
+def test_dac_stage_shapes(S, C, d):
+    T = 1000 if C >= 384 else 2500  # ragged: not a multiple of 128
+    x, alpha, W, b = rand_case(1, C, C, T, seed=C + d)
+    y = torch.full((1, C, T), float("nan"), device="cuda")
+    S.fused_snake_conv1d(x.cuda(), alpha.cuda(), W.cuda(), b.cuda(), padding=3 * d, dilation=d, out=y)
+    torch.cuda.synchronize()
+    truth = O.snake_conv1d_ref(x.numpy(), alpha.numpy(), W.numpy(), b.numpy(), padding=3 * d, dilation=d)
+    check(y.cpu().numpy(), truth)
+
+
+@pytest.mark.parametrize("B,Cin,Cout,T,pad,d", [
+    (2, 48, 80, 333, 3, 1),     # channel counts not multiples of 64 / 32
+    (3, 16, 16, 129, 0, 2),     # no padding: Tout < T
+    (1, 64, 272, 300, 9, 3),    # Cout > 256: two output tiles
+    (1, 32, 32, 5, 27, 9),      # T shorter than the halo
+])
+def test_odd_shapes(S, B, Cin, Cout, T, pad, d):
+    x, alpha, W, b = rand_case(B, Cin, Cout, T, seed=T)
+    y = S.fused_snake_conv1d(x.cuda(), alpha.cuda(), W.cuda(), b.cuda(), padding=pad, dilation=d)
+    torch.cuda.synchronize()
+    truth = O.snake_conv1d_ref(x.numpy(), alpha.numpy(), W.numpy(), b.numpy(), padding=pad, dilation=d)
+    check(y.cpu().numpy(), truth)
+
+
+def test_no_bias_and_large_activations(S):
+    x, alpha, W, b = rand_case(1, 64, 64, 700, seed=9, xscale=6.0)
+    y = S.fused_snake_conv1d(x.cuda(), alpha.cuda(), W.cuda(), None, padding=9, dilation=3)
+    torch.cuda.synchronize()
+    truth = O.snake_conv1d_ref(x.numpy(), alpha.numpy(), W.numpy(), None, padding=9, dilation=3)
+    y = y.cpu().numpy()
+    # larger |y| here: hold the same relative bound
+    assert np.abs(y - truth).max() <= MAX_ABS * max(1.0, np.abs(truth).max())
+    assert O.cosine(y, truth) >= COS_MIN
+
+
+def test_full_size_stage_vs_torch_fp32(S):
+    """BASELINE's largest stage at full length, checked against cuDNN fp32
+    (TF32 off) -- the oracle is too slow at 441k samples x 96 channels."""
+    C, T, d = 96, 441344, 9
+    x, alpha, W, b = S.dac_stage_inputs(C, T, seed=3)
+    y = S.fused_snake_conv1d(x, alpha, W, b, padding=3 * d, dilation=d)
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = S.reference_snake_conv1d(x.double(), alpha.double(), W.double(), b.double(), padding=3 * d,
+                                   dilation=d)
+    torch.cuda.synchronize()
+    err = (y.double() - ref).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(y.double().flatten(), ref.flatten(), dim=0).item()
+    assert err <= MAX_ABS and cos >= COS_MIN, (err, cos)
+
+
+def test_validation_errors(S):
+    x = torch.randn(1, 4, 16, device="cuda")
+    with pytest.raises(ValueError):
+        S.fused_snake_conv1d(x, torch.ones(4, device="cuda"), torch.randn(3, 2, 3, device="cuda"),
+                             torch.zeros(3, device="cuda"))
+    with pytest.raises(ValueError):
+        S.fused_snake_conv1d(x, torch.ones(3, device="cuda"), torch.randn(3, 4, 3, device="cuda"),
+                             torch.zeros(3, device="cuda"))
+    with pytest.raises(ValueError):
+        S.fused_snake_conv1d(x, torch.ones(4, device="cuda"), torch.randn(3, 4, 3, device="cuda"),
+                             torch.zeros(5, device="cuda"))
+
+
+def test_no_device_timeouts(cuda_lib):
+    assert cuda_lib.sn_device_status(1, None) == 0
