@@ -346,6 +346,66 @@ def run_ours(args):
     return 0
 
 
+def run_case(args):
+    """One hot-path kernel on one shape, timed with CUDA events (also the
+    command behind every ncu capture summarised in profiles/)."""
+    dist_setup(1)
+    shape = [int(v) for v in args.shape.split("x")] if args.shape else []
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = {"case": args.case, "shape": args.shape}
+    if args.case == "gemv":
+        from sonata_b200.kernels import gemv as G
+        N, K, M = (shape + [8512, 2048, 1][len(shape):])[:3]
+        Ws = [(torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(8)]
+        x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        run = lambda: [G.gemv(x, W, out=y) for W in Ws]
+        per = len(Ws)
+        algo = (N * K + M * K + M * N) * 2
+    elif args.case == "snake":
+        from sonata_b200.kernels import fused_snake_conv as S
+        C, T, d = (shape + [384, 55168, 3][len(shape):])[:3]
+        x, al, W, b = S.dac_stage_inputs(C, T)
+        y = torch.empty_like(x)
+        run = lambda: S.fused_snake_conv1d(x, al, W, b, padding=3 * d, dilation=d, out=y)
+        per = 1
+        algo = 2 * C * C * 7 * T  # useful flops
+    elif args.case == "head":
+        from sonata_b200.kernels import bmm as Bm
+        (B,) = (shape + [64])[:1]
+        head = Bm.CodebookHead((torch.randn(9, 2048, 1025, device="cuda") * 0.02).to(torch.bfloat16))
+        h = torch.randn(9, B, 2048, device="cuda").to(torch.bfloat16)
+        o = torch.empty(9, B, 1025, device="cuda")
+        run = lambda: head(h, out=o)
+        per = 1
+        algo = 9 * 2048 * 1025 * 2 + 9 * B * 2048 * 2 + 9 * B * 1025 * 4
+    elif args.case == "ssd":
+        from sonata_b200.kernels import bmm as Bm
+        (L,) = (shape + [4096])[:1]
+        C = torch.randn(1, L, 1, 128, device="cuda").to(torch.bfloat16)
+        Bt = torch.randn(1, L, 1, 128, device="cuda").to(torch.bfloat16)
+        nch = (L + 255) // 256
+        o = torch.empty(1, nch, 1, 256, 256, device="cuda")
+        run = lambda: Bm.launch_bmm(C, Bt, 1, L, 1, 128, 256, nch, o)
+        per = 1
+        algo = 2 * L * 128 * 2 + nch * 256 * 256 * 4
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(args.steps):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(e) * 1e3 / (args.steps * per)
+    out["us_per_call"] = round(us, 3)
+    out["algorithmic_units_per_s"] = round(algo / (us * 1e-6), 1)
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def run_reference(args):
     """The reference's own CPU path (torch F.linear in bf16) on the host cores."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -397,11 +457,16 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-snake", action="store_true")
+    ap.add_argument("--case", choices=["gemv", "snake", "head", "ssd"], default=None,
+                    help="run one kernel on one shape (profiling / microbenchmark)")
+    ap.add_argument("--shape", default="", help="e.g. 8512x2048x1 (gemv N x K x M), 384x55168x3 (snake C x T x d)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.case:
+        return run_case(args)
     return run_ours(args)
 
 
