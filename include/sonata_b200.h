@@ -34,6 +34,7 @@ extern "C" {
 #define SN_ERR_LAUNCH (-4)           /* the CUDA launch itself failed */
 #define SN_ERR_DEVICE (-5)           /* current device is not sm_100 */
 #define SN_ERR_TIMEOUT (-6)          /* a bounded device-side wait ran out */
+#define SN_ERR_SCRATCH_LIMIT (-7)    /* needs more scratch than the allocation-free entry point holds */
 
 /* ---- dtype codes for outputs ---- */
 #define SN_DTYPE_BF16 0
@@ -144,6 +145,30 @@ size_t sn_snake_conv1d_workspace_size(int Cin, int Cout, int K);
 int sn_snake_conv1d(const float *x, const float *alpha, const float *W, const float *bias, float *y, int B,
                     int Cin, int Cout, int T, int K, int stride, int padding, int dilation, float eps,
                     void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Allocation-free Snake + Conv1d.  No counterpart in the reference.
+ *
+ * For callers that must not allocate device memory at all: a host that runs
+ * the vocoder from a real-time audio callback (cudaMalloc can block and
+ * synchronise the whole device), or an application that loads this library
+ * through the C ABI from another runtime that gives it no CUDA allocator.
+ * Same computation and arguments as sn_snake_conv1d minus the workspace: the
+ * packed weights go to a static device array of
+ * SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH bytes (16 MiB, enough for the largest
+ * DAC unit, Cin = Cout = 768, K = 7) that every GPU loading the library keeps
+ * until the process exits.  Problems with Cin * Cout * K * 4 bytes of packed
+ * weights above that limit return SN_ERR_SCRATCH_LIMIT.  The function itself
+ * calls no cudaMalloc / cudaFree.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, with that device current), so
+ * make that first call before capturing any stream.  All calls share the one
+ * array: calls that may overlap on the GPU (other streams, other threads) race
+ * on it and must be ordered by the caller.
+ */
+#define SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH (16u * 1024u * 1024u)
+int sn_snake_conv1d_noalloc(const float *x, const float *alpha, const float *W, const float *bias, float *y,
+                            int B, int Cin, int Cout, int T, int K, int stride, int padding, int dilation,
+                            float eps, void *stream);
 
 #ifdef __cplusplus
 }

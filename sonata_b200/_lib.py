@@ -41,6 +41,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_snake_conv1d_workspace_size": ([_I, _I, _I], ctypes.c_size_t),
     "sn_snake_conv1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P, ctypes.c_size_t,
                          _P], _I),
+    "sn_snake_conv1d_noalloc": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P], _I),
 }
 
 _lib = None

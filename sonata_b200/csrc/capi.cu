@@ -33,6 +33,8 @@ const char* sn_status_string(int status) {
     case SN_ERR_LAUNCH: return "CUDA kernel launch failed";
     case SN_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
     case SN_ERR_TIMEOUT: return "a bounded device-side wait ran out";
+    case SN_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the allocation-free entry point's static array holds";
     default: return "unknown status";
   }
 }

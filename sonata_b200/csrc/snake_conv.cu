@@ -28,6 +28,7 @@
 #include "tc.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace sn {
 namespace {
@@ -381,6 +382,48 @@ int sn_snake_conv1d(const float* x, const float* alpha, const float* W, const fl
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 32));
   return sn::launch(sn::snake_conv_simt_kernel, dim3(blocks), dim3(256), 0, st, false, x, alpha, W, bias, y, B, Cin,
                     Cout, T, Tout, K, stride, padding, dilation, eps);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Its scratch (the packed bf16 hi/lo weights) lives
+// in this file-scope device array instead of a caller-provided workspace; the
+// array exists once per GPU that loads the library, for the life of the
+// process.  Host code cannot use the array's name as a device address: the
+// address is looked up with cudaGetSymbolAddress, once per device, on the
+// first call made while that device is current.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_snake_noalloc_scratch[SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH];
+
+static void* snake_noalloc_scratch() {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_snake_noalloc_scratch) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+int sn_snake_conv1d_noalloc(const float* x, const float* alpha, const float* W, const float* bias, float* y, int B,
+                            int Cin, int Cout, int T, int K, int stride, int padding, int dilation, float eps,
+                            void* stream) {
+  if (Cin < 1 || Cout < 1 || K < 1) return SN_ERR_INVALID_ARGUMENT;
+  if (sn_snake_conv1d_workspace_size(Cin, Cout, K) > SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH)
+    return SN_ERR_SCRATCH_LIMIT;
+  void* scratch = snake_noalloc_scratch();
+  if (!scratch) return SN_ERR_DEVICE;
+  return sn_snake_conv1d(x, alpha, W, bias, y, B, Cin, Cout, T, K, stride, padding, dilation, eps, scratch,
+                         SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH, stream);
 }
 
 }  // extern "C"

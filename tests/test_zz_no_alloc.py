@@ -1,0 +1,66 @@
+"""The allocation-free Snake + Conv1d entry point, called through the C ABI.
+
+sn_snake_conv1d_noalloc exists for callers that cannot allocate device
+memory -- a real-time audio thread that must never block in cudaMalloc, or a
+host runtime that loads the library over the C ABI without a CUDA allocator.
+It keeps its packed-weight scratch in a static device array instead of a
+caller workspace.  These tests check that it agrees with the regular entry
+point (the workspace-taking sn_snake_conv1d behind fused_snake_conv1d) within
+the same tolerance the other Snake+Conv1d tests use, on two calls in a row
+with different weights -- the shared array must carry the second call's
+weights, not the first's -- and that oversized problems are refused.
+
+This file is collected last on purpose (tests/test_zz_*): a failure here does
+not hide any other test in a run that stops at the first failure.
+"""
+import ctypes
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999
+MAX_ABS = 2e-3
+
+
+def _case(C, T, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(1, C, T, device="cuda", generator=g)
+    alpha = torch.rand(C, device="cuda", generator=g) + 0.5
+    W = torch.randn(C, C, 7, device="cuda", generator=g) / math.sqrt(7 * C)
+    b = torch.randn(C, device="cuda", generator=g)
+    return x, alpha, W, b
+
+
+def _noalloc(lib, x, alpha, W, b, y, d):
+    B, Cin, T = x.shape
+    Cout, _, K = W.shape
+    return lib.sn_snake_conv1d_noalloc(x.data_ptr(), alpha.data_ptr(), W.data_ptr(), b.data_ptr(), y.data_ptr(), B,
+                                       Cin, Cout, T, K, 1, 3 * d, d, ctypes.c_float(1e-9),
+                                       torch.cuda.current_stream().cuda_stream)
+
+
+def test_noalloc_matches_regular_entry_point_twice(cuda_lib):
+    from sonata_b200.kernels import fused_snake_conv as S
+    for call, (C, T, d) in enumerate([(768, 1500, 3), (384, 2200, 9)]):
+        x, alpha, W, b = _case(C, T, seed=100 + call)
+        y = torch.full_like(x, float("nan"))
+        assert _noalloc(cuda_lib, x, alpha, W, b, y, d) == 0
+        ref = S.fused_snake_conv1d(x, alpha, W, b, padding=3 * d, dilation=d)
+        torch.cuda.synchronize()
+        assert torch.isfinite(y).all()
+        err = (y - ref).abs().max().item()
+        cos = torch.nn.functional.cosine_similarity(y.flatten().double(), ref.flatten().double(), dim=0).item()
+        assert err <= MAX_ABS and cos >= COS_MIN, (call, err, cos)
+    assert cuda_lib.sn_device_status(1, None) == 0
+
+
+def test_noalloc_refuses_problems_beyond_its_scratch(cuda_lib):
+    # 1024 x 1024 x 7 packed weights need 28 MiB > the 16 MiB static array;
+    # refused on the host before any device work
+    p = ctypes.c_void_p(16)
+    rc = cuda_lib.sn_snake_conv1d_noalloc(p, p, p, p, p, 1, 1024, 1024, 128, 7, 1, 3, 1, ctypes.c_float(1e-9), None)
+    assert rc == -7
+    assert b"scratch" in cuda_lib.sn_status_string(rc)
