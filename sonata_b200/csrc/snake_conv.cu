@@ -28,15 +28,19 @@
 #include "tc.cuh"
 
 #include <algorithm>
+#include <climits>
+#include <cstdint>
 #include <mutex>
 
 namespace sn {
 namespace {
 
 constexpr int kScProducerWarps = 8;
-constexpr int kScThreads = (2 + kScProducerWarps) * 32;  // TMA, MMA, 8 producers
+constexpr int kScEpilogueWarps = 4;
+constexpr int kScThreads = (2 + kScProducerWarps + kScEpilogueWarps) * 32;  // TMA, MMA, producers, epilogue
 constexpr int kScWStages = 2;
 constexpr int kMaxTaps = 7;
+constexpr int kMaxRowIters = 7;  // activation rows per chunk <= 32 * 7 = 224 ((K-1)*d <= 72)
 
 struct ScParams {
   const float* x;      // [B, Cin, T]
@@ -45,11 +49,12 @@ struct ScParams {
   float* y;            // [B, Cout, Tout]
   int B, Cin, Cout, T, Tout, K, pad, dil;
   float eps;
-  int nt;              // output channels per tile (UMMA N)
-  int ntiles_o, ntiles_t;
+  int nt;              // output channels per tile (UMMA N, multiple of 32)
+  int ntiles_o, ntiles_t, ntiles;
   int rows;            // activation rows per chunk (128 + (K-1)*d, rounded up to 8)
   uint32_t a_bytes;    // one activation plane (rows * 128)
   uint32_t w_bytes;    // one weight plane (nt * 128)
+  uint32_t tcols;      // TMEM columns per accumulator buffer
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -62,11 +67,17 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return a | (b << 16);
 }
 
+// Persistent: CTA c handles tiles c, c + G, c + 2G, ...; every role walks its
+// own sequence (tiles x chunks x taps) and every mbarrier phase in order.
+//   warp 0      TMA of the weight planes, one (hi, lo) pair per (chunk, tap)
+//   warp 1      TMEM owner; lane 0 issues the MMAs into accumulator (j & 1)
+//   warps 2-9   snake producers (activation buffer g & 1 for chunk g)
+//   warps 10-13 epilogue: drain accumulator (j & 1) while tile j+1 computes
 __global__ void __launch_bounds__(kScThreads, 1)
     snake_conv_mma_kernel(const __grid_constant__ CUtensorMap mapW, const ScParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // layout: [A buf0 hi][A buf0 lo][A buf1 hi][A buf1 lo][W stage0 hi][lo][W stage1 hi][lo][barriers]
+  // layout: [A0 hi][A0 lo][A1 hi][A1 lo][W0 hi][W0 lo][W1 hi][W1 lo][barriers]
   uint8_t* abuf = smem;
   uint8_t* wbuf = smem + 4 * p.a_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(wbuf + 2 * kScWStages * p.w_bytes);
@@ -74,42 +85,50 @@ __global__ void __launch_bounds__(kScThreads, 1)
   uint64_t* a_empty = bars + 2;
   uint64_t* w_full = bars + 4;
   uint64_t* w_empty = w_full + kScWStages;
-  uint64_t* done = w_empty + kScWStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* t_full = w_empty + kScWStages;
+  uint64_t* t_empty = t_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(t_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int u = blockIdx.x;
-  const int ot = u % p.ntiles_o;
-  u /= p.ntiles_o;
-  const int tt = u % p.ntiles_t;
-  const int b = u / p.ntiles_t;
-  const int o0 = ot * p.nt, t0 = tt * 128;
   const int nchunks = (p.Cin + 63) / 64;
-  const uint32_t tcols = tc::tmem_cols_for(p.nt);
+  const int my_tiles = p.ntiles > static_cast<int>(blockIdx.x)
+                           ? (p.ntiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                           : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(a_full + i, kScProducerWarps);
       mbar_init(a_empty + i, 1);
+      mbar_init(t_full + i, 1);
+      mbar_init(t_empty + i, kScEpilogueWarps);
     }
     for (int i = 0; i < kScWStages; ++i) {
       mbar_init(w_full + i, 1);
       mbar_init(w_empty + i, 1);
     }
-    mbar_init(done, 1);
     fence_barrier_init();
     tc::prefetch_map(&mapW);
   }
-  if (warp == 1) tc::tmem_alloc(tmem_slot, tcols);
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 2 * p.tcols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
+  auto tile_coords = [&](int j, int& b, int& t0, int& o0) {
+    int u = static_cast<int>(blockIdx.x) + j * static_cast<int>(gridDim.x);
+    const int ot = u % p.ntiles_o;
+    u /= p.ntiles_o;
+    const int tt = u % p.ntiles_t;
+    b = u / p.ntiles_t;
+    t0 = tt * 128;
+    o0 = ot * p.nt;
+  };
+
   if (warp == 0) {
-    // ---------------- weight TMA: per (chunk, tap) the hi and lo planes ------
+    // ---------------- weight TMA ----------------
     if (lane == 0) {
-      const int total = nchunks * p.K;
+      const int total = my_tiles * nchunks * p.K;
       int q = 0;
       for (; q < total; ++q) {
         const int s = q % kScWStages, k = q / kScWStages;
@@ -117,13 +136,17 @@ __global__ void __launch_bounds__(kScThreads, 1)
           record_status(SN_ERR_TIMEOUT);
           break;
         }
-        const int c = q / p.K, tap = q - c * p.K;
+        const int tap = q % p.K;
+        const int c = (q / p.K) % nchunks;
+        const int j = q / (p.K * nchunks);
+        int b, t0, o0;
+        tile_coords(j, b, t0, o0);
         uint8_t* dst = wbuf + static_cast<size_t>(s) * 2 * p.w_bytes;
         mbar_arrive_expect_tx(w_full + s, 2 * p.w_bytes);
         tc::tma_load_3d(dst, &mapW, c * 64, o0, tap * 2 + 0, w_full + s);
         tc::tma_load_3d(dst + p.w_bytes, &mapW, c * 64, o0, tap * 2 + 1, w_full + s);
       }
-      if (q < total) {
+      if (q < total) {  // error path: let issued copies land before exit
         for (int j = (q > kScWStages ? q - kScWStages : 0); j < q; ++j)
           mbar_wait_bounded(w_full + j % kScWStages, (j / kScWStages) & 1);
       }
@@ -133,115 +156,147 @@ __global__ void __launch_bounds__(kScThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_bf16_f32(128, p.nt);
       bool ok = true;
-      int q = 0;
-      for (int c = 0; c < nchunks && ok; ++c) {
-        const int ab = c & 1;
-        if (!mbar_wait_bounded(a_full + ab, (c >> 1) & 1)) {
+      int q = 0, g = 0;
+      for (int j = 0; j < my_tiles && ok; ++j) {
+        const int tb = j & 1;
+        if (j >= 2 && !mbar_wait_bounded(t_empty + tb, ((j >> 1) - 1) & 1)) {
           record_status(SN_ERR_TIMEOUT);
-          ok = false;
           break;
         }
         tc::fence_after_sync();
-        const int ksteps = min(4, (p.Cin - c * 64) / 16);  // 16-channel MMA steps in this chunk
-        const uint64_t a_hi = tc::smem_desc_sw128(abuf + (2 * ab + 0) * p.a_bytes);
-        const uint64_t a_lo = tc::smem_desc_sw128(abuf + (2 * ab + 1) * p.a_bytes);
-        for (int tap = 0; tap < p.K; ++tap, ++q) {
-          const int s = q % kScWStages;
-          if (!mbar_wait_bounded(w_full + s, (q / kScWStages) & 1)) {
+        const uint32_t acc_tmem = tmem + static_cast<uint32_t>(tb) * p.tcols;
+        for (int c = 0; c < nchunks && ok; ++c, ++g) {
+          const int ab = g & 1;
+          if (!mbar_wait_bounded(a_full + ab, (g >> 1) & 1)) {
             record_status(SN_ERR_TIMEOUT);
             ok = false;
             break;
           }
           tc::fence_after_sync();
-          const uint8_t* w = wbuf + static_cast<size_t>(s) * 2 * p.w_bytes;
-          const uint64_t w_hi = tc::smem_desc_sw128(w), w_lo = tc::smem_desc_sw128(w + p.w_bytes);
-          const uint64_t shift = static_cast<uint64_t>(tap * p.dil * 128) >> 4;  // tap rows further on
-          for (int kk = 0; kk < ksteps; ++kk) {
-            const uint32_t acc0 = (c | tap | kk) != 0;
-            tc::mma_bf16(tmem, a_hi + shift + 2 * kk, w_hi + 2 * kk, idesc, acc0);
-            tc::mma_bf16(tmem, a_lo + shift + 2 * kk, w_hi + 2 * kk, idesc, 1);
-            tc::mma_bf16(tmem, a_hi + shift + 2 * kk, w_lo + 2 * kk, idesc, 1);
+          const int ksteps = min(4, (p.Cin - c * 64) / 16);  // 16-channel MMA steps in this chunk
+          const uint64_t a_hi = tc::smem_desc_sw128(abuf + (2 * ab + 0) * p.a_bytes);
+          const uint64_t a_lo = tc::smem_desc_sw128(abuf + (2 * ab + 1) * p.a_bytes);
+          for (int tap = 0; tap < p.K; ++tap, ++q) {
+            const int s = q % kScWStages;
+            if (!mbar_wait_bounded(w_full + s, (q / kScWStages) & 1)) {
+              record_status(SN_ERR_TIMEOUT);
+              ok = false;
+              break;
+            }
+            tc::fence_after_sync();
+            const uint8_t* w = wbuf + static_cast<size_t>(s) * 2 * p.w_bytes;
+            const uint64_t w_hi = tc::smem_desc_sw128(w), w_lo = tc::smem_desc_sw128(w + p.w_bytes);
+            const uint64_t shift = static_cast<uint64_t>(tap * p.dil * 128) >> 4;  // tap rows further on
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const uint32_t acc0 = (c | tap | kk) != 0;
+              tc::mma_bf16(acc_tmem, a_hi + shift + 2 * kk, w_hi + 2 * kk, idesc, acc0);
+              tc::mma_bf16(acc_tmem, a_lo + shift + 2 * kk, w_hi + 2 * kk, idesc, 1);
+              tc::mma_bf16(acc_tmem, a_hi + shift + 2 * kk, w_lo + 2 * kk, idesc, 1);
+            }
+            tc::mma_commit(w_empty + s);
           }
-          tc::mma_commit(w_empty + s);
+          tc::mma_commit(a_empty + ab);
         }
-        tc::mma_commit(a_empty + ab);
+        tc::mma_commit(t_full + tb);
       }
-      tc::mma_commit(done);
     }
-  } else {
-    // ---------------- snake producers, then the epilogue ----------------
-    const int pw = warp - 2;  // 0..7: the 8-channel group of every chunk this warp fills
-    const float* xb = p.x + static_cast<int64_t>(b) * p.Cin * p.T;
-    const int tin0 = t0 - p.pad;  // input time of activation row 0
-    bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
-      const int ab = c & 1;
-      if (c >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(a_empty + ab, ((c >> 1) - 1) & 1))) {
-        record_status(SN_ERR_TIMEOUT);
-        ok = false;
-        break;
-      }
-      uint8_t* ahi = abuf + (2 * ab + 0) * p.a_bytes;
-      uint8_t* alo = abuf + (2 * ab + 1) * p.a_bytes;
-      const int i0 = c * 64 + pw * 8;  // first input channel of this warp's group
-      float al[8], inv[8];
+  } else if (warp < 2 + kScProducerWarps) {
+    // ---------------- snake producers ----------------
+    const int pw = warp - 2;  // the 8-channel group of every chunk this warp fills
+    int g = 0;
+    for (int j = 0; j < my_tiles; ++j) {
+      int b, t0, o0;
+      tile_coords(j, b, t0, o0);
+      const float* xb = p.x + static_cast<int64_t>(b) * p.Cin * p.T;
+      const int tin0 = t0 - p.pad;  // input time of activation row 0
+      for (int c = 0; c < nchunks; ++c, ++g) {
+        const int ab = g & 1;
+        const int i0 = c * 64 + pw * 8;  // first input channel of this warp's group
+        // issue every x load of this chunk before the first use (memory-level
+        // parallelism: 8 channels x up to 7 rows per lane in flight)
+        float v[kMaxRowIters][8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int i = i0 + e;
-        al[e] = i < p.Cin ? p.alpha[i] : 0.f;
-        inv[e] = 1.0f / (al[e] + p.eps);
-      }
-      for (int r = lane; r < p.rows; r += 32) {
-        const int tin = tin0 + r;
-        const bool in_t = tin >= 0 && tin < p.T;
-        float hi[8], lo[8];
+        for (int it = 0; it < kMaxRowIters; ++it) {
+          const int r = lane + 32 * it;
+          const int tin = tin0 + r;
+          const bool in_t = r < p.rows && tin >= 0 && tin < p.T;
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.T + tin) : 0.f;
+        }
+        float al[8], inv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int i = i0 + e;
-          float v = 0.f;
-          if (in_t && i < p.Cin) v = xb[static_cast<int64_t>(i) * p.T + tin];
-          const float sv = __sinf(al[e] * v);
-          const float s = fmaf(sv * sv, inv[e], v);  // snake(v); snake(0) == 0
-          hi[e] = __bfloat162float(__float2bfloat16_rn(s));
-          lo[e] = s - hi[e];
+          al[e] = (i0 + e < p.Cin) ? __ldg(p.alpha + i0 + e) : 0.f;
+          inv[e] = 1.0f / (al[e] + p.eps);
         }
-        // 16-byte chunk pw of row r, XOR-swizzled with the row's low 3 bits
-        const uint32_t off = static_cast<uint32_t>(r) * 128u + ((static_cast<uint32_t>(pw) ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(ahi + off) = make_uint4(pack_bf16x2(hi[0], hi[1]), pack_bf16x2(hi[2], hi[3]),
-                                                          pack_bf16x2(hi[4], hi[5]), pack_bf16x2(hi[6], hi[7]));
-        *reinterpret_cast<uint4*>(alo + off) = make_uint4(pack_bf16x2(lo[0], lo[1]), pack_bf16x2(lo[2], lo[3]),
-                                                          pack_bf16x2(lo[4], lo[5]), pack_bf16x2(lo[6], lo[7]));
+        if (g >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(a_empty + ab, ((g >> 1) - 1) & 1))) {
+          record_status(SN_ERR_TIMEOUT);
+          j = my_tiles;  // unwind
+          break;
+        }
+        uint8_t* ahi = abuf + (2 * ab + 0) * p.a_bytes;
+        uint8_t* alo = abuf + (2 * ab + 1) * p.a_bytes;
+#pragma unroll
+        for (int it = 0; it < kMaxRowIters; ++it) {
+          const int r = lane + 32 * it;
+          if (r < p.rows) {
+            float hi[8], lo[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float sv = __sinf(al[e] * v[it][e]);
+              const float s = fmaf(sv * sv, inv[e], v[it][e]);  // snake(v); snake(0) == 0
+              hi[e] = __bfloat162float(__float2bfloat16_rn(s));
+              lo[e] = s - hi[e];
+            }
+            // 16-byte chunk pw of row r, XOR-swizzled with the row's low 3 bits
+            const uint32_t off =
+                static_cast<uint32_t>(r) * 128u + ((static_cast<uint32_t>(pw) ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(ahi + off) = make_uint4(pack_bf16x2(hi[0], hi[1]), pack_bf16x2(hi[2], hi[3]),
+                                                              pack_bf16x2(hi[4], hi[5]), pack_bf16x2(hi[6], hi[7]));
+            *reinterpret_cast<uint4*>(alo + off) = make_uint4(pack_bf16x2(lo[0], lo[1]), pack_bf16x2(lo[2], lo[3]),
+                                                              pack_bf16x2(lo[4], lo[5]), pack_bf16x2(lo[6], lo[7]));
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a_full + ab);
       }
-      fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
-      __syncwarp();
-      if (lane == 0) mbar_arrive(a_full + ab);
     }
-    // epilogue: a warp may only read the TMEM lane quarter (warp id % 4); warps
-    // 2-5 drain the first half of the columns, warps 6-9 the second half
-    if (ok && __all_sync(0xffffffffu, mbar_wait_bounded(done, 0))) {
+  } else {
+    // ---------------- epilogue ----------------
+    const int q4 = warp & 3;  // a warp may only read TMEM lanes 32*(warp id % 4) ..
+    for (int j = 0; j < my_tiles; ++j) {
+      const int tb = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(t_full + tb, (j >> 1) & 1))) {
+        record_status(SN_ERR_TIMEOUT);
+        break;
+      }
       tc::fence_after_sync();
-      const int q4 = warp & 3, half = pw >> 2;
+      int b, t0, o0;
+      tile_coords(j, b, t0, o0);
       const int t = t0 + q4 * 32 + lane;
-      const int cols = p.nt / 2;  // nt is a multiple of 32 here
       float* yb = p.y + static_cast<int64_t>(b) * p.Cout * p.Tout;
-      for (int cc = half * cols; cc < (half + 1) * cols; cc += 16) {
-        float v[16];
-        tc::tmem_ld16(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + cc, v);
+      const uint32_t base = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(tb) * p.tcols;
+      for (int cc = 0; cc < p.nt; cc += 16) {
+        float vv[16];
+        tc::tmem_ld16(base + cc, vv);
         if (t < p.Tout) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int o = o0 + cc + j;
-            if (o < p.Cout) yb[static_cast<int64_t>(o) * p.Tout + t] = v[j] + (p.bias ? p.bias[o] : 0.f);
+          for (int e = 0; e < 16; ++e) {
+            const int o = o0 + cc + e;
+            if (o < p.Cout) yb[static_cast<int64_t>(o) * p.Tout + t] = vv[e] + (p.bias ? __ldg(p.bias + o) : 0.f);
           }
         }
       }
-    } else if (ok) {
-      record_status(SN_ERR_TIMEOUT);
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(t_empty + tb);
     }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) tc::tmem_dealloc(tmem, tcols);
+  if (warp == 1) tc::tmem_dealloc(tmem, 2 * p.tcols);
 }
 
 // W fp32 [Cout, Cin, K] -> bf16 planes Wp[(k*2 + h)][o][i], h = 0 hi, 1 lo.
@@ -298,11 +353,23 @@ bool fast_path_ok(int Cin, int Cout, int K, int stride, int dil, int Tout) {
          Cout % 16 == 0 && Tout >= 1;
 }
 
-int out_tile(int Cout) {
-  // output-channel tile: <= 256, a multiple of 32, splitting Cout evenly
-  const int tiles = (Cout + 255) / 256;
-  int nt = (Cout + tiles - 1) / tiles;
-  return (nt + 31) / 32 * 32;
+// Output-channel tile (UMMA N, a multiple of 32, <= 256): the width that
+// minimises (tiles per SM) x (width + 64) over a persistent grid of `sms`
+// CTAs.  The 64 stands for the per-tile cost that does not scale with the
+// width (snake re-evaluated for every output tile, prologue, epilogue);
+// ties go to the wider tile.
+int out_tile(int Cout, int64_t time_tiles, int sms) {
+  int best = 32;
+  int64_t best_cost = INT64_MAX;
+  for (int nt = std::min(256, (Cout + 31) / 32 * 32); nt >= 32; nt -= 32) {
+    const int64_t tiles = time_tiles * ((Cout + nt - 1) / nt);
+    const int64_t cost = (tiles + sms - 1) / sms * (nt + 64);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = nt;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -349,15 +416,20 @@ int sn_snake_conv1d(const float* x, const float* alpha, const float* W, const fl
     p.pad = padding;
     p.dil = dilation;
     p.eps = eps;
-    p.nt = sn::out_tile(Cout);
-    p.ntiles_o = (Cout + p.nt - 1) / p.nt;
     p.ntiles_t = (Tout + 127) / 128;
+    const int sms = sn::sm_count();
+    p.nt = sn::out_tile(Cout, static_cast<int64_t>(B) * p.ntiles_t, sms);
+    p.ntiles_o = (Cout + p.nt - 1) / p.nt;
+    p.tcols = sn::tc::tmem_cols_for(p.nt);
     p.rows = (128 + (K - 1) * dilation + 7) / 8 * 8;
     p.a_bytes = static_cast<uint32_t>(p.rows) * 128;
     p.w_bytes = static_cast<uint32_t>(p.nt) * 128;
     const size_t smem = 1024 + 4 * static_cast<size_t>(p.a_bytes) +
                         2 * sn::kScWStages * static_cast<size_t>(p.w_bytes) + 256;
-    if (smem <= 227 * 1024 && static_cast<int64_t>(B) * p.ntiles_t * p.ntiles_o < (int64_t(1) << 31)) {
+    const int64_t ntiles64 = static_cast<int64_t>(B) * p.ntiles_t * p.ntiles_o;
+    p.ntiles = static_cast<int>(std::min<int64_t>(ntiles64, INT32_MAX));
+    if (smem <= 227 * 1024 && ntiles64 < (int64_t(1) << 31) && p.rows <= 32 * sn::kMaxRowIters &&
+        2 * p.tcols <= 512) {
       __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
       const int64_t tot = static_cast<int64_t>(Cout) * Cin * K;
       const int blocks = static_cast<int>(std::min<int64_t>((tot + 255) / 256, 148 * 8));
@@ -371,8 +443,8 @@ int sn_snake_conv1d(const float* x, const float* alpha, const float* W, const fl
       if (sn::tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box)) {
         if (cudaFuncSetAttribute(sn::snake_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem)) == cudaSuccess) {
-          const int units = B * p.ntiles_t * p.ntiles_o;
-          return sn::launch(sn::snake_conv_mma_kernel, dim3(units), dim3(sn::kScThreads), smem, st, false, mapW, p);
+          const int grid = std::min(p.ntiles, sms);
+          return sn::launch(sn::snake_conv_mma_kernel, dim3(grid), dim3(sn::kScThreads), smem, st, false, mapW, p);
         }
         cudaGetLastError();
       }
