@@ -394,6 +394,51 @@ __device__ __forceinline__ void chunk_fma2(const uint4& w, const __nv_bfloat16* 
   }
 }
 
+// Same as chunk_fma2 with the x words already in registers: xv[m][0] holds
+// the 16 bytes of x at chunk idx (bf16 weights), xv[m][0..1] the two planes'
+// halves (8-bit weights).
+template <int WK, int MT>
+__device__ __forceinline__ void chunk_fma2_x(const uint4& w, const uint4 (&xv)[MT][2], float2 (&acc)[MT][2]) {
+  if constexpr (WK == W_BF16) {
+    const float2 w0 = make_float2(bf16lo(w.x), bf16hi(w.x));
+    const float2 w1 = make_float2(bf16lo(w.y), bf16hi(w.y));
+    const float2 w2 = make_float2(bf16lo(w.z), bf16hi(w.z));
+    const float2 w3 = make_float2(bf16lo(w.w), bf16hi(w.w));
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const uint4& x = xv[m][0];
+      acc[m][0] = __ffma2_rn(w0, make_float2(bf16lo(x.x), bf16hi(x.x)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(w1, make_float2(bf16lo(x.y), bf16hi(x.y)), acc[m][1]);
+      acc[m][0] = __ffma2_rn(w2, make_float2(bf16lo(x.z), bf16hi(x.z)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(w3, make_float2(bf16lo(x.w), bf16hi(x.w)), acc[m][1]);
+    }
+  } else {
+    float2 v[8];
+    dequant16<WK>(w, v);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const uint4& xa = xv[m][0];
+      const uint4& xb = xv[m][1];
+      acc[m][0] = __ffma2_rn(v[0], make_float2(bf16lo(xa.x), bf16hi(xa.x)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(v[1], make_float2(bf16lo(xa.y), bf16hi(xa.y)), acc[m][1]);
+      acc[m][0] = __ffma2_rn(v[2], make_float2(bf16lo(xa.z), bf16hi(xa.z)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(v[3], make_float2(bf16lo(xa.w), bf16hi(xa.w)), acc[m][1]);
+      acc[m][0] = __ffma2_rn(v[4], make_float2(bf16lo(xb.x), bf16hi(xb.x)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(v[5], make_float2(bf16lo(xb.y), bf16hi(xb.y)), acc[m][1]);
+      acc[m][0] = __ffma2_rn(v[6], make_float2(bf16lo(xb.z), bf16hi(xb.z)), acc[m][0]);
+      acc[m][1] = __ffma2_rn(v[7], make_float2(bf16lo(xb.w), bf16hi(xb.w)), acc[m][1]);
+    }
+  }
+}
+
+// Chunks a consumer lane loads before its first FMA: as many independent
+// 16-byte shared-memory loads in flight as the register budget allows.
+template <int WK, int MT>
+struct Batch {
+  static constexpr int XW = (WK == W_BF16) ? 1 : 2;  // 16-byte x words per chunk and row
+  static constexpr int U = (8 / (MT * XW)) < 1 ? 1 : (8 / (MT * XW));
+};
+
 template <int WK, int MT>
 __global__ void __launch_bounds__(kBulkThreads, 2) gemv_bulk_kernel(const GemvParams p, const BulkShape sh) {
   constexpr int EPC = WT<WK>::EPC;
@@ -506,8 +551,27 @@ __global__ void __launch_bounds__(kBulkThreads, 2) gemv_bulk_kernel(const GemvPa
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[m][0] = acc[m][1] = make_float2(0.f, 0.f);
     if (has_row) {
-#pragma unroll 4
-      for (int idx = lane; idx < nck; idx += 32) chunk_fma2<WK, MT>(wr[idx], xb, p.Kp, idx, acc);
+      constexpr int U = Batch<WK, MT>::U;
+      for (int base = lane; base < nck; base += 32 * U) {
+        // issue every load of the batch, then the arithmetic
+        uint4 wv[U];
+        uint4 xv[U][MT][2];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int idx = base + 32 * u;
+          const bool ok = idx < nck;
+          wv[u] = ok ? wr[idx] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            xv[u][m][0] = ok ? *reinterpret_cast<const uint4*>(xb + m * p.Kp + idx * 8) : make_uint4(0, 0, 0, 0);
+            if constexpr (Batch<WK, MT>::XW == 2)
+              xv[u][m][1] = ok ? *reinterpret_cast<const uint4*>(xb + m * p.Kp + (p.Kp >> 1) + idx * 8)
+                               : make_uint4(0, 0, 0, 0);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) chunk_fma2_x<WK, MT>(wv[u], xv[u], acc);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + s);
