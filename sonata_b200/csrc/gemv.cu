@@ -5,23 +5,30 @@
 // only simulates.  The path is HBM-bound: the weight is streamed once, x and y
 // are a few KB.
 //
-// Fast path (gemv_bulk_kernel): one CTA per SM owns an equal contiguous range
-// of weight rows.  A producer lane streams ~32 KB chunks of whole rows
-// (cp.async.bulk, L2 evict-first) into a shared-memory ring; eight consumer
-// warps each reduce one row of a chunk with packed f32x2 FMAs (FFMA2) against
-// x staged once as bf16 in shared memory, then warp-shuffle and store.  The
-// CTA uses about half an SM, and the producer issues its weight copies
-// before griddepcontrol.wait: launched with programmatic dependent launch, the
-// next GEMV of a decode step is resident beside this one and streams its
-// weights while this one drains.  Measured on B200: the 156-GEMV decode chain
-// of BASELINE config 2 runs about 1.5x faster than cuBLAS in the same graph;
-// what remains is the latency of each kernel boundary (waiting for the
-// producer of x, then loading x), not the arithmetic.
+// bf16 fast path (gemv_mma_kernel): one CTA per SM owns an equal contiguous
+// range of weight rows.  A producer lane streams 32 KB slots of whole rows
+// (cp.async.bulk, L2 evict-first) into a shared-memory ring before
+// griddepcontrol.wait, so under programmatic dependent launch the next GEMV of
+// a decode step streams its weights while this one drains.  The dot products
+// run on the tensor core (tcgen05.mma, fp32 accumulation in TMEM): each row is
+// cut into segments that form the 8-row groups of an M = 128 operand, x is
+// the matching B operand, and the epilogue sums the diagonal partial products
+// with a warp-shuffle reduction.  A slot is released the moment its MMAs
+// retire, and the CUDA cores issue a few instructions per 32 KB.
+//
+// 8-bit weights and batched calls (gemv_bulk_kernel): the same ring, with
+// eight consumer warps reducing one row each with packed f32x2 FMAs (FFMA2)
+// against x staged as bf16 in shared memory.
+//
+// Measured on B200: the 156-GEMV decode chain of BASELINE config 2 runs about
+// 1.6x faster than cuBLAS in the same graph; what remains is the latency of
+// each kernel boundary (waiting for the producer of x, then loading x), not
+// the arithmetic.
 //
 // Fallbacks: gemv_vec_kernel (16-byte register loads; rows whose length is not
 // a multiple of 16 bytes or longer than 64 KB) and gemv_scalar_kernel (rows
 // that are not 16-byte aligned).
-#include "common.cuh"
+#include "tc.cuh"
 
 #include <algorithm>
 #include <cstdlib>
@@ -590,6 +597,233 @@ __global__ void __launch_bounds__(kBulkThreads, 2) gemv_bulk_kernel(const GemvPa
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core decode GEMV (bf16 weights, one batch entry, K % 256 == 0).
+//
+// The same bulk-copy ring as gemv_bulk_kernel, but the tensor core does the
+// dot products, so the CUDA cores issue almost nothing per weight byte and a
+// ring slot is released as soon as its MMAs retire.
+//
+// A slot holds R whole weight rows back to back (row r at r * K * 2 bytes).
+// Each row is cut into S segments of L = K / S elements, and the R * S = 16
+// segments are the sixteen 8-row groups of an M = 128 A operand in the
+// no-swizzle K-major layout: group g = r * S + s starts at g * L * 2 bytes
+// (stride byte offset = L * 2), and inside a group the eight 16-byte "rows"
+// are eight consecutive 8-element pieces of the segment, the K = 8..15 half
+// of each MMA 64 elements further on (leading byte offset = 128).  One
+// K = 16 MMA therefore consumes 128 consecutive elements of every segment,
+// and L / 128 MMAs consume the slot.
+//
+// x is staged once as plain bf16 [MT][K] and described the same way, B group
+// G = m * S + s being segment s of x row m (stride L * 2 again).  Then
+//   D[lane 8g + j][column 8G + j] = sum over that segment piece of W * x
+// whenever g and G name the same segment s; y[row r, m] is the sum of those
+// entries over (s, j).  The epilogue reads them with one TMEM load per x row
+// (lane l of the warp takes column l mod 8S) and a shuffle reduction over the
+// 8S lanes of a weight row.  The MMA computes N = 8 * S * MT columns where
+// MT are needed; at HBM speed the tensor core has room for that many times
+// over.
+//
+// Warps: 0 = weight producer (no griddepcontrol.wait: weights are frozen),
+// 1 = TMEM owner, x copy and MMA issuer, 2..5 = epilogue (TMEM lane
+// quarter = warp % 4).  Two accumulators in TMEM let the epilogue of one
+// slot overlap the MMAs of the next.
+// ---------------------------------------------------------------------------
+constexpr int kMmaGemvThreads = 192;
+
+struct MmaShape {
+  int ns;              // ring slots
+  int S;               // segments per row (2 or 4); R = 16 / S rows per slot
+  int N;               // MMA N = 8 * S * MT
+  uint32_t slot_bytes; // R * K * 2
+  uint32_t xs_off;     // byte offset of staged x
+  uint32_t ring_off;   // byte offset of slot 0
+  uint32_t tcols;      // TMEM columns allocated (two accumulators)
+};
+
+// v[idx] for a lane-dependent idx without local-memory indexing.
+template <int W>
+__device__ __forceinline__ float pick(const float (&v)[W], int idx) {
+  float t[W];
+#pragma unroll
+  for (int i = 0; i < W; ++i) t[i] = v[i];
+#pragma unroll
+  for (int w = W / 2; w >= 1; w >>= 1) {
+    const bool hi = (idx & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) t[i] = hi ? t[i + w] : t[i];
+  }
+  return t[0];
+}
+
+template <int MT, int S>
+__device__ __forceinline__ void mma_gemv_epilogue(const GemvParams& p, uint32_t taddr, int q, int lane, int row0,
+                                                  int cnt) {
+  constexpr int G = 8 * S;  // lanes (and columns) per weight row
+  constexpr int W = G < 32 ? G : 32;
+  const int i = q * 32 + lane;  // A row = TMEM lane
+  const int r = i / G;          // weight row inside the slot
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    float v = 0.f;
+    if constexpr (W == 16) {
+      float t[16];
+      tc::tmem_ld16(taddr + m * G, t);
+      v = pick<16>(t, lane & 15);
+    } else {
+      float t[32];
+      tc::tmem_ld32(taddr + m * G, t);
+      v = pick<32>(t, lane);
+    }
+#pragma unroll
+    for (int o = G / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((lane & (G - 1)) == 0 && r < cnt) store_row<MT>(p, p.y, row0 + r, m, v);
+  }
+}
+
+template <int MT, int S>
+__global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const GemvParams p, const MmaShape sh) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int R = 16 / S;
+  const int ns = sh.ns;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + ns;
+  uint64_t* tfull = empty + ns;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint64_t* xbar = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 1);
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + sh.xs_off);
+  uint8_t* ring = smem + sh.ring_off;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
+  const int r1 = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
+  const int nrows = r1 - r0;
+  const uint32_t row_bytes = static_cast<uint32_t>(p.K) * 2;
+  const int ntiles = (nrows + R - 1) / R;
+  uint32_t tmem = 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);  // released by the MMA commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, 4);  // one arrive per epilogue warp
+    }
+    mbar_init(done, 1);
+    mbar_init(xbar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- producer: weights only, so no griddepcontrol.wait ----
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int t = 0;
+      for (; t < ntiles; ++t) {
+        const int s = t % ns, k = t / ns;
+        if (k > 0 && !mbar_wait_bounded(empty + s, (k - 1) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          break;
+        }
+        const int first = r0 + t * R;
+        const int cnt = min(R, r1 - first);
+        uint8_t* dst = ring + static_cast<size_t>(s) * sh.slot_bytes;
+        mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(cnt) * row_bytes);
+        if (p.ldw == p.K) {
+          bulk_g2s(dst, p.W + static_cast<int64_t>(first) * p.ldw * 2, static_cast<uint32_t>(cnt) * row_bytes,
+                   full + s, pol);
+        } else {
+          for (int r = 0; r < cnt; ++r)
+            bulk_g2s(dst + static_cast<size_t>(r) * row_bytes, p.W + static_cast<int64_t>(first + r) * p.ldw * 2,
+                     row_bytes, full + s, pol);
+        }
+      }
+      if (t < ntiles) {  // error path: let the copies in flight land before exit
+        for (int j = (t > ns ? t - ns : 0); j < t; ++j) mbar_wait_bounded(full + j % ns, (j / ns) & 1);
+      }
+    }
+  } else {
+    // TMEM (warp 1) and the x copy overlap the first weight copies; the
+    // producer never waits for either.  x rows arrive by bulk copy (one L2
+    // round trip after the grid dependency resolves); padding rows M..MT-1
+    // are zeroed by the epilogue warps meanwhile.
+    if (warp == 1) tc::tmem_alloc(tmem_slot, sh.tcols);
+    pdl_wait();  // x and y belong to the previous kernel from here on
+    if (warp == 1) {
+      if (lane == 0) {
+        const uint64_t pol = l2_policy_evict_normal();
+        mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * row_bytes);
+        for (int m = 0; m < p.M; ++m) bulk_g2s(xs + m * p.K, p.x + m * p.ldx, row_bytes, xbar, pol);
+      }
+    } else if (MT > 1) {
+      const int cpr = p.K >> 3;
+      for (int i = threadIdx.x - 64 + p.M * cpr; i < MT * cpr; i += 128)
+        *reinterpret_cast<uint4*>(xs + i * 8) = make_uint4(0, 0, 0, 0);
+      tc::fence_proxy_async_smem();
+    }
+    tc::fence_before_sync();
+    named_bar_sync(1, 160);
+    tc::fence_after_sync();
+    tmem = *tmem_slot;
+
+    const uint32_t L2 = row_bytes / S;  // segment bytes = stride between 8-row groups
+    const uint32_t nk = L2 / 256;       // MMAs per slot
+    if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      if (lane == 0) {
+        const uint32_t idesc = tc::idesc_bf16_f32(128, sh.N);
+        const uint64_t db0 = tc::smem_desc_noswz(xs, 128, L2);
+        const bool x_ok = mbar_wait_bounded(xbar, 0);
+        if (!x_ok) record_status(SN_ERR_TIMEOUT);
+        for (int t = 0; t < ntiles && x_ok; ++t) {
+          const int s = t % ns, b = t & 1;
+          if (!mbar_wait_bounded(full + s, (t / ns) & 1) ||
+              (t >= 2 && !mbar_wait_bounded(tempty + b, ((t >> 1) - 1) & 1))) {
+            record_status(SN_ERR_TIMEOUT);
+            break;
+          }
+          tc::fence_after_sync();
+          const uint64_t da0 = tc::smem_desc_noswz(ring + static_cast<size_t>(s) * sh.slot_bytes, 128, L2);
+          const uint32_t d = tmem + static_cast<uint32_t>(b * sh.N);
+          for (uint32_t k = 0; k < nk; ++k)  // 256 bytes = 128 elements of every segment per MMA
+            tc::mma_bf16(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+          tc::mma_commit(empty + s);
+          tc::mma_commit(tfull + b);
+        }
+        tc::mma_commit(done);
+        if (!mbar_wait_bounded(done, 0)) record_status(SN_ERR_TIMEOUT);
+      }
+      __syncwarp();
+    } else {
+      // ---------------- epilogue ----------------
+      const int q = warp & 3;
+      for (int t = 0; t < ntiles; ++t) {
+        const int b = t & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(tfull + b, (t >> 1) & 1))) {
+          record_status(SN_ERR_TIMEOUT);
+          break;
+        }
+        tc::fence_after_sync();
+        const int first = r0 + t * R;
+        mma_gemv_epilogue<MT, S>(p, tmem + (static_cast<uint32_t>(q * 32) << 16) + b * sh.N, q, lane, first,
+                                 min(R, r1 - first));
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty + b);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, sh.tcols);
+}
+
 // Opt a kernel into more than 48 KB of dynamic shared memory, once per
 // (kernel, device); the table is keyed by the kernel's address.
 inline bool ensure_smem(const void* kern, size_t bytes) {
@@ -618,12 +852,14 @@ inline bool ensure_smem(const void* kern, size_t bytes) {
   return true;
 }
 
-// Kernel selection override for measurement: SONATA_GEMV_KERNEL = bulk | regs.
+// Kernel selection override for measurement:
+// SONATA_GEMV_KERNEL = mma (default) | bulk | regs.
 int gemv_kernel_choice() {
   static int v = [] {
     const char* e = getenv("SONATA_GEMV_KERNEL");
     if (e && strcmp(e, "regs") == 0) return 2;
-    return 1;
+    if (e && strcmp(e, "bulk") == 0) return 1;
+    return 0;
   }();
   return v;
 }
@@ -684,11 +920,66 @@ int dispatch_bulk(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
   return launch(kern, dim3(grid), dim3(kBulkThreads), smem, st, pdl, p, sh);
 }
 
+// Segments per weight row of the tensor-core GEMV (SONATA_GEMV_MMA_S forces 2
+// or 4): the smallest that keeps a slot of 16 / S rows within 32 KB.
+int mma_segments(int K) {
+  static int forced = [] {
+    const char* e = getenv("SONATA_GEMV_MMA_S");
+    const int v = e ? atoi(e) : 0;
+    return (v == 2 || v == 4) ? v : 0;
+  }();
+  auto ok = [K](int S) { return K % (128 * S) == 0; };
+  if (forced) return ok(forced) ? forced : 0;
+  if (ok(2) && K <= 2048) return 2;
+  if (ok(4)) return 4;
+  return ok(2) ? 2 : 0;
+}
+
+// Returns SN_ERR_UNSUPPORTED when the tensor-core GEMV does not apply
+// (bf16 weights, one batch entry, aligned rows and x, K % 256 == 0).
+template <int MT>
+int dispatch_mma(const GemvParams& p, cudaStream_t st, bool pdl) {
+  if (!p.x_vec || (reinterpret_cast<uintptr_t>(p.W) & 15) || (p.ldw * 2) % 16 != 0) return SN_ERR_UNSUPPORTED;
+  const int S = mma_segments(p.K);
+  if (S == 0) return SN_ERR_UNSUPPORTED;
+  const int R = 16 / S;
+  MmaShape sh;
+  sh.S = S;
+  sh.N = 8 * S * MT;
+  sh.tcols = tc::tmem_cols_for(2 * sh.N);
+  sh.slot_bytes = static_cast<uint32_t>(R) * p.K * 2;
+  const int grid = std::min(sm_count(), p.N);
+  const int rows_per_cta = (p.N + grid - 1) / grid;
+  const int tiles_per_cta = (rows_per_cta + R - 1) / R;
+  const int ns_max = 16;
+  sh.xs_off = 1024;  // barriers + TMEM address below
+  sh.ring_off = round_up_u32(sh.xs_off + static_cast<uint32_t>(MT) * p.K * 2, 128);
+  const size_t budget = bulk_smem_budget();
+  const size_t room = budget > sh.ring_off ? budget - sh.ring_off : 0;
+  int ns = static_cast<int>(std::min<size_t>(ns_max, room / sh.slot_bytes));
+  ns = std::min(ns, tiles_per_cta);
+  ns = std::max(ns, 2);
+  sh.ns = ns;
+  const size_t smem = sh.ring_off + static_cast<size_t>(ns) * sh.slot_bytes;
+  if (smem > 220 * 1024) return SN_ERR_UNSUPPORTED;
+  const void* kern = S == 2 ? reinterpret_cast<const void*>(gemv_mma_kernel<MT, 2>)
+                            : reinterpret_cast<const void*>(gemv_mma_kernel<MT, 4>);
+  if (!ensure_smem(kern, smem)) return SN_ERR_UNSUPPORTED;
+  if (S == 2) return launch(gemv_mma_kernel<MT, 2>, dim3(grid), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
+  return launch(gemv_mma_kernel<MT, 4>, dim3(grid), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
+}
+
 template <int WK, int MT>
 int dispatch_mt(const GemvParams& p, int batch, size_t smem, cudaStream_t st, bool pdl, bool wvec) {
   constexpr int EPC = WT<WK>::EPC;
   if (!wvec) return launch_gemv(gemv_scalar_kernel<WK, MT>, p, kWarps, batch, smem, st, pdl);
-  if (gemv_kernel_choice() == 1) {
+  if constexpr (WK == W_BF16) {
+    if (gemv_kernel_choice() == 0 && batch == 1) {
+      const int rc = dispatch_mma<MT>(p, st, pdl);
+      if (rc != SN_ERR_UNSUPPORTED) return rc;
+    }
+  }
+  if (gemv_kernel_choice() <= 1) {
     const int rc = dispatch_bulk<WK, MT>(p, batch, st, pdl);
     if (rc != SN_ERR_UNSUPPORTED) return rc;
   }

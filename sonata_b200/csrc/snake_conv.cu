@@ -57,10 +57,6 @@ struct ScParams {
   uint32_t tcols;      // TMEM columns per accumulator buffer
 };
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
   const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
@@ -258,7 +254,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
                                                               pack_bf16x2(lo[4], lo[5]), pack_bf16x2(lo[6], lo[7]));
           }
         }
-        fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+        tc::fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
         __syncwarp();
         if (lane == 0) mbar_arrive(a_full + ab);
       }
