@@ -31,6 +31,7 @@
 #include "tc.cuh"
 
 #include <algorithm>
+#include <climits>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -598,47 +599,59 @@ __global__ void __launch_bounds__(kBulkThreads, 2) gemv_bulk_kernel(const GemvPa
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core decode GEMV (bf16 weights, one batch entry, K % 256 == 0).
+// Tensor-core decode GEMV (bf16 or int8 weights, one batch entry).
 //
 // The same bulk-copy ring as gemv_bulk_kernel, but the tensor core does the
 // dot products, so the CUDA cores issue almost nothing per weight byte and a
 // ring slot is released as soon as its MMAs retire.
 //
-// A slot holds R whole weight rows back to back (row r at r * K * 2 bytes).
-// Each row is cut into S segments of L = K / S elements, and the R * S = 16
+// A slot holds R whole weight rows back to back (row r at r * K * esz bytes).
+// Each row is cut into S segments of L = K * esz / S bytes, and the R * S = 16
 // segments are the sixteen 8-row groups of an M = 128 A operand in the
-// no-swizzle K-major layout: group g = r * S + s starts at g * L * 2 bytes
-// (stride byte offset = L * 2), and inside a group the eight 16-byte "rows"
-// are eight consecutive 8-element pieces of the segment, the K = 8..15 half
-// of each MMA 64 elements further on (leading byte offset = 128).  One
-// K = 16 MMA therefore consumes 128 consecutive elements of every segment,
-// and L / 128 MMAs consume the slot.
+// no-swizzle K-major layout: group g = r * S + s starts at g * L bytes
+// (stride byte offset = L), and inside a group the eight 16-byte "rows" are
+// eight consecutive 16-byte pieces of the segment, the second K half of each
+// MMA 128 bytes further on (leading byte offset).  One MMA (K = 16 bf16 or
+// K = 32 int8) therefore consumes 256 consecutive bytes of every segment, and
+// L / 256 MMAs consume the slot.
 //
-// x is staged once as plain bf16 [MT][K] and described the same way, B group
-// G = m * S + s being segment s of x row m (stride L * 2 again).  Then
+// x is the B operand, laid out the same way: B group G = (d * MT + m) * S + s
+// is segment s of x row m (digit plane d for int8).  Then
 //   D[lane 8g + j][column 8G + j] = sum over that segment piece of W * x
 // whenever g and G name the same segment s; y[row r, m] is the sum of those
 // entries over (s, j).  The epilogue reads them with one TMEM load per x row
-// (lane l of the warp takes column l mod 8S) and a shuffle reduction over the
-// 8S lanes of a weight row.  The MMA computes N = 8 * S * MT columns where
-// MT are needed; at HBM speed the tensor core has room for that many times
-// over.
+// and digit (lane l of the warp takes column l mod 8S) and a shuffle
+// reduction over the 8S lanes of a weight row.  The MMA computes
+// N = 8 * S * MT * digits columns where MT * digits are needed; the tensor
+// core has room for that at HBM speed.
+//
+// bf16: x staged once by one bulk copy per row, kind::f16, fp32 in TMEM.
+// int8: the int8 codes feed kind::i8 directly (no conversion on the CUDA
+// cores).  x row m is rounded once to the integer X = rint(x * 2^e_m) with
+// max|X| in [2^21, 2^22) and split into three signed base-256 digits, each an
+// int8 plane of B; TMEM holds three exact s32 partial sums per row, combined
+// in 64-bit integers: y = (sum_k q_k X_k) * 2^-e_m * scale_row.  The only
+// approximation is the rounding of x to 22 significant bits (absolute error
+// at most 2^-23 of max|x| per element).  An x row holding inf or NaN gives
+// NaN outputs.
 //
 // Warps: 0 = weight producer (no griddepcontrol.wait: weights are frozen),
-// 1 = TMEM owner, x copy and MMA issuer, 2..5 = epilogue (TMEM lane
-// quarter = warp % 4).  Two accumulators in TMEM let the epilogue of one
-// slot overlap the MMAs of the next.
+// 1 = TMEM owner and MMA issuer (bf16: also the x copy), 2..5 = epilogue
+// (TMEM lane quarter = warp % 4; int8: also the x digits).  Up to four
+// accumulators in TMEM let the epilogue lag the MMAs by several slots.
 // ---------------------------------------------------------------------------
 constexpr int kMmaGemvThreads = 192;
+constexpr int kAccMax = 4;  // TMEM accumulators: the MMAs of slot t wait for the epilogue of slot t - nacc
 
 struct MmaShape {
   int ns;              // ring slots
-  int S;               // segments per row (2 or 4); R = 16 / S rows per slot
-  int N;               // MMA N = 8 * S * MT
-  uint32_t slot_bytes; // R * K * 2
-  uint32_t xs_off;     // byte offset of staged x
+  int N;               // MMA N = 8 * S * MT * digits
+  int acc_log2;        // log2 of the TMEM accumulators (0, 1 or 2)
+  uint32_t slot_bytes; // R * K * esz
+  uint32_t xs_off;     // byte offset of the B operand (x, or x digits)
+  uint32_t xraw_off;   // int8: byte offset of x as copied (bf16 [MT][K])
   uint32_t ring_off;   // byte offset of slot 0
-  uint32_t tcols;      // TMEM columns allocated (two accumulators)
+  uint32_t tcols;      // TMEM columns allocated
 };
 
 // v[idx] for a lane-dependent idx without local-memory indexing.
@@ -656,52 +669,47 @@ __device__ __forceinline__ float pick(const float (&v)[W], int idx) {
   return t[0];
 }
 
-template <int MT, int S>
-__device__ __forceinline__ void mma_gemv_epilogue(const GemvParams& p, uint32_t taddr, int q, int lane, int row0,
-                                                  int cnt) {
-  constexpr int G = 8 * S;  // lanes (and columns) per weight row
-  constexpr int W = G < 32 ? G : 32;
-  const int i = q * 32 + lane;  // A row = TMEM lane
-  const int r = i / G;          // weight row inside the slot
-#pragma unroll
-  for (int m = 0; m < MT; ++m) {
-    float v = 0.f;
-    if constexpr (W == 16) {
-      float t[16];
-      tc::tmem_ld16(taddr + m * G, t);
-      v = pick<16>(t, lane & 15);
-    } else {
-      float t[32];
-      tc::tmem_ld32(taddr + m * G, t);
-      v = pick<32>(t, lane);
-    }
-#pragma unroll
-    for (int o = G / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if ((lane & (G - 1)) == 0 && r < cnt) store_row<MT>(p, p.y, row0 + r, m, v);
+// This lane's diagonal entry of the 8S TMEM columns starting at taddr.
+template <int S>
+__device__ __forceinline__ float diag_entry(uint32_t taddr, int lane) {
+  if constexpr (S == 2) {
+    float t[16];
+    tc::tmem_ld16(taddr, t);
+    return pick<16>(t, lane & 15);
+  } else {
+    float t[32];
+    tc::tmem_ld32(taddr, t);
+    return pick<32>(t, lane);
   }
 }
 
-template <int MT, int S>
+template <int WK, int MT, int S>
 __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const GemvParams p, const MmaShape sh) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int R = 16 / S;
+  constexpr int G = 8 * S;  // TMEM lanes (and columns) per weight row
+  constexpr int ESZ = WT<WK>::ESZ;
+  constexpr int ND = (WK == W_INT8) ? 3 : 1;  // B planes per x row
   const int ns = sh.ns;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + ns;
   uint64_t* tfull = empty + ns;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* done = tempty + 2;
+  uint64_t* tempty = tfull + kAccMax;
+  uint64_t* done = tempty + kAccMax;
   uint64_t* xbar = done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 1);
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + sh.xs_off);
+  uint32_t* xmax = tmem_slot + 1;            // int8: [MT] max |x| (bf16 bit patterns)
+  int* xexp = reinterpret_cast<int*>(xmax + MT);  // int8: [MT] e_m (x row m scaled by 2^e_m)
+  uint8_t* xs = smem + sh.xs_off;
   uint8_t* ring = smem + sh.ring_off;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
   const int r1 = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
   const int nrows = r1 - r0;
-  const uint32_t row_bytes = static_cast<uint32_t>(p.K) * 2;
+  const uint32_t row_bytes = static_cast<uint32_t>(p.K) * ESZ;
   const int ntiles = (nrows + R - 1) / R;
+  const int nacc = 1 << sh.acc_log2;
   uint32_t tmem = 0;
 
   if (threadIdx.x == 0) {
@@ -709,12 +717,13 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);  // released by the MMA commit
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAccMax; ++b) {
       mbar_init(tfull + b, 1);
       mbar_init(tempty + b, 4);  // one arrive per epilogue warp
     }
     mbar_init(done, 1);
     mbar_init(xbar, 1);
+    for (int m = 0; m < MT; ++m) xmax[m] = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -736,11 +745,11 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
         uint8_t* dst = ring + static_cast<size_t>(s) * sh.slot_bytes;
         mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(cnt) * row_bytes);
         if (p.ldw == p.K) {
-          bulk_g2s(dst, p.W + static_cast<int64_t>(first) * p.ldw * 2, static_cast<uint32_t>(cnt) * row_bytes,
+          bulk_g2s(dst, p.W + static_cast<int64_t>(first) * p.ldw * ESZ, static_cast<uint32_t>(cnt) * row_bytes,
                    full + s, pol);
         } else {
           for (int r = 0; r < cnt; ++r)
-            bulk_g2s(dst + static_cast<size_t>(r) * row_bytes, p.W + static_cast<int64_t>(first + r) * p.ldw * 2,
+            bulk_g2s(dst + static_cast<size_t>(r) * row_bytes, p.W + static_cast<int64_t>(first + r) * p.ldw * ESZ,
                      row_bytes, full + s, pol);
         }
       }
@@ -749,50 +758,122 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
       }
     }
   } else {
-    // TMEM (warp 1) and the x copy overlap the first weight copies; the
-    // producer never waits for either.  x rows arrive by bulk copy (one L2
-    // round trip after the grid dependency resolves); padding rows M..MT-1
-    // are zeroed by the epilogue warps meanwhile.
+    // TMEM (warp 1) and the x staging overlap the first weight copies; the
+    // producer never waits for either.
     if (warp == 1) tc::tmem_alloc(tmem_slot, sh.tcols);
     pdl_wait();  // x and y belong to the previous kernel from here on
-    if (warp == 1) {
-      if (lane == 0) {
-        const uint64_t pol = l2_policy_evict_normal();
-        mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * row_bytes);
-        for (int m = 0; m < p.M; ++m) bulk_g2s(xs + m * p.K, p.x + m * p.ldx, row_bytes, xbar, pol);
+    const int cpr = p.K >> 3;  // 16-byte pieces of a bf16 x row
+    if constexpr (WK == W_BF16) {
+      // x rows by bulk copy (one L2 round trip); padding rows zeroed meanwhile
+      if (warp == 1) {
+        if (lane == 0) {
+          const uint64_t pol = l2_policy_evict_normal();
+          mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * row_bytes);
+          for (int m = 0; m < p.M; ++m)
+            bulk_g2s(xs + static_cast<size_t>(m) * row_bytes, p.x + m * p.ldx, row_bytes, xbar, pol);
+        }
+      } else if (MT > 1) {
+        for (int i = threadIdx.x - 64 + p.M * cpr; i < MT * cpr; i += 128)
+          reinterpret_cast<uint4*>(xs)[i] = make_uint4(0, 0, 0, 0);
+        tc::fence_proxy_async_smem();
       }
-    } else if (MT > 1) {
-      const int cpr = p.K >> 3;
-      for (int i = threadIdx.x - 64 + p.M * cpr; i < MT * cpr; i += 128)
-        *reinterpret_cast<uint4*>(xs + i * 8) = make_uint4(0, 0, 0, 0);
-      tc::fence_proxy_async_smem();
+    } else {
+      // x rows by bulk copy, then three int8 digit planes of rint(x * 2^e_m)
+      if (warp >= 2) {
+        const int xt = threadIdx.x - 64;  // 0..127
+        const __nv_bfloat16* xraw = reinterpret_cast<const __nv_bfloat16*>(smem + sh.xraw_off);
+        if (xt == 0) {
+          const uint64_t pol = l2_policy_evict_normal();
+          mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * p.K * 2);
+          for (int m = 0; m < p.M; ++m)
+            bulk_g2s(const_cast<__nv_bfloat16*>(xraw) + m * p.K, p.x + m * p.ldx, p.K * 2, xbar, pol);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) record_status(SN_ERR_TIMEOUT);
+        const uint4* xr = reinterpret_cast<const uint4*>(xraw);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {  // max |x| (bit patterns of non-negative values order like them)
+          uint32_t mx = 0;
+          if (m < p.M) {
+            for (int c = xt; c < cpr; c += 128) {
+              const uint4 v = xr[m * cpr + c];
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) mx = max(mx, max(w[j] & 0x7FFFu, (w[j] >> 16) & 0x7FFFu));
+            }
+          }
+          mx = __reduce_max_sync(0xffffffffu, mx);
+          if (lane == 0) atomicMax(xmax + m, mx);
+        }
+        named_bar_sync(2, 128);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          // max|x| < 2^(E+1) with E = biased exponent - 127 (subnormal rows
+          // too: E = -127): scale by 2^e, e = 21 - E, as two exact
+          // power-of-two factors (e in [-107, 148])
+          const int ebits = static_cast<int>(xmax[m] >> 7);
+          const int e = 21 - (ebits - 127);
+          const float up1 = __uint_as_float(static_cast<uint32_t>(127 + e / 2) << 23);
+          const float up2 = __uint_as_float(static_cast<uint32_t>(127 + (e - e / 2)) << 23);
+          if (xt == 0) xexp[m] = (ebits == 255) ? INT_MIN : e;  // non-finite x row
+          for (int c = xt; c < cpr; c += 128) {
+            uint32_t dg[3][2] = {{0, 0}, {0, 0}, {0, 0}};  // digit d of 8 elements
+            if (m < p.M) {
+              const uint4 v = xr[m * cpr + c];
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const uint32_t h = w[e >> 1];
+                const float xf = (e & 1) ? bf16hi(h) : bf16lo(h);
+                int X = __float2int_rn((xf * up1) * up2);  // |X| < 2^22
+                const int d0 = static_cast<int8_t>(X & 0xFF);
+                X = (X - d0) >> 8;
+                const int d1 = static_cast<int8_t>(X & 0xFF);
+                const int d2 = (X - d1) >> 8;  // |d2| <= 64
+                dg[0][e >> 2] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * (e & 3));
+                dg[1][e >> 2] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * (e & 3));
+                dg[2][e >> 2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * (e & 3));
+              }
+            }
+#pragma unroll
+            for (int d = 0; d < 3; ++d)
+              *reinterpret_cast<uint2*>(xs + (static_cast<size_t>(d) * MT + m) * p.K + c * 8) =
+                  make_uint2(dg[d][0], dg[d][1]);
+          }
+        }
+        tc::fence_proxy_async_smem();
+      }
     }
     tc::fence_before_sync();
-    named_bar_sync(1, 160);
+    named_bar_sync(1, 160);  // warps 1..5: TMEM allocated, x staged (bf16: copy issued)
     tc::fence_after_sync();
     tmem = *tmem_slot;
 
-    const uint32_t L2 = row_bytes / S;  // segment bytes = stride between 8-row groups
-    const uint32_t nk = L2 / 256;       // MMAs per slot
+    const uint32_t L = row_bytes / S;  // segment bytes = stride between 8-row groups
+    const uint32_t nk = L / 256;       // MMAs per slot
     if (warp == 1) {
       // ---------------- MMA issuer ----------------
       if (lane == 0) {
-        const uint32_t idesc = tc::idesc_bf16_f32(128, sh.N);
-        const uint64_t db0 = tc::smem_desc_noswz(xs, 128, L2);
-        const bool x_ok = mbar_wait_bounded(xbar, 0);
+        const uint32_t idesc = (WK == W_INT8) ? tc::idesc_s8_s32(128, sh.N) : tc::idesc_bf16_f32(128, sh.N);
+        const uint64_t db0 = tc::smem_desc_noswz(xs, 128, L);
+        bool x_ok = true;
+        if constexpr (WK == W_BF16) x_ok = mbar_wait_bounded(xbar, 0);
         if (!x_ok) record_status(SN_ERR_TIMEOUT);
         for (int t = 0; t < ntiles && x_ok; ++t) {
-          const int s = t % ns, b = t & 1;
+          const int s = t % ns, b = t & (nacc - 1);
           if (!mbar_wait_bounded(full + s, (t / ns) & 1) ||
-              (t >= 2 && !mbar_wait_bounded(tempty + b, ((t >> 1) - 1) & 1))) {
+              (t >= nacc && !mbar_wait_bounded(tempty + b, ((t >> sh.acc_log2) - 1) & 1))) {
             record_status(SN_ERR_TIMEOUT);
             break;
           }
           tc::fence_after_sync();
-          const uint64_t da0 = tc::smem_desc_noswz(ring + static_cast<size_t>(s) * sh.slot_bytes, 128, L2);
+          const uint64_t da0 = tc::smem_desc_noswz(ring + static_cast<size_t>(s) * sh.slot_bytes, 128, L);
           const uint32_t d = tmem + static_cast<uint32_t>(b * sh.N);
-          for (uint32_t k = 0; k < nk; ++k)  // 256 bytes = 128 elements of every segment per MMA
-            tc::mma_bf16(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+          for (uint32_t k = 0; k < nk; ++k) {  // 256 bytes of every segment per MMA
+            if constexpr (WK == W_INT8)
+              tc::mma_s8(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+            else
+              tc::mma_bf16(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+          }
           tc::mma_commit(empty + s);
           tc::mma_commit(tfull + b);
         }
@@ -803,16 +884,54 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
     } else {
       // ---------------- epilogue ----------------
       const int q = warp & 3;
+      const int i = q * 32 + lane;  // A row = TMEM lane
+      const int r = i / G;          // weight row inside the slot
+      // int8 row scales are frozen weights: fetch slot t + 1's while slot t computes
+      float rs_next = 0.f;
+      if constexpr (WK == W_INT8) rs_next = (r < min(R, nrows)) ? p.scale[r0 + r] : 0.f;
       for (int t = 0; t < ntiles; ++t) {
-        const int b = t & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(tfull + b, (t >> 1) & 1))) {
+        const int b = t & (nacc - 1);
+        const int first = r0 + t * R;
+        const int cnt = min(R, r1 - first);
+        float rs = 0.f;
+        if constexpr (WK == W_INT8) {
+          rs = rs_next;
+          if (t + 1 < ntiles) rs_next = (r < min(R, nrows - (t + 1) * R)) ? p.scale[first + R + r] : 0.f;
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(tfull + b, (t >> sh.acc_log2) & 1))) {
           record_status(SN_ERR_TIMEOUT);
           break;
         }
         tc::fence_after_sync();
-        const int first = r0 + t * R;
-        mma_gemv_epilogue<MT, S>(p, tmem + (static_cast<uint32_t>(q * 32) << 16) + b * sh.N, q, lane, first,
-                                 min(R, r1 - first));
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * sh.N;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if constexpr (WK == W_BF16) {
+            float v = diag_entry<S>(taddr + m * G, lane);
+#pragma unroll
+            for (int o = G / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if ((lane & (G - 1)) == 0 && r < cnt) store_row<MT>(p, p.y, first + r, m, v);
+          } else {
+            int v[3];
+#pragma unroll
+            for (int d = 0; d < 3; ++d) {
+              v[d] = __float_as_int(diag_entry<S>(taddr + (d * MT + m) * G, lane));
+#pragma unroll
+              for (int o = G / 2; o >= 1; o >>= 1) v[d] += __shfl_xor_sync(0xffffffffu, v[d], o);
+            }
+            if ((lane & (G - 1)) == 0 && r < cnt) {
+              const long long acc = static_cast<long long>(v[0]) + (static_cast<long long>(v[1]) << 8) +
+                                    (static_cast<long long>(v[2]) << 16);
+              const int e = xexp[m];
+              // sum_k q_k X_k exactly, times 2^-e (exact in double), rounded once to fp32
+              const float dot = (e == INT_MIN)
+                                    ? __int_as_float(0x7FC00000)
+                                    : static_cast<float>(static_cast<double>(acc) *
+                                                         __longlong_as_double(static_cast<long long>(1023 - e) << 52));
+              store_row<MT>(p, p.y, first + r, m, dot * rs);
+            }
+          }
+        }
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(tempty + b);
@@ -920,40 +1039,49 @@ int dispatch_bulk(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
   return launch(kern, dim3(grid), dim3(kBulkThreads), smem, st, pdl, p, sh);
 }
 
-// Segments per weight row of the tensor-core GEMV (SONATA_GEMV_MMA_S forces 2
-// or 4): the smallest that keeps a slot of 16 / S rows within 32 KB.
-int mma_segments(int K) {
+// Segments per weight row of the tensor-core GEMV: the smallest S in {2, 4}
+// whose segments are whole MMAs (K * esz / S a multiple of 256 bytes), whose
+// slot of 16 / S rows stays within 32 KB and whose N = 8 * S * MT * digits
+// fits one MMA (<= 256).  SONATA_GEMV_MMA_S forces 2 or 4 where valid.
+int mma_segments(int K, int esz, int MT, int nd) {
   static int forced = [] {
     const char* e = getenv("SONATA_GEMV_MMA_S");
     const int v = e ? atoi(e) : 0;
     return (v == 2 || v == 4) ? v : 0;
   }();
-  auto ok = [K](int S) { return K % (128 * S) == 0; };
+  const int64_t row = static_cast<int64_t>(K) * esz;
+  auto ok = [&](int S) { return row % (256 * S) == 0 && 8 * S * MT * nd <= 256; };
+  auto small = [&](int S) { return (16 / S) * row <= 32 * 1024; };
   if (forced) return ok(forced) ? forced : 0;
-  if (ok(2) && K <= 2048) return 2;
-  if (ok(4)) return 4;
-  return ok(2) ? 2 : 0;
+  if (ok(2) && small(2)) return 2;
+  if (ok(4) && small(4)) return 4;
+  if (ok(2)) return 2;
+  return ok(4) ? 4 : 0;
 }
 
 // Returns SN_ERR_UNSUPPORTED when the tensor-core GEMV does not apply
-// (bf16 weights, one batch entry, aligned rows and x, K % 256 == 0).
-template <int MT>
+// (bf16 or int8 weights, one batch entry, aligned rows and x).
+template <int WK, int MT>
 int dispatch_mma(const GemvParams& p, cudaStream_t st, bool pdl) {
-  if (!p.x_vec || (reinterpret_cast<uintptr_t>(p.W) & 15) || (p.ldw * 2) % 16 != 0) return SN_ERR_UNSUPPORTED;
-  const int S = mma_segments(p.K);
+  constexpr int ESZ = WT<WK>::ESZ;
+  constexpr int ND = (WK == W_INT8) ? 3 : 1;
+  if (!p.x_vec || (reinterpret_cast<uintptr_t>(p.W) & 15) || (p.ldw * ESZ) % 16 != 0) return SN_ERR_UNSUPPORTED;
+  const int S = mma_segments(p.K, ESZ, MT, ND);
   if (S == 0) return SN_ERR_UNSUPPORTED;
   const int R = 16 / S;
   MmaShape sh;
-  sh.S = S;
-  sh.N = 8 * S * MT;
-  sh.tcols = tc::tmem_cols_for(2 * sh.N);
-  sh.slot_bytes = static_cast<uint32_t>(R) * p.K * 2;
+  sh.N = 8 * S * MT * ND;
+  // two CTAs per SM share 512 TMEM columns: at most 256 each
+  sh.acc_log2 = (4 * sh.N <= 256) ? 2 : (2 * sh.N <= 256) ? 1 : 0;
+  sh.tcols = tc::tmem_cols_for(sh.N << sh.acc_log2);
+  sh.slot_bytes = static_cast<uint32_t>(R) * p.K * ESZ;
   const int grid = std::min(sm_count(), p.N);
   const int rows_per_cta = (p.N + grid - 1) / grid;
   const int tiles_per_cta = (rows_per_cta + R - 1) / R;
   const int ns_max = 16;
-  sh.xs_off = 1024;  // barriers + TMEM address below
-  sh.ring_off = round_up_u32(sh.xs_off + static_cast<uint32_t>(MT) * p.K * 2, 128);
+  sh.xs_off = 1024;  // barriers, TMEM address and x scales below
+  sh.xraw_off = round_up_u32(sh.xs_off + static_cast<uint32_t>(MT * ND) * p.K * ESZ, 128);
+  sh.ring_off = (WK == W_INT8) ? round_up_u32(sh.xraw_off + static_cast<uint32_t>(MT) * p.K * 2, 128) : sh.xraw_off;
   const size_t budget = bulk_smem_budget();
   const size_t room = budget > sh.ring_off ? budget - sh.ring_off : 0;
   int ns = static_cast<int>(std::min<size_t>(ns_max, room / sh.slot_bytes));
@@ -962,20 +1090,21 @@ int dispatch_mma(const GemvParams& p, cudaStream_t st, bool pdl) {
   sh.ns = ns;
   const size_t smem = sh.ring_off + static_cast<size_t>(ns) * sh.slot_bytes;
   if (smem > 220 * 1024) return SN_ERR_UNSUPPORTED;
-  const void* kern = S == 2 ? reinterpret_cast<const void*>(gemv_mma_kernel<MT, 2>)
-                            : reinterpret_cast<const void*>(gemv_mma_kernel<MT, 4>);
+  auto k2 = gemv_mma_kernel<WK, MT, 2>;
+  auto k4 = gemv_mma_kernel<WK, MT, 4>;
+  const void* kern = S == 2 ? reinterpret_cast<const void*>(k2) : reinterpret_cast<const void*>(k4);
   if (!ensure_smem(kern, smem)) return SN_ERR_UNSUPPORTED;
-  if (S == 2) return launch(gemv_mma_kernel<MT, 2>, dim3(grid), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
-  return launch(gemv_mma_kernel<MT, 4>, dim3(grid), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
+  if (S == 2) return launch(k2, dim3(grid), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
+  return launch(k4, dim3(grid), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
 }
 
 template <int WK, int MT>
 int dispatch_mt(const GemvParams& p, int batch, size_t smem, cudaStream_t st, bool pdl, bool wvec) {
   constexpr int EPC = WT<WK>::EPC;
   if (!wvec) return launch_gemv(gemv_scalar_kernel<WK, MT>, p, kWarps, batch, smem, st, pdl);
-  if constexpr (WK == W_BF16) {
+  if constexpr (WK != W_E4M3) {
     if (gemv_kernel_choice() == 0 && batch == 1) {
-      const int rc = dispatch_mma<MT>(p, st, pdl);
+      const int rc = dispatch_mma<WK, MT>(p, st, pdl);
       if (rc != SN_ERR_UNSUPPORTED) return rc;
     }
   }

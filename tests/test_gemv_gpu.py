@@ -56,7 +56,7 @@ def test_bf16_gemv_decode_shapes(G, name, M):
     assert O.rel_err_inf(y32.cpu().numpy(), truth) <= 1e-5
 
 
-@pytest.mark.parametrize("N,K,M", [(1, 8, 1), (7, 24, 3), (1025, 2048, 4), (33, 1000, 2), (300, 12, 1),
+@pytest.mark.parametrize("N,K,M", [(1, 8, 1), (7, 24, 3), (1025, 2048, 4), (300, 1280, 3), (33, 1000, 2), (300, 12, 1),
                                    (96, 6152, 2), (130, 16384, 1)])
 def test_bf16_gemv_odd_shapes(G, N, K, M):
     x, W = make(N, K, M, seed=N + K)
@@ -145,7 +145,7 @@ def test_quantize_codes_bit_exact(G, kind):
 
 @pytest.mark.parametrize("kind", ["int8", "e4m3"])
 @pytest.mark.parametrize("M", [1, 2, 4])
-@pytest.mark.parametrize("NK", [(8512, 2048), (2048, 4096), (1000, 1040), (64, 24)])
+@pytest.mark.parametrize("NK", [(8512, 2048), (2048, 4096), (777, 1280), (1000, 1040), (64, 24)])
 def test_quantized_gemv_matches_dequant_oracle(G, kind, M, NK):
     N, K = NK
     x, W = make(N, K, M, seed=11)
@@ -158,6 +158,26 @@ def test_quantized_gemv_matches_dequant_oracle(G, kind, M, NK):
     yb = G.gemv_quantized(x, qw, out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
     assert O.rel_err_inf(yb.float().cpu().numpy(), truth) <= 1e-2
+
+
+@pytest.mark.parametrize("kind", ["int8", "e4m3"])
+def test_quantized_gemv_extreme_activations(G, kind):
+    # The tensor-core path stages x as f16 times a power of two per x row:
+    # activations far outside f16's range must come through unchanged.
+    x, W = make(1024, 2048, 2, seed=17)
+    x = x.float()
+    x[0] *= 3.0e6      # beyond f16's largest finite value
+    x[1] *= 1.0e-30    # far below f16's smallest subnormal
+    x = x.to(torch.bfloat16)
+    qw = G.quantize_weight(W, kind)
+    y = G.gemv_quantized(x, qw)
+    torch.cuda.synchronize()
+    truth = O.dequant_gemv_ref(bits(x), qw.q.cpu().numpy(), qw.scale.cpu().numpy(), kind)
+    out = y.cpu().numpy()
+    for m in range(2):
+        t = np.asarray(truth[m], np.float64)
+        assert np.isfinite(out[m]).all() and np.abs(t).max() > 0
+        assert np.abs(out[m] - t).max() / np.abs(t).max() <= 1e-3
 
 
 def test_quantized_gemv_unaligned_rows(G):
