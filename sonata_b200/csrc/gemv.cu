@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(kBulkThreads, 2) gemv_bulk_kernel(const GemvPa
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core decode GEMV (bf16 or int8 weights, one batch entry).
+// Tensor-core decode GEMV (bf16, int8 or e4m3 weights, one batch entry).
 //
 // The same bulk-copy ring as gemv_bulk_kernel, but the tensor core does the
 // dot products, so the CUDA cores issue almost nothing per weight byte and a
@@ -632,8 +632,13 @@ __global__ void __launch_bounds__(kBulkThreads, 2) gemv_bulk_kernel(const GemvPa
 // int8 plane of B; TMEM holds three exact s32 partial sums per row, combined
 // in 64-bit integers: y = (sum_k q_k X_k) * 2^-e_m * scale_row.  The only
 // approximation is the rounding of x to 22 significant bits (absolute error
-// at most 2^-23 of max|x| per element).  An x row holding inf or NaN gives
-// NaN outputs.
+// at most 2^-23 of max|x| per element).
+// e4m3: the codes feed kind::f8f6f4 directly.  x row m is scaled by 2^e_m
+// (max in [2^7, 2^8)) and written as the sum of two e4m3 terms t1 = rn(x),
+// t2 = rn(x - t1): exact for every element of at least 2^-2 (bf16 has 8
+// significant bits, e4m3 4), absolute error at most 2^-10 below that (2^-17
+// of max|x|).  Two B planes, products exact, fp32 accumulation in TMEM.
+// An x row holding inf or NaN gives NaN outputs on both 8-bit paths.
 //
 // Warps: 0 = weight producer (no griddepcontrol.wait: weights are frozen),
 // 1 = TMEM owner and MMA issuer (bf16: also the x copy), 2..5 = epilogue
@@ -689,7 +694,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
   constexpr int R = 16 / S;
   constexpr int G = 8 * S;  // TMEM lanes (and columns) per weight row
   constexpr int ESZ = WT<WK>::ESZ;
-  constexpr int ND = (WK == W_INT8) ? 3 : 1;  // B planes per x row
+  constexpr int ND = (WK == W_INT8) ? 3 : (WK == W_E4M3) ? 2 : 1;  // B planes per x row
   const int ns = sh.ns;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + ns;
@@ -778,7 +783,8 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
         tc::fence_proxy_async_smem();
       }
     } else {
-      // x rows by bulk copy, then three int8 digit planes of rint(x * 2^e_m)
+      // x rows by bulk copy, then the B planes of x * 2^e_m: three int8 digits
+      // of rint(x * 2^e_m), or two e4m3 terms
       if (warp >= 2) {
         const int xt = threadIdx.x - 64;  // 0..127
         const __nv_bfloat16* xraw = reinterpret_cast<const __nv_bfloat16*>(smem + sh.xraw_off);
@@ -811,12 +817,12 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
           // too: E = -127): scale by 2^e, e = 21 - E, as two exact
           // power-of-two factors (e in [-107, 148])
           const int ebits = static_cast<int>(xmax[m] >> 7);
-          const int e = 21 - (ebits - 127);
+          const int e = (WK == W_INT8 ? 21 : 7) - (ebits - 127);
           const float up1 = __uint_as_float(static_cast<uint32_t>(127 + e / 2) << 23);
           const float up2 = __uint_as_float(static_cast<uint32_t>(127 + (e - e / 2)) << 23);
           if (xt == 0) xexp[m] = (ebits == 255) ? INT_MIN : e;  // non-finite x row
           for (int c = xt; c < cpr; c += 128) {
-            uint32_t dg[3][2] = {{0, 0}, {0, 0}, {0, 0}};  // digit d of 8 elements
+            uint32_t dg[ND][2] = {};  // plane d of 8 elements
             if (m < p.M) {
               const uint4 v = xr[m * cpr + c];
               const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -824,18 +830,31 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
               for (int e = 0; e < 8; ++e) {
                 const uint32_t h = w[e >> 1];
                 const float xf = (e & 1) ? bf16hi(h) : bf16lo(h);
-                int X = __float2int_rn((xf * up1) * up2);  // |X| < 2^22
-                const int d0 = static_cast<int8_t>(X & 0xFF);
-                X = (X - d0) >> 8;
-                const int d1 = static_cast<int8_t>(X & 0xFF);
-                const int d2 = (X - d1) >> 8;  // |d2| <= 64
-                dg[0][e >> 2] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * (e & 3));
-                dg[1][e >> 2] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * (e & 3));
-                dg[2][e >> 2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * (e & 3));
+                const float xs = (xf * up1) * up2;
+                uint32_t b[ND];
+                if constexpr (WK == W_INT8) {
+                  int X = __float2int_rn(xs);  // |X| < 2^22
+                  const int d0 = static_cast<int8_t>(X & 0xFF);
+                  X = (X - d0) >> 8;
+                  const int d1 = static_cast<int8_t>(X & 0xFF);
+                  const int d2 = (X - d1) >> 8;  // |d2| <= 64
+                  b[0] = static_cast<uint32_t>(d0) & 0xFFu;
+                  b[1] = static_cast<uint32_t>(d1) & 0xFFu;
+                  b[2] = static_cast<uint32_t>(d2) & 0xFFu;
+                } else {
+                  // |xs| < 2^8: no saturation; t1 + t2 reproduces xs to 2^-10
+                  const __nv_fp8_storage_t t1 = __nv_cvt_float_to_fp8(xs, __NV_SATFINITE, __NV_E4M3);
+                  const float r = xs - __half2float(__half(__nv_cvt_fp8_to_halfraw(t1, __NV_E4M3)));
+                  const __nv_fp8_storage_t t2 = __nv_cvt_float_to_fp8(r, __NV_SATFINITE, __NV_E4M3);
+                  b[0] = t1;
+                  b[1] = t2;
+                }
+#pragma unroll
+                for (int d = 0; d < ND; ++d) dg[d][e >> 2] |= b[d] << (8 * (e & 3));
               }
             }
 #pragma unroll
-            for (int d = 0; d < 3; ++d)
+            for (int d = 0; d < ND; ++d)
               *reinterpret_cast<uint2*>(xs + (static_cast<size_t>(d) * MT + m) * p.K + c * 8) =
                   make_uint2(dg[d][0], dg[d][1]);
           }
@@ -853,7 +872,9 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
     if (warp == 1) {
       // ---------------- MMA issuer ----------------
       if (lane == 0) {
-        const uint32_t idesc = (WK == W_INT8) ? tc::idesc_s8_s32(128, sh.N) : tc::idesc_bf16_f32(128, sh.N);
+        const uint32_t idesc = (WK == W_INT8)   ? tc::idesc_s8_s32(128, sh.N)
+                               : (WK == W_E4M3) ? tc::idesc_e4m3_f32(128, sh.N)
+                                                : tc::idesc_bf16_f32(128, sh.N);
         const uint64_t db0 = tc::smem_desc_noswz(xs, 128, L);
         bool x_ok = true;
         if constexpr (WK == W_BF16) x_ok = mbar_wait_bounded(xbar, 0);
@@ -871,6 +892,8 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
           for (uint32_t k = 0; k < nk; ++k) {  // 256 bytes of every segment per MMA
             if constexpr (WK == W_INT8)
               tc::mma_s8(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+            else if constexpr (WK == W_E4M3)
+              tc::mma_e4m3(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
             else
               tc::mma_bf16(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
           }
@@ -886,15 +909,15 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
       const int q = warp & 3;
       const int i = q * 32 + lane;  // A row = TMEM lane
       const int r = i / G;          // weight row inside the slot
-      // int8 row scales are frozen weights: fetch slot t + 1's while slot t computes
+      // 8-bit row scales are frozen weights: fetch slot t + 1's while slot t computes
       float rs_next = 0.f;
-      if constexpr (WK == W_INT8) rs_next = (r < min(R, nrows)) ? p.scale[r0 + r] : 0.f;
+      if constexpr (WK != W_BF16) rs_next = (r < min(R, nrows)) ? p.scale[r0 + r] : 0.f;
       for (int t = 0; t < ntiles; ++t) {
         const int b = t & (nacc - 1);
         const int first = r0 + t * R;
         const int cnt = min(R, r1 - first);
         float rs = 0.f;
-        if constexpr (WK == W_INT8) {
+        if constexpr (WK != W_BF16) {
           rs = rs_next;
           if (t + 1 < ntiles) rs_next = (r < min(R, nrows - (t + 1) * R)) ? p.scale[first + R + r] : 0.f;
         }
@@ -911,6 +934,19 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
 #pragma unroll
             for (int o = G / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             if ((lane & (G - 1)) == 0 && r < cnt) store_row<MT>(p, p.y, first + r, m, v);
+          } else if constexpr (WK == W_E4M3) {
+            float v = 0.f;
+#pragma unroll
+            for (int d = 0; d < ND; ++d) v += diag_entry<S>(taddr + (d * MT + m) * G, lane);
+#pragma unroll
+            for (int o = G / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if ((lane & (G - 1)) == 0 && r < cnt) {
+              const int e = xexp[m];
+              const float dot = (e == INT_MIN) ? __int_as_float(0x7FC00000)
+                                               : static_cast<float>(static_cast<double>(v) *
+                                                                    __longlong_as_double(static_cast<long long>(1023 - e) << 52));
+              store_row<MT>(p, p.y, first + r, m, dot * rs);
+            }
           } else {
             int v[3];
 #pragma unroll
@@ -1064,7 +1100,7 @@ int mma_segments(int K, int esz, int MT, int nd) {
 template <int WK, int MT>
 int dispatch_mma(const GemvParams& p, cudaStream_t st, bool pdl) {
   constexpr int ESZ = WT<WK>::ESZ;
-  constexpr int ND = (WK == W_INT8) ? 3 : 1;
+  constexpr int ND = (WK == W_INT8) ? 3 : (WK == W_E4M3) ? 2 : 1;
   if (!p.x_vec || (reinterpret_cast<uintptr_t>(p.W) & 15) || (p.ldw * ESZ) % 16 != 0) return SN_ERR_UNSUPPORTED;
   const int S = mma_segments(p.K, ESZ, MT, ND);
   if (S == 0) return SN_ERR_UNSUPPORTED;
@@ -1081,7 +1117,7 @@ int dispatch_mma(const GemvParams& p, cudaStream_t st, bool pdl) {
   const int ns_max = 16;
   sh.xs_off = 1024;  // barriers, TMEM address and x scales below
   sh.xraw_off = round_up_u32(sh.xs_off + static_cast<uint32_t>(MT * ND) * p.K * ESZ, 128);
-  sh.ring_off = (WK == W_INT8) ? round_up_u32(sh.xraw_off + static_cast<uint32_t>(MT) * p.K * 2, 128) : sh.xraw_off;
+  sh.ring_off = (WK != W_BF16) ? round_up_u32(sh.xraw_off + static_cast<uint32_t>(MT) * p.K * 2, 128) : sh.xraw_off;
   const size_t budget = bulk_smem_budget();
   const size_t room = budget > sh.ring_off ? budget - sh.ring_off : 0;
   int ns = static_cast<int>(std::min<size_t>(ns_max, room / sh.slot_bytes));
@@ -1102,11 +1138,9 @@ template <int WK, int MT>
 int dispatch_mt(const GemvParams& p, int batch, size_t smem, cudaStream_t st, bool pdl, bool wvec) {
   constexpr int EPC = WT<WK>::EPC;
   if (!wvec) return launch_gemv(gemv_scalar_kernel<WK, MT>, p, kWarps, batch, smem, st, pdl);
-  if constexpr (WK != W_E4M3) {
-    if (gemv_kernel_choice() == 0 && batch == 1) {
-      const int rc = dispatch_mma<WK, MT>(p, st, pdl);
-      if (rc != SN_ERR_UNSUPPORTED) return rc;
-    }
+  if (gemv_kernel_choice() == 0 && batch == 1) {
+    const int rc = dispatch_mma<WK, MT>(p, st, pdl);
+    if (rc != SN_ERR_UNSUPPORTED) return rc;
   }
   if (gemv_kernel_choice() <= 1) {
     const int rc = dispatch_bulk<WK, MT>(p, batch, st, pdl);
