@@ -298,6 +298,9 @@ def run_ours(args):
                "sample": f"torch F.linear bf16 over 2 of the 26 layers' 6 GEMVs (283.6 MB), "
                          f"{it} passes in {secs:.1f} s"}
 
+    if world > 1:  # every collective of the run is done: leave the group on every rank
+        import torch.distributed as dist
+        dist.destroy_process_group()
     if rank != 0:
         return 0
     achieved = sb / (t / args.steps) / 1e9  # per launch: (bytes/156) / (time/156)
@@ -336,7 +339,7 @@ def run_ours(args):
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": world * launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
