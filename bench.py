@@ -22,7 +22,9 @@ its decode step.  A step is one replay of that graph.
 * ``cpu_baseline``: the reference's CPU path (torch ``F.linear`` in bf16, see
   oracle/cpu_baseline.py) on the host cores, rank 0 at N=1 only.
 * ``snake_conv``: the second half of the metric -- the DAC fused Snake+Conv1d
-  in microseconds per second of 44.1 kHz audio.
+  in microseconds per second of 44.1 kHz audio, one stream.
+* ``snake_conv_64_streams`` / ``head_256_streams``: BASELINE configs 5 and 4
+  with their independent streams sharded over the N GPUs (strong scaling).
 
 Multi-GPU: config 2 is batch-1 decode, so N GPUs run N independent replicas
 (weak scaling, no collective on the data path); torch.distributed (NCCL) only
@@ -244,6 +246,59 @@ def bench_snake_conv(warmup=2, reps=3):
 
 
 # ---------------------------------------------------------------------------
+# Configs 4 and 5 on N GPUs: independent streams sharded over the ranks
+# (sonata_b200.shard.shard_range), no collective on the data path; the job
+# time is the max over ranks of each rank's CUDA-event time (strong scaling:
+# the total number of streams is fixed).
+# ---------------------------------------------------------------------------
+SNAKE_STREAMS = 64
+HEAD_STREAMS = 256
+
+
+def sharded_snake(world, rank):
+    from sonata_b200.kernels import fused_snake_conv as fsc
+    from sonata_b200.shard import shard_range
+    a, b = shard_range(SNAKE_STREAMS, world, rank)
+    barrier(world)
+    r = fsc.bench_dac_stream(warmup=1, reps=2, streams=b - a)
+    t_us = max_over_ranks(r["us_per_pass"], world)
+    audio = fsc.AUDIO_SECONDS * SNAKE_STREAMS
+    flops = fsc.stream_flops(SNAKE_STREAMS)
+    return {"metric": "DAC snake-conv µs per audio-sec, 64 streams sharded over the GPUs",
+            "value": round(t_us / audio, 3), "unit": "us per audio-second", "streams": SNAKE_STREAMS,
+            "streams_per_gpu": b - a, "n_gpus": world, "us_per_pass": round(t_us, 1),
+            "realtime_factor": round(audio / (t_us * 1e-6), 1),
+            "useful_tflops": round(flops / (t_us * 1e-6) / 1e12, 1), "scaling": "strong"}
+
+
+def sharded_head(world, rank, reps=20):
+    from sonata_b200.kernels.bmm import CodebookHead
+    from sonata_b200.shard import shard_range
+    ncb, K, N = 9, 2048, 1025
+    a, b = shard_range(HEAD_STREAMS, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(4321)
+    head = CodebookHead((torch.randn(ncb, K, N, device="cuda", generator=g) * 0.02).to(torch.bfloat16))
+    hid = torch.randn(ncb, b - a, K, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty(ncb, b - a, N, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        head(hid, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        head(hid, out=out)
+    t = time_replays(gr, reps, 3, world)
+    t_us = max_over_ranks(t, world) / reps * 1e6
+    del gr
+    bytes_job = world * ncb * K * N * 2 + HEAD_STREAMS * ncb * (K * 2 + N * 4)
+    return {"metric": "codebook-head BMM µs per call, 256 streams sharded over the GPUs", "value": round(t_us, 2),
+            "unit": "us", "streams": HEAD_STREAMS, "streams_per_gpu": b - a, "n_gpus": world,
+            "gbs": round(bytes_job / (t_us * 1e-6) / 1e9, 1),
+            "tflops": round(2 * ncb * HEAD_STREAMS * K * N / (t_us * 1e-6) / 1e12, 1), "scaling": "strong"}
+
+
+# ---------------------------------------------------------------------------
 def run_ours(args):
     world, rank, local = dist_setup(args.gpus)
     hbm, tf_burst, tf_sust, peak_kind = peaks()
@@ -298,6 +353,11 @@ def run_ours(args):
                "sample": f"torch F.linear bf16 over 2 of the 26 layers' 6 GEMVs (283.6 MB), "
                          f"{it} passes in {secs:.1f} s"}
 
+    sharded = {}
+    if not args.skip_sharded:
+        sharded["snake_conv_64_streams"] = sharded_snake(world, rank)
+        sharded["head_256_streams"] = sharded_head(world, rank)
+
     if world > 1:  # every collective of the run is done: leave the group on every rank
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -345,6 +405,7 @@ def run_ours(args):
     }
     if snake is not None:
         line["snake_conv"] = snake
+    line.update(sharded)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -460,6 +521,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-snake", action="store_true")
+    ap.add_argument("--skip-sharded", action="store_true", help="skip the stream-sharded config 4 / 5 sections")
     ap.add_argument("--case", choices=["gemv", "snake", "head", "ssd"], default=None,
                     help="run one kernel on one shape (profiling / microbenchmark)")
     ap.add_argument("--shape", default="", help="e.g. 8512x2048x1 (gemv N x K x M), 384x55168x3 (snake C x T x d)")

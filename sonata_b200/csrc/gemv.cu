@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(kBulkThreads, 2) gemv_bulk_kernel(const GemvPa
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core decode GEMV (bf16, int8 or e4m3 weights, one batch entry).
+// Tensor-core decode GEMV (bf16, int8 or e4m3 weights; grid.y = batch entry).
 //
 // The same bulk-copy ring as gemv_bulk_kernel, but the tensor core does the
 // dot products, so the CUDA cores issue almost nothing per weight byte and a
@@ -709,6 +709,11 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
   uint8_t* ring = smem + sh.ring_off;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // batch entry blockIdx.y (independent W, x, y, scale); rows split over blockIdx.x
+  const uint8_t* Wb = p.W + static_cast<int64_t>(blockIdx.y) * p.sW * ESZ;
+  const __nv_bfloat16* xb = p.x + static_cast<int64_t>(blockIdx.y) * p.sx;
+  void* yb = reinterpret_cast<uint8_t*>(p.y) + static_cast<int64_t>(blockIdx.y) * p.sy * (p.y_f32 ? 4 : 2);
+  const float* sb = (WK != W_BF16) ? p.scale + static_cast<int64_t>(blockIdx.y) * p.sS : nullptr;
   const int r0 = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
   const int r1 = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
   const int nrows = r1 - r0;
@@ -750,11 +755,11 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
         uint8_t* dst = ring + static_cast<size_t>(s) * sh.slot_bytes;
         mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(cnt) * row_bytes);
         if (p.ldw == p.K) {
-          bulk_g2s(dst, p.W + static_cast<int64_t>(first) * p.ldw * ESZ, static_cast<uint32_t>(cnt) * row_bytes,
+          bulk_g2s(dst, Wb + static_cast<int64_t>(first) * p.ldw * ESZ, static_cast<uint32_t>(cnt) * row_bytes,
                    full + s, pol);
         } else {
           for (int r = 0; r < cnt; ++r)
-            bulk_g2s(dst + static_cast<size_t>(r) * row_bytes, p.W + static_cast<int64_t>(first + r) * p.ldw * ESZ,
+            bulk_g2s(dst + static_cast<size_t>(r) * row_bytes, Wb + static_cast<int64_t>(first + r) * p.ldw * ESZ,
                      row_bytes, full + s, pol);
         }
       }
@@ -775,7 +780,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
           const uint64_t pol = l2_policy_evict_normal();
           mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * row_bytes);
           for (int m = 0; m < p.M; ++m)
-            bulk_g2s(xs + static_cast<size_t>(m) * row_bytes, p.x + m * p.ldx, row_bytes, xbar, pol);
+            bulk_g2s(xs + static_cast<size_t>(m) * row_bytes, xb + m * p.ldx, row_bytes, xbar, pol);
         }
       } else if (MT > 1) {
         for (int i = threadIdx.x - 64 + p.M * cpr; i < MT * cpr; i += 128)
@@ -792,7 +797,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
           const uint64_t pol = l2_policy_evict_normal();
           mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * p.K * 2);
           for (int m = 0; m < p.M; ++m)
-            bulk_g2s(const_cast<__nv_bfloat16*>(xraw) + m * p.K, p.x + m * p.ldx, p.K * 2, xbar, pol);
+            bulk_g2s(const_cast<__nv_bfloat16*>(xraw) + m * p.K, xb + m * p.ldx, p.K * 2, xbar, pol);
         }
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) record_status(SN_ERR_TIMEOUT);
         const uint4* xr = reinterpret_cast<const uint4*>(xraw);
@@ -911,7 +916,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
       const int r = i / G;          // weight row inside the slot
       // 8-bit row scales are frozen weights: fetch slot t + 1's while slot t computes
       float rs_next = 0.f;
-      if constexpr (WK != W_BF16) rs_next = (r < min(R, nrows)) ? p.scale[r0 + r] : 0.f;
+      if constexpr (WK != W_BF16) rs_next = (r < min(R, nrows)) ? sb[r0 + r] : 0.f;
       for (int t = 0; t < ntiles; ++t) {
         const int b = t & (nacc - 1);
         const int first = r0 + t * R;
@@ -919,7 +924,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
         float rs = 0.f;
         if constexpr (WK != W_BF16) {
           rs = rs_next;
-          if (t + 1 < ntiles) rs_next = (r < min(R, nrows - (t + 1) * R)) ? p.scale[first + R + r] : 0.f;
+          if (t + 1 < ntiles) rs_next = (r < min(R, nrows - (t + 1) * R)) ? sb[first + R + r] : 0.f;
         }
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(tfull + b, (t >> sh.acc_log2) & 1))) {
           record_status(SN_ERR_TIMEOUT);
@@ -933,7 +938,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
             float v = diag_entry<S>(taddr + m * G, lane);
 #pragma unroll
             for (int o = G / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if ((lane & (G - 1)) == 0 && r < cnt) store_row<MT>(p, p.y, first + r, m, v);
+            if ((lane & (G - 1)) == 0 && r < cnt) store_row<MT>(p, yb, first + r, m, v);
           } else if constexpr (WK == W_E4M3) {
             float v = 0.f;
 #pragma unroll
@@ -945,7 +950,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
               const float dot = (e == INT_MIN) ? __int_as_float(0x7FC00000)
                                                : static_cast<float>(static_cast<double>(v) *
                                                                     __longlong_as_double(static_cast<long long>(1023 - e) << 52));
-              store_row<MT>(p, p.y, first + r, m, dot * rs);
+              store_row<MT>(p, yb, first + r, m, dot * rs);
             }
           } else {
             int v[3];
@@ -964,7 +969,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
                                     ? __int_as_float(0x7FC00000)
                                     : static_cast<float>(static_cast<double>(acc) *
                                                          __longlong_as_double(static_cast<long long>(1023 - e) << 52));
-              store_row<MT>(p, p.y, first + r, m, dot * rs);
+              store_row<MT>(p, yb, first + r, m, dot * rs);
             }
           }
         }
@@ -1096,10 +1101,11 @@ int mma_segments(int K, int esz, int MT, int nd) {
 }
 
 // Returns SN_ERR_UNSUPPORTED when the tensor-core GEMV does not apply
-// (bf16 or int8 weights, one batch entry, aligned rows and x).
+// (16-byte aligned rows, x rows and batch strides; K within mma_segments' rules).
 template <int WK, int MT>
-int dispatch_mma(const GemvParams& p, cudaStream_t st, bool pdl) {
+int dispatch_mma(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
   constexpr int ESZ = WT<WK>::ESZ;
+  if (batch > 1 && ((p.sW * ESZ) % 16 != 0 || p.sx % 8 != 0)) return SN_ERR_UNSUPPORTED;
   constexpr int ND = (WK == W_INT8) ? 3 : (WK == W_E4M3) ? 2 : 1;
   if (!p.x_vec || (reinterpret_cast<uintptr_t>(p.W) & 15) || (p.ldw * ESZ) % 16 != 0) return SN_ERR_UNSUPPORTED;
   const int S = mma_segments(p.K, ESZ, MT, ND);
@@ -1111,7 +1117,8 @@ int dispatch_mma(const GemvParams& p, cudaStream_t st, bool pdl) {
   sh.acc_log2 = (4 * sh.N <= 256) ? 2 : (2 * sh.N <= 256) ? 1 : 0;
   sh.tcols = tc::tmem_cols_for(sh.N << sh.acc_log2);
   sh.slot_bytes = static_cast<uint32_t>(R) * p.K * ESZ;
-  const int grid = std::min(sm_count(), p.N);
+  // CTAs per batch entry: the SMs shared out over the entries
+  const int grid = std::max(1, std::min(p.N, sm_count() / batch));
   const int rows_per_cta = (p.N + grid - 1) / grid;
   const int tiles_per_cta = (rows_per_cta + R - 1) / R;
   const int ns_max = 16;
@@ -1130,16 +1137,16 @@ int dispatch_mma(const GemvParams& p, cudaStream_t st, bool pdl) {
   auto k4 = gemv_mma_kernel<WK, MT, 4>;
   const void* kern = S == 2 ? reinterpret_cast<const void*>(k2) : reinterpret_cast<const void*>(k4);
   if (!ensure_smem(kern, smem)) return SN_ERR_UNSUPPORTED;
-  if (S == 2) return launch(k2, dim3(grid), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
-  return launch(k4, dim3(grid), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
+  if (S == 2) return launch(k2, dim3(grid, batch), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
+  return launch(k4, dim3(grid, batch), dim3(kMmaGemvThreads), smem, st, pdl, p, sh);
 }
 
 template <int WK, int MT>
 int dispatch_mt(const GemvParams& p, int batch, size_t smem, cudaStream_t st, bool pdl, bool wvec) {
   constexpr int EPC = WT<WK>::EPC;
   if (!wvec) return launch_gemv(gemv_scalar_kernel<WK, MT>, p, kWarps, batch, smem, st, pdl);
-  if (gemv_kernel_choice() == 0 && batch == 1) {
-    const int rc = dispatch_mma<WK, MT>(p, st, pdl);
+  if (gemv_kernel_choice() == 0) {
+    const int rc = dispatch_mma<WK, MT>(p, batch, st, pdl);
     if (rc != SN_ERR_UNSUPPORTED) return rc;
   }
   if (gemv_kernel_choice() <= 1) {
