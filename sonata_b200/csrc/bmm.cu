@@ -146,6 +146,261 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) tc::tmem_dealloc(tmem, tcols);
 }
 
+// ---------------------------------------------------------------------------
+// codebook head, K split over a CTA pair (B >= 5)
+//
+// The 128-row weight tiles x stream tiles are spread over clusters of two
+// CTAs (one per SM, 74 clusters on 148 SMs; a cluster loops if there are more
+// tiles).  CTA rank r accumulates the K half r of its tile in TMEM.  The pair
+// then reduces through distributed shared memory in a fixed order: each CTA
+// owns half of the stream columns, sends the other half of its partial tile
+// to its peer (st.shared::cluster), and adds the peer's half to its own,
+// k-half 0 first, so the result does not depend on timing.  Rows past the
+// last full 128-row tile (row 1024 of the 1025-row head) are dot products on
+// the CUDA cores of the epilogue warps of every CTA, while the MMAs run.
+// ---------------------------------------------------------------------------
+constexpr int kSkThreads = 192;
+constexpr int kSkStagesMax = 8;
+
+struct HeadSkParams {
+  float* out;                    // [ncb, B, N]
+  const __nv_bfloat16* hidden;   // [ncb, B, K]
+  const __nv_bfloat16* Wt;       // [ncb, N, K]
+  int ncb, B, K, N;
+  int bt, nbt;                   // stream tile (UMMA N, multiple of 32) and tiles per codebook
+  int nrt;                       // full 128-row tiles per codebook
+  int ntiles;                    // ncb * nrt * nbt
+  int stages;
+  uint32_t stage_bytes, a_bytes;
+  uint32_t recv_off, bar_off;    // recv: [bt / 2 columns][128 rows] fp32
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// arrive on an mbarrier of another CTA of the cluster, ordering this thread's
+// earlier (distributed) shared-memory writes before it
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (globaltimer_ns() - t0 > 1000000000ull) return false;
+  }
+  return true;
+}
+// every thread of both CTAs, exactly once per call site
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kSkThreads, 1)
+    head_splitk_kernel(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapH,
+                       const HeadSkParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int ns = p.stages;
+  float* recv = reinterpret_cast<float*>(smem + p.recv_off);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+  uint64_t* empty = full + ns;
+  uint64_t* tfull = empty + ns;
+  uint64_t* tempty = tfull + 1;
+  uint64_t* rfull = tempty + 1;   // peer's half of my columns has landed in recv
+  uint64_t* rempty = rfull + 1;   // peer has read my half of its columns (recv reusable)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int nkb = p.K / 64, kb_half = nkb / 2, kb0 = static_cast<int>(rank) * kb_half;
+  const uint32_t tcols = tc::tmem_cols_for(p.bt);
+  const int half = p.bt / 2;
+  const int own_lo = static_cast<int>(rank) * half, peer_lo = static_cast<int>(peer) * half;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 4);
+    mbar_init(rfull, 128);   // every epilogue thread of the peer
+    mbar_init(rempty, 128);
+    fence_barrier_init();
+    tc::prefetch_map(&mapW);
+    tc::prefetch_map(&mapH);
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, tcols);
+  tc::fence_before_sync();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer: K half `rank` of each tile ----------------
+    int it = 0;
+    bool ok = true;
+    for (int t = cluster; t < p.ntiles && ok; t += nclusters) {
+      const int bti = t % p.nbt, rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);
+      for (int j = 0; j < kb_half; ++j, ++it) {
+        const int s = it % ns, k = it / ns;
+        if (k > 0 && !mbar_wait_bounded(empty + s, (k - 1) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        uint8_t* a = smem + s * p.stage_bytes;
+        mbar_arrive_expect_tx(full + s, p.stage_bytes);
+        tc::tma_load_3d(a, &mapW, (kb0 + j) * 64, rt * 128, cb, full + s);
+        tc::tma_load_3d(a + p.a_bytes, &mapH, (kb0 + j) * 64, bti * p.bt, cb, full + s);
+      }
+    }
+    if (!ok) {  // error path: let issued copies land before the CTA exits
+      for (int j = (it > ns ? it - ns : 0); j < it; ++j) mbar_wait_bounded(full + j % ns, (j / ns) & 1);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = tc::idesc_bf16_f32(128, p.bt);
+    int it = 0, j = 0;
+    bool ok = true;
+    for (int t = cluster; t < p.ntiles && ok; t += nclusters, ++j) {
+      if (j > 0 && !mbar_wait_bounded(tempty, (j - 1) & 1)) {
+        record_status(SN_ERR_TIMEOUT);
+        break;
+      }
+      tc::fence_after_sync();
+      for (int kb = 0; kb < kb_half; ++kb, ++it) {
+        const int s = it % ns;
+        if (!mbar_wait_bounded(full + s, (it / ns) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint8_t* a = smem + s * p.stage_bytes;
+        const uint64_t da = tc::smem_desc_sw128(a), db = tc::smem_desc_sw128(a + p.a_bytes);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) tc::mma_bf16(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+        tc::mma_commit(empty + s);
+      }
+      tc::mma_commit(tfull);
+    }
+  } else if (warp >= 2) {
+    // ---- rows past the last full tile (row 1024 of the head): CUDA-core dot
+    // products, done while this CTA's MMAs run; all loads of a dot issued first
+    {
+      const int nx = p.N - p.nrt * 128;
+      const int64_t items = static_cast<int64_t>(p.ncb) * p.B * nx;
+      const int gw = blockIdx.x * 4 + (warp - 2), nw = gridDim.x * 4;
+      const int nck = p.K / 8;  // 16-byte chunks per row
+      for (int64_t e = gw; e < items; e += nw) {
+        const int x = static_cast<int>(e % nx);
+        const int b = static_cast<int>((e / nx) % p.B);
+        const int cb = static_cast<int>(e / (static_cast<int64_t>(nx) * p.B));
+        const int n = p.nrt * 128 + x;
+        const uint4* hr = reinterpret_cast<const uint4*>(p.hidden + (static_cast<int64_t>(cb) * p.B + b) * p.K);
+        const uint4* wr = reinterpret_cast<const uint4*>(p.Wt + (static_cast<int64_t>(cb) * p.N + n) * p.K);
+        float acc = 0.f;
+        for (int i0 = lane; i0 < nck; i0 += 32 * 8) {
+          uint4 hv[8], wv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = i0 + 32 * u;
+            hv[u] = i < nck ? hr[i] : make_uint4(0, 0, 0, 0);
+            wv[u] = i < nck ? wr[i] : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t hw[4] = {hv[u].x, hv[u].y, hv[u].z, hv[u].w}, ww[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              acc = fmaf(bf16lo(hw[v]), bf16lo(ww[v]), acc);
+              acc = fmaf(bf16hi(hw[v]), bf16hi(ww[v]), acc);
+            }
+          }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) p.out[(static_cast<int64_t>(cb) * p.B + b) * p.N + n] = acc;
+      }
+    }
+    // ---------------- epilogue: exchange halves with the peer, add, store ----
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // TMEM lane = weight row inside the tile
+    const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t peer_recv = mapa_shared(smem_u32(recv), peer);
+    const uint32_t peer_rfull = mapa_shared(smem_u32(rfull), peer);
+    const uint32_t peer_rempty = mapa_shared(smem_u32(rempty), peer);
+    int j = 0;
+    for (int t = cluster; t < p.ntiles; t += nclusters, ++j) {
+      const int bti = t % p.nbt, rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);
+      bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(tfull, j & 1));
+      // the peer's recv buffer is free once it has read the previous tile's
+      if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait_cluster_bounded(rempty, (j - 1) & 1));
+      if (!ok) {
+        record_status(SN_ERR_TIMEOUT);
+        break;
+      }
+      tc::fence_after_sync();
+      for (int c = 0; c < half; c += 16) {  // the peer's columns of my partial -> its recv[c][row]
+        float v[16];
+        tc::tmem_ld16(tq + peer_lo + c, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) st_cluster_f32(peer_recv + static_cast<uint32_t>(((c + i) * 128 + row) * 4), v[i]);
+      }
+      mbar_arrive_remote(peer_rfull);
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster_bounded(rfull, j & 1))) {
+        record_status(SN_ERR_TIMEOUT);
+        break;
+      }
+      const int n = rt * 128 + row;
+      float* ob = p.out + (static_cast<int64_t>(cb) * p.B) * p.N + n;
+      for (int c = 0; c < half; c += 16) {  // my columns: k-half 0 + k-half 1
+        float v[16];
+        tc::tmem_ld16(tq + own_lo + c, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float r = recv[(c + i) * 128 + row];
+          const float y = (rank == 0) ? (v[i] + r) : (r + v[i]);
+          const int b = bti * p.bt + own_lo + c + i;
+          if (b < p.B) ob[static_cast<int64_t>(b) * p.N] = y;
+        }
+      }
+      mbar_arrive_remote(peer_rempty);  // my recv may be refilled
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty);
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still touch its shared memory
+  if (warp == 1) tc::tmem_dealloc(tmem, tcols);
+}
+
 // W [ncb, K, N] -> Wt [ncb, N, K] (32 x 32 tiles through shared memory)
 __global__ void transpose_kn_kernel(const __nv_bfloat16* __restrict__ W, __nv_bfloat16* __restrict__ Wt, int K,
                                     int N) {
@@ -286,6 +541,66 @@ __global__ void ssd_simt_kernel(const __nv_bfloat16* __restrict__ C, const __nv_
 }  // namespace
 
 int tu_status_bmm(bool reset, cudaStream_t st, int* out) { return read_tu_status(reset, st, out); }
+
+// Codebook head for B >= 5 with K split over CTA pairs; SN_ERR_UNSUPPORTED when
+// the cluster launch or the shared-memory plan does not fit.
+int head_splitk(const void* hidden, const void* Wt, float* logits, int ncb, int B, int K, int N, cudaStream_t st) {
+  HeadSkParams p;
+  p.out = logits;
+  p.hidden = static_cast<const __nv_bfloat16*>(hidden);
+  p.Wt = static_cast<const __nv_bfloat16*>(Wt);
+  p.ncb = ncb;
+  p.B = B;
+  p.K = K;
+  p.N = N;
+  p.bt = std::min(256, (B + 31) / 32 * 32);  // halves of 16-column chunks
+  p.nbt = (B + p.bt - 1) / p.bt;
+  p.nrt = N / 128;
+  p.ntiles = ncb * p.nrt * p.nbt;
+  p.a_bytes = 128 * 64 * 2;
+  p.stage_bytes = p.a_bytes + static_cast<uint32_t>(p.bt) * 64 * 2;
+  const uint32_t recv_bytes = static_cast<uint32_t>(p.bt / 2) * 128 * 4;
+  const size_t cap = 227 * 1024 - 1024 - 256;  // opt-in maximum less the alignment slack and the barriers
+  int stages = static_cast<int>(std::min<size_t>(kSkStagesMax, (cap - recv_bytes) / p.stage_bytes));
+  stages = std::min(stages, K / 128);
+  if (stages < 2) return SN_ERR_UNSUPPORTED;
+  p.stages = stages;
+  p.recv_off = static_cast<uint32_t>(stages) * p.stage_bytes;
+  p.bar_off = p.recv_off + recv_bytes;
+  const size_t smem = 1024 + p.bar_off + 8 * (2 * stages + 4) + 16;
+  CUtensorMap mapW, mapH;
+  const uint64_t dW[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint64_t>(ncb)};
+  const uint64_t sW[2] = {static_cast<uint64_t>(K) * 2, static_cast<uint64_t>(N) * K * 2};
+  const uint32_t bW[3] = {64, 128, 1};
+  const uint64_t dH[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(B), static_cast<uint64_t>(ncb)};
+  const uint64_t sH[2] = {static_cast<uint64_t>(K) * 2, static_cast<uint64_t>(B) * K * 2};
+  const uint32_t bH[3] = {64, static_cast<uint32_t>(p.bt), 1};
+  if (!tc::make_map_bf16_sw128(&mapW, Wt, 3, dW, sW, bW) || !tc::make_map_bf16_sw128(&mapH, hidden, 3, dH, sH, bH))
+    return SN_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(head_splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_UNSUPPORTED;
+  }
+  const int clusters = std::max(1, sm_count() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kSkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, head_splitk_kernel, mapW, mapH, p) != cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_LAUNCH;
+  }
+  return SN_OK;
+}
 }  // namespace sn
 
 extern "C" {
@@ -313,6 +628,10 @@ int sn_codebook_head_bmm(const void* hidden, const void* Wt, float* logits, int 
       if (rc != SN_OK) return rc;
     }
     return SN_OK;
+  }
+  if (K % 128 == 0 && N >= 128) {
+    const int rc = sn::head_splitk(hidden, Wt, logits, ncb, B, K, N, st);
+    if (rc != SN_ERR_UNSUPPORTED) return rc;
   }
   sn::HeadParams p;
   p.out = logits;
