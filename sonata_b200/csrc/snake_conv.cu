@@ -208,6 +208,29 @@ __global__ void __launch_bounds__(kScThreads, 1)
       for (int c = 0; c < nchunks; ++c, ++g) {
         const int ab = g & 1;
         const int i0 = c * 64 + pw * 8;  // first input channel of this warp's group
+        {
+          // pull the next chunk's x lines (this warp's 8 channels x rows) into L2
+          // while this chunk's loads are outstanding: one 128-byte line per lane
+          // and (channel, 32-row step) pair
+          int nb = b, nt0 = tin0, ni0 = i0 + 64;
+          if (c + 1 == nchunks) {
+            int t1, o1;
+            if (j + 1 < my_tiles) {
+              tile_coords(j + 1, nb, t1, o1);
+              nt0 = t1 - p.pad;
+            }
+            ni0 = pw * 8;
+          }
+          const bool more = (c + 1 < nchunks) || (j + 1 < my_tiles);
+          const float* nxb = p.x + static_cast<int64_t>(nb) * p.Cin * p.T;
+#pragma unroll
+          for (int k = lane; k < 8 * kMaxRowIters; k += 32) {
+            const int e = k & 7, it = k >> 3;
+            const int tin = max(nt0 + 32 * it, 0);
+            if (more && ni0 + e < p.Cin && 32 * it < p.rows && tin < p.T)
+              asm volatile("prefetch.global.L2 [%0];" ::"l"(nxb + static_cast<int64_t>(ni0 + e) * p.T + tin));
+          }
+        }
         // issue every x load of this chunk before the first use (memory-level
         // parallelism: 8 channels x up to 7 rows per lane in flight)
         float v[kMaxRowIters][8];
