@@ -13,6 +13,7 @@
 //    with the masked semantics of bmm.py:205-212 (positions >= SEQLEN are
 //    zero): the 4-D TMA maps give the sequence dimension the extent SEQLEN, so
 //    the ragged tail of the last chunk is filled with zeros by the copy engine.
+//    One CTA per 128 x 128 output tile (UMMA M = N = 128).
 //
 // Roles in the tensor-core kernels: warp 0 lane 0 issues TMA, warp 1 owns TMEM
 // and lane 0 of it issues tcgen05.mma, warps 2-5 drain TMEM (32x32b loads, one
@@ -426,7 +427,8 @@ __global__ void transpose_kn_kernel(const __nv_bfloat16* __restrict__ W, __nv_bf
 struct SsdParams {
   float* out;  // [BATCH, NCH, NG, CH, CH]
   int batch, seqlen, ng, dstate, ch, nch;
-  int mtiles;  // CH / 128
+  int mtiles;  // CH / 128 row tiles
+  int ntiles;  // CH / 128 column tiles (UMMA N = 128)
   uint32_t a_bytes, b_bytes;  // per 64-wide K block
 };
 
@@ -443,6 +445,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int u = blockIdx.x;
+  const int nt = u % p.ntiles;
+  u /= p.ntiles;
   const int mt = u % p.mtiles;
   u /= p.mtiles;
   const int g = u % p.ng;
@@ -450,8 +454,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int c = u % p.nch;
   const int b = u / p.nch;
   const int i0 = c * p.ch + mt * 128;  // first sequence row of the A tile
-  const int j0 = c * p.ch;             // first sequence row of the B tile
-  const uint32_t tcols = tc::tmem_cols_for(p.ch);
+  const int j0 = c * p.ch + nt * 128;  // first sequence row of the B tile
+  const uint32_t tcols = 128;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < nkb; ++s) mbar_init(full + s, 1);
@@ -474,7 +478,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::tma_load_4d(a + p.a_bytes, &mapB, kb * 64, g, j0, b, full + kb);
     }
   } else if (warp == 1 && lane == 0) {
-    const uint32_t idesc = tc::idesc_bf16_f32(128, p.ch);
+    const uint32_t idesc = tc::idesc_bf16_f32(128, 128);
     for (int kb = 0; kb < nkb; ++kb) {
       if (!mbar_wait_bounded(full + kb, 0)) {
         record_status(SN_ERR_TIMEOUT);
@@ -492,8 +496,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (__all_sync(0xffffffffu, mbar_wait_bounded(done, 0))) {
       tc::fence_after_sync();
       const int i = mt * 128 + q * 32 + lane;  // row within the chunk
-      float* row = p.out + ((((static_cast<int64_t>(b) * p.nch + c) * p.ng + g) * p.ch) + i) * p.ch;
-      for (int j = 0; j < p.ch; j += 16) {
+      float* row = p.out + ((((static_cast<int64_t>(b) * p.nch + c) * p.ng + g) * p.ch) + i) * p.ch + nt * 128;
+      for (int j = 0; j < 128; j += 16) {
         float v[16];
         tc::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + j, v);
         float4* dst = reinterpret_cast<float4*>(row + j);
@@ -681,8 +685,9 @@ int sn_ssd_chunk_bmm(const void* C, const void* Bm, int64_t sCb, int64_t sCt, in
   p.ch = chunk;
   p.nch = nchunks;
   p.mtiles = chunk / 128;
+  p.ntiles = chunk / 128;
   p.a_bytes = 128 * 64 * 2;
-  p.b_bytes = static_cast<uint32_t>(chunk) * 64 * 2;
+  p.b_bytes = 128 * 64 * 2;
   const bool tc_ok = (chunk == 128 || chunk == 256) && dstate % 64 == 0 && dstate <= 256 && seqlen > 0 &&
                      sn::aligned16(C) && sn::aligned16(Bm) && ((sCg * 2) % 16 == 0) && ((sCt * 2) % 16 == 0) &&
                      ((sCb * 2) % 16 == 0) && ((sBg * 2) % 16 == 0) && ((sBt * 2) % 16 == 0) &&
@@ -697,12 +702,12 @@ int sn_ssd_chunk_bmm(const void* C, const void* Bm, int64_t sCb, int64_t sCt, in
     const uint64_t stB[3] = {static_cast<uint64_t>(sBg) * 2, static_cast<uint64_t>(sBt) * 2,
                              static_cast<uint64_t>(sBb) * 2};
     const uint32_t boxC[4] = {64, 1, 128, 1};
-    const uint32_t boxB[4] = {64, 1, static_cast<uint32_t>(chunk), 1};
+    const uint32_t boxB[4] = {64, 1, 128, 1};
     if (sn::tc::make_map_bf16_sw128(&mapC, C, 4, dims, stC, boxC) &&
         sn::tc::make_map_bf16_sw128(&mapB, Bm, 4, dims, stB, boxB)) {
       if (cudaFuncSetAttribute(sn::ssd_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
           cudaSuccess) {
-        const int units = batch * nchunks * ngroups * p.mtiles;
+        const int units = batch * nchunks * ngroups * p.mtiles * p.ntiles;
         return sn::launch(sn::ssd_mma_kernel, dim3(units), dim3(sn::kTcThreads), smem, st, false, mapC, mapB, p);
       }
       cudaGetLastError();

@@ -97,6 +97,24 @@ def test_codebook_head(Bm, B):
     assert O.rel_err_inf(out.cpu().numpy(), truth) <= 1e-4
 
 
+@pytest.mark.parametrize("ncb,B,K,N", [(9, 8, 2048, 300), (9, 64, 1024, 100), (2, 5, 512, 129),
+                                        (4, 16, 2048, 256), (3, 40, 2048, 1025), (9, 33, 4096, 1025)])
+def test_codebook_head_shapes(Bm, ncb, B, K, N):
+    # row counts with and without a remainder past the last 128-row tile, K
+    # halves of 256..2048, stream tiles that do not fill the MMA N, and
+    # N < 128 (no full tile: the single-CTA tensor-core kernel)
+    g = torch.Generator().manual_seed(ncb * 1000 + B + N)
+    hidden = torch.randn(ncb, B, K, generator=g).to(torch.bfloat16)
+    W = (torch.randn(ncb, K, N, generator=g) * 0.02).to(torch.bfloat16)
+    head = Bm.CodebookHead(W.cuda())
+    out = torch.full((ncb, B, N), float("nan"), device="cuda")
+    head(hidden.cuda(), out=out)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    truth = O.codebook_head_ref(bits(hidden), bits(W))
+    assert O.rel_err_inf(out.cpu().numpy(), truth) <= 1e-4
+
+
 def test_codebook_head_functional_raw_weight(Bm):
     g = torch.Generator().manual_seed(3)
     hidden = torch.randn(3, 16, 256, generator=g).to(torch.bfloat16).cuda()
