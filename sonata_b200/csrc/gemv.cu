@@ -1095,9 +1095,8 @@ int mma_segments(int K, int esz, int MT, int nd) {
   auto small = [&](int S) { return (16 / S) * row <= 32 * 1024; };
   if (forced) return ok(forced) ? forced : 0;
   if (ok(2) && small(2)) return 2;
-  if (ok(4) && small(4)) return 4;
-  if (ok(2)) return 2;
-  return ok(4) ? 4 : 0;
+  if (ok(4)) return 4;  // smaller slots than S = 2 even when above 32 KB
+  return ok(2) ? 2 : 0;
 }
 
 // Returns SN_ERR_UNSUPPORTED when the tensor-core GEMV does not apply
@@ -1113,19 +1112,44 @@ int dispatch_mma(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
   const int R = 16 / S;
   MmaShape sh;
   sh.N = 8 * S * MT * ND;
-  // two CTAs per SM share 512 TMEM columns: at most 256 each
-  sh.acc_log2 = (4 * sh.N <= 256) ? 2 : (2 * sh.N <= 256) ? 1 : 0;
-  sh.tcols = tc::tmem_cols_for(sh.N << sh.acc_log2);
   sh.slot_bytes = static_cast<uint32_t>(R) * p.K * ESZ;
-  // CTAs per batch entry: the SMs shared out over the entries
-  const int grid = std::max(1, std::min(p.N, sm_count() / batch));
+  // CTAs per SM from the weight bytes each SM streams: up to one ring's worth
+  // (~96 KB) one CTA, prefetched whole under programmatic dependent launch;
+  // up to two rings' worth two CTAs; beyond that three, whose three rings
+  // keep more bytes in flight than the next kernel's prefetch would
+  // (measured per shape on B200).  SONATA_GEMV_CTAS_PER_SM overrides (1..4).
+  static const int cps_env = [] {
+    const char* e = getenv("SONATA_GEMV_CTAS_PER_SM");
+    const int v = e ? atoi(e) : 0;
+    return (v >= 1 && v <= 4) ? v : 0;
+  }();
+  const int64_t bytes_per_sm = static_cast<int64_t>(p.N) * p.K * ESZ * batch / sm_count();
+  int cps = cps_env ? cps_env : bytes_per_sm <= 96 * 1024 ? 1 : bytes_per_sm <= 192 * 1024 ? 2 : 3;
+  // TMEM: this kernel's CTAs and the next kernel's (programmatic dependent
+  // launch) share an SM's 512 columns, so each CTA takes at most 512 / (2 cps)
+  // (a CTA whose allocation does not fit would wait for another to exit)
+  auto max_cols = [](int c) { return c == 1 ? 256 : c == 2 ? 128 : 64; };
+  while (cps > 1 && static_cast<int>(tc::tmem_cols_for(sh.N)) > max_cols(cps)) --cps;
+  auto acc_log2_for = [&](int c) {
+    int a = 2;
+    while (a > 0 && static_cast<int>(tc::tmem_cols_for(sh.N << a)) > max_cols(c)) --a;
+    return a;
+  };
+  // at least two accumulators (the MMAs of a slot must not wait for the
+  // previous slot's epilogue): fewer CTAs per SM rather than one accumulator
+  while (cps > 1 && acc_log2_for(cps) == 0) --cps;
+  sh.acc_log2 = acc_log2_for(cps);
+  sh.tcols = tc::tmem_cols_for(sh.N << sh.acc_log2);
+  const int grid = std::max(1, std::min(p.N, cps * sm_count() / batch));
   const int rows_per_cta = (p.N + grid - 1) / grid;
   const int tiles_per_cta = (rows_per_cta + R - 1) / R;
   const int ns_max = 16;
   sh.xs_off = 1024;  // barriers, TMEM address and x scales below
   sh.xraw_off = round_up_u32(sh.xs_off + static_cast<uint32_t>(MT * ND) * p.K * ESZ, 128);
   sh.ring_off = (WK != W_BF16) ? round_up_u32(sh.xraw_off + static_cast<uint32_t>(MT) * p.K * 2, 128) : sh.xraw_off;
-  const size_t budget = bulk_smem_budget();
+  // shared memory: ~half an SM per CTA at one CTA per SM, ~72 KB (two slots)
+  // at two or three (SONATA_GEMV_SMEM_KB overrides)
+  const size_t budget = getenv("SONATA_GEMV_SMEM_KB") ? bulk_smem_budget() : cps == 1 ? 110 * 1024 : 72 * 1024;
   const size_t room = budget > sh.ring_off ? budget - sh.ring_off : 0;
   int ns = static_cast<int>(std::min<size_t>(ns_max, room / sh.slot_bytes));
   ns = std::min(ns, tiles_per_cta);
