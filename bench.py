@@ -55,7 +55,7 @@ LAYERS = 26
 NOMINAL_HBM_GBS = 8000.0
 # Per-launch DRAM traffic of the GEMV kernel from one ncu capture of in_proj
 # (profiles/gemv_mma_kernel_in_proj.md): dram__bytes_read.sum + write.sum.
-NCU_TRAFFIC_IN_PROJ = 34_892_288 + 0
+NCU_TRAFFIC_IN_PROJ = 34_893_568 + 0
 IN_PROJ_ALGO_BYTES = (8512 * 2048 + 2048 + 8512) * 2
 
 
