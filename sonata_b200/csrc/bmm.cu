@@ -176,45 +176,8 @@ struct HeadSkParams {
   uint32_t recv_off, bar_off;    // recv: [bt / 2 columns][128 rows] fp32
 };
 
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
 __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-// arrive on an mbarrier of another CTA of the cluster, ordering this thread's
-// earlier (distributed) shared-memory writes before it
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait_cluster(bar, parity)) {
-    if (globaltimer_ns() - t0 > 1000000000ull) return false;
-  }
-  return true;
-}
-// every thread of both CTAs, exactly once per call site
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(kSkThreads, 1)
@@ -233,7 +196,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
+  const uint32_t rank = tc::cluster_ctarank(), peer = rank ^ 1u;
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
   const int nkb = p.K / 64, kb_half = nkb / 2, kb0 = static_cast<int>(rank) * kb_half;
   const uint32_t tcols = tc::tmem_cols_for(p.bt);
@@ -256,7 +219,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   if (warp == 1) tc::tmem_alloc(tmem_slot, tcols);
   tc::fence_before_sync();
   __syncthreads();
-  cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
+  tc::cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
@@ -351,15 +314,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;  // TMEM lane = weight row inside the tile
     const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    const uint32_t peer_recv = mapa_shared(smem_u32(recv), peer);
-    const uint32_t peer_rfull = mapa_shared(smem_u32(rfull), peer);
-    const uint32_t peer_rempty = mapa_shared(smem_u32(rempty), peer);
+    const uint32_t peer_recv = tc::mapa_shared(smem_u32(recv), peer);
+    const uint32_t peer_rfull = tc::mapa_shared(smem_u32(rfull), peer);
+    const uint32_t peer_rempty = tc::mapa_shared(smem_u32(rempty), peer);
     int j = 0;
     for (int t = cluster; t < p.ntiles; t += nclusters, ++j) {
       const int bti = t % p.nbt, rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);
       bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(tfull, j & 1));
       // the peer's recv buffer is free once it has read the previous tile's
-      if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait_cluster_bounded(rempty, (j - 1) & 1));
+      if (ok && j > 0) ok = __all_sync(0xffffffffu, tc::mbar_wait_cluster_bounded(rempty, (j - 1) & 1));
       if (!ok) {
         record_status(SN_ERR_TIMEOUT);
         break;
@@ -371,8 +334,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) st_cluster_f32(peer_recv + static_cast<uint32_t>(((c + i) * 128 + row) * 4), v[i]);
       }
-      mbar_arrive_remote(peer_rfull);
-      if (!__all_sync(0xffffffffu, mbar_wait_cluster_bounded(rfull, j & 1))) {
+      tc::mbar_arrive_remote(peer_rfull);
+      if (!__all_sync(0xffffffffu, tc::mbar_wait_cluster_bounded(rfull, j & 1))) {
         record_status(SN_ERR_TIMEOUT);
         break;
       }
@@ -389,7 +352,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           if (b < p.B) ob[static_cast<int64_t>(b) * p.N] = y;
         }
       }
-      mbar_arrive_remote(peer_rempty);  // my recv may be refilled
+      tc::mbar_arrive_remote(peer_rempty);  // my recv may be refilled
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty);
@@ -398,7 +361,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 
   tc::fence_before_sync();
   __syncthreads();
-  cluster_sync_all();  // no CTA leaves while its peer may still touch its shared memory
+  tc::cluster_sync_all();  // no CTA leaves while its peer may still touch its shared memory
   if (warp == 1) tc::tmem_dealloc(tmem, tcols);
 }
 

@@ -29,6 +29,8 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstring>
+#include <cstdlib>
 #include <cstdint>
 #include <mutex>
 
@@ -39,6 +41,7 @@ constexpr int kScProducerWarps = 8;
 constexpr int kScEpilogueWarps = 4;
 constexpr int kScThreads = (2 + kScProducerWarps + kScEpilogueWarps) * 32;  // TMA, MMA, producers, epilogue
 constexpr int kScWStages = 2;
+constexpr int kScPairWStages = 2;  // weight stages in the CTA-pair kernel (4 measured no faster)
 constexpr int kMaxTaps = 7;
 constexpr int kMaxRowIters = 7;  // activation rows per chunk <= 32 * 7 = 224 ((K-1)*d <= 72)
 
@@ -55,6 +58,7 @@ struct ScParams {
   uint32_t a_bytes;    // one activation plane (rows * 128)
   uint32_t w_bytes;    // one weight plane (nt * 128)
   uint32_t tcols;      // TMEM columns per accumulator buffer
+  int ntiles_t2, ntiles2;  // CTA-pair kernel: 256-row time tiles and pair tiles
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -318,6 +322,250 @@ __global__ void __launch_bounds__(kScThreads, 1)
   if (warp == 1) tc::tmem_dealloc(tmem, 2 * p.tcols);
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2).  A cluster of two CTAs computes a tile of
+// 256 output times x nt output channels with M = 256 MMAs: CTA r owns time
+// rows [128 r, 128 r + 128) of the tile (its own snake producers, activation
+// buffers, TMEM accumulator rows and epilogue) and holds nt / 2 rows of each
+// weight plane; the even CTA issues the MMAs, which read both CTAs' shared
+// memory.  Every weight byte read by the tensor core now feeds 256 rows
+// instead of 128, which is what bounds the single-CTA kernel (operand reads).
+// Synchronisation: producers and epilogue warps of the odd CTA arrive on the
+// even CTA's barriers remotely (release / acquire at cluster scope); weight
+// TMA of both CTAs completes on the even CTA's barrier; MMA commits are
+// multicast to the same barrier offset in both CTAs.  Every wait is bounded,
+// and a cluster barrier at exit keeps each CTA alive while its peer may
+// still read its shared memory.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kScThreads, 1)
+    snake_conv_pair_kernel(const __grid_constant__ CUtensorMap mapW, const ScParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // layout: [A0 hi][A0 lo][A1 hi][A1 lo][W0 hi/2][W0 lo/2][W1 hi/2][W1 lo/2][barriers]
+  const uint32_t wh = p.w_bytes / 2;  // this CTA's half of one weight plane
+  uint8_t* abuf = smem;
+  uint8_t* wbuf = smem + 4 * p.a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wbuf + 2 * kScPairWStages * wh);
+  uint64_t* a_full = bars;        // even CTA: both CTAs' producers
+  uint64_t* a_empty = bars + 2;   // both CTAs: MMA commit
+  uint64_t* w_full = bars + 4;    // even CTA: both CTAs' weight bytes
+  uint64_t* w_empty = w_full + kScPairWStages;  // both CTAs: MMA commit
+  uint64_t* t_full = w_empty + kScPairWStages;  // both CTAs: MMA commit
+  uint64_t* t_empty = t_full + 2;           // even CTA: both CTAs' epilogues
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(t_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const int nchunks = (p.Cin + 63) / 64;
+  const int my_tiles = p.ntiles2 > pair ? (p.ntiles2 - 1 - pair) / npairs + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(a_full + i, 2 * kScProducerWarps);
+      mbar_init(a_empty + i, 1);
+      mbar_init(t_full + i, 1);
+      mbar_init(t_empty + i, 2 * kScEpilogueWarps);
+    }
+    for (int i = 0; i < kScPairWStages; ++i) {
+      mbar_init(w_full + i, 1);
+      mbar_init(w_empty + i, 1);
+    }
+    fence_barrier_init();
+    tc::prefetch_map(&mapW);
+  }
+  if (warp == 1) tc::tmem_alloc_pair(tmem_slot, 2 * p.tcols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::cluster_sync_all();  // both CTAs' barriers and TMEM exist before any remote use
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  // the even CTA's barriers, addressed from either CTA
+  const uint32_t a_full0 = tc::mapa_shared(smem_u32(a_full), 0);
+  const uint32_t w_full0 = tc::mapa_shared(smem_u32(w_full), 0);
+  const uint32_t t_empty0 = tc::mapa_shared(smem_u32(t_empty), 0);
+
+  // pair tile j of this cluster -> batch, first time of THIS CTA's rows, first output channel
+  auto tile_coords = [&](int j, int& b, int& t0, int& o0) {
+    int u = pair + j * npairs;
+    const int ot = u % p.ntiles_o;
+    u /= p.ntiles_o;
+    const int tt = u % p.ntiles_t2;
+    b = u / p.ntiles_t2;
+    t0 = tt * 256 + static_cast<int>(rank) * 128;
+    o0 = ot * p.nt;
+  };
+
+  if (warp == 0) {
+    // ---------------- weight TMA: this CTA's half of each (chunk, tap) ----------
+    if (lane == 0) {
+      const int total = my_tiles * nchunks * p.K;
+      int q = 0;
+      for (; q < total; ++q) {
+        const int s = q % kScPairWStages, k = q / kScPairWStages;
+        if (k > 0 && !mbar_wait_bounded(w_empty + s, (k - 1) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          break;
+        }
+        const int tap = q % p.K;
+        const int c = (q / p.K) % nchunks;
+        const int j = q / (p.K * nchunks);
+        int b, t0, o0;
+        tile_coords(j, b, t0, o0);
+        uint8_t* dst = wbuf + static_cast<size_t>(s) * 2 * wh;
+        if (rank == 0) mbar_arrive_expect_tx(w_full + s, 4 * wh);  // both halves of both planes
+        const int orow = o0 + static_cast<int>(rank) * (p.nt / 2);
+        tc::tma_load_3d_pair(dst, &mapW, c * 64, orow, tap * 2 + 0, w_full0 + 8u * s);
+        tc::tma_load_3d_pair(dst + wh, &mapW, c * 64, orow, tap * 2 + 1, w_full0 + 8u * s);
+      }
+      (void)q;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA) ----------------
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = tc::idesc_bf16_f32(256, p.nt);
+      bool ok = true;
+      int q = 0, g = 0;
+      for (int j = 0; j < my_tiles && ok; ++j) {
+        const int tb = j & 1;
+        if (j >= 2 && !tc::mbar_wait_cluster_bounded(t_empty + tb, ((j >> 1) - 1) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t acc_tmem = tmem + static_cast<uint32_t>(tb) * p.tcols;
+        for (int c = 0; c < nchunks && ok; ++c, ++g) {
+          const int ab = g & 1;
+          if (!tc::mbar_wait_cluster_bounded(a_full + ab, (g >> 1) & 1)) {
+            record_status(SN_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const int ksteps = min(4, (p.Cin - c * 64) / 16);
+          const uint64_t a_hi = tc::smem_desc_sw128(abuf + (2 * ab + 0) * p.a_bytes);
+          const uint64_t a_lo = tc::smem_desc_sw128(abuf + (2 * ab + 1) * p.a_bytes);
+          for (int tap = 0; tap < p.K; ++tap, ++q) {
+            const int s = q % kScPairWStages;
+            if (!mbar_wait_bounded(w_full + s, (q / kScPairWStages) & 1)) {
+              record_status(SN_ERR_TIMEOUT);
+              ok = false;
+              break;
+            }
+            tc::fence_after_sync();
+            const uint8_t* w = wbuf + static_cast<size_t>(s) * 2 * wh;
+            const uint64_t w_hi = tc::smem_desc_sw128(w), w_lo = tc::smem_desc_sw128(w + wh);
+            const uint64_t shift = static_cast<uint64_t>(tap * p.dil * 128) >> 4;
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const uint32_t acc0 = (c | tap | kk) != 0;
+              tc::mma_bf16_pair(acc_tmem, a_hi + shift + 2 * kk, w_hi + 2 * kk, idesc, acc0);
+              tc::mma_bf16_pair(acc_tmem, a_lo + shift + 2 * kk, w_hi + 2 * kk, idesc, 1);
+              tc::mma_bf16_pair(acc_tmem, a_hi + shift + 2 * kk, w_lo + 2 * kk, idesc, 1);
+            }
+            tc::mma_commit_pair(w_empty + s);
+          }
+          tc::mma_commit_pair(a_empty + ab);
+        }
+        tc::mma_commit_pair(t_full + tb);
+      }
+    }
+  } else if (warp < 2 + kScProducerWarps) {
+    // ---------------- snake producers (this CTA's 128 rows + halo) -------------
+    const int pw = warp - 2;
+    int g = 0;
+    for (int j = 0; j < my_tiles; ++j) {
+      int b, t0, o0;
+      tile_coords(j, b, t0, o0);
+      const float* xb = p.x + static_cast<int64_t>(b) * p.Cin * p.T;
+      const int tin0 = t0 - p.pad;
+      for (int c = 0; c < nchunks; ++c, ++g) {
+        const int ab = g & 1;
+        const int i0 = c * 64 + pw * 8;
+        float v[kMaxRowIters][8];
+#pragma unroll
+        for (int it = 0; it < kMaxRowIters; ++it) {
+          const int r = lane + 32 * it;
+          const int tin = tin0 + r;
+          const bool in_t = r < p.rows && tin >= 0 && tin < p.T;
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.T + tin) : 0.f;
+        }
+        float al[8], inv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          al[e] = (i0 + e < p.Cin) ? __ldg(p.alpha + i0 + e) : 0.f;
+          inv[e] = 1.0f / (al[e] + p.eps);
+        }
+        if (g >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(a_empty + ab, ((g >> 1) - 1) & 1))) {
+          record_status(SN_ERR_TIMEOUT);
+          j = my_tiles;
+          break;
+        }
+        uint8_t* ahi = abuf + (2 * ab + 0) * p.a_bytes;
+        uint8_t* alo = abuf + (2 * ab + 1) * p.a_bytes;
+#pragma unroll
+        for (int it = 0; it < kMaxRowIters; ++it) {
+          const int r = lane + 32 * it;
+          if (r < p.rows) {
+            float hi[8], lo[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float sv = __sinf(al[e] * v[it][e]);
+              const float s = fmaf(sv * sv, inv[e], v[it][e]);
+              hi[e] = __bfloat162float(__float2bfloat16_rn(s));
+              lo[e] = s - hi[e];
+            }
+            const uint32_t off =
+                static_cast<uint32_t>(r) * 128u + ((static_cast<uint32_t>(pw) ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(ahi + off) = make_uint4(pack_bf16x2(hi[0], hi[1]), pack_bf16x2(hi[2], hi[3]),
+                                                              pack_bf16x2(hi[4], hi[5]), pack_bf16x2(hi[6], hi[7]));
+            *reinterpret_cast<uint4*>(alo + off) = make_uint4(pack_bf16x2(lo[0], lo[1]), pack_bf16x2(lo[2], lo[3]),
+                                                              pack_bf16x2(lo[4], lo[5]), pack_bf16x2(lo[6], lo[7]));
+          }
+        }
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive_remote(a_full0 + 8u * ab);  // the even CTA's barrier (own CTA if even)
+      }
+    }
+  } else {
+    // ---------------- epilogue: this CTA's 128 time rows ----------------
+    const int q4 = warp & 3;
+    for (int j = 0; j < my_tiles; ++j) {
+      const int tb = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(t_full + tb, (j >> 1) & 1))) {
+        record_status(SN_ERR_TIMEOUT);
+        break;
+      }
+      tc::fence_after_sync();
+      int b, t0, o0;
+      tile_coords(j, b, t0, o0);
+      const int t = t0 + q4 * 32 + lane;
+      float* yb = p.y + static_cast<int64_t>(b) * p.Cout * p.Tout;
+      const uint32_t base = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(tb) * p.tcols;
+      for (int cc = 0; cc < p.nt; cc += 16) {
+        float vv[16];
+        tc::tmem_ld16(base + cc, vv);
+        if (t < p.Tout) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int o = o0 + cc + e;
+            if (o < p.Cout) yb[static_cast<int64_t>(o) * p.Tout + t] = vv[e] + (p.bias ? __ldg(p.bias + o) : 0.f);
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_remote(t_empty0 + 8u * tb);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::cluster_sync_all();  // neither CTA leaves while the other may read its shared memory or TMEM
+  if (warp == 1) tc::tmem_dealloc_pair(tmem, 2 * p.tcols);
+}
+
 // W fp32 [Cout, Cin, K] -> bf16 planes Wp[(k*2 + h)][o][i], h = 0 hi, 1 lo.
 __global__ void pack_weights_kernel(const float* __restrict__ W, __nv_bfloat16* __restrict__ Wp, int Cout,
                                     int Cin, int K) {
@@ -377,6 +625,15 @@ bool fast_path_ok(int Cin, int Cout, int K, int stride, int dil, int Tout) {
 // CTAs.  The 64 stands for the per-tile cost that does not scale with the
 // width (snake re-evaluated for every output tile, prologue, epilogue);
 // ties go to the wider tile.
+// The CTA-pair kernel (SONATA_SNAKE_PAIR=0 selects the single-CTA kernel).
+bool snake_pair_enabled() {
+  static bool v = [] {
+    const char* e = getenv("SONATA_SNAKE_PAIR");
+    return !(e && strcmp(e, "0") == 0);
+  }();
+  return v;
+}
+
 int out_tile(int Cout, int64_t time_tiles, int sms) {
   int best = 32;
   int64_t best_cost = INT64_MAX;
@@ -458,6 +715,42 @@ int sn_snake_conv1d(const float* x, const float* alpha, const float* W, const fl
       const uint64_t dims[3] = {static_cast<uint64_t>(Cin), static_cast<uint64_t>(Cout),
                                 static_cast<uint64_t>(2 * K)};
       const uint64_t strides[2] = {static_cast<uint64_t>(Cin) * 2, static_cast<uint64_t>(Cout) * Cin * 2};
+      // CTA pairs pay off from Cout = 192 up (measured: -3 to -4% at C = 192 and
+      // 384, even at 768, +9% at C = 96 where nt / 2 = 48 weight rows per CTA)
+      if (sn::snake_pair_enabled() && Cout >= 128) {
+        // CTA-pair kernel: 256-row time tiles, each CTA holding nt / 2 weight rows
+        sn::ScParams q = p;
+        q.ntiles_t2 = (Tout + 255) / 256;
+        const int npairs = std::max(1, sms / 2);
+        q.nt = sn::out_tile(Cout, static_cast<int64_t>(B) * q.ntiles_t2, npairs);
+        q.ntiles_o = (Cout + q.nt - 1) / q.nt;
+        q.tcols = sn::tc::tmem_cols_for(q.nt);
+        q.w_bytes = static_cast<uint32_t>(q.nt) * 128;
+        const int64_t nt2 = static_cast<int64_t>(B) * q.ntiles_t2 * q.ntiles_o;
+        q.ntiles2 = static_cast<int>(std::min<int64_t>(nt2, INT32_MAX));
+        const size_t smem2 = 1024 + 4 * static_cast<size_t>(q.a_bytes) +
+                             sn::kScPairWStages * static_cast<size_t>(q.w_bytes) + 256;
+        const uint32_t box2[3] = {64, static_cast<uint32_t>(q.nt / 2), 1};
+        if (nt2 < (int64_t(1) << 31) && 2 * q.tcols <= 512 && smem2 <= 227 * 1024 &&
+            sn::tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box2) &&
+            cudaFuncSetAttribute(sn::snake_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem2)) == cudaSuccess) {
+          cudaLaunchConfig_t cfg = {};
+          cfg.gridDim = dim3(2 * std::min(q.ntiles2, npairs));
+          cfg.blockDim = dim3(sn::kScThreads);
+          cfg.dynamicSmemBytes = smem2;
+          cfg.stream = st;
+          cudaLaunchAttribute attr[1];
+          attr[0].id = cudaLaunchAttributeClusterDimension;
+          attr[0].val.clusterDim.x = 2;
+          attr[0].val.clusterDim.y = 1;
+          attr[0].val.clusterDim.z = 1;
+          cfg.attrs = attr;
+          cfg.numAttrs = 1;
+          if (cudaLaunchKernelEx(&cfg, sn::snake_conv_pair_kernel, mapW, q) == cudaSuccess) return SN_OK;
+        }
+        cudaGetLastError();
+      }
       const uint32_t box[3] = {64, static_cast<uint32_t>(p.nt), 1};
       if (sn::tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box)) {
         if (cudaFuncSetAttribute(sn::snake_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
