@@ -74,6 +74,8 @@ def test_dac_stage_shapes(S, C, d):
     (3, 16, 16, 129, 0, 2),     # no padding: Tout < T
     (1, 64, 272, 300, 9, 3),    # Cout > 256: two output tiles
     (1, 32, 32, 5, 27, 9),      # T shorter than the halo
+    (2, 192, 192, 100, 3, 1),   # CTA pairs: the odd CTA's 128 rows all past Tout
+    (3, 160, 320, 700, 9, 3),   # CTA pairs: batch > 1, two output tiles, ragged last pair
 ])
 def test_odd_shapes(S, B, Cin, Cout, T, pad, d):
     x, alpha, W, b = rand_case(B, Cin, Cout, T, seed=T)
