@@ -47,6 +47,11 @@ extern "C" {
  * the weight (or scale) buffer -- e.g. frozen nn.Linear weights. */
 #define SN_FLAG_PDL 1u
 
+/* ---- weight kinds of sn_gemv_ex ---- */
+#define SN_WEIGHT_BF16 0
+#define SN_WEIGHT_INT8 1
+#define SN_WEIGHT_E4M3 2
+
 /* Library version (major * 10000 + minor * 100 + patch). */
 int sn_version(void);
 /* Static description of a status code. */
@@ -78,6 +83,22 @@ int sn_gemv_int8(const int8_t *q, int64_t ldq, const float *scale, const void *x
 int sn_gemv_fp8e4m3(const uint8_t *q, int64_t ldq, const float *scale, const void *x, int64_t ldx,
                     void *y, int64_t ldy, int M, int N, int K, int y_dtype, unsigned flags,
                     void *stream);
+
+/*
+ * Any of the three GEMVs above (w_kind SN_WEIGHT_*; scale ignored for bf16)
+ * with a prefetch hint for the decode chain: next_W (kind next_kind, [next_N,
+ * next_K], row stride next_ldw elements) is the weight of the GEMV that
+ * follows on the stream.  When each CTA's own weight reads have landed, it
+ * prefetches the first bytes of the matching CTA ranges of that launch into
+ * L2 (8 MB in all), so that HBM keeps streaming across the kernel boundary.  The result is identical with or without the hint; next_W == NULL
+ * gives the plain call.  A next weight whose rows a bulk prefetch cannot
+ * address (not 16-byte aligned) is not prefetched.  Same decode-chain role as
+ * the back-to-back GEMV launches of kernels/patch.py:54-66 under a CUDA graph
+ * (no counterpart in the reference).
+ */
+int sn_gemv_ex(int w_kind, const void *W, int64_t ldw, const float *scale, const void *x, int64_t ldx,
+               void *y, int64_t ldy, int M, int N, int K, int y_dtype, unsigned flags, void *stream,
+               int next_kind, const void *next_W, int64_t next_ldw, int next_N, int next_K);
 
 /*
  * Per-output-channel weight quantisation on the device (bit-identical to

@@ -18,6 +18,9 @@ SN_OK = 0
 SN_DTYPE_BF16 = 0
 SN_DTYPE_F32 = 1
 SN_FLAG_PDL = 1
+SN_WEIGHT_BF16 = 0
+SN_WEIGHT_INT8 = 1
+SN_WEIGHT_E4M3 = 2
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -31,6 +34,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_gemv_bf16": ([_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
     "sn_gemv_int8": ([_P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
     "sn_gemv_fp8e4m3": ([_P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
+    "sn_gemv_ex": ([_I, _P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P, _I, _P, _I64, _I, _I], _I),
     "sn_quantize_rows_int8": ([_P, _I64, _I, _I, _P, _I64, _P, _P], _I),
     "sn_quantize_rows_fp8e4m3": ([_P, _I64, _I, _I, _P, _I64, _P, _P], _I),
     "sn_device_status": ([_I, _P], _I),

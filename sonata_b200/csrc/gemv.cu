@@ -63,6 +63,16 @@ struct GemvParams {
   int Kp;     // padded fp32 row stride of x in shared memory
   int y_f32;
   int x_vec;  // x rows are 16-byte aligned and K % 8 == 0
+  // Next-weight L2 prefetch (tensor-core GEMV only; pf == nullptr: none).
+  // The next GEMV's pf_rows rows (pf_row_bytes each, pf_ld bytes apart) are
+  // cut into pf_parts equal ranges, one per CTA of its launch; the first
+  // pf_part_bytes of every range are prefetched once this GEMV has issued
+  // all of its own weight copies.
+  const uint8_t* pf;
+  int64_t pf_ld;
+  int pf_rows, pf_parts;
+  uint32_t pf_row_bytes, pf_part_bytes;
+  int pf_lead;  // issue once all but this many of the CTA's own tiles have landed (< 0: at once)
 };
 
 constexpr int kWarps = 8;
@@ -688,6 +698,29 @@ __device__ __forceinline__ float diag_entry(uint32_t taddr, int lane) {
   }
 }
 
+// The next GEMV's weights are frozen too: while this kernel's last weight
+// copies are in flight, HBM reads the first bytes of every CTA range of the
+// next launch into L2, so that the next kernel's first ring fills hit L2 and
+// HBM is not idle across the kernel boundary.  One thread per CTA; ranges
+// are dealt out round-robin over this launch's CTAs.
+__device__ __forceinline__ void prefetch_next_weights(const GemvParams& p) {
+  constexpr uint32_t kPiece = 32 * 1024;
+  const int nblk = static_cast<int>(gridDim.x * gridDim.y);
+  for (int j = static_cast<int>(blockIdx.y * gridDim.x + blockIdx.x); j < p.pf_parts; j += nblk) {
+    const int64_t a = static_cast<int64_t>(p.pf_rows) * j / p.pf_parts;
+    const int64_t b = static_cast<int64_t>(p.pf_rows) * (j + 1) / p.pf_parts;
+    const int64_t bytes = min(static_cast<int64_t>(p.pf_part_bytes), (b - a) * p.pf_row_bytes);
+    if (p.pf_ld == static_cast<int64_t>(p.pf_row_bytes)) {
+      const uint8_t* src = p.pf + a * p.pf_ld;
+      for (int64_t o = 0; o < bytes; o += kPiece)
+        bulk_prefetch_l2(src + o, static_cast<uint32_t>(min(static_cast<int64_t>(kPiece), bytes - o)));
+    } else {
+      for (int64_t r = a, left = bytes; left > 0; ++r, left -= p.pf_row_bytes)
+        bulk_prefetch_l2(p.pf + r * p.pf_ld, static_cast<uint32_t>(min(static_cast<int64_t>(p.pf_row_bytes), left)));
+    }
+  }
+}
+
 template <int WK, int MT, int S>
 __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const GemvParams p, const MmaShape sh) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -765,6 +798,12 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
       }
       if (t < ntiles) {  // error path: let the copies in flight land before exit
         for (int j = (t > ns ? t - ns : 0); j < t; ++j) mbar_wait_bounded(full + j % ns, (j / ns) & 1);
+      } else if (p.pf != nullptr) {
+        // once this CTA's own reads are (nearly) all served: wait until tile
+        // ntiles - 1 - lead has landed (lead < ns, so its slot was not reused)
+        const int lead = min(p.pf_lead, ns - 1);
+        const int j = ntiles - 1 - lead;
+        if (lead < 0 || j < 0 || mbar_wait_bounded(full + j % ns, (j / ns) & 1)) prefetch_next_weights(p);
       }
     }
   } else {
@@ -1099,20 +1138,16 @@ int mma_segments(int K, int esz, int MT, int nd) {
   return ok(2) ? 2 : 0;
 }
 
-// Returns SN_ERR_UNSUPPORTED when the tensor-core GEMV does not apply
-// (16-byte aligned rows, x rows and batch strides; K within mma_segments' rules).
-template <int WK, int MT>
-int dispatch_mma(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
-  constexpr int ESZ = WT<WK>::ESZ;
-  if (batch > 1 && ((p.sW * ESZ) % 16 != 0 || p.sx % 8 != 0)) return SN_ERR_UNSUPPORTED;
-  constexpr int ND = (WK == W_INT8) ? 3 : (WK == W_E4M3) ? 2 : 1;
-  if (!p.x_vec || (reinterpret_cast<uintptr_t>(p.W) & 15) || (p.ldw * ESZ) % 16 != 0) return SN_ERR_UNSUPPORTED;
-  const int S = mma_segments(p.K, ESZ, MT, ND);
-  if (S == 0) return SN_ERR_UNSUPPORTED;
-  const int R = 16 / S;
-  MmaShape sh;
-  sh.N = 8 * S * MT * ND;
-  sh.slot_bytes = static_cast<uint32_t>(R) * p.K * ESZ;
+// Launch geometry of the tensor-core GEMV for an [N, K] weight of esz-byte
+// elements with nd B planes per x row (MT x rows, `batch` weights along
+// grid.y).  False when mma_segments finds no valid S.
+struct MmaGrid {
+  int S, cps, acc_log2, grid;
+};
+bool mma_grid(int esz, int nd, int MT, int N, int K, int batch, MmaGrid& g) {
+  g.S = mma_segments(K, esz, MT, nd);
+  if (g.S == 0) return false;
+  const int n_mma = 8 * g.S * MT * nd;
   // CTAs per SM from the weight bytes each SM streams: up to one ring's worth
   // (~96 KB) one CTA, prefetched whole under programmatic dependent launch;
   // up to two rings' worth two CTAs; beyond that three, whose three rings
@@ -1123,24 +1158,44 @@ int dispatch_mma(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
     const int v = e ? atoi(e) : 0;
     return (v >= 1 && v <= 4) ? v : 0;
   }();
-  const int64_t bytes_per_sm = static_cast<int64_t>(p.N) * p.K * ESZ * batch / sm_count();
+  const int64_t bytes_per_sm = static_cast<int64_t>(N) * K * esz * batch / sm_count();
   int cps = cps_env ? cps_env : bytes_per_sm <= 96 * 1024 ? 1 : bytes_per_sm <= 192 * 1024 ? 2 : 3;
   // TMEM: this kernel's CTAs and the next kernel's (programmatic dependent
   // launch) share an SM's 512 columns, so each CTA takes at most 512 / (2 cps)
   // (a CTA whose allocation does not fit would wait for another to exit)
   auto max_cols = [](int c) { return c == 1 ? 256 : c == 2 ? 128 : 64; };
-  while (cps > 1 && static_cast<int>(tc::tmem_cols_for(sh.N)) > max_cols(cps)) --cps;
+  while (cps > 1 && static_cast<int>(tc::tmem_cols_for(n_mma)) > max_cols(cps)) --cps;
   auto acc_log2_for = [&](int c) {
     int a = 2;
-    while (a > 0 && static_cast<int>(tc::tmem_cols_for(sh.N << a)) > max_cols(c)) --a;
+    while (a > 0 && static_cast<int>(tc::tmem_cols_for(n_mma << a)) > max_cols(c)) --a;
     return a;
   };
   // at least two accumulators (the MMAs of a slot must not wait for the
   // previous slot's epilogue): fewer CTAs per SM rather than one accumulator
   while (cps > 1 && acc_log2_for(cps) == 0) --cps;
-  sh.acc_log2 = acc_log2_for(cps);
+  g.cps = cps;
+  g.acc_log2 = acc_log2_for(cps);
+  g.grid = std::max(1, std::min(N, cps * sm_count() / batch));
+  return true;
+}
+
+// Returns SN_ERR_UNSUPPORTED when the tensor-core GEMV does not apply
+// (16-byte aligned rows, x rows and batch strides; K within mma_segments' rules).
+template <int WK, int MT>
+int dispatch_mma(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
+  constexpr int ESZ = WT<WK>::ESZ;
+  if (batch > 1 && ((p.sW * ESZ) % 16 != 0 || p.sx % 8 != 0)) return SN_ERR_UNSUPPORTED;
+  constexpr int ND = (WK == W_INT8) ? 3 : (WK == W_E4M3) ? 2 : 1;
+  if (!p.x_vec || (reinterpret_cast<uintptr_t>(p.W) & 15) || (p.ldw * ESZ) % 16 != 0) return SN_ERR_UNSUPPORTED;
+  MmaGrid g;
+  if (!mma_grid(ESZ, ND, MT, p.N, p.K, batch, g)) return SN_ERR_UNSUPPORTED;
+  const int S = g.S, cps = g.cps, grid = g.grid;
+  const int R = 16 / S;
+  MmaShape sh;
+  sh.N = 8 * S * MT * ND;
+  sh.slot_bytes = static_cast<uint32_t>(R) * p.K * ESZ;
+  sh.acc_log2 = g.acc_log2;
   sh.tcols = tc::tmem_cols_for(sh.N << sh.acc_log2);
-  const int grid = std::max(1, std::min(p.N, cps * sm_count() / batch));
   const int rows_per_cta = (p.N + grid - 1) / grid;
   const int tiles_per_cta = (rows_per_cta + R - 1) / R;
   const int ns_max = 16;
@@ -1196,12 +1251,63 @@ int dispatch_mt(const GemvParams& p, int batch, size_t smem, cudaStream_t st, bo
 
 int tu_status_gemv(bool reset, cudaStream_t st, int* out) { return read_tu_status(reset, st, out); }
 
+namespace {
+// The weight of the GEMV that follows on the stream (L2 prefetch hint).
+struct GemvNext {
+  int wk;
+  const void* W;
+  int64_t ldw;
+  int N, K;
+};
+
+// Bytes of the next weight prefetched into L2: 8 MB, about what HBM moves
+// while a launch drains and the next one starts (measured best of 4..48 MB
+// on the config-2 chain; SONATA_GEMV_PREFETCH_MB overrides, 0 disables).
+// When a CTA issues the prefetch: once all but this many of its own tiles
+// have landed (0: the last one; < 0: as soon as its last copy is issued,
+// which competes with its own reads and measured slower).
+// SONATA_GEMV_PREFETCH_LEAD overrides.
+int prefetch_lead() {
+  static const int v = [] {
+    const char* e = getenv("SONATA_GEMV_PREFETCH_LEAD");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
+
+int64_t prefetch_budget() {
+  static const int64_t v = [] {
+    const char* e = getenv("SONATA_GEMV_PREFETCH_MB");
+    const long mb = e ? strtol(e, nullptr, 10) : 8;
+    return static_cast<int64_t>(std::max(0L, std::min(mb, 96L))) << 20;
+  }();
+  return v;
+}
+
+int nd_of(int wk) { return wk == W_INT8 ? 3 : wk == W_E4M3 ? 2 : 1; }
+
+int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS, const void* x,
+              int64_t ldx, int64_t sx, void* y, int64_t ldy, int64_t sy, int M, int N, int K, int batch,
+              int y_dtype, unsigned flags, cudaStream_t st, const GemvNext* next);
+}  // namespace
+
 // Shared by the C entry points and the codebook-head BMM (batch > 1).
 int gemv_any(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS,
              const void* x, int64_t ldx, int64_t sx, void* y, int64_t ldy, int64_t sy, int M, int N, int K,
              int batch, int y_dtype, unsigned flags, cudaStream_t st) {
+  return gemv_impl(wk, W, ldw, sW, scale, sS, x, ldx, sx, y, ldy, sy, M, N, K, batch, y_dtype, flags, st,
+                   nullptr);
+}
+
+namespace {
+int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS, const void* x,
+              int64_t ldx, int64_t sx, void* y, int64_t ldy, int64_t sy, int M, int N, int K, int batch,
+              int y_dtype, unsigned flags, cudaStream_t st, const GemvNext* next) {
   if (!W || !x || !y) return SN_ERR_INVALID_ARGUMENT;
   if (wk != W_BF16 && !scale) return SN_ERR_INVALID_ARGUMENT;
+  if (next && next->W &&
+      (next->wk < W_BF16 || next->wk > W_E4M3 || next->N < 1 || next->K < 1 || next->ldw < next->K))
+    return SN_ERR_INVALID_ARGUMENT;
   if (M < 1 || M > 4 || N < 1 || K < 1 || batch < 1 || batch > 65535) return SN_ERR_INVALID_ARGUMENT;
   if (ldw < K || ldx < K || ldy < N) return SN_ERR_INVALID_ARGUMENT;
   if (y_dtype != SN_DTYPE_BF16 && y_dtype != SN_DTYPE_F32) return SN_ERR_INVALID_ARGUMENT;
@@ -1226,6 +1332,28 @@ int gemv_any(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale,
   const int esz = (wk == W_BF16) ? 2 : 1;
   const bool wvec = aligned16(W) && ((ldw * esz) % 16 == 0) && (batch == 1 || (sW * esz) % 16 == 0);
   const int MT = M == 1 ? 1 : (M == 2 ? 2 : 4);
+  p.pf = nullptr;
+  p.pf_ld = 0;
+  p.pf_rows = p.pf_parts = 0;
+  p.pf_row_bytes = p.pf_part_bytes = 0;
+  p.pf_lead = prefetch_lead();
+  if (next && next->W) {
+    const int nesz = (next->wk == W_BF16) ? 2 : 1;
+    const int64_t row_b = static_cast<int64_t>(next->K) * nesz;
+    const int64_t want = std::min(static_cast<int64_t>(next->N) * row_b, prefetch_budget());
+    // a hint: weights a bulk prefetch cannot address (16-byte rules) are skipped
+    if (want > 0 && aligned16(next->W) && (next->ldw * nesz) % 16 == 0 && row_b % 16 == 0 && row_b < (1 << 30)) {
+      MmaGrid g;
+      const int parts = mma_grid(nesz, nd_of(next->wk), MT, next->N, next->K, 1, g) ? g.grid : sm_count();
+      p.pf = static_cast<const uint8_t*>(next->W);
+      p.pf_ld = next->ldw * nesz;
+      p.pf_rows = next->N;
+      p.pf_parts = parts;
+      p.pf_row_bytes = static_cast<uint32_t>(row_b);
+      const int64_t per_part = ((want + parts - 1) / parts + 127) / 128 * 128;  // whole 128-byte lines
+      p.pf_part_bytes = static_cast<uint32_t>(std::min<int64_t>(per_part, int64_t(1) << 30));
+    }
+  }
   const size_t smem = (size_t)MT * p.Kp * sizeof(float);
   if (smem > 200 * 1024) return SN_ERR_UNSUPPORTED;  // x must fit in shared memory
   const bool pdl = (flags & SN_FLAG_PDL) != 0;
@@ -1243,6 +1371,7 @@ int gemv_any(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale,
   }
 #undef SN_DISPATCH
 }
+}  // namespace
 
 // ---------------------------------------------------------------------------
 // Device-side per-row quantisation (bit-identical to scripts/fake_quant.py:37-40
@@ -1300,6 +1429,15 @@ int sn_gemv_fp8e4m3(const uint8_t* q, int64_t ldq, const float* scale, const voi
                     int64_t ldy, int M, int N, int K, int y_dtype, unsigned flags, void* stream) {
   return sn::gemv_any(sn::W_E4M3, q, ldq, 0, scale, 0, x, ldx, 0, y, ldy, 0, M, N, K, 1, y_dtype, flags,
                       static_cast<cudaStream_t>(stream));
+}
+
+int sn_gemv_ex(int w_kind, const void* W, int64_t ldw, const float* scale, const void* x, int64_t ldx, void* y,
+               int64_t ldy, int M, int N, int K, int y_dtype, unsigned flags, void* stream, int next_kind,
+               const void* next_W, int64_t next_ldw, int next_N, int next_K) {
+  if (w_kind < SN_WEIGHT_BF16 || w_kind > SN_WEIGHT_E4M3) return SN_ERR_INVALID_ARGUMENT;
+  const sn::GemvNext nx{next_kind, next_W, next_ldw, next_N, next_K};
+  return sn::gemv_impl(w_kind, W, ldw, 0, w_kind == SN_WEIGHT_BF16 ? nullptr : scale, 0, x, ldx, 0, y, ldy, 0,
+                       M, N, K, 1, y_dtype, flags, static_cast<cudaStream_t>(stream), next_W ? &nx : nullptr);
 }
 
 static int quantize_rows(bool e4m3, const void* W, int64_t ldw, int N, int K, void* q, int64_t ldq, float* scale,

@@ -49,12 +49,31 @@ def _check_gemv(x: torch.Tensor, W: torch.Tensor):
     return M, N, K
 
 
+def _next_args(next_weight, device) -> tuple:
+    """(kind, pointer, row stride, N, K) of sn_gemv_ex's next-weight hint."""
+    if next_weight is None:
+        return (_lib.SN_WEIGHT_BF16, None, 0, 0, 0)
+    if isinstance(next_weight, QuantizedWeight):
+        t = next_weight.q
+        kind = _lib.SN_WEIGHT_INT8 if next_weight.kind == "int8" else _lib.SN_WEIGHT_E4M3
+    else:
+        t = next_weight
+        require_cuda("next_weight", t, _BF16, 2)
+        kind = _lib.SN_WEIGHT_BF16
+    if t.dim() != 2 or t.device != device:
+        raise ValueError("next_weight must be a 2-D weight on the GEMV's device")
+    return (kind, t.data_ptr(), row_major("next_weight", t), int(t.shape[0]), int(t.shape[1]))
+
+
 def gemv(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor | None = None, out_dtype=_BF16,
-         pdl: bool = False, stream=None) -> torch.Tensor:
+         pdl: bool = False, stream=None, next_weight=None) -> torch.Tensor:
     """y = x @ W.T with fp32 accumulation; y is bf16 (RNE) or fp32.
 
     ``pdl=True`` lets the kernel overlap the previous kernel on the stream;
-    only use it when that kernel does not write W.
+    only use it when that kernel does not write W.  ``next_weight`` (a bf16
+    weight or a ``QuantizedWeight``) names the weight of the GEMV launched
+    next on the stream: its first bytes are prefetched into L2 while this one
+    drains.  It changes no result.
     """
     M, N, K = _check_gemv(x, W)
     if out is None:
@@ -62,9 +81,15 @@ def gemv(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor | None = None, out_
     require_cuda("out", out, None, 2)
     if out.shape != (M, N) or out.dtype not in (_BF16, torch.float32):
         raise ValueError(f"out must be [{M}, {N}] bf16 or fp32")
-    call("sn_gemv_bf16", W.data_ptr(), row_major("W", W), x.data_ptr(), row_major("x", x), out.data_ptr(),
-         row_major("out", out), M, N, K, _lib.SN_DTYPE_F32 if out.dtype == torch.float32 else _lib.SN_DTYPE_BF16,
-         _lib.SN_FLAG_PDL if pdl else 0, stream_handle(stream))
+    y_dtype = _lib.SN_DTYPE_F32 if out.dtype == torch.float32 else _lib.SN_DTYPE_BF16
+    flags = _lib.SN_FLAG_PDL if pdl else 0
+    if next_weight is None:
+        call("sn_gemv_bf16", W.data_ptr(), row_major("W", W), x.data_ptr(), row_major("x", x), out.data_ptr(),
+             row_major("out", out), M, N, K, y_dtype, flags, stream_handle(stream))
+    else:
+        call("sn_gemv_ex", _lib.SN_WEIGHT_BF16, W.data_ptr(), row_major("W", W), None, x.data_ptr(),
+             row_major("x", x), out.data_ptr(), row_major("out", out), M, N, K, y_dtype, flags,
+             stream_handle(stream), *_next_args(next_weight, x.device))
     return out
 
 
@@ -153,8 +178,10 @@ def quantize_weight(W: torch.Tensor, kind: str = "int8", stream=None) -> Quantiz
 
 
 def gemv_quantized(x: torch.Tensor, qw: QuantizedWeight, out: torch.Tensor | None = None,
-                   out_dtype=torch.float32, pdl: bool = False, stream=None) -> torch.Tensor:
-    """y[m, n] = scale[n] * sum_k x[m, k] * q[n, k] with the dequant fused in-kernel."""
+                   out_dtype=torch.float32, pdl: bool = False, stream=None, next_weight=None) -> torch.Tensor:
+    """y[m, n] = scale[n] * sum_k x[m, k] * q[n, k] with the dequant fused in-kernel.
+
+    ``pdl`` and ``next_weight`` as for ``gemv``."""
     require_cuda("x", x, _BF16, 2)
     q, scale = qw.q, qw.scale
     require_cuda("q", q, None, 2)
@@ -169,10 +196,17 @@ def gemv_quantized(x: torch.Tensor, qw: QuantizedWeight, out: torch.Tensor | Non
         out = torch.empty(M, N, device=x.device, dtype=out_dtype)
     if out.shape != (M, N) or out.dtype not in (_BF16, torch.float32):
         raise ValueError(f"out must be [{M}, {N}] bf16 or fp32")
-    fn = {"int8": "sn_gemv_int8", "e4m3": "sn_gemv_fp8e4m3"}[qw.kind]
-    call(fn, q.data_ptr(), row_major("q", q), scale.data_ptr(), x.data_ptr(), row_major("x", x), out.data_ptr(),
-         row_major("out", out), M, N, K, _lib.SN_DTYPE_F32 if out.dtype == torch.float32 else _lib.SN_DTYPE_BF16,
-         _lib.SN_FLAG_PDL if pdl else 0, stream_handle(stream))
+    y_dtype = _lib.SN_DTYPE_F32 if out.dtype == torch.float32 else _lib.SN_DTYPE_BF16
+    flags = _lib.SN_FLAG_PDL if pdl else 0
+    if next_weight is None:
+        fn = {"int8": "sn_gemv_int8", "e4m3": "sn_gemv_fp8e4m3"}[qw.kind]
+        call(fn, q.data_ptr(), row_major("q", q), scale.data_ptr(), x.data_ptr(), row_major("x", x),
+             out.data_ptr(), row_major("out", out), M, N, K, y_dtype, flags, stream_handle(stream))
+    else:
+        kind = _lib.SN_WEIGHT_INT8 if qw.kind == "int8" else _lib.SN_WEIGHT_E4M3
+        call("sn_gemv_ex", kind, q.data_ptr(), row_major("q", q), scale.data_ptr(), x.data_ptr(),
+             row_major("x", x), out.data_ptr(), row_major("out", out), M, N, K, y_dtype, flags,
+             stream_handle(stream), *_next_args(next_weight, x.device))
     return out
 
 

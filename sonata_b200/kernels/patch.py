@@ -18,12 +18,20 @@ semantics:
   ``model.backbone``, skipping attention layers unless ``include_attn``
   (patch.py:79-98).  Returns the number patched.
 
-B200 addition: ``weight_format="int8" | "e4m3"`` quantises the weight once
-per output channel on the device and routes decode calls through the
-fused-dequant GEMV (bf16 output, as the Linear would produce); prefill keeps
-the original bf16 forward.  Patched GEMVs are launched with programmatic
-dependent launch, which is valid because a frozen Linear weight is never
-written by the kernel before it in the decode step.
+B200 additions:
+
+* ``weight_format="int8" | "e4m3"`` quantises the weight once per output
+  channel on the device and routes decode calls through the fused-dequant
+  GEMV (bf16 output, as the Linear would produce); prefill keeps the original
+  bf16 forward.
+* Patched GEMVs are launched with programmatic dependent launch, which is
+  valid because a frozen Linear weight is never written by the kernel before
+  it in the decode step.
+* ``link_decode_chain(linears)`` tells each patched Linear which one the
+  decode step calls next; its GEMV then prefetches the start of that weight
+  into L2 while it drains (a hint: a wrong order costs bandwidth, never
+  results).  ``patch_zonos_projections(..., prefetch_chain=True)`` links the
+  patched Linears in module order, which is the order Zonos' blocks call them.
 """
 from __future__ import annotations
 
@@ -36,26 +44,37 @@ from .gemv import MAX_M, QuantizedWeight, quantize_weight
 _TARGETS = ("in_proj", "out_proj", "fc1", "fc2")
 
 
-def _make_launch(W: torch.Tensor, qw: QuantizedWeight | None):
-    """Bind the weight once; return launch(x_contig, y, M)."""
+def _make_launch(W: torch.Tensor, qw: QuantizedWeight | None, lin: torch.nn.Linear):
+    """Bind the weight once; return launch(x_contig, y, M).  The next-weight
+    hint is read from ``lin._gemv_next`` at every call (set by
+    link_decode_chain)."""
     N, K = W.shape
     lib = _lib.lib()
     flags = _lib.SN_FLAG_PDL
+    ex = lib.sn_gemv_ex
     if qw is None:
         fn = lib.sn_gemv_bf16
-        w_ptr = W.data_ptr()
+        kind, w_ptr, s_ptr = _lib.SN_WEIGHT_BF16, W.data_ptr(), None
 
-        def launch(xc: torch.Tensor, y: torch.Tensor, M: int) -> None:
-            _lib.check("sn_gemv_bf16", fn(w_ptr, K, xc.data_ptr(), K, y.data_ptr(), N, M, N, K,
-                                          _lib.SN_DTYPE_BF16, flags, stream_handle()))
+        def plain(xc, y, M):
+            return fn(w_ptr, K, xc.data_ptr(), K, y.data_ptr(), N, M, N, K, _lib.SN_DTYPE_BF16, flags,
+                      stream_handle())
     else:
-        name = "sn_gemv_int8" if qw.kind == "int8" else "sn_gemv_fp8e4m3"
-        fn = getattr(lib, name)
-        q_ptr, s_ptr = qw.q.data_ptr(), qw.scale.data_ptr()
+        fn = lib.sn_gemv_int8 if qw.kind == "int8" else lib.sn_gemv_fp8e4m3
+        kind = _lib.SN_WEIGHT_INT8 if qw.kind == "int8" else _lib.SN_WEIGHT_E4M3
+        w_ptr, s_ptr = qw.q.data_ptr(), qw.scale.data_ptr()
 
-        def launch(xc: torch.Tensor, y: torch.Tensor, M: int) -> None:
-            _lib.check(name, fn(q_ptr, K, s_ptr, xc.data_ptr(), K, y.data_ptr(), N, M, N, K,
-                                _lib.SN_DTYPE_BF16, flags, stream_handle()))
+        def plain(xc, y, M):
+            return fn(w_ptr, K, s_ptr, xc.data_ptr(), K, y.data_ptr(), N, M, N, K, _lib.SN_DTYPE_BF16, flags,
+                      stream_handle())
+
+    def launch(xc: torch.Tensor, y: torch.Tensor, M: int) -> None:
+        nxt = getattr(lin, "_gemv_next", None)
+        if nxt is None:
+            _lib.check("sn_gemv", plain(xc, y, M))
+        else:
+            _lib.check("sn_gemv_ex", ex(kind, w_ptr, K, s_ptr, xc.data_ptr(), K, y.data_ptr(), N, M, N, K,
+                                        _lib.SN_DTYPE_BF16, flags, stream_handle(), *nxt[0]))
     return launch
 
 
@@ -76,7 +95,7 @@ def patch_linear(lin: torch.nn.Linear, batches=(1, 2), weight_format: str = "bf1
         qw = quantize_weight(W, weight_format)
     else:
         raise ValueError(f"weight_format must be bf16 | int8 | e4m3, got {weight_format!r}")
-    launch = _make_launch(W, qw)
+    launch = _make_launch(W, qw, lin)
     ybuf = {M: torch.empty(M, N, device=W.device, dtype=torch.bfloat16) for M in batches}
     orig = lin.forward
 
@@ -101,8 +120,32 @@ def unpatch_linear(lin: torch.nn.Linear):
     if hasattr(lin, "_gemv_orig"):
         lin.forward = lin._gemv_orig
         del lin._gemv_orig
-        if hasattr(lin, "_gemv_keepalive"):
-            del lin._gemv_keepalive
+        for attr in ("_gemv_keepalive", "_gemv_next"):
+            if hasattr(lin, attr):
+                delattr(lin, attr)
+
+
+def link_decode_chain(linears, cyclic: bool = False) -> None:
+    """Give each patched Linear of ``linears`` (in decode-step call order) the
+    weight of the one after it as an L2 prefetch hint (sn_gemv_ex).  The last
+    one gets none unless ``cyclic``.  Only patched Linears are linked; a
+    Linear's hint is replaced by a later call and cleared by unpatch_linear.
+    Launches already captured in a CUDA graph keep the hint they were
+    captured with."""
+    mods = [m for m in linears if hasattr(m, "_gemv_keepalive")]
+    for i, m in enumerate(mods):
+        j = i + 1
+        if j == len(mods):
+            if not cyclic or len(mods) < 2:
+                m._gemv_next = None
+                continue
+            j = 0
+        W, qw, _ = mods[j]._gemv_keepalive
+        t = W if qw is None else qw.q
+        kind = (_lib.SN_WEIGHT_BF16 if qw is None else
+                _lib.SN_WEIGHT_INT8 if qw.kind == "int8" else _lib.SN_WEIGHT_E4M3)
+        # (sn_gemv_ex's trailing arguments, the tensor they point into)
+        m._gemv_next = ((kind, t.data_ptr(), t.stride(0), int(t.shape[0]), int(t.shape[1])), t)
 
 
 def zonos_patch_targets(model, include_attn: bool = False):
@@ -121,14 +164,20 @@ def zonos_patch_targets(model, include_attn: bool = False):
     return out
 
 
-def patch_zonos_projections(model, include_attn=False, verbose=False, weight_format: str = "bf16") -> int:
+def patch_zonos_projections(model, include_attn=False, verbose=False, weight_format: str = "bf16",
+                            prefetch_chain: bool = True) -> int:
     """Patch decode-shaped, bias-free projection Linears across the backbone:
     Mamba2 in_proj/out_proj always; attention qkv/out_proj and MLP fc1/fc2 when
-    include_attn=True.  Returns the number of Linears patched."""
+    include_attn=True.  With ``prefetch_chain`` the patched Linears are linked
+    in module order (link_decode_chain).  Returns the number patched."""
     n = 0
+    mods = []
     for name, mod in zonos_patch_targets(model, include_attn):
         patch_linear(mod, weight_format=weight_format)
+        mods.append(mod)
         n += 1
         if verbose:
             print(f"  patched {name}: {tuple(mod.weight.shape)}")
+    if prefetch_chain:
+        link_decode_chain(mods)
     return n

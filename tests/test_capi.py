@@ -43,6 +43,12 @@ def test_gemv_rejects_bad_arguments_on_host(L):
     assert L.sn_gemv_bf16(p, 8, p, 8, p, 8, 1, 8, 8, 7, 0, None) == -1
     # quantised GEMV without a scale
     assert L.sn_gemv_int8(p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None) == -1
+    # sn_gemv_ex: weight kind, and the next-weight hint's kind / shape / stride
+    assert L.sn_gemv_ex(3, p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None, 0, None, 0, 0, 0) == -1
+    assert L.sn_gemv_ex(1, p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None, 0, None, 0, 0, 0) == -1
+    assert L.sn_gemv_ex(0, p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None, 5, p, 8, 8, 8) == -1
+    assert L.sn_gemv_ex(0, p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None, 0, p, 4, 8, 8) == -1
+    assert L.sn_gemv_ex(0, p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None, 0, p, 8, 0, 8) == -1
     assert L.sn_quantize_rows_int8(None, 8, 8, 8, p, 8, p, None) == -1
     assert L.sn_quantize_rows_fp8e4m3(p, 4, 8, 8, p, 8, p, None) == -1
 

@@ -191,6 +191,63 @@ def test_quantized_gemv_unaligned_rows(G):
         assert O.rel_err_inf(y.cpu().numpy(), truth) <= 1e-3
 
 
+# ---------------- next-weight L2 prefetch hint (sn_gemv_ex) ----------------
+
+@pytest.mark.parametrize("M", [1, 2, 4])
+def test_next_weight_hint_is_result_neutral(G, M):
+    x, W = make(8512, 2048, M, seed=3)
+    base = G.gemv(x, W, out_dtype=torch.float32)
+    wide = (torch.randn(3072, 2056, device="cuda") * 0.02).to(torch.bfloat16)
+    nexts = [
+        make(2048, 4096, 1, seed=4)[1],                          # bf16, contiguous rows
+        wide[:, :2048],                                          # rows 4112 bytes apart: one prefetch per row
+        G.quantize_weight(make(1025, 2048, 1, seed=5)[1], "int8"),
+        G.quantize_weight(make(777, 1280, 1, seed=6)[1], "e4m3"),
+        make(5, 7, 1, seed=7)[1],                                # 14-byte rows: not prefetchable, skipped
+        W,                                                       # itself
+    ]
+    for nw in nexts:
+        y = G.gemv(x, W, out_dtype=torch.float32, next_weight=nw)
+        torch.cuda.synchronize()
+        assert torch.equal(y, base)
+        assert torch.equal(G.gemv(x, W, next_weight=nw), G.gemv(x, W))
+    for kind in ("int8", "e4m3"):
+        qw = G.quantize_weight(W, kind)
+        yq = G.gemv_quantized(x, qw)
+        for nw in (nexts[0], nexts[2]):
+            assert torch.equal(G.gemv_quantized(x, qw, next_weight=nw), yq)
+    with pytest.raises(ValueError):
+        G.gemv(x, W, next_weight=torch.zeros(4, 8, 8, device="cuda", dtype=torch.bfloat16).view(4, 64)[:, ::2])
+
+
+def test_next_weight_chain_in_graph_with_pdl(G):
+    """The config-2 call pattern: a PDL chain in one CUDA graph, every GEMV
+    hinting the next one's weight, equals the same chain without hints."""
+    shapes = [(8512, 2048), (2048, 4096), (3072, 2048), (2048, 2048), (11264, 2048), (2048, 5632)] * 2
+    Ws = [make(N, K, 1, seed=20 + i)[1] for i, (N, K) in enumerate(shapes)]
+    xs = [make(N, K, 1, seed=40 + i)[0] for i, (N, K) in enumerate(shapes)]
+    ys = [torch.empty(1, N, device="cuda", dtype=torch.bfloat16) for (N, K) in shapes]
+    ref = [G.gemv(x, W) for x, W in zip(xs, Ws)]
+
+    def chain():
+        for i in range(len(Ws)):
+            G.gemv(xs[i], Ws[i], out=ys[i], pdl=True, next_weight=Ws[i + 1] if i + 1 < len(Ws) else None)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chain()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    for y, r in zip(ys, ref):
+        assert torch.equal(y, r)
+
+
 # ---------------- nn.Linear patch ----------------
 
 def test_patch_linear_on_gpu_and_in_graph(cuda_lib):
@@ -240,3 +297,22 @@ def test_patch_linear_quantized(cuda_lib, fmt):
     torch.cuda.synchronize()
     truth = O.dequant_gemv_ref(bits(x), qw.q.cpu().numpy(), qw.scale.cpu().numpy(), fmt)
     assert O.rel_err_inf(y.float().cpu().numpy(), truth) <= 1e-2
+
+
+def test_patch_linear_decode_chain(cuda_lib):
+    """link_decode_chain: bf16 and quantised patched Linears hinting each
+    other give the outputs they give unlinked."""
+    from sonata_b200.kernels.patch import link_decode_chain, patch_linear
+    torch.manual_seed(2)
+    lins = [torch.nn.Linear(K, N, bias=False, device="cuda", dtype=torch.bfloat16)
+            for (N, K) in [(8512, 2048), (2048, 4096), (3072, 2048)]]
+    for lin, fmt in zip(lins, ["bf16", "int8", "e4m3"]):
+        patch_linear(lin, batches=(1, 2), weight_format=fmt)
+    xs = [torch.randn(2, lin.in_features, device="cuda", dtype=torch.bfloat16) for lin in lins]
+    with torch.no_grad():
+        ref = [lin(x).clone() for lin, x in zip(lins, xs)]
+        link_decode_chain(lins, cyclic=True)
+        out = [lin(x).clone() for lin, x in zip(lins, xs)]
+    torch.cuda.synchronize()
+    for a, b in zip(out, ref):
+        assert torch.equal(a, b)

@@ -17,9 +17,10 @@ from sonata_b200.kernels import patch as P
 def cpu_patch(monkeypatch):
     calls = []
 
-    def fake_make_launch(W, qw):
+    def fake_make_launch(W, qw, lin):
         def launch(xc, y, M):
-            calls.append((tuple(xc.shape), M, y.data_ptr()))
+            nxt = getattr(lin, "_gemv_next", None)
+            calls.append((tuple(xc.shape), M, y.data_ptr(), None if nxt is None else nxt[0]))
             y.copy_((xc.float() @ W.float().t()).to(y.dtype))
         return launch
 
@@ -122,3 +123,44 @@ def test_patch_zonos_projections_counts(cpu_patch):
     for p in m2.parameters():
         p.data = p.data.to(torch.bfloat16)
     assert P.patch_zonos_projections(m2, include_attn=True) == 7
+
+
+def test_link_decode_chain_hints_the_next_weight(cpu_patch):
+    lins = [_lin(N=16 * (i + 1), K=32) for i in range(3)]
+    for lin in lins:
+        P.patch_linear(lin, batches=(1,))
+    plain = torch.nn.Linear(32, 8, bias=False)  # not patched: skipped by the chain
+    P.link_decode_chain([lins[0], plain, lins[1], lins[2]])
+    x = torch.randn(1, 32).to(torch.bfloat16)
+    for lin in lins:
+        lin(x)
+    hints = [c[3] for c in cpu_patch[-3:]]
+    for i in range(2):
+        W1 = lins[i + 1]._gemv_keepalive[0]
+        assert hints[i] == (0, W1.data_ptr(), 32, W1.shape[0], 32)
+    assert hints[2] is None  # the last one has no successor
+    P.link_decode_chain(lins, cyclic=True)
+    lins[2](x)
+    assert cpu_patch[-1][3][1] == lins[0]._gemv_keepalive[0].data_ptr()
+    # outputs do not depend on the hint
+    y_hint = lins[0](x).clone()
+    P.unpatch_linear(lins[1])
+    assert not hasattr(lins[1], "_gemv_next")
+    lins[0]._gemv_next = None
+    torch.testing.assert_close(lins[0](x), y_hint)
+
+
+def test_patch_zonos_projections_links_in_module_order(cpu_patch):
+    m = _model()
+    for p in m.parameters():
+        p.data = p.data.to(torch.bfloat16)
+    P.patch_zonos_projections(m)
+    mods = [mod for _, mod in P.zonos_patch_targets(m)]
+    for a, b in zip(mods, mods[1:]):
+        assert a._gemv_next[0][1] == b._gemv_keepalive[0].data_ptr()
+    assert mods[-1]._gemv_next is None
+    m2 = _model()
+    for p in m2.parameters():
+        p.data = p.data.to(torch.bfloat16)
+    P.patch_zonos_projections(m2, prefetch_chain=False)
+    assert all(getattr(mod, "_gemv_next", None) is None for _, mod in P.zonos_patch_targets(m2))
