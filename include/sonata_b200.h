@@ -168,6 +168,45 @@ int sn_snake_conv1d(const float *x, const float *alpha, const float *W, const fl
                     void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * The DAC decoder's other Snake -> conv edges (the HF transformers DacDecoder
+ * the reference decodes with, modeling_dac.py DacResidualUnit / DacDecoder;
+ * edge list in docs/dac_architecture.md:137-168, 306-314).
+ *
+ * sn_snake_conv1d_ex: sn_snake_conv1d plus
+ *   act      SN_ACT_SNAKE (as sn_snake_conv1d) or SN_ACT_NONE (no activation:
+ *            the decoder's stem conv1; alpha may be NULL),
+ *   residual fp32 [B, Cout, Tout] added after the bias (the residual unit's
+ *            "hidden_state + conv2(snake2(...))"), or NULL,
+ *   post     SN_POST_NONE or SN_POST_TANH (the decoder's final tanh), applied last.
+ * residual must not alias y.
+ */
+#define SN_ACT_SNAKE 0
+#define SN_ACT_NONE 1
+#define SN_POST_NONE 0
+#define SN_POST_TANH 1
+int sn_snake_conv1d_ex(const float *x, const float *alpha, const float *W, const float *bias,
+                       const float *residual, float *y, int B, int Cin, int Cout, int T, int K, int stride,
+                       int padding, int dilation, float eps, int act, int post, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
+/*
+ * Fused Snake + ConvTranspose1d (the DacDecoderBlock's snake1 -> conv_t1):
+ *   y[b, o, t] = bias[o] + sum over (i, k, j) with t = j*stride - padding + k of
+ *                snake(x[b, i, j]) * W[i, o, k]
+ * x: fp32 [B, Cin, T]; W: fp32 [Cin, Cout, K] (torch ConvTranspose1d layout,
+ * groups 1, dilation 1, output_padding 0); y: fp32 [B, Cout, Ty], Ty =
+ * sn_snake_conv_transpose1d_output_length.  Workspace as sn_snake_conv1d
+ * (sn_snake_conv1d_workspace_size(Cin, Cout, K) bytes).  K a multiple of
+ * stride with Cin and Cout * stride multiples of 16 runs on the tensor cores
+ * as a polyphase GEMM (K / stride taps, one GEMM column per (o, phase));
+ * other shapes run a per-output fallback.
+ */
+int64_t sn_snake_conv_transpose1d_output_length(int64_t T, int K, int stride, int padding);
+int sn_snake_conv_transpose1d(const float *x, const float *alpha, const float *W, const float *bias, float *y,
+                              int B, int Cin, int Cout, int T, int K, int stride, int padding, float eps,
+                              void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * Allocation-free Snake + Conv1d.  No counterpart in the reference.
  *
  * For callers that must not allocate device memory at all: a host that runs

@@ -253,6 +253,87 @@ def snake_conv1d_ref(x: np.ndarray, alpha: np.ndarray, weight: np.ndarray, bias:
     return y
 
 
+def conv1d_ref(x: np.ndarray, weight: np.ndarray, bias: np.ndarray | None, stride: int = 1, padding: int = 0,
+               dilation: int = 1) -> np.ndarray:
+    """Plain Conv1d in float64 (F.conv1d semantics; the DAC decoder's stem
+    conv1 has no Snake in front, transformers modeling_dac.py DacDecoder)."""
+    x = np.asarray(x, np.float64)
+    Bn, Cin, T = x.shape
+    Cout, Cw, K = weight.shape
+    if Cw != Cin:
+        raise ValueError("Only groups=1 is supported.")
+    Tout = conv1d_output_length(T, K, stride, padding, dilation)
+    padded = np.zeros((Bn, Cin, T + 2 * padding), np.float64)
+    padded[:, :, padding:padding + T] = x
+    w = np.asarray(weight, np.float64)
+    y = np.zeros((Bn, Cout, Tout), np.float64)
+    span = (Tout - 1) * stride + 1
+    for k in range(K):
+        y += np.einsum("oi,bit->bot", w[:, :, k], padded[:, :, k * dilation:k * dilation + span:stride],
+                       optimize=True)
+    if bias is not None:
+        y += np.asarray(bias, np.float64).reshape(1, -1, 1)
+    return y
+
+
+def conv_transpose1d_output_length(T: int, K: int, stride: int, padding: int) -> int:
+    """torch ConvTranspose1d output length (dilation 1, output_padding 0)."""
+    return (T - 1) * stride - 2 * padding + K
+
+
+def snake_conv_transpose1d_ref(x: np.ndarray, alpha: np.ndarray, weight: np.ndarray, bias: np.ndarray | None,
+                               stride: int, padding: int, eps: float = 1e-9) -> np.ndarray:
+    """Snake then ConvTranspose1d in float64, by its definition: input j, tap
+    k lands on output j * stride - padding + k (torch ConvTranspose1d,
+    weight [Cin, Cout, K]; the DacDecoderBlock's snake1 -> conv_t1,
+    transformers modeling_dac.py DacDecoderBlock.forward)."""
+    act = snake_ref(x, alpha, eps)
+    Bn, Cin, T = act.shape
+    Cw, Cout, K = weight.shape
+    if Cw != Cin:
+        raise ValueError("Only groups=1 is supported.")
+    Ty = conv_transpose1d_output_length(T, K, stride, padding)
+    full = np.zeros((Bn, Cout, (T - 1) * stride + K), np.float64)
+    w = np.asarray(weight, np.float64)
+    for k in range(K):
+        contrib = np.einsum("io,bit->bot", w[:, :, k], act, optimize=True)  # [B, Cout, T]
+        full[:, :, k:k + (T - 1) * stride + 1:stride] += contrib
+    y = full[:, :, padding:padding + Ty]
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64).reshape(1, -1, 1)
+    return y
+
+
+def dac_residual_unit_ref(x: np.ndarray, p: dict, prefix: str, dilation: int, eps: float = 1e-9) -> np.ndarray:
+    """x + conv2(snake2(conv1(snake1(x)))) (transformers modeling_dac.py
+    DacResidualUnit.forward; conv1 k = 7 with padding 3 * dilation, conv2 k = 1,
+    so the crop of its residual is 0).  p: the decoder's state dict (numpy)."""
+    a1 = np.asarray(p[f"{prefix}.snake1.alpha"]).reshape(-1)
+    a2 = np.asarray(p[f"{prefix}.snake2.alpha"]).reshape(-1)
+    y = snake_conv1d_ref(x, a1, p[f"{prefix}.conv1.weight"], p[f"{prefix}.conv1.bias"], padding=3 * dilation,
+                         dilation=dilation, eps=eps)
+    y = snake_conv1d_ref(y, a2, p[f"{prefix}.conv2.weight"], p[f"{prefix}.conv2.bias"], eps=eps)
+    return np.asarray(x, np.float64) + y
+
+
+def dac_decoder_ref(latent: np.ndarray, p: dict, upsampling_ratios, eps: float = 1e-9) -> np.ndarray:
+    """The DAC decoder (transformers modeling_dac.py DacDecoder.forward, the
+    module layout of docs/dac_architecture.md:37-133): stem conv1 (k 7, pad 3),
+    per block snake1 -> ConvTranspose1d (kernel 2 s, stride s, padding
+    ceil(s / 2)) -> residual units with dilations 1, 3, 9, then snake1 ->
+    conv2 (k 7, pad 3) -> tanh.  float64; p holds the state dict (numpy)."""
+    h = conv1d_ref(latent, p["conv1.weight"], p["conv1.bias"], padding=3)
+    for i, s in enumerate(upsampling_ratios):
+        b = f"block.{i}"
+        h = snake_conv_transpose1d_ref(h, np.asarray(p[f"{b}.snake1.alpha"]).reshape(-1), p[f"{b}.conv_t1.weight"],
+                                       p[f"{b}.conv_t1.bias"], stride=s, padding=(s + 1) // 2, eps=eps)
+        for j, d in enumerate((1, 3, 9)):
+            h = dac_residual_unit_ref(h, p, f"{b}.res_unit{j + 1}", d, eps)
+    h = snake_conv1d_ref(h, np.asarray(p["snake1.alpha"]).reshape(-1), p["conv2.weight"], p["conv2.bias"],
+                         padding=3, eps=eps)
+    return np.tanh(h)
+
+
 def cosine(a: np.ndarray, b: np.ndarray) -> float:
     a = np.asarray(a, np.float64).ravel()
     b = np.asarray(b, np.float64).ravel()

@@ -21,6 +21,10 @@ SN_FLAG_PDL = 1
 SN_WEIGHT_BF16 = 0
 SN_WEIGHT_INT8 = 1
 SN_WEIGHT_E4M3 = 2
+SN_ACT_SNAKE = 0
+SN_ACT_NONE = 1
+SN_POST_NONE = 0
+SN_POST_TANH = 1
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -46,6 +50,11 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_snake_conv1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P, ctypes.c_size_t,
                          _P], _I),
     "sn_snake_conv1d_noalloc": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P], _I),
+    "sn_snake_conv1d_ex": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _P,
+                            ctypes.c_size_t, _P], _I),
+    "sn_snake_conv_transpose1d_output_length": ([_I64, _I, _I, _I], _I64),
+    "sn_snake_conv_transpose1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P,
+                                   ctypes.c_size_t, _P], _I),
 }
 
 _lib = None

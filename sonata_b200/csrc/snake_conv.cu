@@ -59,7 +59,73 @@ struct ScParams {
   uint32_t w_bytes;    // one weight plane (nt * 128)
   uint32_t tcols;      // TMEM columns per accumulator buffer
   int ntiles_t2, ntiles2;  // CTA-pair kernel: 256-row time tiles and pair tiles
+  // epilogue / activation variants
+  const float* res;    // [B, Cout, Tout] added to the output (DAC residual unit), or nullptr
+  int act;             // SN_ACT_SNAKE or SN_ACT_NONE (the producers store x itself)
+  int post;            // SN_POST_NONE or SN_POST_TANH (applied last)
+  // transposed convolution as a polyphase GEMM (up_s > 0): GEMM column
+  // o' = o * up_s + r, row q holds y[b, o, up_s * q + r - up_p]; y is
+  // [B, Cy, Ty].  up_s == 0: plain convolution, column o, row t of y[b, o, t].
+  int up_s, up_p, Cy, Ty;
 };
+
+// Pull a tile's residual (GEMM rows t0 .. t0 + 127, columns o0 .. o0 + nt - 1)
+// into L2 while its MMAs run, so that the epilogue's reads hit L2: one
+// 128-byte line per (channel, 32-row segment), spread over the 128 epilogue
+// threads (et = 0 .. 127).
+__device__ __forceinline__ void sc_prefetch_res(const ScParams& p, int b, int t0, int o0, int et) {
+  if (!p.res || p.up_s != 0) return;
+  const float* rb = p.res + static_cast<int64_t>(b) * p.Cy * p.Tout;
+  for (int l = et; l < p.nt * 4; l += 128) {
+    const int o = o0 + (l >> 2), t = t0 + 32 * (l & 3);
+    if (o < p.Cy && t < p.Tout)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(rb + static_cast<int64_t>(o) * p.Tout + t));
+  }
+}
+
+// One TMEM row chunk of the epilogue: 16 GEMM columns starting at o_base of
+// GEMM row t (output time, or polyphase row q), plus bias, residual and the
+// post-op, stored to y.  Plain stores are coalesced along time across the warp;
+// the 16 residual reads are all issued before the first store.
+__device__ __forceinline__ void sc_store16(const ScParams& p, int b, int t, int o_base, const float (&vv)[16]) {
+  if (t >= p.Tout) return;
+  if (p.up_s == 0) {
+    float* yb = p.y + static_cast<int64_t>(b) * p.Cy * p.Tout;
+    float rv[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) rv[e] = 0.f;
+    if (p.res) {
+      const float* rb = p.res + static_cast<int64_t>(b) * p.Cy * p.Tout;
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (o_base + e < p.Cy) rv[e] = __ldg(rb + static_cast<int64_t>(o_base + e) * p.Tout + t);
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int o = o_base + e;
+      if (o < p.Cy) {
+        float v = vv[e] + (p.bias ? __ldg(p.bias + o) : 0.f) + rv[e];
+        if (p.post == SN_POST_TANH) v = tanhf(v);
+        yb[static_cast<int64_t>(o) * p.Tout + t] = v;
+      }
+    }
+  } else {
+    float* yb = p.y + static_cast<int64_t>(b) * p.Cy * p.Ty;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int oc = o_base + e;
+      if (oc < p.Cout) {
+        const int o = oc / p.up_s, r = oc - o * p.up_s;
+        const int ty = p.up_s * t + r - p.up_p;
+        if (ty >= 0 && ty < p.Ty) {
+          float v = vv[e] + (p.bias ? __ldg(p.bias + o) : 0.f);
+          if (p.post == SN_POST_TANH) v = tanhf(v);
+          yb[static_cast<int64_t>(o) * p.Ty + ty] = v;
+        }
+      }
+    }
+  }
+}
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
@@ -250,7 +316,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
         float al[8], inv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          al[e] = (i0 + e < p.Cin) ? __ldg(p.alpha + i0 + e) : 0.f;
+          al[e] = (p.act == SN_ACT_SNAKE && i0 + e < p.Cin) ? __ldg(p.alpha + i0 + e) : 0.f;
           inv[e] = 1.0f / (al[e] + p.eps);
         }
         if (g >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(a_empty + ab, ((g >> 1) - 1) & 1))) {
@@ -267,8 +333,11 @@ __global__ void __launch_bounds__(kScThreads, 1)
             float hi[8], lo[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float sv = __sinf(al[e] * v[it][e]);
-              const float s = fmaf(sv * sv, inv[e], v[it][e]);  // snake(v); snake(0) == 0
+              float s = v[it][e];
+              if (p.act == SN_ACT_SNAKE) {
+                const float sv = __sinf(al[e] * s);
+                s = fmaf(sv * sv, inv[e], s);  // snake(v); snake(0) == 0
+              }
               hi[e] = __bfloat162float(__float2bfloat16_rn(s));
               lo[e] = s - hi[e];
             }
@@ -291,6 +360,11 @@ __global__ void __launch_bounds__(kScThreads, 1)
     const int q4 = warp & 3;  // a warp may only read TMEM lanes 32*(warp id % 4) ..
     for (int j = 0; j < my_tiles; ++j) {
       const int tb = j & 1;
+      {
+        int b, t0, o0;
+        tile_coords(j, b, t0, o0);
+        sc_prefetch_res(p, b, t0, o0, threadIdx.x - 32 * (2 + kScProducerWarps));
+      }
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(t_full + tb, (j >> 1) & 1))) {
         record_status(SN_ERR_TIMEOUT);
         break;
@@ -299,18 +373,11 @@ __global__ void __launch_bounds__(kScThreads, 1)
       int b, t0, o0;
       tile_coords(j, b, t0, o0);
       const int t = t0 + q4 * 32 + lane;
-      float* yb = p.y + static_cast<int64_t>(b) * p.Cout * p.Tout;
       const uint32_t base = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(tb) * p.tcols;
       for (int cc = 0; cc < p.nt; cc += 16) {
         float vv[16];
         tc::tmem_ld16(base + cc, vv);
-        if (t < p.Tout) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int o = o0 + cc + e;
-            if (o < p.Cout) yb[static_cast<int64_t>(o) * p.Tout + t] = vv[e] + (p.bias ? __ldg(p.bias + o) : 0.f);
-          }
-        }
+        sc_store16(p, b, t, o0 + cc, vv);
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -494,7 +561,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
         float al[8], inv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          al[e] = (i0 + e < p.Cin) ? __ldg(p.alpha + i0 + e) : 0.f;
+          al[e] = (p.act == SN_ACT_SNAKE && i0 + e < p.Cin) ? __ldg(p.alpha + i0 + e) : 0.f;
           inv[e] = 1.0f / (al[e] + p.eps);
         }
         if (g >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(a_empty + ab, ((g >> 1) - 1) & 1))) {
@@ -511,8 +578,11 @@ __global__ void __launch_bounds__(kScThreads, 1)
             float hi[8], lo[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float sv = __sinf(al[e] * v[it][e]);
-              const float s = fmaf(sv * sv, inv[e], v[it][e]);
+              float s = v[it][e];
+              if (p.act == SN_ACT_SNAKE) {
+                const float sv = __sinf(al[e] * s);
+                s = fmaf(sv * sv, inv[e], s);
+              }
               hi[e] = __bfloat162float(__float2bfloat16_rn(s));
               lo[e] = s - hi[e];
             }
@@ -534,6 +604,11 @@ __global__ void __launch_bounds__(kScThreads, 1)
     const int q4 = warp & 3;
     for (int j = 0; j < my_tiles; ++j) {
       const int tb = j & 1;
+      {
+        int b, t0, o0;
+        tile_coords(j, b, t0, o0);
+        sc_prefetch_res(p, b, t0, o0, threadIdx.x - 32 * (2 + kScProducerWarps));
+      }
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(t_full + tb, (j >> 1) & 1))) {
         record_status(SN_ERR_TIMEOUT);
         break;
@@ -542,18 +617,11 @@ __global__ void __launch_bounds__(kScThreads, 1)
       int b, t0, o0;
       tile_coords(j, b, t0, o0);
       const int t = t0 + q4 * 32 + lane;
-      float* yb = p.y + static_cast<int64_t>(b) * p.Cout * p.Tout;
       const uint32_t base = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(tb) * p.tcols;
       for (int cc = 0; cc < p.nt; cc += 16) {
         float vv[16];
         tc::tmem_ld16(base + cc, vv);
-        if (t < p.Tout) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int o = o0 + cc + e;
-            if (o < p.Cout) yb[static_cast<int64_t>(o) * p.Tout + t] = vv[e] + (p.bias ? __ldg(p.bias + o) : 0.f);
-          }
-        }
+        sc_store16(p, b, t, o0 + cc, vv);
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -566,30 +634,92 @@ __global__ void __launch_bounds__(kScThreads, 1)
   if (warp == 1) tc::tmem_dealloc_pair(tmem, 2 * p.tcols);
 }
 
-// W fp32 [Cout, Cin, K] -> bf16 planes Wp[(k*2 + h)][o][i], h = 0 hi, 1 lo.
+// W fp32 [Cout, Cin, K] -> bf16 planes Wp[(k*2 + h)][o][i], h = 0 hi, 1 lo,
+// o < Cg (the GEMM width, Cout rounded up to 16; rows past Cout are zero).
 __global__ void pack_weights_kernel(const float* __restrict__ W, __nv_bfloat16* __restrict__ Wp, int Cout,
-                                    int Cin, int K) {
-  const int64_t total = static_cast<int64_t>(Cout) * Cin * K;
+                                    int Cin, int K, int Cg) {
+  const int64_t total = static_cast<int64_t>(Cg) * Cin * K;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int k = static_cast<int>(e % K);
     const int64_t oi = e / K;
     const int i = static_cast<int>(oi % Cin);
     const int o = static_cast<int>(oi / Cin);
-    const float w = W[e];
+    const float w = o < Cout ? W[e] : 0.f;
     const __nv_bfloat16 h = __float2bfloat16_rn(w);
     const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
-    const int64_t plane = static_cast<int64_t>(Cout) * Cin;
+    const int64_t plane = static_cast<int64_t>(Cg) * Cin;
     Wp[(static_cast<int64_t>(k) * 2 + 0) * plane + static_cast<int64_t>(o) * Cin + i] = h;
     Wp[(static_cast<int64_t>(k) * 2 + 1) * plane + static_cast<int64_t>(o) * Cin + i] = l;
   }
 }
 
+// ConvTranspose1d weight W fp32 [Cin, Cout, K] (K = m * s) -> the polyphase
+// GEMM's bf16 planes Wp[(k'*2 + h)][o * s + r][i]: GEMM tap k' (reading input
+// q - (m - 1) + k') of phase r uses W[i, o, r + (m - 1 - k') * s].
+__global__ void pack_weights_t_kernel(const float* __restrict__ W, __nv_bfloat16* __restrict__ Wp, int Cin,
+                                      int Cout, int K, int s) {
+  const int m = K / s;
+  const int64_t total = static_cast<int64_t>(Cin) * Cout * K;
+  const int64_t plane = static_cast<int64_t>(Cout) * s * Cin;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(e % K);
+    const int o = static_cast<int>((e / K) % Cout);
+    const int i = static_cast<int>(e / (static_cast<int64_t>(K) * Cout));
+    const int r = k % s, kt = m - 1 - k / s;
+    const float w = W[e];
+    const __nv_bfloat16 h = __float2bfloat16_rn(w);
+    const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
+    const int64_t col = (static_cast<int64_t>(o) * s + r) * Cin + i;
+    Wp[(static_cast<int64_t>(kt) * 2 + 0) * plane + col] = h;
+    Wp[(static_cast<int64_t>(kt) * 2 + 1) * plane + col] = l;
+  }
+}
+
+__device__ __forceinline__ float sc_act(int act, float v, float a, float inv) {
+  if (act != SN_ACT_SNAKE) return v;
+  const float sv = sinf(a * v);
+  return fmaf(sv * sv, inv, v);
+}
+
 // Fallback: one thread per output element, the reference's loop order.
 __global__ void snake_conv_simt_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
                                        const float* __restrict__ W, const float* __restrict__ bias,
-                                       float* __restrict__ y, int B, int Cin, int Cout, int T, int Tout, int K,
-                                       int stride, int pad, int dil, float eps) {
+                                       const float* __restrict__ res, float* __restrict__ y, int B, int Cin,
+                                       int Cout, int T, int Tout, int K, int stride, int pad, int dil, float eps,
+                                       int act, int post) {
+  const int64_t total = static_cast<int64_t>(B) * Cout * Tout;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(e % Tout);
+    const int64_t r = e / Tout;
+    const int o = static_cast<int>(r % Cout);
+    const int b = static_cast<int>(r / Cout);
+    float acc = bias ? bias[o] : 0.f;
+    for (int i = 0; i < Cin; ++i) {
+      const float a = act == SN_ACT_SNAKE ? alpha[i] : 0.f;
+      const float inv = 1.0f / (a + eps);
+      const float* xr = x + (static_cast<int64_t>(b) * Cin + i) * T;
+      const float* wr = W + (static_cast<int64_t>(o) * Cin + i) * K;
+      for (int k = 0; k < K; ++k) {
+        const int ti = t * stride - pad + k * dil;
+        if (ti < 0 || ti >= T) continue;
+        acc = fmaf(sc_act(act, xr[ti], a, inv), wr[k], acc);
+      }
+    }
+    if (res) acc += res[e];
+    if (post == SN_POST_TANH) acc = tanhf(acc);
+    y[e] = acc;
+  }
+}
+
+// Transposed fallback: y[b, o, t] = bias[o] + sum over (i, k) with
+// t = j * s - p + k, 0 <= j < T, of snake(x[b, i, j]) * W[i, o, k].
+__global__ void snake_convt_simt_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
+                                        const float* __restrict__ W, const float* __restrict__ bias,
+                                        float* __restrict__ y, int B, int Cin, int Cout, int T, int Tout, int K,
+                                        int stride, int pad, float eps) {
   const int64_t total = static_cast<int64_t>(B) * Cout * Tout;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -602,19 +732,20 @@ __global__ void snake_conv_simt_kernel(const float* __restrict__ x, const float*
       const float a = alpha[i];
       const float inv = 1.0f / (a + eps);
       const float* xr = x + (static_cast<int64_t>(b) * Cin + i) * T;
-      const float* wr = W + (static_cast<int64_t>(o) * Cin + i) * K;
+      const float* wr = W + (static_cast<int64_t>(i) * Cout + o) * K;
       for (int k = 0; k < K; ++k) {
-        const int ti = t * stride - pad + k * dil;
-        if (ti < 0 || ti >= T) continue;
-        const float v = xr[ti];
-        const float sv = sinf(a * v);
-        acc = fmaf(fmaf(sv * sv, inv, v), wr[k], acc);
+        const int num = t + pad - k;  // j * stride
+        if (num < 0 || num % stride != 0) continue;
+        const int j = num / stride;
+        if (j >= T) continue;
+        acc = fmaf(sc_act(SN_ACT_SNAKE, xr[j], a, inv), wr[k], acc);
       }
     }
     y[e] = acc;
   }
 }
 
+// Cout: the GEMM width (a multiple of 16: the plain convolution pads it).
 bool fast_path_ok(int Cin, int Cout, int K, int stride, int dil, int Tout) {
   return stride == 1 && K >= 1 && K <= kMaxTaps && dil >= 1 && (K - 1) * dil <= 72 && Cin % 16 == 0 &&
          Cout % 16 == 0 && Tout >= 1;
@@ -662,110 +793,201 @@ int64_t sn_snake_conv1d_output_length(int64_t T, int K, int stride, int padding,
 }
 
 size_t sn_snake_conv1d_workspace_size(int Cin, int Cout, int K) {
-  return static_cast<size_t>(Cin) * Cout * K * 2 * sizeof(__nv_bfloat16);
+  return static_cast<size_t>(Cin) * ((Cout + 15) / 16 * 16) * K * 2 * sizeof(__nv_bfloat16);
 }
 
 int sn_snake_conv1d(const float* x, const float* alpha, const float* W, const float* bias, float* y, int B, int Cin,
                     int Cout, int T, int K, int stride, int padding, int dilation, float eps, void* workspace,
                     size_t workspace_bytes, void* stream) {
-  if (!x || !alpha || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0 ||
+  return sn_snake_conv1d_ex(x, alpha, W, bias, nullptr, y, B, Cin, Cout, T, K, stride, padding, dilation, eps,
+                            SN_ACT_SNAKE, SN_POST_NONE, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"
+
+namespace sn {
+namespace {
+
+// The tensor-core path for a GEMM-shaped problem: p carries B, Cin, Cout (GEMM
+// columns), T, Tout (GEMM rows), K (taps), pad, dil, eps and the epilogue
+// variant; `pack` writes the bf16 hi/lo planes [K][2][Cout][Cin] into Wp.
+// SN_ERR_UNSUPPORTED when the shape or the resources rule the path out.
+template <typename Pack>
+int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
+  p.ntiles_t = (p.Tout + 127) / 128;
+  const int sms = sm_count();
+  p.nt = out_tile(p.Cout, static_cast<int64_t>(p.B) * p.ntiles_t, sms);
+  p.ntiles_o = (p.Cout + p.nt - 1) / p.nt;
+  p.tcols = tc::tmem_cols_for(p.nt);
+  p.rows = (128 + (p.K - 1) * p.dil + 7) / 8 * 8;
+  p.a_bytes = static_cast<uint32_t>(p.rows) * 128;
+  p.w_bytes = static_cast<uint32_t>(p.nt) * 128;
+  const size_t smem = 1024 + 4 * static_cast<size_t>(p.a_bytes) + 2 * kScWStages * static_cast<size_t>(p.w_bytes) + 256;
+  const int64_t ntiles64 = static_cast<int64_t>(p.B) * p.ntiles_t * p.ntiles_o;
+  p.ntiles = static_cast<int>(std::min<int64_t>(ntiles64, INT32_MAX));
+  if (!(smem <= 227 * 1024 && ntiles64 < (int64_t(1) << 31) && p.rows <= 32 * kMaxRowIters && 2 * p.tcols <= 512))
+    return SN_ERR_UNSUPPORTED;
+  int rc = pack();
+  if (rc != SN_OK) return rc;
+  CUtensorMap mapW;
+  const uint64_t dims[3] = {static_cast<uint64_t>(p.Cin), static_cast<uint64_t>(p.Cout),
+                            static_cast<uint64_t>(2 * p.K)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(p.Cin) * 2, static_cast<uint64_t>(p.Cout) * p.Cin * 2};
+  // CTA pairs pay off from Cout = 192 up (measured: -3 to -4% at C = 192 and
+  // 384, even at 768, +9% at C = 96 where nt / 2 = 48 weight rows per CTA)
+  if (snake_pair_enabled() && p.Cout >= 128) {
+    // CTA-pair kernel: 256-row time tiles, each CTA holding nt / 2 weight rows
+    ScParams q = p;
+    q.ntiles_t2 = (p.Tout + 255) / 256;
+    const int npairs = std::max(1, sms / 2);
+    q.nt = out_tile(p.Cout, static_cast<int64_t>(p.B) * q.ntiles_t2, npairs);
+    q.ntiles_o = (p.Cout + q.nt - 1) / q.nt;
+    q.tcols = tc::tmem_cols_for(q.nt);
+    q.w_bytes = static_cast<uint32_t>(q.nt) * 128;
+    const int64_t nt2 = static_cast<int64_t>(p.B) * q.ntiles_t2 * q.ntiles_o;
+    q.ntiles2 = static_cast<int>(std::min<int64_t>(nt2, INT32_MAX));
+    const size_t smem2 = 1024 + 4 * static_cast<size_t>(q.a_bytes) + kScPairWStages * static_cast<size_t>(q.w_bytes) + 256;
+    const uint32_t box2[3] = {64, static_cast<uint32_t>(q.nt / 2), 1};
+    if (nt2 < (int64_t(1) << 31) && 2 * q.tcols <= 512 && smem2 <= 227 * 1024 &&
+        tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box2) &&
+        cudaFuncSetAttribute(snake_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem2)) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * std::min(q.ntiles2, npairs));
+      cfg.blockDim = dim3(kScThreads);
+      cfg.dynamicSmemBytes = smem2;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, snake_conv_pair_kernel, mapW, q) == cudaSuccess) return SN_OK;
+    }
+    cudaGetLastError();
+  }
+  const uint32_t box[3] = {64, static_cast<uint32_t>(p.nt), 1};
+  if (tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box)) {
+    if (cudaFuncSetAttribute(snake_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) == cudaSuccess) {
+      const int grid = std::min(p.ntiles, sms);
+      return launch(snake_conv_mma_kernel, dim3(grid), dim3(kScThreads), smem, st, false, mapW, p);
+    }
+    cudaGetLastError();
+  }
+  return SN_ERR_UNSUPPORTED;
+}
+
+ScParams base_params(const float* x, const float* alpha, const float* bias, float* y, int B, int Cin, float eps) {
+  ScParams p = {};
+  p.x = x;
+  p.alpha = alpha;
+  p.bias = bias;
+  p.y = y;
+  p.B = B;
+  p.Cin = Cin;
+  p.eps = eps;
+  p.res = nullptr;
+  p.act = SN_ACT_SNAKE;
+  p.post = SN_POST_NONE;
+  p.up_s = p.up_p = 0;
+  return p;
+}
+
+int blocks_for(int64_t total, int per_sm) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, int64_t(148) * per_sm)));
+}
+
+}  // namespace
+}  // namespace sn
+
+extern "C" {
+
+int sn_snake_conv1d_ex(const float* x, const float* alpha, const float* W, const float* bias, const float* residual,
+                       float* y, int B, int Cin, int Cout, int T, int K, int stride, int padding, int dilation,
+                       float eps, int act, int post, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0 ||
       dilation < 1)
     return SN_ERR_INVALID_ARGUMENT;
+  if ((act != SN_ACT_SNAKE && act != SN_ACT_NONE) || (post != SN_POST_NONE && post != SN_POST_TANH))
+    return SN_ERR_INVALID_ARGUMENT;
+  if (act == SN_ACT_SNAKE && !alpha) return SN_ERR_INVALID_ARGUMENT;
   const int64_t tout64 = sn_snake_conv1d_output_length(T, K, stride, padding, dilation);
   if (tout64 < 1 || tout64 > (int64_t(1) << 31) - 1) return SN_ERR_INVALID_ARGUMENT;
   const int Tout = static_cast<int>(tout64);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool fast = sn::fast_path_ok(Cin, Cout, K, stride, dilation, Tout) && workspace &&
-                    workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && sn::aligned16(workspace);
-  if (fast) {
-    sn::ScParams p;
-    p.x = x;
-    p.alpha = alpha;
-    p.bias = bias;
-    p.y = y;
-    p.B = B;
-    p.Cin = Cin;
-    p.Cout = Cout;
+  const int Cg = (Cout + 15) / 16 * 16;  // GEMM width: zero weight rows past Cout
+  if (sn::fast_path_ok(Cin, Cg, K, stride, dilation, Tout) && workspace &&
+      workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && sn::aligned16(workspace)) {
+    sn::ScParams p = sn::base_params(x, alpha, bias, y, B, Cin, eps);
+    p.Cout = Cg;
     p.T = T;
     p.Tout = Tout;
     p.K = K;
     p.pad = padding;
     p.dil = dilation;
-    p.eps = eps;
-    p.ntiles_t = (Tout + 127) / 128;
-    const int sms = sn::sm_count();
-    p.nt = sn::out_tile(Cout, static_cast<int64_t>(B) * p.ntiles_t, sms);
-    p.ntiles_o = (Cout + p.nt - 1) / p.nt;
-    p.tcols = sn::tc::tmem_cols_for(p.nt);
-    p.rows = (128 + (K - 1) * dilation + 7) / 8 * 8;
-    p.a_bytes = static_cast<uint32_t>(p.rows) * 128;
-    p.w_bytes = static_cast<uint32_t>(p.nt) * 128;
-    const size_t smem = 1024 + 4 * static_cast<size_t>(p.a_bytes) +
-                        2 * sn::kScWStages * static_cast<size_t>(p.w_bytes) + 256;
-    const int64_t ntiles64 = static_cast<int64_t>(B) * p.ntiles_t * p.ntiles_o;
-    p.ntiles = static_cast<int>(std::min<int64_t>(ntiles64, INT32_MAX));
-    if (smem <= 227 * 1024 && ntiles64 < (int64_t(1) << 31) && p.rows <= 32 * sn::kMaxRowIters &&
-        2 * p.tcols <= 512) {
-      __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
-      const int64_t tot = static_cast<int64_t>(Cout) * Cin * K;
-      const int blocks = static_cast<int>(std::min<int64_t>((tot + 255) / 256, 148 * 8));
-      int rc = sn::launch(sn::pack_weights_kernel, dim3(blocks), dim3(256), 0, st, false, W, Wp, Cout, Cin, K);
-      if (rc != SN_OK) return rc;
-      CUtensorMap mapW;
-      const uint64_t dims[3] = {static_cast<uint64_t>(Cin), static_cast<uint64_t>(Cout),
-                                static_cast<uint64_t>(2 * K)};
-      const uint64_t strides[2] = {static_cast<uint64_t>(Cin) * 2, static_cast<uint64_t>(Cout) * Cin * 2};
-      // CTA pairs pay off from Cout = 192 up (measured: -3 to -4% at C = 192 and
-      // 384, even at 768, +9% at C = 96 where nt / 2 = 48 weight rows per CTA)
-      if (sn::snake_pair_enabled() && Cout >= 128) {
-        // CTA-pair kernel: 256-row time tiles, each CTA holding nt / 2 weight rows
-        sn::ScParams q = p;
-        q.ntiles_t2 = (Tout + 255) / 256;
-        const int npairs = std::max(1, sms / 2);
-        q.nt = sn::out_tile(Cout, static_cast<int64_t>(B) * q.ntiles_t2, npairs);
-        q.ntiles_o = (Cout + q.nt - 1) / q.nt;
-        q.tcols = sn::tc::tmem_cols_for(q.nt);
-        q.w_bytes = static_cast<uint32_t>(q.nt) * 128;
-        const int64_t nt2 = static_cast<int64_t>(B) * q.ntiles_t2 * q.ntiles_o;
-        q.ntiles2 = static_cast<int>(std::min<int64_t>(nt2, INT32_MAX));
-        const size_t smem2 = 1024 + 4 * static_cast<size_t>(q.a_bytes) +
-                             sn::kScPairWStages * static_cast<size_t>(q.w_bytes) + 256;
-        const uint32_t box2[3] = {64, static_cast<uint32_t>(q.nt / 2), 1};
-        if (nt2 < (int64_t(1) << 31) && 2 * q.tcols <= 512 && smem2 <= 227 * 1024 &&
-            sn::tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box2) &&
-            cudaFuncSetAttribute(sn::snake_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem2)) == cudaSuccess) {
-          cudaLaunchConfig_t cfg = {};
-          cfg.gridDim = dim3(2 * std::min(q.ntiles2, npairs));
-          cfg.blockDim = dim3(sn::kScThreads);
-          cfg.dynamicSmemBytes = smem2;
-          cfg.stream = st;
-          cudaLaunchAttribute attr[1];
-          attr[0].id = cudaLaunchAttributeClusterDimension;
-          attr[0].val.clusterDim.x = 2;
-          attr[0].val.clusterDim.y = 1;
-          attr[0].val.clusterDim.z = 1;
-          cfg.attrs = attr;
-          cfg.numAttrs = 1;
-          if (cudaLaunchKernelEx(&cfg, sn::snake_conv_pair_kernel, mapW, q) == cudaSuccess) return SN_OK;
-        }
-        cudaGetLastError();
-      }
-      const uint32_t box[3] = {64, static_cast<uint32_t>(p.nt), 1};
-      if (sn::tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box)) {
-        if (cudaFuncSetAttribute(sn::snake_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)) == cudaSuccess) {
-          const int grid = std::min(p.ntiles, sms);
-          return sn::launch(sn::snake_conv_mma_kernel, dim3(grid), dim3(sn::kScThreads), smem, st, false, mapW, p);
-        }
-        cudaGetLastError();
-      }
-    }
+    p.res = residual;
+    p.act = act;
+    p.post = post;
+    p.Cy = Cout;
+    p.Ty = Tout;
+    __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
+    const int rc = sn::snake_fast(p, Wp, st, [&] {
+      const int64_t tot = static_cast<int64_t>(Cg) * Cin * K;
+      return sn::launch(sn::pack_weights_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0, st, false, W, Wp, Cout,
+                        Cin, K, Cg);
+    });
+    if (rc != SN_ERR_UNSUPPORTED) return rc;
   }
   const int64_t total = static_cast<int64_t>(B) * Cout * Tout;
-  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 32));
-  return sn::launch(sn::snake_conv_simt_kernel, dim3(blocks), dim3(256), 0, st, false, x, alpha, W, bias, y, B, Cin,
-                    Cout, T, Tout, K, stride, padding, dilation, eps);
+  return sn::launch(sn::snake_conv_simt_kernel, dim3(sn::blocks_for(total, 32)), dim3(256), 0, st, false, x, alpha,
+                    W, bias, residual, y, B, Cin, Cout, T, Tout, K, stride, padding, dilation, eps, act, post);
+}
+
+int64_t sn_snake_conv_transpose1d_output_length(int64_t T, int K, int stride, int padding) {
+  if (T < 1 || stride < 1 || K < 1 || padding < 0) return -1;
+  return (T - 1) * stride - 2 * static_cast<int64_t>(padding) + K;
+}
+
+int sn_snake_conv_transpose1d(const float* x, const float* alpha, const float* W, const float* bias, float* y, int B,
+                              int Cin, int Cout, int T, int K, int stride, int padding, float eps, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (!x || !alpha || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0)
+    return SN_ERR_INVALID_ARGUMENT;
+  const int64_t ty64 = sn_snake_conv_transpose1d_output_length(T, K, stride, padding);
+  if (ty64 < 1 || ty64 > (int64_t(1) << 31) - 1) return SN_ERR_INVALID_ARGUMENT;
+  const int Ty = static_cast<int>(ty64);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // polyphase GEMM: m = K / s taps per phase over rows q in [0, T + m - 1)
+  const int m = (K % stride == 0) ? K / stride : 0;
+  const int64_t gcols = static_cast<int64_t>(Cout) * stride;
+  if (m >= 1 && gcols <= INT32_MAX && static_cast<int64_t>(T) + m - 1 <= INT32_MAX &&
+      sn::fast_path_ok(Cin, static_cast<int>(gcols), m, 1, 1, T + m - 1) && workspace &&
+      workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && sn::aligned16(workspace)) {
+    sn::ScParams p = sn::base_params(x, alpha, bias, y, B, Cin, eps);
+    p.Cout = static_cast<int>(gcols);
+    p.T = T;
+    p.Tout = T + m - 1;
+    p.K = m;
+    p.pad = m - 1;
+    p.dil = 1;
+    p.up_s = stride;
+    p.up_p = padding;
+    p.Cy = Cout;
+    p.Ty = Ty;
+    __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
+    const int rc = sn::snake_fast(p, Wp, st, [&] {
+      const int64_t tot = static_cast<int64_t>(Cin) * Cout * K;
+      return sn::launch(sn::pack_weights_t_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0, st, false, W, Wp, Cin,
+                        Cout, K, stride);
+    });
+    if (rc != SN_ERR_UNSUPPORTED) return rc;
+  }
+  const int64_t total = static_cast<int64_t>(B) * Cout * Ty;
+  return sn::launch(sn::snake_convt_simt_kernel, dim3(sn::blocks_for(total, 32)), dim3(256), 0, st, false, x, alpha,
+                    W, bias, y, B, Cin, Cout, T, Ty, K, stride, padding, eps);
 }
 
 // ---------------------------------------------------------------------------

@@ -44,12 +44,89 @@ def _workspace(device, nbytes: int) -> torch.Tensor:
     return buf
 
 
+_ACTS = {"snake": _lib.SN_ACT_SNAKE, "none": _lib.SN_ACT_NONE}
+_POSTS = {None: _lib.SN_POST_NONE, "tanh": _lib.SN_POST_TANH}
+
+
 def fused_snake_conv1d(x: torch.Tensor, alpha: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
                        stride: int = 1, padding: int = 0, dilation: int = 1, eps: float = 1e-9,
-                       out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    """Validate inputs and run the fused Snake -> Conv1d kernel."""
+                       out: torch.Tensor | None = None, stream=None, *, residual: torch.Tensor | None = None,
+                       activation: str = "snake", post: str | None = None) -> torch.Tensor:
+    """Validate inputs and run the fused Snake -> Conv1d kernel.
+
+    Keyword-only additions for the rest of the DAC decoder: ``residual``
+    (fp32, the output's shape) is added after the bias, ``activation="none"``
+    skips the Snake (alpha may then be None), ``post="tanh"`` applies tanh
+    last."""
     batch_size, input_channels, input_length = x.shape
     output_channels, weight_channels, kernel_size = weight.shape
+    if activation not in _ACTS:
+        raise ValueError(f"activation must be one of {sorted(_ACTS)}, got {activation!r}")
+    if post not in _POSTS:
+        raise ValueError(f"post must be None or 'tanh', got {post!r}")
+    snake = activation == "snake"
+    if weight_channels != input_channels:
+        raise ValueError("Only groups=1 is currently supported.")
+    if snake and alpha.numel() != input_channels:
+        raise ValueError("alpha must contain one value per input channel.")
+    if bias is not None and bias.numel() != output_channels:
+        raise ValueError("bias must contain one value per output channel.")
+    require_cuda("x", x, torch.float32, 3)
+    if snake:
+        require_cuda("alpha", alpha, torch.float32)
+    require_cuda("weight", weight, torch.float32, 3)
+    if bias is not None:
+        require_cuda("bias", bias, torch.float32)
+    output_length = conv1d_output_length(input_length, kernel_size, stride, padding, dilation)
+    if output_length < 1:
+        raise ValueError("the convolution has no output positions")
+    x = x.contiguous()
+    weight = weight.contiguous()
+    alpha_c = alpha.contiguous().view(-1) if snake else None
+    bias_c = bias.contiguous().view(-1) if bias is not None else None
+    if out is None:
+        out = torch.empty((batch_size, output_channels, output_length), device=x.device, dtype=x.dtype)
+    elif tuple(out.shape) != (batch_size, output_channels, output_length) or not out.is_contiguous():
+        raise ValueError("out has the wrong shape or is not contiguous")
+    res_c = None
+    if residual is not None:
+        require_cuda("residual", residual, torch.float32, 3)
+        if tuple(residual.shape) != tuple(out.shape):
+            raise ValueError(f"residual must have the output's shape {tuple(out.shape)}")
+        res_c = residual.contiguous()
+        if res_c.data_ptr() == out.data_ptr():
+            raise ValueError("residual must not alias out")
+    lib = _lib.lib()
+    ws_bytes = lib.sn_snake_conv1d_workspace_size(input_channels, output_channels, kernel_size)
+    ws = _workspace(x.device, ws_bytes)
+    if res_c is None and snake and post is None:
+        _lib.check("sn_snake_conv1d", lib.sn_snake_conv1d(
+            x.data_ptr(), alpha_c.data_ptr(), weight.data_ptr(), bias_c.data_ptr() if bias_c is not None else None,
+            out.data_ptr(), batch_size, input_channels, output_channels, input_length, kernel_size, stride, padding,
+            dilation, float(eps), ws.data_ptr(), ws.numel(), stream_handle(stream)))
+    else:
+        _lib.check("sn_snake_conv1d_ex", lib.sn_snake_conv1d_ex(
+            x.data_ptr(), alpha_c.data_ptr() if alpha_c is not None else None, weight.data_ptr(),
+            bias_c.data_ptr() if bias_c is not None else None, res_c.data_ptr() if res_c is not None else None,
+            out.data_ptr(), batch_size, input_channels, output_channels, input_length, kernel_size, stride, padding,
+            dilation, float(eps), _ACTS[activation], _POSTS[post], ws.data_ptr(), ws.numel(),
+            stream_handle(stream)))
+    return out
+
+
+def conv_transpose1d_output_length(input_length: int, kernel_size: int, stride: int, padding: int) -> int:
+    """PyTorch ConvTranspose1d's output length (dilation 1, output_padding 0)."""
+    return (input_length - 1) * stride - 2 * padding + kernel_size
+
+
+def fused_snake_conv_transpose1d(x: torch.Tensor, alpha: torch.Tensor, weight: torch.Tensor,
+                                 bias: torch.Tensor | None = None, stride: int = 1, padding: int = 0,
+                                 eps: float = 1e-9, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Snake -> ConvTranspose1d (the DacDecoderBlock's snake1 -> conv_t1):
+    ``conv_transpose1d(snake(x), weight, bias, stride, padding)`` with weight
+    in torch's [Cin, Cout, K] layout; runs ``sn_snake_conv_transpose1d``."""
+    batch_size, input_channels, input_length = x.shape
+    weight_channels, output_channels, kernel_size = weight.shape
     if weight_channels != input_channels:
         raise ValueError("Only groups=1 is currently supported.")
     if alpha.numel() != input_channels:
@@ -61,9 +138,9 @@ def fused_snake_conv1d(x: torch.Tensor, alpha: torch.Tensor, weight: torch.Tenso
     require_cuda("weight", weight, torch.float32, 3)
     if bias is not None:
         require_cuda("bias", bias, torch.float32)
-    output_length = conv1d_output_length(input_length, kernel_size, stride, padding, dilation)
+    output_length = conv_transpose1d_output_length(input_length, kernel_size, stride, padding)
     if output_length < 1:
-        raise ValueError("the convolution has no output positions")
+        raise ValueError("the transposed convolution has no output positions")
     x = x.contiguous()
     weight = weight.contiguous()
     alpha = alpha.contiguous().view(-1)
@@ -73,12 +150,11 @@ def fused_snake_conv1d(x: torch.Tensor, alpha: torch.Tensor, weight: torch.Tenso
     elif tuple(out.shape) != (batch_size, output_channels, output_length) or not out.is_contiguous():
         raise ValueError("out has the wrong shape or is not contiguous")
     lib = _lib.lib()
-    ws_bytes = lib.sn_snake_conv1d_workspace_size(input_channels, output_channels, kernel_size)
-    ws = _workspace(x.device, ws_bytes)
-    _lib.check("sn_snake_conv1d", lib.sn_snake_conv1d(
+    ws = _workspace(x.device, lib.sn_snake_conv1d_workspace_size(input_channels, output_channels, kernel_size))
+    _lib.check("sn_snake_conv_transpose1d", lib.sn_snake_conv_transpose1d(
         x.data_ptr(), alpha.data_ptr(), weight.data_ptr(), bias_c.data_ptr() if bias_c is not None else None,
         out.data_ptr(), batch_size, input_channels, output_channels, input_length, kernel_size, stride, padding,
-        dilation, float(eps), ws.data_ptr(), ws.numel(), stream_handle(stream)))
+        float(eps), ws.data_ptr(), ws.numel(), stream_handle(stream)))
     return out
 
 

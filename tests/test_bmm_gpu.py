@@ -98,11 +98,14 @@ def test_codebook_head(Bm, B):
 
 
 @pytest.mark.parametrize("ncb,B,K,N", [(9, 8, 2048, 300), (9, 64, 1024, 100), (2, 5, 512, 129),
-                                        (4, 16, 2048, 256), (3, 40, 2048, 1025), (9, 33, 4096, 1025)])
+                                        (4, 16, 2048, 256), (3, 40, 2048, 1025), (9, 33, 4096, 1025),
+                                        (2, 7, 192, 300), (2, 3, 100, 130), (1, 2, 64, 128)])
 def test_codebook_head_shapes(Bm, ncb, B, K, N):
     # row counts with and without a remainder past the last 128-row tile, K
-    # halves of 256..2048, stream tiles that do not fill the MMA N, and
-    # N < 128 (no full tile: the single-CTA tensor-core kernel)
+    # halves of 256..2048, stream tiles that do not fill the MMA N, N < 128
+    # (no full tile: CUDA cores only), K = 192 (a multiple of 64, not of 128:
+    # the single-CTA tensor-core kernel plus the remainder-row kernel), K = 100
+    # (K-major packing: the decode GEMV) and K = 64 with one exact tile
     g = torch.Generator().manual_seed(ncb * 1000 + B + N)
     hidden = torch.randn(ncb, B, K, generator=g).to(torch.bfloat16)
     W = (torch.randn(ncb, K, N, generator=g) * 0.02).to(torch.bfloat16)
@@ -111,6 +114,26 @@ def test_codebook_head_shapes(Bm, ncb, B, K, N):
     head(hidden.cuda(), out=out)
     torch.cuda.synchronize()
     assert torch.isfinite(out).all()
+    truth = O.codebook_head_ref(bits(hidden), bits(W))
+    assert O.rel_err_inf(out.cpu().numpy(), truth) <= 1e-4
+
+
+def test_codebook_head_unaligned_hidden(Bm):
+    # hidden 2 bytes past a 16-byte boundary (the C ABI takes any bf16
+    # pointer): no TMA, every logit on the CUDA cores
+    from sonata_b200 import _lib
+    g = torch.Generator().manual_seed(11)
+    ncb, B, K, N = 3, 6, 256, 200
+    hidden = torch.randn(ncb, B, K, generator=g).to(torch.bfloat16)
+    W = (torch.randn(ncb, K, N, generator=g) * 0.02).to(torch.bfloat16)
+    head = Bm.CodebookHead(W.cuda())
+    buf = torch.zeros(ncb * B * K + 8, dtype=torch.bfloat16, device="cuda")
+    buf[1:1 + ncb * B * K] = hidden.reshape(-1).cuda()
+    out = torch.full((ncb, B, N), float("nan"), device="cuda")
+    rc = _lib.lib().sn_codebook_head_bmm(buf.data_ptr() + 2, head.Wt.data_ptr(), out.data_ptr(), ncb, B, K, N, 0,
+                                         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0
     truth = O.codebook_head_ref(bits(hidden), bits(W))
     assert O.rel_err_inf(out.cpu().numpy(), truth) <= 1e-4
 

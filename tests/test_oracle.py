@@ -150,3 +150,65 @@ def test_conv1d_output_length(golden):
     sc = golden("snake_conv")
     for L, K, s, p, d, out in sc["output_length_cases"].tolist():
         assert O.conv1d_output_length(L, K, s, p, d) == out
+
+
+# ---------------- DAC decoder (transformers DacDecoder, pinned in dac.npz) ----------------
+
+@pytest.mark.parametrize("n", range(4))
+def test_snake_conv_transpose_oracle_matches_torch(golden, n):
+    g = golden("dac")
+    s, K, p = g[f"convt_{n}__meta"].tolist()
+    y = O.snake_conv_transpose1d_ref(g[f"convt_{n}__x"], g[f"convt_{n}__alpha"], g[f"convt_{n}__w"],
+                                     g[f"convt_{n}__b"], stride=s, padding=p)
+    yr = g[f"convt_{n}__y"]
+    assert y.shape == yr.shape
+    np.testing.assert_allclose(y, yr, rtol=0, atol=1e-5 * max(1.0, np.abs(yr).max()))
+
+
+def _polyphase_convt(x, alpha, w, b, s, p):
+    """The CUDA path's decomposition, restated in numpy: a stride-1 conv with
+    m = K / s taps (input q - (m - 1) + k') over GEMM columns o * s + r, tap k'
+    of phase r weighted by W[:, o, r + (m - 1 - k') * s], row q scattered to
+    output time s * q + r - p (sn_snake_conv_transpose1d)."""
+    act = O.snake_ref(x, alpha)
+    Bn, Cin, T = act.shape
+    _, Cout, K = w.shape
+    m = K // s
+    Ty = O.conv_transpose1d_output_length(T, K, s, p)
+    Wg = np.zeros((Cout * s, Cin, m))
+    for o in range(Cout):
+        for r in range(s):
+            for kt in range(m):
+                Wg[o * s + r, :, kt] = w[:, o, r + (m - 1 - kt) * s]
+    G = O.conv1d_ref(act, Wg, None, padding=m - 1)  # [B, Cout * s, T + m - 1]
+    y = np.zeros((Bn, Cout, Ty))
+    for q in range(G.shape[2]):
+        for o in range(Cout):
+            for r in range(s):
+                t = s * q + r - p
+                if 0 <= t < Ty:
+                    y[:, o, t] = G[:, o * s + r, q] + b[o]
+    return y
+
+
+@pytest.mark.parametrize("n", range(4))
+def test_polyphase_decomposition_equals_conv_transpose(golden, n):
+    g = golden("dac")
+    s, K, p = g[f"convt_{n}__meta"].tolist()
+    y = _polyphase_convt(g[f"convt_{n}__x"], g[f"convt_{n}__alpha"], g[f"convt_{n}__w"], g[f"convt_{n}__b"], s, p)
+    yr = g[f"convt_{n}__y"]
+    np.testing.assert_allclose(y, yr, rtol=0, atol=1e-5 * max(1.0, np.abs(yr).max()))
+
+
+def test_dac_decoder_oracle_matches_transformers(golden):
+    from sonata_b200.kernels.dac import init_decoder_params
+    g = golden("dac")
+    cfg = {"hidden_size": 32, "decoder_hidden_size": 256, "upsampling_ratios": (8, 8, 4, 2)}
+    params = init_decoder_params(cfg, seed=int(g["decoder__param_seed"]))
+    # the seeded draw reproduces the weights the fixture was made with
+    assert abs(sum(float(v.double().sum()) for v in params.values()) - float(g["decoder__param_sum"])) < 1e-9
+    audio = O.dac_decoder_ref(g["decoder__latent"], {k: v.numpy() for k, v in params.items()},
+                              cfg["upsampling_ratios"])
+    ref = g["decoder__audio"]
+    assert audio.shape == ref.shape == (2, 1, 3 * 512)
+    np.testing.assert_allclose(audio, ref, rtol=0, atol=1e-4)
