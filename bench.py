@@ -288,8 +288,14 @@ def time_replays(g, steps, warmup, world, before=None, after=None):
 
 
 # ---------------------------------------------------------------------------
-# Snake + Conv1d (config 5): microseconds per second of audio
+# Snake + Conv1d (config 5) and the whole DAC decoder: microseconds per second
+# of audio
 # ---------------------------------------------------------------------------
+def bench_dac_decoder(warmup=2, reps=3):
+    from sonata_b200.kernels import dac
+    return dac.bench_dac_decoder(warmup=warmup, reps=reps)
+
+
 def bench_snake_conv(warmup=2, reps=3):
     try:
         from sonata_b200.kernels import fused_snake_conv as fsc
@@ -403,8 +409,10 @@ def run_ours(args):
         raise RuntimeError(f"graph replay output does not match F.linear (rel err {rel:.3e})")
 
     snake = None
+    dac = None
     if rank == 0 and not args.skip_snake:
         snake = bench_snake_conv()
+        dac = bench_dac_decoder()
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -470,6 +478,8 @@ def run_ours(args):
     }
     if snake is not None:
         line["snake_conv"] = snake
+    if dac is not None:
+        line["dac_decoder"] = dac
     line.update(sharded)
     print(json.dumps(line), flush=True)
     return 0

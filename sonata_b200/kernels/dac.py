@@ -141,3 +141,41 @@ def dac_residual_unit(x: torch.Tensor, alpha1, w1, b1, alpha2, w2, b2, dilation:
     k = w1.shape[-1]
     y = fused_snake_conv1d(x, alpha1, w1, b1, padding=(k - 1) * dilation // 2, dilation=dilation, stream=stream)
     return fused_snake_conv1d(y, alpha2, w2, b2, stream=stream, residual=x)
+
+
+def bench_dac_decoder(warmup: int = 2, reps: int = 3, frames: int = 862, seed: int = 0) -> dict:
+    """Microseconds per second of audio for the whole 44.1 kHz decoder (one
+    stream, `frames` latent frames = 10.0 s at 862), on device-resident
+    synthetic weights and latent; CUDA events around `reps` forwards."""
+    cfg = dac_decoder_config()
+    dec = DacDecoder(init_decoder_params(cfg, seed=seed), cfg)
+    latent = torch.randn(1, cfg["hidden_size"], frames, device="cuda",
+                         generator=torch.Generator(device="cuda").manual_seed(seed + 1))
+    for _ in range(warmup):
+        audio = dec(latent)
+    torch.cuda.synchronize()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        audio = dec(latent)
+    e.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(e) * 1e3 / reps
+    hop = math.prod(cfg["upsampling_ratios"])
+    seconds = frames * hop / 44100.0
+    flops = dec.flops(frames)
+    if not torch.isfinite(audio).all():
+        raise RuntimeError("DAC decoder produced non-finite audio")
+    return {
+        "metric": "DAC decoder µs per audio-sec",
+        "value": round(us / seconds, 2),
+        "unit": "us per audio-second",
+        "us_per_pass": round(us, 1),
+        "audio_seconds": round(seconds, 3),
+        "realtime_factor": round(seconds / (us * 1e-6), 1),
+        "useful_tflops": round(flops / (us * 1e-6) / 1e12, 1),
+        "workload": "full 44.1 kHz DAC decoder (transformers DacDecoder layout): stem conv 1024->1536 k7, 4 blocks of "
+                    "Snake+ConvTranspose1d (strides 8,8,4,2) and 3 residual units (Snake+Conv1d k7 d=1,3,9, "
+                    "Snake+Conv1d k1 + residual), Snake+Conv1d 96->1 k7 + tanh; synthetic weights, fp32 in/out",
+        "launches_per_pass": 2 * (2 + 4 + 24),
+    }
