@@ -85,15 +85,22 @@ __device__ __forceinline__ void sc_prefetch_res(const ScParams& p, int b, int t0
 
 // One TMEM row chunk of the epilogue: 16 GEMM columns starting at o_base of
 // GEMM row t (output time, or polyphase row q), plus bias, residual and the
-// post-op, stored to y.  Plain stores are coalesced along time across the warp;
-// the 16 residual reads are all issued before the first store.
+// post-op, stored to y.  Plain stores are coalesced along time across the warp.
+// Every bias and residual read of the chunk is issued before its first store:
+// y may alias them as far as the compiler knows, so a read placed after a
+// store would wait out its whole latency once per element (measured: the
+// epilogue then bounds the kernel for Cout <= 192).
 __device__ __forceinline__ void sc_store16(const ScParams& p, int b, int t, int o_base, const float (&vv)[16]) {
   if (t >= p.Tout) return;
+  float bv[16];
   if (p.up_s == 0) {
     float* yb = p.y + static_cast<int64_t>(b) * p.Cy * p.Tout;
     float rv[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) rv[e] = 0.f;
+    for (int e = 0; e < 16; ++e) {
+      bv[e] = (p.bias && o_base + e < p.Cy) ? __ldg(p.bias + o_base + e) : 0.f;
+      rv[e] = 0.f;
+    }
     if (p.res) {
       const float* rb = p.res + static_cast<int64_t>(b) * p.Cy * p.Tout;
 #pragma unroll
@@ -104,7 +111,7 @@ __device__ __forceinline__ void sc_store16(const ScParams& p, int b, int t, int 
     for (int e = 0; e < 16; ++e) {
       const int o = o_base + e;
       if (o < p.Cy) {
-        float v = vv[e] + (p.bias ? __ldg(p.bias + o) : 0.f) + rv[e];
+        float v = vv[e] + bv[e] + rv[e];
         if (p.post == SN_POST_TANH) v = tanhf(v);
         yb[static_cast<int64_t>(o) * p.Tout + t] = v;
       }
@@ -112,13 +119,16 @@ __device__ __forceinline__ void sc_store16(const ScParams& p, int b, int t, int 
   } else {
     float* yb = p.y + static_cast<int64_t>(b) * p.Cy * p.Ty;
 #pragma unroll
+    for (int e = 0; e < 16; ++e)
+      bv[e] = (p.bias && o_base + e < p.Cout) ? __ldg(p.bias + (o_base + e) / p.up_s) : 0.f;
+#pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int oc = o_base + e;
       if (oc < p.Cout) {
         const int o = oc / p.up_s, r = oc - o * p.up_s;
         const int ty = p.up_s * t + r - p.up_p;
         if (ty >= 0 && ty < p.Ty) {
-          float v = vv[e] + (p.bias ? __ldg(p.bias + o) : 0.f);
+          float v = vv[e] + bv[e];
           if (p.post == SN_POST_TANH) v = tanhf(v);
           yb[static_cast<int64_t>(o) * p.Ty + ty] = v;
         }
