@@ -67,6 +67,7 @@ struct ScParams {
   // o' = o * up_s + r, row q holds y[b, o, up_s * q + r - up_p]; y is
   // [B, Cy, Ty].  up_s == 0: plain convolution, column o, row t of y[b, o, t].
   int up_s, up_p, Cy, Ty;
+  int up_vec;          // widest vector store (1, 2 or 4 floats) the phase runs of y allow
 };
 
 // Pull a tile's residual (GEMM rows t0 .. t0 + 127, columns o0 .. o0 + nt - 1)
@@ -83,44 +84,106 @@ __device__ __forceinline__ void sc_prefetch_res(const ScParams& p, int b, int t0
   }
 }
 
-// One TMEM row chunk of the epilogue: 16 GEMM columns starting at o_base of
-// GEMM row t (output time, or polyphase row q), plus bias, residual and the
-// post-op, stored to y.  Plain stores are coalesced along time across the warp.
-// Every bias and residual read of the chunk is issued before its first store:
-// y may alias them as far as the compiler knows, so a read placed after a
-// store would wait out its whole latency once per element (measured: the
-// epilogue then bounds the kernel for Cout <= 192).
-__device__ __forceinline__ void sc_store16(const ScParams& p, int b, int t, int o_base, const float (&vv)[16]) {
+// The epilogue works on 16 GEMM columns of GEMM row t (output time, or
+// polyphase row q) at a time: sc_load_bias16 / sc_load_res16 read the chunk's
+// bias and residual values, sc_emit16 adds them to the accumulator values,
+// applies the post-op and stores to y (plain stores are coalesced along time
+// across the warp).  Every read of a chunk is issued before the chunk's first
+// store: y may alias the bias and residual as far as the compiler knows, so a
+// read placed after a store would wait out its whole latency once per element
+// (measured: the epilogue then bounds the kernel for Cout <= 192).
+struct ScChunk {
+  float bv[16], rv[16];
+};
+
+template <bool UP>
+__device__ __forceinline__ void sc_load_bias16(const ScParams& p, int o_base, float (&bv)[16]) {
+  if constexpr (!UP) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) bv[e] = (p.bias && o_base + e < p.Cy) ? __ldg(p.bias + o_base + e) : 0.f;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      bv[e] = (p.bias && o_base + e < p.Cout) ? __ldg(p.bias + (o_base + e) / p.up_s) : 0.f;
+  }
+}
+
+__device__ __forceinline__ void sc_load_res16(const ScParams& p, int b, int t, int o_base, float (&rv)[16]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) rv[e] = 0.f;
+  if (p.res && p.up_s == 0 && t < p.Tout) {
+    const float* rb = p.res + static_cast<int64_t>(b) * p.Cy * p.Tout;
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (o_base + e < p.Cy) rv[e] = __ldg(rb + static_cast<int64_t>(o_base + e) * p.Tout + t);
+  }
+}
+
+// Polyphase store for a stride S dividing 16: the chunk covers 16 / S whole
+// output channels, whose S phases of row t are S consecutive output times
+// starting at S * t - padding, written as up_vec-float vectors away from the
+// edges.
+template <int S>
+__device__ __forceinline__ void sc_emit16_phases(const ScParams& p, float* yb, int t, int o_base,
+                                                 const float (&vv)[16], const ScChunk& c) {
+  constexpr int G = 16 / S;
+  const int o_first = o_base / S;
+  const int ty0 = S * t - p.up_p;
+  const bool inside = ty0 >= 0 && ty0 + S <= p.Ty;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int o = o_first + g;
+    if (o >= p.Cy) break;
+    float w[S];
+#pragma unroll
+    for (int r = 0; r < S; ++r) {
+      w[r] = vv[g * S + r] + c.bv[g * S + r];
+      if (p.post == SN_POST_TANH) w[r] = tanhf(w[r]);
+    }
+    float* dst = yb + static_cast<int64_t>(o) * p.Ty + ty0;
+    if constexpr (S % 4 == 0) {
+      if (inside && p.up_vec == 4) {
+#pragma unroll
+        for (int r = 0; r < S; r += 4) *reinterpret_cast<float4*>(dst + r) = make_float4(w[r], w[r + 1], w[r + 2], w[r + 3]);
+        continue;
+      }
+    }
+    if constexpr (S % 2 == 0) {
+      if (inside && p.up_vec >= 2) {
+#pragma unroll
+        for (int r = 0; r < S; r += 2) *reinterpret_cast<float2*>(dst + r) = make_float2(w[r], w[r + 1]);
+        continue;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < S; ++r)
+      if (ty0 + r >= 0 && ty0 + r < p.Ty) dst[r] = w[r];
+  }
+}
+
+template <bool UP>
+__device__ __forceinline__ void sc_emit16(const ScParams& p, int b, int t, int o_base, const float (&vv)[16],
+                                          const ScChunk& c) {
   if (t >= p.Tout) return;
-  float bv[16];
-  if (p.up_s == 0) {
+  if constexpr (!UP) {
     float* yb = p.y + static_cast<int64_t>(b) * p.Cy * p.Tout;
-    float rv[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      bv[e] = (p.bias && o_base + e < p.Cy) ? __ldg(p.bias + o_base + e) : 0.f;
-      rv[e] = 0.f;
-    }
-    if (p.res) {
-      const float* rb = p.res + static_cast<int64_t>(b) * p.Cy * p.Tout;
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-        if (o_base + e < p.Cy) rv[e] = __ldg(rb + static_cast<int64_t>(o_base + e) * p.Tout + t);
-    }
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int o = o_base + e;
       if (o < p.Cy) {
-        float v = vv[e] + bv[e] + rv[e];
+        float v = vv[e] + c.bv[e] + c.rv[e];
         if (p.post == SN_POST_TANH) v = tanhf(v);
         yb[static_cast<int64_t>(o) * p.Tout + t] = v;
       }
     }
   } else {
     float* yb = p.y + static_cast<int64_t>(b) * p.Cy * p.Ty;
-#pragma unroll
-    for (int e = 0; e < 16; ++e)
-      bv[e] = (p.bias && o_base + e < p.Cout) ? __ldg(p.bias + (o_base + e) / p.up_s) : 0.f;
+    switch (p.up_s) {  // the DAC strides; o_base is a multiple of 16
+      case 2: sc_emit16_phases<2>(p, yb, t, o_base, vv, c); return;
+      case 4: sc_emit16_phases<4>(p, yb, t, o_base, vv, c); return;
+      case 8: sc_emit16_phases<8>(p, yb, t, o_base, vv, c); return;
+      default: break;
+    }
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int oc = o_base + e;
@@ -128,12 +191,37 @@ __device__ __forceinline__ void sc_store16(const ScParams& p, int b, int t, int 
         const int o = oc / p.up_s, r = oc - o * p.up_s;
         const int ty = p.up_s * t + r - p.up_p;
         if (ty >= 0 && ty < p.Ty) {
-          float v = vv[e] + bv[e];
+          float v = vv[e] + c.bv[e];
           if (p.post == SN_POST_TANH) v = tanhf(v);
           yb[static_cast<int64_t>(o) * p.Ty + ty] = v;
         }
       }
     }
+  }
+}
+
+// One tile's epilogue: TMEM accumulator columns [0, nt) of this thread's row.
+// With a residual (HBM reads) chunk c + 1's residual is read before chunk c is
+// stored; bias reads (L1 hits) go just before their own chunk's stores.
+template <bool UP>
+__device__ __forceinline__ void sc_epilogue_tile(const ScParams& p, uint32_t base, int b, int t, int o0) {
+  ScChunk c;
+  float rnext[16];
+  const bool res = !UP && p.res;
+  if (res) sc_load_res16(p, b, t, o0, rnext);
+  for (int cc = 0; cc < p.nt; cc += 16) {
+    float vv[16];
+    tc::tmem_ld16(base + cc, vv);
+    if (res) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) c.rv[e] = rnext[e];
+      if (cc + 16 < p.nt) sc_load_res16(p, b, t, o0 + cc + 16, rnext);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) c.rv[e] = 0.f;
+    }
+    sc_load_bias16<UP>(p, o0 + cc, c.bv);
+    sc_emit16<UP>(p, b, t, o0 + cc, vv, c);
   }
 }
 
@@ -149,6 +237,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 //   warp 1      TMEM owner; lane 0 issues the MMAs into accumulator (j & 1)
 //   warps 2-9   snake producers (activation buffer g & 1 for chunk g)
 //   warps 10-13 epilogue: drain accumulator (j & 1) while tile j+1 computes
+// UP: the polyphase (transposed-convolution) epilogue, compiled separately so
+// that the plain convolutions carry none of its code.
+template <bool UP>
 __global__ void __launch_bounds__(kScThreads, 1)
     snake_conv_mma_kernel(const __grid_constant__ CUtensorMap mapW, const ScParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -384,11 +475,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
       tile_coords(j, b, t0, o0);
       const int t = t0 + q4 * 32 + lane;
       const uint32_t base = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(tb) * p.tcols;
-      for (int cc = 0; cc < p.nt; cc += 16) {
-        float vv[16];
-        tc::tmem_ld16(base + cc, vv);
-        sc_store16(p, b, t, o0 + cc, vv);
-      }
+      sc_epilogue_tile<UP>(p, base, b, t, o0);
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(t_empty + tb);
@@ -414,6 +501,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
 // and a cluster barrier at exit keeps each CTA alive while its peer may
 // still read its shared memory.
 // ---------------------------------------------------------------------------
+template <bool UP>
 __global__ void __launch_bounds__(kScThreads, 1)
     snake_conv_pair_kernel(const __grid_constant__ CUtensorMap mapW, const ScParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -628,11 +716,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
       tile_coords(j, b, t0, o0);
       const int t = t0 + q4 * 32 + lane;
       const uint32_t base = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(tb) * p.tcols;
-      for (int cc = 0; cc < p.nt; cc += 16) {
-        float vv[16];
-        tc::tmem_ld16(base + cc, vv);
-        sc_store16(p, b, t, o0 + cc, vv);
-      }
+      sc_epilogue_tile<UP>(p, base, b, t, o0);
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive_remote(t_empty0 + 8u * tb);
@@ -839,6 +923,8 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
     return SN_ERR_UNSUPPORTED;
   int rc = pack();
   if (rc != SN_OK) return rc;
+  auto mma_kern = p.up_s > 0 ? snake_conv_mma_kernel<true> : snake_conv_mma_kernel<false>;
+  auto pair_kern = p.up_s > 0 ? snake_conv_pair_kernel<true> : snake_conv_pair_kernel<false>;
   CUtensorMap mapW;
   const uint64_t dims[3] = {static_cast<uint64_t>(p.Cin), static_cast<uint64_t>(p.Cout),
                             static_cast<uint64_t>(2 * p.K)};
@@ -860,7 +946,7 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
     const uint32_t box2[3] = {64, static_cast<uint32_t>(q.nt / 2), 1};
     if (nt2 < (int64_t(1) << 31) && 2 * q.tcols <= 512 && smem2 <= 227 * 1024 &&
         tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box2) &&
-        cudaFuncSetAttribute(snake_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(pair_kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem2)) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * std::min(q.ntiles2, npairs));
@@ -874,16 +960,16 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, snake_conv_pair_kernel, mapW, q) == cudaSuccess) return SN_OK;
+      if (cudaLaunchKernelEx(&cfg, pair_kern, mapW, q) == cudaSuccess) return SN_OK;
     }
     cudaGetLastError();
   }
   const uint32_t box[3] = {64, static_cast<uint32_t>(p.nt), 1};
   if (tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box)) {
-    if (cudaFuncSetAttribute(snake_conv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(mma_kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) == cudaSuccess) {
       const int grid = std::min(p.ntiles, sms);
-      return launch(snake_conv_mma_kernel, dim3(grid), dim3(kScThreads), smem, st, false, mapW, p);
+      return launch(mma_kern, dim3(grid), dim3(kScThreads), smem, st, false, mapW, p);
     }
     cudaGetLastError();
   }
@@ -903,6 +989,7 @@ ScParams base_params(const float* x, const float* alpha, const float* bias, floa
   p.act = SN_ACT_SNAKE;
   p.post = SN_POST_NONE;
   p.up_s = p.up_p = 0;
+  p.up_vec = 1;
   return p;
 }
 
@@ -987,6 +1074,12 @@ int sn_snake_conv_transpose1d(const float* x, const float* alpha, const float* W
     p.up_p = padding;
     p.Cy = Cout;
     p.Ty = Ty;
+    // phase runs start at stride * q - padding: vector stores when that, Ty
+    // and y keep 16 (8) byte alignment
+    const uintptr_t ya = reinterpret_cast<uintptr_t>(y);
+    p.up_vec = (stride % 4 == 0 && padding % 4 == 0 && Ty % 4 == 0 && ya % 16 == 0)   ? 4
+               : (stride % 2 == 0 && padding % 2 == 0 && Ty % 2 == 0 && ya % 8 == 0) ? 2
+                                                                                       : 1;
     __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
     const int rc = sn::snake_fast(p, Wp, st, [&] {
       const int64_t tot = static_cast<int64_t>(Cin) * Cout * K;
