@@ -46,6 +46,10 @@ extern "C" {
  * before waiting for it.  Only valid when the previous kernel does not write
  * the weight (or scale) buffer -- e.g. frozen nn.Linear weights. */
 #define SN_FLAG_PDL 1u
+/* sn_snake_conv1d_ex / sn_snake_conv_transpose1d: the workspace already holds
+ * the weights packed by sn_snake_conv1d_pack / sn_snake_conv_transpose1d_pack
+ * (same W and shape), so the call does not pack them again. */
+#define SN_FLAG_PREPACKED 2u
 
 /* ---- weight kinds of sn_gemv_ex ---- */
 #define SN_WEIGHT_BF16 0
@@ -178,7 +182,8 @@ int sn_snake_conv1d(const float *x, const float *alpha, const float *W, const fl
  *   residual fp32 [B, Cout, Tout] added after the bias (the residual unit's
  *            "hidden_state + conv2(snake2(...))"), or NULL,
  *   post     SN_POST_NONE or SN_POST_TANH (the decoder's final tanh), applied last.
- * residual must not alias y.
+ * residual must not alias y.  flags: 0 or SN_FLAG_PREPACKED (workspace holds
+ * sn_snake_conv1d_pack(W) output; W is still read by the fallback path).
  */
 #define SN_ACT_SNAKE 0
 #define SN_ACT_NONE 1
@@ -186,8 +191,13 @@ int sn_snake_conv1d(const float *x, const float *alpha, const float *W, const fl
 #define SN_POST_TANH 1
 int sn_snake_conv1d_ex(const float *x, const float *alpha, const float *W, const float *bias,
                        const float *residual, float *y, int B, int Cin, int Cout, int T, int K, int stride,
-                       int padding, int dilation, float eps, int act, int post, void *workspace,
+                       int padding, int dilation, float eps, int act, int post, unsigned flags, void *workspace,
                        size_t workspace_bytes, void *stream);
+/* Pack W [Cout, Cin, K] once into the tensor-core layout (packed_bytes >=
+ * sn_snake_conv1d_workspace_size(Cin, Cout, K), 16-byte aligned), for calls
+ * with SN_FLAG_PREPACKED: a decoder packs its weights at load time. */
+int sn_snake_conv1d_pack(const float *W, int Cin, int Cout, int K, void *packed, size_t packed_bytes,
+                         void *stream);
 
 /*
  * Fused Snake + ConvTranspose1d (the DacDecoderBlock's snake1 -> conv_t1):
@@ -204,7 +214,11 @@ int sn_snake_conv1d_ex(const float *x, const float *alpha, const float *W, const
 int64_t sn_snake_conv_transpose1d_output_length(int64_t T, int K, int stride, int padding);
 int sn_snake_conv_transpose1d(const float *x, const float *alpha, const float *W, const float *bias, float *y,
                               int B, int Cin, int Cout, int T, int K, int stride, int padding, float eps,
-                              void *workspace, size_t workspace_bytes, void *stream);
+                              unsigned flags, void *workspace, size_t workspace_bytes, void *stream);
+/* Pack W [Cin, Cout, K] into the polyphase planes for SN_FLAG_PREPACKED calls;
+ * SN_ERR_UNSUPPORTED when K is not a multiple of stride (no polyphase GEMM). */
+int sn_snake_conv_transpose1d_pack(const float *W, int Cin, int Cout, int K, int stride, void *packed,
+                                   size_t packed_bytes, void *stream);
 
 /*
  * Allocation-free Snake + Conv1d.  No counterpart in the reference.

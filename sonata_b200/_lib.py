@@ -18,6 +18,7 @@ SN_OK = 0
 SN_DTYPE_BF16 = 0
 SN_DTYPE_F32 = 1
 SN_FLAG_PDL = 1
+SN_FLAG_PREPACKED = 2
 SN_WEIGHT_BF16 = 0
 SN_WEIGHT_INT8 = 1
 SN_WEIGHT_E4M3 = 2
@@ -50,10 +51,12 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_snake_conv1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P, ctypes.c_size_t,
                          _P], _I),
     "sn_snake_conv1d_noalloc": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P], _I),
-    "sn_snake_conv1d_ex": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _P,
-                            ctypes.c_size_t, _P], _I),
+    "sn_snake_conv1d_ex": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _U,
+                            _P, ctypes.c_size_t, _P], _I),
+    "sn_snake_conv1d_pack": ([_P, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
+    "sn_snake_conv_transpose1d_pack": ([_P, _I, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
     "sn_snake_conv_transpose1d_output_length": ([_I64, _I, _I, _I], _I64),
-    "sn_snake_conv_transpose1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _P,
+    "sn_snake_conv_transpose1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _U, _P,
                                    ctypes.c_size_t, _P], _I),
 }
 

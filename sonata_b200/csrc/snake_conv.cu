@@ -732,42 +732,47 @@ __global__ void __launch_bounds__(kScThreads, 1)
 // o < Cg (the GEMM width, Cout rounded up to 16; rows past Cout are zero).
 __global__ void pack_weights_kernel(const float* __restrict__ W, __nv_bfloat16* __restrict__ Wp, int Cout,
                                     int Cin, int K, int Cg) {
-  const int64_t total = static_cast<int64_t>(Cg) * Cin * K;
+  // one thread per (o, i), i fastest: the K taps are one contiguous read, and
+  // each tap's plane write is coalesced across the warp
+  const int64_t total = static_cast<int64_t>(Cg) * Cin;
+  const int64_t plane = static_cast<int64_t>(Cg) * Cin;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int k = static_cast<int>(e % K);
-    const int64_t oi = e / K;
-    const int i = static_cast<int>(oi % Cin);
-    const int o = static_cast<int>(oi / Cin);
-    const float w = o < Cout ? W[e] : 0.f;
-    const __nv_bfloat16 h = __float2bfloat16_rn(w);
-    const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
-    const int64_t plane = static_cast<int64_t>(Cg) * Cin;
-    Wp[(static_cast<int64_t>(k) * 2 + 0) * plane + static_cast<int64_t>(o) * Cin + i] = h;
-    Wp[(static_cast<int64_t>(k) * 2 + 1) * plane + static_cast<int64_t>(o) * Cin + i] = l;
+    const int i = static_cast<int>(e % Cin);
+    const int o = static_cast<int>(e / Cin);
+    for (int k = 0; k < K; ++k) {
+      const float w = o < Cout ? W[(static_cast<int64_t>(o) * Cin + i) * K + k] : 0.f;
+      const __nv_bfloat16 h = __float2bfloat16_rn(w);
+      const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
+      Wp[(static_cast<int64_t>(k) * 2 + 0) * plane + e] = h;
+      Wp[(static_cast<int64_t>(k) * 2 + 1) * plane + e] = l;
+    }
   }
 }
 
 // ConvTranspose1d weight W fp32 [Cin, Cout, K] (K = m * s) -> the polyphase
 // GEMM's bf16 planes Wp[(k'*2 + h)][o * s + r][i]: GEMM tap k' (reading input
-// q - (m - 1) + k') of phase r uses W[i, o, r + (m - 1 - k') * s].
+// q - (m - 1) + k') of phase r uses W[i, o, r + (m - 1 - k') * s].  One thread
+// per (o, i), i fastest: coalesced plane writes, K contiguous reads a thread.
 __global__ void pack_weights_t_kernel(const float* __restrict__ W, __nv_bfloat16* __restrict__ Wp, int Cin,
                                       int Cout, int K, int s) {
   const int m = K / s;
-  const int64_t total = static_cast<int64_t>(Cin) * Cout * K;
+  const int64_t total = static_cast<int64_t>(Cout) * Cin;
   const int64_t plane = static_cast<int64_t>(Cout) * s * Cin;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int k = static_cast<int>(e % K);
-    const int o = static_cast<int>((e / K) % Cout);
-    const int i = static_cast<int>(e / (static_cast<int64_t>(K) * Cout));
-    const int r = k % s, kt = m - 1 - k / s;
-    const float w = W[e];
-    const __nv_bfloat16 h = __float2bfloat16_rn(w);
-    const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
-    const int64_t col = (static_cast<int64_t>(o) * s + r) * Cin + i;
-    Wp[(static_cast<int64_t>(kt) * 2 + 0) * plane + col] = h;
-    Wp[(static_cast<int64_t>(kt) * 2 + 1) * plane + col] = l;
+    const int i = static_cast<int>(e % Cin);
+    const int o = static_cast<int>(e / Cin);
+    const float* wr = W + (static_cast<int64_t>(i) * Cout + o) * K;
+    for (int k = 0; k < K; ++k) {
+      const int r = k % s, kt = m - 1 - k / s;
+      const float w = wr[k];
+      const __nv_bfloat16 h = __float2bfloat16_rn(w);
+      const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
+      const int64_t col = (static_cast<int64_t>(o) * s + r) * Cin + i;
+      Wp[(static_cast<int64_t>(kt) * 2 + 0) * plane + col] = h;
+      Wp[(static_cast<int64_t>(kt) * 2 + 1) * plane + col] = l;
+    }
   }
 }
 
@@ -894,7 +899,7 @@ int sn_snake_conv1d(const float* x, const float* alpha, const float* W, const fl
                     int Cout, int T, int K, int stride, int padding, int dilation, float eps, void* workspace,
                     size_t workspace_bytes, void* stream) {
   return sn_snake_conv1d_ex(x, alpha, W, bias, nullptr, y, B, Cin, Cout, T, K, stride, padding, dilation, eps,
-                            SN_ACT_SNAKE, SN_POST_NONE, workspace, workspace_bytes, stream);
+                            SN_ACT_SNAKE, SN_POST_NONE, 0u, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"
@@ -1002,12 +1007,39 @@ int blocks_for(int64_t total, int per_sm) {
 
 extern "C" {
 
+int sn_snake_conv1d_pack(const float* W, int Cin, int Cout, int K, void* packed, size_t packed_bytes,
+                         void* stream) {
+  if (!W || !packed || Cin < 1 || Cout < 1 || K < 1) return SN_ERR_INVALID_ARGUMENT;
+  if (packed_bytes < sn_snake_conv1d_workspace_size(Cin, Cout, K)) return SN_ERR_INVALID_ARGUMENT;
+  if (!sn::aligned16(packed)) return SN_ERR_MISALIGNED;
+  const int Cg = (Cout + 15) / 16 * 16;
+  const int64_t tot = static_cast<int64_t>(Cg) * Cin;
+  return sn::launch(sn::pack_weights_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, W, static_cast<__nv_bfloat16*>(packed), Cout, Cin, K,
+                    Cg);
+}
+
+int sn_snake_conv_transpose1d_pack(const float* W, int Cin, int Cout, int K, int stride, void* packed,
+                                   size_t packed_bytes, void* stream) {
+  if (!W || !packed || Cin < 1 || Cout < 1 || K < 1 || stride < 1) return SN_ERR_INVALID_ARGUMENT;
+  if (K % stride != 0) return SN_ERR_UNSUPPORTED;  // no polyphase GEMM: the fallback reads W itself
+  if (packed_bytes < sn_snake_conv1d_workspace_size(Cin, Cout, K)) return SN_ERR_INVALID_ARGUMENT;
+  if (!sn::aligned16(packed)) return SN_ERR_MISALIGNED;
+  const int64_t tot = static_cast<int64_t>(Cin) * Cout;
+  return sn::launch(sn::pack_weights_t_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, W, static_cast<__nv_bfloat16*>(packed), Cin, Cout, K,
+                    stride);
+}
+
 int sn_snake_conv1d_ex(const float* x, const float* alpha, const float* W, const float* bias, const float* residual,
                        float* y, int B, int Cin, int Cout, int T, int K, int stride, int padding, int dilation,
-                       float eps, int act, int post, void* workspace, size_t workspace_bytes, void* stream) {
+                       float eps, int act, int post, unsigned flags, void* workspace, size_t workspace_bytes,
+                       void* stream) {
   if (!x || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0 ||
       dilation < 1)
     return SN_ERR_INVALID_ARGUMENT;
+  if (flags & ~SN_FLAG_PREPACKED) return SN_ERR_INVALID_ARGUMENT;
+  const bool prepacked = (flags & SN_FLAG_PREPACKED) != 0;
   if ((act != SN_ACT_SNAKE && act != SN_ACT_NONE) || (post != SN_POST_NONE && post != SN_POST_TANH))
     return SN_ERR_INVALID_ARGUMENT;
   if (act == SN_ACT_SNAKE && !alpha) return SN_ERR_INVALID_ARGUMENT;
@@ -1032,7 +1064,8 @@ int sn_snake_conv1d_ex(const float* x, const float* alpha, const float* W, const
     p.Ty = Tout;
     __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
     const int rc = sn::snake_fast(p, Wp, st, [&] {
-      const int64_t tot = static_cast<int64_t>(Cg) * Cin * K;
+      if (prepacked) return static_cast<int>(SN_OK);
+      const int64_t tot = static_cast<int64_t>(Cg) * Cin;
       return sn::launch(sn::pack_weights_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0, st, false, W, Wp, Cout,
                         Cin, K, Cg);
     });
@@ -1049,10 +1082,12 @@ int64_t sn_snake_conv_transpose1d_output_length(int64_t T, int K, int stride, in
 }
 
 int sn_snake_conv_transpose1d(const float* x, const float* alpha, const float* W, const float* bias, float* y, int B,
-                              int Cin, int Cout, int T, int K, int stride, int padding, float eps, void* workspace,
-                              size_t workspace_bytes, void* stream) {
+                              int Cin, int Cout, int T, int K, int stride, int padding, float eps, unsigned flags,
+                              void* workspace, size_t workspace_bytes, void* stream) {
   if (!x || !alpha || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0)
     return SN_ERR_INVALID_ARGUMENT;
+  if (flags & ~SN_FLAG_PREPACKED) return SN_ERR_INVALID_ARGUMENT;
+  const bool prepacked = (flags & SN_FLAG_PREPACKED) != 0;
   const int64_t ty64 = sn_snake_conv_transpose1d_output_length(T, K, stride, padding);
   if (ty64 < 1 || ty64 > (int64_t(1) << 31) - 1) return SN_ERR_INVALID_ARGUMENT;
   const int Ty = static_cast<int>(ty64);
@@ -1082,7 +1117,8 @@ int sn_snake_conv_transpose1d(const float* x, const float* alpha, const float* W
                                                                                        : 1;
     __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
     const int rc = sn::snake_fast(p, Wp, st, [&] {
-      const int64_t tot = static_cast<int64_t>(Cin) * Cout * K;
+      if (prepacked) return static_cast<int>(SN_OK);
+      const int64_t tot = static_cast<int64_t>(Cin) * Cout;
       return sn::launch(sn::pack_weights_t_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0, st, false, W, Wp, Cin,
                         Cout, K, stride);
     });

@@ -17,7 +17,8 @@ docs/dac_architecture.md:37-133, 306-314.  Each edge is one kernel launch:
 
 Weights are a state dict with the transformers names (``conv1.weight``,
 ``block.0.conv_t1.weight``, ``block.0.res_unit1.snake1.alpha`` ...), the
-effective weights of a checkpoint (weight norm folded in).  No checkpoint is
+effective weights of a checkpoint (weight norm folded in), packed once into
+the tensor-core layout when the decoder is built.  No checkpoint is
 available offline; ``init_decoder_params`` draws seeded synthetic ones.
 """
 from __future__ import annotations
@@ -26,7 +27,8 @@ import math
 
 import torch
 
-from .fused_snake_conv import fused_snake_conv1d, fused_snake_conv_transpose1d
+from .fused_snake_conv import (fused_snake_conv1d, fused_snake_conv_transpose1d, pack_conv1d_weight,
+                               pack_conv_transpose1d_weight)
 
 DILATIONS = (1, 3, 9)
 
@@ -99,26 +101,38 @@ class DacDecoder:
         missing = set(decoder_shapes(config)) - set(self.p)
         if missing:
             raise ValueError(f"missing decoder parameters: {sorted(missing)[:4]} ...")
+        # every conv weight packed once into the tensor-core layout
+        self.packed = {}
+        for name, w in self.p.items():
+            if not name.endswith("weight"):
+                continue
+            if "conv_t1" in name:
+                s = self.config["upsampling_ratios"][int(name.split(".")[1])]
+                self.packed[name] = pack_conv_transpose1d_weight(w, s)
+            else:
+                self.packed[name] = pack_conv1d_weight(w)
 
     def _a(self, name: str) -> torch.Tensor:
         return self.p[name].view(-1)
 
     def __call__(self, latent: torch.Tensor, stream=None) -> torch.Tensor:
         p = self.p
+        k = self.packed
         h = fused_snake_conv1d(latent, None, p["conv1.weight"], p["conv1.bias"], padding=3, stream=stream,
-                               activation="none")
+                               activation="none", packed=k["conv1.weight"])
         for i, s in enumerate(self.config["upsampling_ratios"]):
             b = f"block.{i}"
             h = fused_snake_conv_transpose1d(h, self._a(f"{b}.snake1.alpha"), p[f"{b}.conv_t1.weight"],
-                                             p[f"{b}.conv_t1.bias"], stride=s, padding=(s + 1) // 2, stream=stream)
+                                             p[f"{b}.conv_t1.bias"], stride=s, padding=(s + 1) // 2, stream=stream,
+                                             packed=k[f"{b}.conv_t1.weight"])
             for j, d in enumerate(DILATIONS):
                 r = f"{b}.res_unit{j + 1}"
                 y = fused_snake_conv1d(h, self._a(f"{r}.snake1.alpha"), p[f"{r}.conv1.weight"], p[f"{r}.conv1.bias"],
-                                       padding=3 * d, dilation=d, stream=stream)
+                                       padding=3 * d, dilation=d, stream=stream, packed=k[f"{r}.conv1.weight"])
                 h = fused_snake_conv1d(y, self._a(f"{r}.snake2.alpha"), p[f"{r}.conv2.weight"], p[f"{r}.conv2.bias"],
-                                       stream=stream, residual=h)
+                                       stream=stream, residual=h, packed=k[f"{r}.conv2.weight"])
         return fused_snake_conv1d(h, self._a("snake1.alpha"), p["conv2.weight"], p["conv2.bias"], padding=3,
-                                  stream=stream, post="tanh")
+                                  stream=stream, post="tanh", packed=k["conv2.weight"])
 
     def flops(self, T0: int, batch: int = 1) -> int:
         """Multiply-add flops (2 per MAC) of one forward over T0 latent frames."""
@@ -177,5 +191,5 @@ def bench_dac_decoder(warmup: int = 2, reps: int = 3, frames: int = 862, seed: i
         "workload": "full 44.1 kHz DAC decoder (transformers DacDecoder layout): stem conv 1024->1536 k7, 4 blocks of "
                     "Snake+ConvTranspose1d (strides 8,8,4,2) and 3 residual units (Snake+Conv1d k7 d=1,3,9, "
                     "Snake+Conv1d k1 + residual), Snake+Conv1d 96->1 k7 + tanh; synthetic weights, fp32 in/out",
-        "launches_per_pass": 2 * (2 + 4 + 24),
+        "launches_per_pass": 2 + 4 + 24,
     }

@@ -51,13 +51,15 @@ _POSTS = {None: _lib.SN_POST_NONE, "tanh": _lib.SN_POST_TANH}
 def fused_snake_conv1d(x: torch.Tensor, alpha: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
                        stride: int = 1, padding: int = 0, dilation: int = 1, eps: float = 1e-9,
                        out: torch.Tensor | None = None, stream=None, *, residual: torch.Tensor | None = None,
-                       activation: str = "snake", post: str | None = None) -> torch.Tensor:
+                       activation: str = "snake", post: str | None = None,
+                       packed: torch.Tensor | None = None) -> torch.Tensor:
     """Validate inputs and run the fused Snake -> Conv1d kernel.
 
     Keyword-only additions for the rest of the DAC decoder: ``residual``
     (fp32, the output's shape) is added after the bias, ``activation="none"``
     skips the Snake (alpha may then be None), ``post="tanh"`` applies tanh
-    last."""
+    last, ``packed`` (from ``pack_conv1d_weight(weight)``) skips the per-call
+    weight pack."""
     batch_size, input_channels, input_length = x.shape
     output_channels, weight_channels, kernel_size = weight.shape
     if activation not in _ACTS:
@@ -98,8 +100,13 @@ def fused_snake_conv1d(x: torch.Tensor, alpha: torch.Tensor, weight: torch.Tenso
             raise ValueError("residual must not alias out")
     lib = _lib.lib()
     ws_bytes = lib.sn_snake_conv1d_workspace_size(input_channels, output_channels, kernel_size)
-    ws = _workspace(x.device, ws_bytes)
-    if res_c is None and snake and post is None:
+    flags = 0
+    if packed is not None:
+        _check_packed(packed, ws_bytes, x.device)
+        ws, flags = packed, _lib.SN_FLAG_PREPACKED
+    else:
+        ws = _workspace(x.device, ws_bytes)
+    if res_c is None and snake and post is None and not flags:
         _lib.check("sn_snake_conv1d", lib.sn_snake_conv1d(
             x.data_ptr(), alpha_c.data_ptr(), weight.data_ptr(), bias_c.data_ptr() if bias_c is not None else None,
             out.data_ptr(), batch_size, input_channels, output_channels, input_length, kernel_size, stride, padding,
@@ -109,9 +116,46 @@ def fused_snake_conv1d(x: torch.Tensor, alpha: torch.Tensor, weight: torch.Tenso
             x.data_ptr(), alpha_c.data_ptr() if alpha_c is not None else None, weight.data_ptr(),
             bias_c.data_ptr() if bias_c is not None else None, res_c.data_ptr() if res_c is not None else None,
             out.data_ptr(), batch_size, input_channels, output_channels, input_length, kernel_size, stride, padding,
-            dilation, float(eps), _ACTS[activation], _POSTS[post], ws.data_ptr(), ws.numel(),
+            dilation, float(eps), _ACTS[activation], _POSTS[post], flags, ws.data_ptr(), ws.numel(),
             stream_handle(stream)))
     return out
+
+
+def _check_packed(packed: torch.Tensor, nbytes: int, device) -> None:
+    if not isinstance(packed, torch.Tensor) or packed.dtype != torch.uint8 or packed.device != device:
+        raise ValueError("packed must be a uint8 tensor from pack_conv1d_weight / pack_conv_transpose1d_weight "
+                         "on the input's device")
+    if packed.numel() < nbytes or not packed.is_contiguous():
+        raise ValueError("packed is too small for this weight shape")
+
+
+def pack_conv1d_weight(weight: torch.Tensor, stream=None) -> torch.Tensor:
+    """Pack a Conv1d weight [Cout, Cin, K] once for ``fused_snake_conv1d(...,
+    packed=)`` (sn_snake_conv1d_pack): the bf16 hi/lo tensor-core planes."""
+    require_cuda("weight", weight, torch.float32, 3)
+    weight = weight.contiguous()
+    cout, cin, k = weight.shape
+    lib = _lib.lib()
+    buf = torch.empty(lib.sn_snake_conv1d_workspace_size(cin, cout, k), device=weight.device, dtype=torch.uint8)
+    _lib.check("sn_snake_conv1d_pack", lib.sn_snake_conv1d_pack(weight.data_ptr(), cin, cout, k, buf.data_ptr(),
+                                                                buf.numel(), stream_handle(stream)))
+    return buf
+
+
+def pack_conv_transpose1d_weight(weight: torch.Tensor, stride: int, stream=None) -> torch.Tensor | None:
+    """Pack a ConvTranspose1d weight [Cin, Cout, K] once into the polyphase
+    planes for ``fused_snake_conv_transpose1d(..., packed=)``; None when K is
+    not a multiple of stride (that shape has no polyphase GEMM to pack for)."""
+    require_cuda("weight", weight, torch.float32, 3)
+    weight = weight.contiguous()
+    cin, cout, k = weight.shape
+    if k % stride:
+        return None
+    lib = _lib.lib()
+    buf = torch.empty(lib.sn_snake_conv1d_workspace_size(cin, cout, k), device=weight.device, dtype=torch.uint8)
+    _lib.check("sn_snake_conv_transpose1d_pack", lib.sn_snake_conv_transpose1d_pack(
+        weight.data_ptr(), cin, cout, k, stride, buf.data_ptr(), buf.numel(), stream_handle(stream)))
+    return buf
 
 
 def conv_transpose1d_output_length(input_length: int, kernel_size: int, stride: int, padding: int) -> int:
@@ -121,10 +165,12 @@ def conv_transpose1d_output_length(input_length: int, kernel_size: int, stride: 
 
 def fused_snake_conv_transpose1d(x: torch.Tensor, alpha: torch.Tensor, weight: torch.Tensor,
                                  bias: torch.Tensor | None = None, stride: int = 1, padding: int = 0,
-                                 eps: float = 1e-9, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+                                 eps: float = 1e-9, out: torch.Tensor | None = None, stream=None, *,
+                                 packed: torch.Tensor | None = None) -> torch.Tensor:
     """Snake -> ConvTranspose1d (the DacDecoderBlock's snake1 -> conv_t1):
     ``conv_transpose1d(snake(x), weight, bias, stride, padding)`` with weight
-    in torch's [Cin, Cout, K] layout; runs ``sn_snake_conv_transpose1d``."""
+    in torch's [Cin, Cout, K] layout; runs ``sn_snake_conv_transpose1d``.
+    ``packed``: from ``pack_conv_transpose1d_weight(weight, stride)``."""
     batch_size, input_channels, input_length = x.shape
     weight_channels, output_channels, kernel_size = weight.shape
     if weight_channels != input_channels:
@@ -150,11 +196,17 @@ def fused_snake_conv_transpose1d(x: torch.Tensor, alpha: torch.Tensor, weight: t
     elif tuple(out.shape) != (batch_size, output_channels, output_length) or not out.is_contiguous():
         raise ValueError("out has the wrong shape or is not contiguous")
     lib = _lib.lib()
-    ws = _workspace(x.device, lib.sn_snake_conv1d_workspace_size(input_channels, output_channels, kernel_size))
+    ws_bytes = lib.sn_snake_conv1d_workspace_size(input_channels, output_channels, kernel_size)
+    flags = 0
+    if packed is not None:
+        _check_packed(packed, ws_bytes, x.device)
+        ws, flags = packed, _lib.SN_FLAG_PREPACKED
+    else:
+        ws = _workspace(x.device, ws_bytes)
     _lib.check("sn_snake_conv_transpose1d", lib.sn_snake_conv_transpose1d(
         x.data_ptr(), alpha.data_ptr(), weight.data_ptr(), bias_c.data_ptr() if bias_c is not None else None,
         out.data_ptr(), batch_size, input_channels, output_channels, input_length, kernel_size, stride, padding,
-        float(eps), ws.data_ptr(), ws.numel(), stream_handle(stream)))
+        float(eps), flags, ws.data_ptr(), ws.numel(), stream_handle(stream)))
     return out
 
 

@@ -49,6 +49,18 @@ def test_gemv_rejects_bad_arguments_on_host(L):
     assert L.sn_gemv_ex(0, p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None, 5, p, 8, 8, 8) == -1
     assert L.sn_gemv_ex(0, p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None, 0, p, 4, 8, 8) == -1
     assert L.sn_gemv_ex(0, p, 8, None, p, 8, p, 8, 1, 8, 8, 0, 0, None, 0, p, 8, 0, 8) == -1
+    # Snake conv variants: unknown flags / activation / post-op, null pack buffers
+    assert L.sn_snake_conv1d_ex(p, p, p, None, None, p, 1, 16, 16, 8, 1, 1, 0, 1, 1e-9, 0, 0, 4, p, 1 << 20,
+                                None) == -1
+    assert L.sn_snake_conv1d_ex(p, p, p, None, None, p, 1, 16, 16, 8, 1, 1, 0, 1, 1e-9, 7, 0, 0, p, 1 << 20,
+                                None) == -1
+    assert L.sn_snake_conv1d_ex(p, p, p, None, None, p, 1, 16, 16, 8, 1, 1, 0, 1, 1e-9, 0, 9, 0, p, 1 << 20,
+                                None) == -1
+    assert L.sn_snake_conv_transpose1d(p, p, p, None, p, 1, 16, 16, 8, 4, 2, 1, 1e-9, 8, p, 1 << 20, None) == -1
+    assert L.sn_snake_conv1d_pack(None, 16, 16, 7, p, 1 << 20, None) == -1
+    assert L.sn_snake_conv1d_pack(p, 16, 16, 7, p, 16, None) == -1
+    assert L.sn_snake_conv_transpose1d_pack(p, 16, 16, 5, 2, p, 1 << 20, None) == -3
+    assert L.sn_snake_conv_transpose1d_output_length(10, 16, 8, 4) == 80
     assert L.sn_quantize_rows_int8(None, 8, 8, 8, p, 8, p, None) == -1
     assert L.sn_quantize_rows_fp8e4m3(p, 4, 8, 8, p, 8, p, None) == -1
 

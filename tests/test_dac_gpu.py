@@ -145,3 +145,27 @@ def test_decoder_full_size_short_latent(cuda_lib):
     assert audio.shape == (1, 1, 1024)
     truth = O.dac_decoder_ref(latent.numpy(), {k: v.numpy() for k, v in params.items()}, cfg["upsampling_ratios"])
     _check(audio, truth)
+
+
+def test_prepacked_weights_give_identical_results(S):
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(1, 64, 300, generator=g).cuda()
+    a = (torch.rand(64, generator=g) + 0.5).cuda()
+    for cout, k, pad in [(64, 7, 9), (20, 1, 0)]:  # plain and padded GEMM width
+        w = (torch.randn(cout, 64, k, generator=g) / np.sqrt(64 * k)).cuda()
+        b = torch.randn(cout, generator=g).cuda()
+        packed = S.pack_conv1d_weight(w)
+        ref = S.fused_snake_conv1d(x, a, w, b, padding=pad, dilation=3 if k == 7 else 1)
+        got = S.fused_snake_conv1d(x, a, w, b, padding=pad, dilation=3 if k == 7 else 1, packed=packed)
+        torch.cuda.synchronize()
+        assert torch.equal(ref, got)
+    wt = (torch.randn(64, 24, 8, generator=g) / np.sqrt(128)).cuda()
+    bt = torch.randn(24, generator=g).cuda()
+    pt = S.pack_conv_transpose1d_weight(wt, 4)
+    ref = S.fused_snake_conv_transpose1d(x, a, wt, bt, stride=4, padding=2)
+    got = S.fused_snake_conv_transpose1d(x, a, wt, bt, stride=4, padding=2, packed=pt)
+    torch.cuda.synchronize()
+    assert torch.equal(ref, got)
+    assert S.pack_conv_transpose1d_weight(torch.randn(16, 16, 5, device="cuda"), 2) is None
+    with pytest.raises(ValueError):
+        S.fused_snake_conv1d(x, a, w, b, packed=packed[:10])
