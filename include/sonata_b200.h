@@ -187,6 +187,7 @@ int sn_snake_conv1d(const float *x, const float *alpha, const float *W, const fl
  */
 #define SN_ACT_SNAKE 0
 #define SN_ACT_NONE 1
+#define SN_ACT_SILU 2 /* sn_causal_conv1d_update only */
 #define SN_POST_NONE 0
 #define SN_POST_TANH 1
 int sn_snake_conv1d_ex(const float *x, const float *alpha, const float *W, const float *bias,
@@ -243,6 +244,51 @@ int sn_snake_conv_transpose1d_pack(const float *W, int Cin, int Cout, int K, int
 int sn_snake_conv1d_noalloc(const float *x, const float *alpha, const float *W, const float *bias, float *y,
                             int B, int Cin, int Cout, int T, int K, int stride, int padding, int dilation,
                             float eps, void *stream);
+
+/*
+ * Mamba2 decode-step ops (bf16 tensors, fp32 arithmetic, bf16 outputs), the
+ * semantics of the libraries the reference's frozen goldens were made with
+ * (scripts/validation_harness.py:39,58-115,140-171: causal_conv1d
+ * 1.6.2.post1, mamba_ssm 2.3.2.post1).  All tensors contiguous.
+ *
+ * sn_causal_conv1d_update (causal_conv1d_update): conv_state [B, D, W]
+ * (W <= 8) shifts one step left and takes x [B, D] as its newest column, in
+ * place; y [B, D] = act(sum_w state[b, d, w] * weight[d, w] + bias[d]),
+ * activation SN_ACT_NONE or SN_ACT_SILU; bias may be NULL.
+ */
+int sn_causal_conv1d_update(const void *x, void *conv_state, const void *weight, const void *bias, void *y, int B,
+                            int D, int W, int activation, void *stream);
+/*
+ * sn_selective_state_update (mamba_ssm selective_state_update): state
+ * [batch, nheads, headdim, dstate] (dstate <= 256) updated in place;
+ * dt' = dt + dt_bias, softplus(dt') when dt_softplus (threshold 20);
+ * state = state * exp(dt' * A) + dt' * B * x;
+ * y = sum_dstate(state * C) + D * x, times SiLU(z).  x, dt, z, y [batch,
+ * nheads, headdim]; A fp32 [nheads, headdim, dstate]; B, C [batch, ngroups,
+ * dstate] (nheads / ngroups heads per group); D, dt_bias [nheads, headdim];
+ * D, z, dt_bias may be NULL.
+ */
+int sn_selective_state_update(void *state, const void *x, const void *dt, const float *A, const void *B,
+                              const void *C, const void *D, const void *z, const void *dt_bias, void *y, int batch,
+                              int nheads, int headdim, int dstate, int ngroups, int dt_softplus, void *stream);
+/*
+ * sn_rmsnorm_gated (mamba_ssm layernorm_gated rmsnorm_fn): rows x [rows, N]
+ * normalised per group of group_size columns (N % group_size == 0,
+ * group_size <= 8192): norm_before_gate 0: y = rms(x * SiLU(z)) * weight
+ * (+ bias); 1: y = rms(x) * weight (+ bias) * SiLU(z).  z, bias may be NULL.
+ */
+int sn_rmsnorm_gated(const void *x, const void *weight, const void *bias, const void *z, void *y, int rows, int N,
+                     int group_size, float eps, int norm_before_gate, void *stream);
+/*
+ * sn_layer_norm_fused (mamba_ssm layer_norm_fn, prenorm add + norm): h = x +
+ * residual (residual bf16, or fp32 when residual_f32; may be NULL) in fp32;
+ * residual_out (may be NULL; bf16, or fp32 when residual_out_f32) = h; out =
+ * LayerNorm(h) (RMSNorm when is_rms_norm) * weight (+ bias), from the
+ * unrounded h.  x, out [rows, N], N <= 8192.
+ */
+int sn_layer_norm_fused(const void *x, const void *residual, int residual_f32, const void *weight,
+                        const void *bias, void *out, void *residual_out, int residual_out_f32, int rows, int N,
+                        float eps, int is_rms_norm, void *stream);
 
 #ifdef __cplusplus
 }

@@ -334,6 +334,98 @@ def dac_decoder_ref(latent: np.ndarray, p: dict, upsampling_ratios, eps: float =
     return np.tanh(h)
 
 
+# --------------------------------------------------------------------------
+# Mamba2 decode-step ops (the reference's frozen goldens,
+# tests/goldens/kernels/*.pt, made by scripts/validation_harness.py:58-115,
+# 140-171 against causal_conv1d 1.6.2.post1 and mamba_ssm 2.3.2.post1,
+# validation_harness.py:39).  float64 restatements of those libraries'
+# published algorithms; bf16 inputs are given as float arrays.
+# --------------------------------------------------------------------------
+
+def _silu(v):
+    return v / (1.0 + np.exp(-v))
+
+
+def causal_conv1d_update_ref(x, conv_state, weight, bias, activation="silu"):
+    """causal_conv1d_update (validation_harness.py:58-66,140-143): the state
+    [B, D, W] shifts left by one step and takes x [B, D] as its newest column;
+    y = sum_w state[:, :, w] * weight[:, w] + bias, then SiLU.  Returns
+    (y, new_state)."""
+    st = np.concatenate([np.asarray(conv_state, np.float64)[:, :, 1:],
+                         np.asarray(x, np.float64)[:, :, None]], axis=2)
+    y = np.einsum("bdw,dw->bd", st, np.asarray(weight, np.float64))
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)[None, :]
+    if activation in ("silu", "swish"):
+        y = _silu(y)
+    return y, st
+
+
+def rmsnorm_gated_ref(x, weight, bias, z, eps, group_size, norm_before_gate=False):
+    """mamba_ssm rmsnorm_fn (validation_harness.py:91-101,153-156): with
+    norm_before_gate False, x * SiLU(z) is RMS-normalised over groups of
+    group_size, times weight (+ bias); with it True the gate follows the norm."""
+    x = np.asarray(x, np.float64)
+    zz = np.asarray(z, np.float64) if z is not None else None
+    if zz is not None and not norm_before_gate:
+        x = x * _silu(zz)
+    shp = x.shape
+    g = x.reshape(shp[:-1] + (shp[-1] // group_size, group_size))
+    r = 1.0 / np.sqrt((g * g).mean(axis=-1, keepdims=True) + eps)
+    y = (g * r).reshape(shp) * np.asarray(weight, np.float64)
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    if zz is not None and norm_before_gate:
+        y = y * _silu(zz)
+    return y
+
+
+def layer_norm_fn_ref(x, weight, bias, residual=None, eps=1e-5, is_rms_norm=False):
+    """mamba_ssm layer_norm_fn (validation_harness.py:104-114,159-171): the
+    residual add happens first (its output is what prenorm returns), the norm
+    runs on the unrounded sum.  Returns (out, residual_out)."""
+    h = np.asarray(x, np.float64)
+    if residual is not None:
+        h = h + np.asarray(residual, np.float64)
+    if is_rms_norm:
+        y = h / np.sqrt((h * h).mean(axis=-1, keepdims=True) + eps)
+    else:
+        mu = h.mean(axis=-1, keepdims=True)
+        y = (h - mu) / np.sqrt(((h - mu) ** 2).mean(axis=-1, keepdims=True) + eps)
+    y = y * np.asarray(weight, np.float64)
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    return y, h
+
+
+def selective_state_update_ref(state, x, dt, A, B, C, D=None, z=None, dt_bias=None, dt_softplus=False):
+    """mamba_ssm selective_state_update (validation_harness.py:69-88,146-150):
+    dt (+ dt_bias, softplus) per (head, dim); state = state * exp(dt * A) +
+    dt * B * x; y = sum over d_state of state * C (+ D * x) (* SiLU(z)).  B, C
+    [batch, ngroups, dstate] shared by nheads / ngroups heads.  Returns
+    (y, new_state)."""
+    st = np.asarray(state, np.float64)
+    xx = np.asarray(x, np.float64)
+    d = np.asarray(dt, np.float64)
+    if dt_bias is not None:
+        d = d + np.asarray(dt_bias, np.float64)
+    if dt_softplus:
+        d = np.where(d <= 20.0, np.log1p(np.exp(np.minimum(d, 20.0))), d)
+    nh = st.shape[1]
+    ng = np.asarray(B).shape[1]
+    hg = nh // ng
+    Bh = np.repeat(np.asarray(B, np.float64), hg, axis=1)  # [batch, nh, ds]
+    Ch = np.repeat(np.asarray(C, np.float64), hg, axis=1)
+    dA = np.exp(d[..., None] * np.asarray(A, np.float64)[None])
+    st = st * dA + (d * xx)[..., None] * Bh[:, :, None, :]
+    y = (st * Ch[:, :, None, :]).sum(axis=-1)
+    if D is not None:
+        y = y + xx * np.asarray(D, np.float64)
+    if z is not None:
+        y = y * _silu(np.asarray(z, np.float64))
+    return y, st
+
+
 def cosine(a: np.ndarray, b: np.ndarray) -> float:
     a = np.asarray(a, np.float64).ravel()
     b = np.asarray(b, np.float64).ravel()

@@ -24,6 +24,7 @@ SN_WEIGHT_INT8 = 1
 SN_WEIGHT_E4M3 = 2
 SN_ACT_SNAKE = 0
 SN_ACT_NONE = 1
+SN_ACT_SILU = 2
 SN_POST_NONE = 0
 SN_POST_TANH = 1
 
@@ -54,6 +55,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_snake_conv1d_ex": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _U,
                             _P, ctypes.c_size_t, _P], _I),
     "sn_snake_conv1d_pack": ([_P, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
+    "sn_causal_conv1d_update": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
+    "sn_selective_state_update": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
+    "sn_rmsnorm_gated": ([_P, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _I, _P], _I),
+    "sn_layer_norm_fused": ([_P, _P, _I, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _I, _P], _I),
     "sn_snake_conv_transpose1d_pack": ([_P, _I, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
     "sn_snake_conv_transpose1d_output_length": ([_I64, _I, _I, _I], _I64),
     "sn_snake_conv_transpose1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _U, _P,

@@ -1,0 +1,389 @@
+// Mamba2 decode-step element ops around the decode GEMVs (bf16, B200).
+//
+// The four ops Mamba2.step() runs between its projections, with the
+// semantics of the libraries the reference pins them to
+// (scripts/validation_harness.py:39, :58-115, :140-171): causal_conv1d
+// 1.6.2.post1 `causal_conv1d_update` and mamba_ssm 2.3.2.post1
+// `selective_state_update`, `rmsnorm_fn` (layernorm_gated) and
+// `layer_norm_fn`.  All arithmetic in fp32, outputs rounded once to bf16, as
+// those kernels do.  Decode shapes are tiny (a few K elements per row, batch
+// 1-2), so each op is one launch sized to the rows it has and bounded by
+// launch latency and one HBM round trip, not bandwidth.
+#include "common.cuh"
+
+#include <climits>
+
+namespace sn {
+namespace {
+
+__device__ __forceinline__ float bf(const __nv_bfloat16* p, int64_t i) { return __bfloat162float(p[i]); }
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+
+// ---------------------------------------------------------------------------
+// causal_conv1d_update: state [B, D, W] shifts one step left and takes x
+// [B, D] as its newest column; y = SiLU?(sum_w state[w] * weight[d, w] + bias).
+// One thread per (b, d).
+// ---------------------------------------------------------------------------
+constexpr int kMaxConvWidth = 8;
+
+__global__ void __launch_bounds__(256) causal_conv1d_update_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                   __nv_bfloat16* __restrict__ state,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   const __nv_bfloat16* __restrict__ bias,
+                                                                   __nv_bfloat16* __restrict__ y, int B, int D,
+                                                                   int W, int act) {
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e >= static_cast<int64_t>(B) * D) return;
+  const int d = static_cast<int>(e % D);
+  __nv_bfloat16* st = state + e * W;
+  float s[kMaxConvWidth];
+#pragma unroll
+  for (int k = 0; k < kMaxConvWidth; ++k) s[k] = (k + 1 < W) ? __bfloat162float(st[k + 1]) : 0.f;
+  const __nv_bfloat16 xv = x[e];
+  float acc = bias ? bf(bias, d) : 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxConvWidth; ++k) {
+    if (k + 1 < W) acc = fmaf(s[k], bf(w, static_cast<int64_t>(d) * W + k), acc);
+  }
+  acc = fmaf(__bfloat162float(xv), bf(w, static_cast<int64_t>(d) * W + W - 1), acc);
+#pragma unroll
+  for (int k = 0; k < kMaxConvWidth; ++k)
+    if (k + 1 < W) st[k] = __float2bfloat16_rn(s[k]);  // exact: bf16 values moved one slot
+  st[W - 1] = xv;
+  y[e] = __float2bfloat16_rn(act ? silu(acc) : acc);
+}
+
+// ---------------------------------------------------------------------------
+// selective_state_update: one warp per (batch, head, headdim row); lane l
+// holds d_state elements l, l + 32, ...  dt (+ dt_bias, softplus) is shared by
+// the row; state = state * exp(dt * A) + dt * B * x; y = sum(state * C) + D * x,
+// times SiLU(z).
+// ---------------------------------------------------------------------------
+constexpr int kMaxStatePerLane = 8;  // d_state <= 256
+
+struct SsuParams {
+  __nv_bfloat16* state;            // [batch, nh, hd, ds]
+  const __nv_bfloat16* x;          // [batch, nh, hd]
+  const __nv_bfloat16* dt;         // [batch, nh, hd]
+  const float* A;                  // [nh, hd, ds]
+  const __nv_bfloat16* Bm;         // [batch, ng, ds]
+  const __nv_bfloat16* Cm;         // [batch, ng, ds]
+  const __nv_bfloat16* D;          // [nh, hd] or nullptr
+  const __nv_bfloat16* z;          // [batch, nh, hd] or nullptr
+  const __nv_bfloat16* dt_bias;    // [nh, hd] or nullptr
+  __nv_bfloat16* y;                // [batch, nh, hd]
+  int batch, nh, hd, ds, ng, softplus;
+};
+
+__global__ void __launch_bounds__(256) selective_state_update_kernel(const SsuParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= static_cast<int64_t>(p.batch) * p.nh * p.hd) return;
+  const int dd = static_cast<int>(row % p.hd);
+  const int h = static_cast<int>((row / p.hd) % p.nh);
+  const int b = static_cast<int>(row / (static_cast<int64_t>(p.hd) * p.nh));
+  const int g = h / (p.nh / p.ng);
+  const int64_t hrow = static_cast<int64_t>(h) * p.hd + dd;  // [nh, hd] index
+  float dt = bf(p.dt, row);
+  if (p.dt_bias) dt += bf(p.dt_bias, hrow);
+  if (p.softplus) dt = dt <= 20.f ? log1pf(expf(dt)) : dt;
+  const float xv = bf(p.x, row);
+  const float dtx = dt * xv;
+  __nv_bfloat16* st = p.state + row * p.ds;
+  const float* Ar = p.A + hrow * p.ds;
+  const __nv_bfloat16* Br = p.Bm + (static_cast<int64_t>(b) * p.ng + g) * p.ds;
+  const __nv_bfloat16* Cr = p.Cm + (static_cast<int64_t>(b) * p.ng + g) * p.ds;
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxStatePerLane; ++i) {
+    const int s = lane + 32 * i;
+    if (s < p.ds) {
+      const float ns = fmaf(__bfloat162float(st[s]), expf(dt * Ar[s]), dtx * __bfloat162float(Br[s]));
+      const __nv_bfloat16 nb = __float2bfloat16_rn(ns);
+      st[s] = nb;
+      acc = fmaf(ns, __bfloat162float(Cr[s]), acc);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    float out = acc;
+    if (p.D) out = fmaf(xv, bf(p.D, hrow), out);
+    if (p.z) out *= silu(bf(p.z, row));
+    p.y[row] = __float2bfloat16_rn(out);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row norms.  A decode step normalises 1-2 rows of a few thousand elements:
+// one CTA per row leaves the reduction latency-bound on a single SM (each
+// warp waits out its own dependent loads and reductions; measured 13 us for
+// 2 x 4096).  So each row (rmsnorm_gated: each group) is spread over a
+// cluster of CL CTAs of 256 threads, at most kNormPer elements a thread, and
+// the row sums are reduced through distributed shared memory: every CTA
+// publishes its partial, a cluster barrier, every CTA adds the CL partials in
+// rank order (the same order everywhere, so every CTA gets the same sum).
+// ---------------------------------------------------------------------------
+constexpr int kNormThreads = 256;
+constexpr int kNormPer = 4;  // elements per thread: rows up to 8 * 256 * 4 = 8192
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+
+// Sum of v over the CL CTAs of the cluster (all threads of every CTA call it;
+// slot: this reduction's index, so consecutive reductions use fresh smem).
+template <int CL>
+__device__ __forceinline__ float cluster_sum(float v, float* red, float* part, int slot) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[slot * 8 + warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < (kNormThreads >> 5) ? red[slot * 8 + lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) part[slot] = t;
+  }
+  if constexpr (CL == 1) {
+    __syncthreads();
+    return part[slot];
+  } else {
+    cluster_barrier();  // every CTA's part[slot] is written and visible
+    float tot = 0.f;
+#pragma unroll
+    for (int r = 0; r < CL; ++r) tot += ld_cluster_f32(part + slot, static_cast<uint32_t>(r));
+    return tot;
+  }
+}
+
+// y = rms_normalise(x * SiLU(z)) * w (+ bias) for norm_before_gate == 0;
+// rms_normalise(x) * w (+ bias) * SiLU(z) otherwise.  Cluster = one (row, group).
+template <int CL>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_gated_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                     const __nv_bfloat16* __restrict__ w,
+                                                                     const __nv_bfloat16* __restrict__ bias,
+                                                                     const __nv_bfloat16* __restrict__ z,
+                                                                     __nv_bfloat16* __restrict__ y, int N, int G,
+                                                                     float eps, int norm_before_gate) {
+  __shared__ float red[16];
+  __shared__ float part[2];
+  const int rank = CL == 1 ? 0 : static_cast<int>(cluster_rank());
+  const int64_t base = static_cast<int64_t>(blockIdx.x / CL) * G;  // element offset of this (row, group)
+  const int c0 = static_cast<int>(base % N);                       // its first column
+  const int span = (G + CL - 1) / CL;                              // columns per CTA
+  const int cb = rank * span, ce = min(G, cb + span);
+  float v[kNormPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormPer; ++i) {
+    const int c = cb + threadIdx.x + i * kNormThreads;
+    float t = 0.f;
+    if (c < ce) {
+      t = bf(x, base + c);
+      if (z && !norm_before_gate) t *= silu(bf(z, base + c));
+    }
+    v[i] = t;
+    ss = fmaf(t, t, ss);
+  }
+  const float r = rsqrtf(cluster_sum<CL>(ss, red, part, 0) / G + eps);
+#pragma unroll
+  for (int i = 0; i < kNormPer; ++i) {
+    const int c = cb + threadIdx.x + i * kNormThreads;
+    if (c < ce) {
+      float o = v[i] * r * bf(w, c0 + c);
+      if (bias) o += bf(bias, c0 + c);
+      if (z && norm_before_gate) o *= silu(bf(z, base + c));
+      y[base + c] = __float2bfloat16_rn(o);
+    }
+  }
+  if constexpr (CL > 1) cluster_barrier();  // no CTA leaves while a peer may read its part[]
+}
+
+// h = x + residual (fp32); residual_out = h (bf16 or fp32) when asked;
+// out = LayerNorm or RMSNorm of h (unrounded) * w + bias.  Cluster = one row.
+template <int CL>
+__global__ void __launch_bounds__(kNormThreads) layer_norm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                  const void* __restrict__ residual, int res_f32,
+                                                                  const __nv_bfloat16* __restrict__ w,
+                                                                  const __nv_bfloat16* __restrict__ bias,
+                                                                  __nv_bfloat16* __restrict__ out,
+                                                                  void* __restrict__ residual_out, int rout_f32,
+                                                                  int N, float eps, int rms) {
+  __shared__ float red[16];
+  __shared__ float part[2];
+  const int rank = CL == 1 ? 0 : static_cast<int>(cluster_rank());
+  const int64_t base = static_cast<int64_t>(blockIdx.x / CL) * N;
+  const int span = (N + CL - 1) / CL;
+  const int cb = rank * span, ce = min(N, cb + span);
+  float v[kNormPer];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormPer; ++i) {
+    const int c = cb + threadIdx.x + i * kNormThreads;
+    float t = 0.f;
+    if (c < ce) {
+      t = bf(x, base + c);
+      if (residual)
+        t += res_f32 ? static_cast<const float*>(residual)[base + c]
+                     : bf(static_cast<const __nv_bfloat16*>(residual), base + c);
+      if (residual_out) {
+        if (rout_f32)
+          static_cast<float*>(residual_out)[base + c] = t;
+        else
+          static_cast<__nv_bfloat16*>(residual_out)[base + c] = __float2bfloat16_rn(t);
+      }
+    }
+    v[i] = t;
+    sum += t;
+  }
+  const float mean = rms ? 0.f : cluster_sum<CL>(sum, red, part, 0) / N;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormPer; ++i) {
+    const int c = cb + threadIdx.x + i * kNormThreads;
+    const float d = c < ce ? v[i] - mean : 0.f;
+    sq = fmaf(d, d, sq);
+  }
+  const float r = rsqrtf(cluster_sum<CL>(sq, red, part, 1) / N + eps);
+#pragma unroll
+  for (int i = 0; i < kNormPer; ++i) {
+    const int c = cb + threadIdx.x + i * kNormThreads;
+    if (c < ce) {
+      float o = (v[i] - mean) * r * bf(w, c);
+      if (bias) o += bf(bias, c);
+      out[base + c] = __float2bfloat16_rn(o);
+    }
+  }
+  if constexpr (CL > 1) cluster_barrier();
+}
+
+// Cluster size for a row of n elements: the fewest CTAs (1, 2, 4, 8) with at
+// most 2 elements a thread, 8 at most (then up to kNormPer).
+inline int norm_cluster(int n) {
+  int cl = 1;
+  while (cl < 8 && n > cl * kNormThreads * 2) cl *= 2;
+  return cl;
+}
+
+template <typename Kern, typename... Args>
+int launch_cluster(Kern kern, int clusters, int cl, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(clusters * cl));
+  cfg.blockDim = dim3(kNormThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, args...) != cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_LAUNCH;
+  }
+  return SN_OK;
+}
+
+}  // namespace
+
+}  // namespace sn
+
+extern "C" {
+
+int sn_causal_conv1d_update(const void* x, void* conv_state, const void* weight, const void* bias, void* y, int B,
+                            int D, int W, int activation, void* stream) {
+  if (!x || !conv_state || !weight || !y || B < 1 || D < 1 || W < 1 || W > sn::kMaxConvWidth)
+    return SN_ERR_INVALID_ARGUMENT;
+  if (activation != SN_ACT_NONE && activation != SN_ACT_SILU) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t n = static_cast<int64_t>(B) * D;
+  return sn::launch(sn::causal_conv1d_update_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, static_cast<const __nv_bfloat16*>(x),
+                    static_cast<__nv_bfloat16*>(conv_state), static_cast<const __nv_bfloat16*>(weight),
+                    static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y), B, D, W,
+                    activation == SN_ACT_SILU ? 1 : 0);
+}
+
+int sn_selective_state_update(void* state, const void* x, const void* dt, const float* A, const void* Bm,
+                              const void* Cm, const void* D, const void* z, const void* dt_bias, void* y, int batch,
+                              int nheads, int headdim, int dstate, int ngroups, int dt_softplus, void* stream) {
+  if (!state || !x || !dt || !A || !Bm || !Cm || !y || batch < 1 || nheads < 1 || headdim < 1 || dstate < 1 ||
+      ngroups < 1)
+    return SN_ERR_INVALID_ARGUMENT;
+  if (nheads % ngroups != 0 || dstate > 32 * sn::kMaxStatePerLane) return SN_ERR_INVALID_ARGUMENT;
+  sn::SsuParams p;
+  p.state = static_cast<__nv_bfloat16*>(state);
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.dt = static_cast<const __nv_bfloat16*>(dt);
+  p.A = A;
+  p.Bm = static_cast<const __nv_bfloat16*>(Bm);
+  p.Cm = static_cast<const __nv_bfloat16*>(Cm);
+  p.D = static_cast<const __nv_bfloat16*>(D);
+  p.z = static_cast<const __nv_bfloat16*>(z);
+  p.dt_bias = static_cast<const __nv_bfloat16*>(dt_bias);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.batch = batch;
+  p.nh = nheads;
+  p.hd = headdim;
+  p.ds = dstate;
+  p.ng = ngroups;
+  p.softplus = dt_softplus ? 1 : 0;
+  const int64_t rows = static_cast<int64_t>(batch) * nheads * headdim;
+  return sn::launch(sn::selective_state_update_kernel, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, p);
+}
+
+int sn_rmsnorm_gated(const void* x, const void* weight, const void* bias, const void* z, void* y, int rows, int N,
+                     int group_size, float eps, int norm_before_gate, void* stream) {
+  if (!x || !weight || !y || rows < 1 || N < 1 || group_size < 1 || N % group_size != 0) return SN_ERR_INVALID_ARGUMENT;
+  if (group_size > 8 * sn::kNormThreads * sn::kNormPer) return SN_ERR_UNSUPPORTED;
+  const int64_t groups = static_cast<int64_t>(rows) * (N / group_size);
+  if (groups * 8 > INT32_MAX) return SN_ERR_UNSUPPORTED;
+  const int cl = sn::norm_cluster(group_size);
+  auto args = [&](auto kern) {
+    return sn::launch_cluster(kern, static_cast<int>(groups), cl, static_cast<cudaStream_t>(stream),
+                              static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
+                              static_cast<const __nv_bfloat16*>(bias), static_cast<const __nv_bfloat16*>(z),
+                              static_cast<__nv_bfloat16*>(y), N, group_size, eps, norm_before_gate ? 1 : 0);
+  };
+  switch (cl) {
+    case 1: return args(sn::rmsnorm_gated_kernel<1>);
+    case 2: return args(sn::rmsnorm_gated_kernel<2>);
+    case 4: return args(sn::rmsnorm_gated_kernel<4>);
+    default: return args(sn::rmsnorm_gated_kernel<8>);
+  }
+}
+
+int sn_layer_norm_fused(const void* x, const void* residual, int residual_f32, const void* weight, const void* bias,
+                        void* out, void* residual_out, int residual_out_f32, int rows, int N, float eps,
+                        int is_rms_norm, void* stream) {
+  if (!x || !weight || !out || rows < 1 || N < 1) return SN_ERR_INVALID_ARGUMENT;
+  if (N > 8 * sn::kNormThreads * sn::kNormPer) return SN_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(rows) * 8 > INT32_MAX) return SN_ERR_UNSUPPORTED;
+  const int cl = sn::norm_cluster(N);
+  auto args = [&](auto kern) {
+    return sn::launch_cluster(kern, rows, cl, static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+                              residual, residual_f32 ? 1 : 0, static_cast<const __nv_bfloat16*>(weight),
+                              static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out),
+                              residual_out, residual_out_f32 ? 1 : 0, N, eps, is_rms_norm ? 1 : 0);
+  };
+  switch (cl) {
+    case 1: return args(sn::layer_norm_kernel<1>);
+    case 2: return args(sn::layer_norm_kernel<2>);
+    case 4: return args(sn::layer_norm_kernel<4>);
+    default: return args(sn::layer_norm_kernel<8>);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,130 @@
+"""Mamba2 decode-step ops on B200: the element ops between the decode GEMVs.
+
+Same call signatures and semantics as the library functions the reference's
+Mamba2.step() uses and its frozen goldens were made with
+(scripts/validation_harness.py:39, 117-171): causal_conv1d's
+``causal_conv1d_update`` and mamba_ssm's ``selective_state_update``,
+``rmsnorm_fn`` (ops/triton/layernorm_gated) and ``layer_norm_fn``
+(ops/triton/layer_norm), restricted to the decode path (bf16 tensors, no
+dropout / second input / rowscale).  Each runs one sm_100a kernel through the
+C ABI (``sn_causal_conv1d_update``, ``sn_selective_state_update``,
+``sn_rmsnorm_gated``, ``sn_layer_norm_fused``); in-place state updates are
+in place, as in those libraries.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from ._common import call, require_cuda, stream_handle
+
+_BF16 = torch.bfloat16
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _bf16(name, t, shape=None):
+    require_cuda(name, t, _BF16)
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+
+
+def causal_conv1d_update(x: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor,
+                         bias: torch.Tensor | None = None, activation: str | None = None, stream=None) -> torch.Tensor:
+    """x [B, D]; conv_state [B, D, W] (updated in place); weight [D, W];
+    bias [D] or None; activation None | "silu" | "swish".  Returns y [B, D]."""
+    if activation not in (None, "silu", "swish"):
+        raise NotImplementedError("activation must be None, silu, or swish")
+    Bn, D = x.shape
+    W = conv_state.shape[-1]
+    _bf16("x", x)
+    _bf16("conv_state", conv_state, (Bn, D, W))
+    _bf16("weight", weight, (D, W))
+    if bias is not None:
+        _bf16("bias", bias, (D,))
+    y = torch.empty_like(x)
+    act = _lib.SN_ACT_NONE if activation is None else _lib.SN_ACT_SILU
+    call("sn_causal_conv1d_update", x.data_ptr(), conv_state.data_ptr(), weight.data_ptr(), _ptr(bias), y.data_ptr(),
+         Bn, D, W, act, stream_handle(stream))
+    return y
+
+
+def selective_state_update(state: torch.Tensor, x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor,
+                           B: torch.Tensor, C: torch.Tensor, D: torch.Tensor | None = None,
+                           z: torch.Tensor | None = None, dt_bias: torch.Tensor | None = None,
+                           dt_softplus: bool = False, stream=None) -> torch.Tensor:
+    """state [batch, nheads, headdim, dstate] (updated in place); x, dt, z
+    [batch, nheads, headdim]; A fp32 [nheads, headdim, dstate]; B, C [batch,
+    ngroups, dstate]; D, dt_bias [nheads, headdim].  Returns y like x."""
+    batch, nh, hd, ds = state.shape
+    ng = B.shape[1]
+    _bf16("state", state)
+    for name, t in (("x", x), ("dt", dt)):
+        _bf16(name, t, (batch, nh, hd))
+    if z is not None:
+        _bf16("z", z, (batch, nh, hd))
+    require_cuda("A", A, torch.float32)
+    if tuple(A.shape) != (nh, hd, ds) or not A.is_contiguous():
+        raise ValueError(f"A must be a contiguous fp32 [{nh}, {hd}, {ds}] tensor")
+    _bf16("B", B, (batch, ng, ds))
+    _bf16("C", C, (batch, ng, ds))
+    for name, t in (("D", D), ("dt_bias", dt_bias)):
+        if t is not None:
+            _bf16(name, t, (nh, hd))
+    y = torch.empty_like(x)
+    call("sn_selective_state_update", state.data_ptr(), x.data_ptr(), dt.data_ptr(), A.data_ptr(), B.data_ptr(),
+         C.data_ptr(), _ptr(D), _ptr(z), _ptr(dt_bias), y.data_ptr(), batch, nh, hd, ds, ng, int(bool(dt_softplus)),
+         stream_handle(stream))
+    return y
+
+
+def rmsnorm_fn(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, z: torch.Tensor | None = None,
+               eps: float = 1e-6, group_size: int | None = None, norm_before_gate: bool = True,
+               stream=None) -> torch.Tensor:
+    """Gated RMSNorm over the last dimension in groups of group_size (None:
+    the whole row); returns a new tensor like x."""
+    N = x.shape[-1]
+    g = N if group_size is None else int(group_size)
+    _bf16("x", x)
+    _bf16("weight", weight, (N,))
+    if bias is not None:
+        _bf16("bias", bias, (N,))
+    if z is not None:
+        _bf16("z", z, tuple(x.shape))
+    y = torch.empty_like(x)
+    call("sn_rmsnorm_gated", x.data_ptr(), weight.data_ptr(), _ptr(bias), _ptr(z), y.data_ptr(), x.numel() // N, N, g,
+         float(eps), int(bool(norm_before_gate)), stream_handle(stream))
+    return y
+
+
+def layer_norm_fn(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, residual=None,
+                  eps: float = 1e-6, prenorm: bool = False, residual_in_fp32: bool = False,
+                  is_rms_norm: bool = False, stream=None):
+    """Fused residual add + LayerNorm / RMSNorm over the last dimension.
+    Returns out, or (out, residual_out) with prenorm; residual_out is x +
+    residual in x's dtype (fp32 with residual_in_fp32)."""
+    N = x.shape[-1]
+    _bf16("x", x)
+    _bf16("weight", weight, (N,))
+    if bias is not None:
+        _bf16("bias", bias, (N,))
+    res_f32 = 0
+    if residual is not None:
+        require_cuda("residual", residual, None)
+        if tuple(residual.shape) != tuple(x.shape) or not residual.is_contiguous():
+            raise ValueError("residual must be contiguous with x's shape")
+        if residual.dtype not in (_BF16, torch.float32):
+            raise TypeError("residual must be bf16 or fp32")
+        res_f32 = int(residual.dtype == torch.float32)
+    out = torch.empty_like(x)
+    rout = None
+    if prenorm:
+        rout = torch.empty(x.shape, device=x.device, dtype=torch.float32 if residual_in_fp32 else x.dtype)
+    call("sn_layer_norm_fused", x.data_ptr(), _ptr(residual), res_f32, weight.data_ptr(), _ptr(bias), out.data_ptr(),
+         _ptr(rout), int(rout is not None and rout.dtype == torch.float32), x.numel() // N, N, float(eps),
+         int(bool(is_rms_norm)), stream_handle(stream))
+    return (out, rout) if prenorm else out

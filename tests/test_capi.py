@@ -61,6 +61,16 @@ def test_gemv_rejects_bad_arguments_on_host(L):
     assert L.sn_snake_conv1d_pack(p, 16, 16, 7, p, 16, None) == -1
     assert L.sn_snake_conv_transpose1d_pack(p, 16, 16, 5, 2, p, 1 << 20, None) == -3
     assert L.sn_snake_conv_transpose1d_output_length(10, 16, 8, 4) == 80
+    # Mamba2 decode-step ops
+    assert L.sn_causal_conv1d_update(None, p, p, None, p, 1, 8, 4, 2, None) == -1
+    assert L.sn_causal_conv1d_update(p, p, p, None, p, 1, 8, 9, 2, None) == -1   # W > 8
+    assert L.sn_causal_conv1d_update(p, p, p, None, p, 1, 8, 4, 0, None) == -1   # snake is not a conv1d act
+    assert L.sn_selective_state_update(p, p, p, p, p, p, None, None, None, p, 1, 6, 4, 8, 4, 1, None) == -1
+    assert L.sn_selective_state_update(p, p, p, p, p, p, None, None, None, p, 1, 4, 4, 512, 1, 1, None) == -1
+    assert L.sn_rmsnorm_gated(p, p, None, None, p, 2, 100, 30, 1e-5, 0, None) == -1
+    assert L.sn_rmsnorm_gated(p, p, None, None, p, 2, 16384, 16384, 1e-5, 0, None) == -3
+    assert L.sn_layer_norm_fused(None, None, 0, p, None, p, None, 0, 2, 64, 1e-5, 0, None) == -1
+    assert L.sn_layer_norm_fused(p, None, 0, p, None, p, None, 0, 2, 9000, 1e-5, 0, None) == -3
     assert L.sn_quantize_rows_int8(None, 8, 8, 8, p, 8, p, None) == -1
     assert L.sn_quantize_rows_fp8e4m3(p, 4, 8, 8, p, 8, p, None) == -1
 
