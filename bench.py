@@ -410,9 +410,13 @@ def run_ours(args):
 
     snake = None
     dac = None
+    step_ops = None
     if rank == 0 and not args.skip_snake:
         snake = bench_snake_conv()
         dac = bench_dac_decoder()
+    if rank == 0:
+        from sonata_b200.kernels import mamba_step
+        step_ops = mamba_step.bench_step_ops()
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -480,6 +484,8 @@ def run_ours(args):
         line["snake_conv"] = snake
     if dac is not None:
         line["dac_decoder"] = dac
+    if step_ops is not None:
+        line["mamba_step_ops"] = step_ops
     line.update(sharded)
     print(json.dumps(line), flush=True)
     return 0
