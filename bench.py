@@ -288,6 +288,97 @@ def time_replays(g, steps, warmup, world, before=None, after=None):
 
 
 # ---------------------------------------------------------------------------
+# Per-config lines (3, 4, 5): absolute time, GB/s and the
+# fraction of the HBM roofline, next to the reference CPU path on the host
+# cores (rank 0 at N=1; bounded CPU samples)
+# ---------------------------------------------------------------------------
+def _graph_us(fn, calls, reps=20):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(calls):
+            fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(e) * 1e3 / (reps * calls)
+
+
+def bench_configs(hbm, with_cpu):
+    """Configs 1, 3 (chains of 26 distinct in_proj weights with programmatic
+    dependent launch, as in the decode graph), config 4 (one head call per
+    graph replay) and config 5's CPU reference.  GB/s are algorithmic bytes."""
+    from oracle import cpu_baseline as cb
+    from sonata_b200.kernels import bmm as Bm
+    from sonata_b200.kernels import gemv as G
+    thr = cb.host_threads()
+    out = {}
+    N, K = 8512, 2048
+    g = torch.Generator(device="cuda").manual_seed(77)
+    Ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for _ in range(26)]
+    x = torch.randn(1, K, device="cuda", generator=g).to(torch.bfloat16)
+    y = torch.empty(1, N, device="cuda", dtype=torch.bfloat16)
+    us = _graph_us(lambda: [G.gemv(x, W, out=y, pdl=True) for W in Ws], 1) / 26
+    byt = (N * K + K + N) * 2
+    c1 = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1), "roofline_frac": round(byt / us / 1e3 / hbm, 4),
+          "bytes": byt, "workload": "in_proj 8512x2048 bf16, M=1, chain of 26 distinct weights (PDL)"}
+    if with_cpu:
+        torch.set_num_threads(thr)
+        xc, Wc = x.cpu(), Ws[0].cpu()
+        t = cb._time(lambda: torch.nn.functional.linear(xc, Wc), 2.0)[0]
+        c1["cpu_baseline"] = {"us": round(t * 1e6, 1), "gbs": round(byt / t / 1e9, 2), "cores": thr,
+                              "kind": "port", "sample": "torch F.linear bf16, 2 s of repeats"}
+    out["config1_gemv_in_proj"] = c1
+    for kind in ("int8", "e4m3"):
+        qws = [G.quantize_weight(W, kind) for W in Ws]
+        yq = torch.empty(1, N, device="cuda", dtype=torch.float32)
+        us = _graph_us(lambda: [G.gemv_quantized(x, q, out=yq, pdl=True) for q in qws], 1) / 26
+        byt = N * K + N * 4 + K * 2 + N * 4
+        c3 = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1), "roofline_frac": round(byt / us / 1e3 / hbm, 4),
+              "bytes": byt, "workload": f"in_proj {kind} codes + fp32 row scales, M=1, fp32 out, chain of 26 (PDL)"}
+        if with_cpu:
+            t = cb.time_quant_gemv(N, K, kind, thr)
+            c3["cpu_baseline"] = {"us": round(t * 1e6, 1), "cores": thr, "kind": "port",
+                                  "sample": "dequantise to fp32 then F.linear fp32, 2 s of repeats"}
+        out[f"config3_gemv_{kind}"] = c3
+        del qws
+    del Ws
+    gh = torch.Generator(device="cuda").manual_seed(78)
+    head = Bm.CodebookHead((torch.randn(9, 2048, 1025, device="cuda", generator=gh) * 0.02).to(torch.bfloat16))
+    for B in (1, 8, 64, 256):
+        h = torch.randn(9, B, 2048, device="cuda", generator=gh).to(torch.bfloat16)
+        o = torch.empty(9, B, 1025, device="cuda")
+        us = _graph_us(lambda: head(h, out=o), 1)
+        byt = 9 * 2048 * 1025 * 2 + 9 * B * 2048 * 2 + 9 * B * 1025 * 4
+        c4 = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1), "roofline_frac": round(byt / us / 1e3 / hbm, 4),
+              "bytes": byt, "tflops": round(2 * 9 * B * 2048 * 1025 / us / 1e6, 1)}
+        if with_cpu and B == 64:
+            t = cb.time_head_bmm(B, thr)
+            c4["cpu_baseline"] = {"us": round(t * 1e6, 1), "cores": thr, "kind": "port",
+                                  "sample": "torch.bmm bf16 over the 9 heads, 2 s of repeats"}
+        out[f"config4_head_B{B}"] = c4
+    if with_cpu:
+        from sonata_b200.kernels import fused_snake_conv as fsc
+        frac = 0.125
+        secs = cb.time_snake_stream(fsc.DAC_STAGES, fsc.DAC_DILATIONS, thr, frames_fraction=frac)
+        out["config5_cpu_baseline"] = {"us_per_audio_second": round(secs / frac / 10.008 * 1e6, 1), "cores": thr,
+                                       "kind": "port",
+                                       "sample": "reference_snake_conv1d fp32, the 12 units on 1/8 of each stage's "
+                                                 "time axis, scaled to the full 10 s"}
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Snake + Conv1d (config 5) and the whole DAC decoder: microseconds per second
 # of audio
 # ---------------------------------------------------------------------------
@@ -414,9 +505,12 @@ def run_ours(args):
     if rank == 0 and not args.skip_snake:
         snake = bench_snake_conv()
         dac = bench_dac_decoder()
+    configs = None
     if rank == 0:
         from sonata_b200.kernels import mamba_step
         step_ops = mamba_step.bench_step_ops()
+        if not args.skip_configs:
+            configs = bench_configs(hbm, with_cpu=(world == 1 and not args.skip_cpu))
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -486,6 +580,8 @@ def run_ours(args):
         line["dac_decoder"] = dac
     if step_ops is not None:
         line["mamba_step_ops"] = step_ops
+    if configs is not None:
+        line["configs"] = configs
     line.update(sharded)
     print(json.dumps(line), flush=True)
     return 0
@@ -602,6 +698,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-snake", action="store_true")
+    ap.add_argument("--skip-configs", action="store_true", help="skip the per-config (1, 3, 4, 5) lines")
     ap.add_argument("--skip-sharded", action="store_true", help="skip the stream-sharded config 4 / 5 sections")
     ap.add_argument("--case", choices=["gemv", "snake", "head", "ssd"], default=None,
                     help="run one kernel on one shape (profiling / microbenchmark)")

@@ -70,3 +70,66 @@ def reference_snake_conv1d(x, alpha, weight, bias=None, stride=1, padding=0, dil
     a = alpha.reshape(1, -1, 1)
     activated = x + torch.sin(a * x).square() / (a + eps)
     return F.conv1d(activated, weight, bias, stride=stride, padding=padding, dilation=dilation)
+
+
+def _time(fn, min_seconds: float):
+    fn()  # warm-up
+    t0 = time.perf_counter()
+    it = 0
+    while True:
+        fn()
+        it += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return el / it, it
+
+
+def time_quant_gemv(N: int, K: int, kind: str, threads: int, min_seconds: float = 2.0):
+    """BASELINE config 3's CPU reference: dequantise the per-row codes to fp32,
+    then matmul in fp32 (the fake-quant probe path, scripts/fake_quant.py:41
+    before its dtype cast).  Returns seconds per GEMV."""
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    W = torch.randn(N, K, generator=g) * 0.02
+    x = torch.randn(1, K, generator=g).to(torch.bfloat16)
+    amax = W.abs().amax(dim=1, keepdim=True).clamp_min(1e-8)
+    if kind == "int8":
+        scale = amax / 127
+        q = torch.round(W / scale).clamp(-127, 127).to(torch.int8)
+        fn = lambda: F.linear(x.float(), q.float() * scale)
+    else:
+        scale = amax / 448
+        q = (W / scale).to(torch.float8_e4m3fn)
+        fn = lambda: F.linear(x.float(), q.float() * scale)
+    return _time(fn, min_seconds)[0]
+
+
+def time_head_bmm(B: int, threads: int, min_seconds: float = 2.0):
+    """BASELINE config 4's CPU reference: torch.bmm in bf16 over the 9 heads.
+    Returns seconds per call."""
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    h = torch.randn(9, B, 2048, generator=g).to(torch.bfloat16)
+    W = (torch.randn(9, 2048, 1025, generator=g) * 0.02).to(torch.bfloat16)
+    return _time(lambda: torch.bmm(h, W), min_seconds)[0]
+
+
+def time_snake_stream(stages, dilations, threads: int, frames_fraction: float = 1.0):
+    """BASELINE config 5's CPU reference: reference_snake_conv1d in fp32 over
+    the 12 units of one stream, each stage's time axis cut to
+    `frames_fraction` of its length (a bounded sample).  Returns seconds for
+    that sample."""
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    total = 0.0
+    for C, T in stages:
+        t = max(64, int(T * frames_fraction))
+        x = torch.randn(1, C, t, generator=g)
+        a = torch.rand(C, generator=g) + 0.5
+        W = torch.randn(C, C, 7, generator=g) / (7 * C) ** 0.5
+        b = torch.randn(C, generator=g)
+        for d in dilations:
+            t0 = time.perf_counter()
+            reference_snake_conv1d(x, a, W, b, padding=3 * d, dilation=d)
+            total += time.perf_counter() - t0
+    return total
