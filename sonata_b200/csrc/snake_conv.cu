@@ -38,7 +38,7 @@ namespace sn {
 namespace {
 
 constexpr int kScProducerWarps = 8;
-constexpr int kScEpilogueWarps = 4;
+constexpr int kScEpilogueWarps = 8;  // two per TMEM lane quarter, half the columns each
 constexpr int kScThreads = (2 + kScProducerWarps + kScEpilogueWarps) * 32;  // TMA, MMA, producers, epilogue
 constexpr int kScWStages = 2;
 constexpr int kScPairWStages = 2;  // weight stages in the CTA-pair kernel (4 measured no faster)
@@ -72,12 +72,12 @@ struct ScParams {
 
 // Pull a tile's residual (GEMM rows t0 .. t0 + 127, columns o0 .. o0 + nt - 1)
 // into L2 while its MMAs run, so that the epilogue's reads hit L2: one
-// 128-byte line per (channel, 32-row segment), spread over the 128 epilogue
-// threads (et = 0 .. 127).
+// 128-byte line per (channel, 32-row segment), spread over the epilogue
+// threads (et = 0 .. 32 * kScEpilogueWarps - 1).
 __device__ __forceinline__ void sc_prefetch_res(const ScParams& p, int b, int t0, int o0, int et) {
   if (!p.res || p.up_s != 0) return;
   const float* rb = p.res + static_cast<int64_t>(b) * p.Cy * p.Tout;
-  for (int l = et; l < p.nt * 4; l += 128) {
+  for (int l = et; l < p.nt * 4; l += 32 * kScEpilogueWarps) {
     const int o = o0 + (l >> 2), t = t0 + 32 * (l & 3);
     if (o < p.Cy && t < p.Tout)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(rb + static_cast<int64_t>(o) * p.Tout + t));
@@ -200,7 +200,8 @@ __device__ __forceinline__ void sc_emit16(const ScParams& p, int b, int t, int o
   }
 }
 
-// One tile's epilogue: TMEM accumulator columns [0, nt) of this thread's row.
+// One tile's epilogue: this thread's row (its TMEM lane), half of the tile's
+// nt accumulator columns.
 // With a residual (HBM reads) chunk c + 1's residual is read before chunk c is
 // stored; bias reads (L1 hits) go just before their own chunk's stores.
 template <bool UP>
@@ -208,14 +209,17 @@ __device__ __forceinline__ void sc_epilogue_tile(const ScParams& p, uint32_t bas
   ScChunk c;
   float rnext[16];
   const bool res = !UP && p.res;
-  if (res) sc_load_res16(p, b, t, o0, rnext);
-  for (int cc = 0; cc < p.nt; cc += 16) {
+  // the two warps of a lane quarter take one half of the tile's columns each
+  const int half = (threadIdx.x - 32 * (2 + kScProducerWarps)) / (32 * 4);
+  const int ccb = half * (p.nt / 2), cce = ccb + p.nt / 2;
+  if (res) sc_load_res16(p, b, t, o0 + ccb, rnext);
+  for (int cc = ccb; cc < cce; cc += 16) {
     float vv[16];
     tc::tmem_ld16(base + cc, vv);
     if (res) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) c.rv[e] = rnext[e];
-      if (cc + 16 < p.nt) sc_load_res16(p, b, t, o0 + cc + 16, rnext);
+      if (cc + 16 < cce) sc_load_res16(p, b, t, o0 + cc + 16, rnext);
     } else {
 #pragma unroll
       for (int e = 0; e < 16; ++e) c.rv[e] = 0.f;
