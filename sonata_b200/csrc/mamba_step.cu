@@ -54,12 +54,14 @@ __global__ void __launch_bounds__(256) causal_conv1d_update_kernel(const __nv_bf
 }
 
 // ---------------------------------------------------------------------------
-// selective_state_update: one warp per (batch, head, headdim row); lane l
-// holds d_state elements l, l + 32, ...  dt (+ dt_bias, softplus) is shared by
-// the row; state = state * exp(dt * A) + dt * B * x; y = sum(state * C) + D * x,
-// times SiLU(z).
+// selective_state_update: per (batch, head, headdim row), dt (+ dt_bias,
+// softplus) is shared by the row; state = state * exp(dt * A) + dt * B * x;
+// y = sum(state * C) + D * x, times SiLU(z).  Every load of a row is issued
+// before its first state store: the state is written through a pointer the
+// compiler cannot prove distinct from A / B / C, so loads interleaved with
+// the stores would wait out one HBM round trip each.
 // ---------------------------------------------------------------------------
-constexpr int kMaxStatePerLane = 8;  // d_state <= 256
+constexpr int kMaxStatePerLane = 8;  // strided kernel: d_state <= 256
 
 struct SsuParams {
   __nv_bfloat16* state;            // [batch, nh, hd, ds]
@@ -75,42 +77,132 @@ struct SsuParams {
   int batch, nh, hd, ds, ng, softplus;
 };
 
-__global__ void __launch_bounds__(256) selective_state_update_kernel(const SsuParams p) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= static_cast<int64_t>(p.batch) * p.nh * p.hd) return;
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return a | (b << 16);
+}
+
+// The row's scalars: dt after bias and softplus, x, D, SiLU(z) inputs.
+struct SsuRow {
+  int64_t row, hrow, bg;  // [batch, nh, hd], [nh, hd] and [batch, ng] indices
+};
+__device__ __forceinline__ SsuRow ssu_row(const SsuParams& p, int64_t row) {
   const int dd = static_cast<int>(row % p.hd);
   const int h = static_cast<int>((row / p.hd) % p.nh);
   const int b = static_cast<int>(row / (static_cast<int64_t>(p.hd) * p.nh));
   const int g = h / (p.nh / p.ng);
-  const int64_t hrow = static_cast<int64_t>(h) * p.hd + dd;  // [nh, hd] index
-  float dt = bf(p.dt, row);
-  if (p.dt_bias) dt += bf(p.dt_bias, hrow);
+  return {row, static_cast<int64_t>(h) * p.hd + dd, static_cast<int64_t>(b) * p.ng + g};
+}
+__device__ __forceinline__ void ssu_finish(const SsuParams& p, const SsuRow& r, float acc, float xv) {
+  float out = acc;
+  if (p.D) out = fmaf(xv, bf(p.D, r.hrow), out);
+  if (p.z) out *= silu(bf(p.z, r.row));
+  p.y[r.row] = __float2bfloat16_rn(out);
+}
+__device__ __forceinline__ float ssu_dt(const SsuParams& p, const SsuRow& r) {
+  float dt = bf(p.dt, r.row);
+  if (p.dt_bias) dt += bf(p.dt_bias, r.hrow);
   if (p.softplus) dt = dt <= 20.f ? log1pf(expf(dt)) : dt;
+  return dt;
+}
+
+// Vector kernel (d_state = 128 NCH, 16-byte aligned state / B / C / A rows):
+// 16 lanes per row, two rows per warp; lane l of a row holds elements
+// 128 c + 8 l .. 128 c + 8 l + 7 of chunk c (one 16-byte bf16 load of state,
+// B and C, two 16-byte loads of A).  Half the threads of a warp per row keep
+// every row of a decode step resident in one wave (8192 rows at the Zonos
+// shapes) at this kernel's register count.
+template <int NCH>
+__global__ void __launch_bounds__(256) selective_state_update_vec_kernel(const SsuParams p) {
+  const int l16 = threadIdx.x & 15;
+  const int64_t rows = static_cast<int64_t>(p.batch) * p.nh * p.hd;
+  const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 4;
+  const bool valid = row < rows;  // no early exit: the half-warp shuffles below need every lane
+  const SsuRow r = ssu_row(p, valid ? row : 0);
+  __nv_bfloat16* st = p.state + r.row * p.ds;
+  const float* Ar = p.A + r.hrow * p.ds;
+  const __nv_bfloat16* Br = p.Bm + r.bg * p.ds;
+  const __nv_bfloat16* Cr = p.Cm + r.bg * p.ds;
+  uint4 sv[NCH], bv[NCH], cv[NCH];
+  float4 av[2 * NCH];
+  if (valid) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int s = 128 * c + 8 * l16;
+      sv[c] = *reinterpret_cast<const uint4*>(st + s);
+      av[2 * c] = *reinterpret_cast<const float4*>(Ar + s);
+      av[2 * c + 1] = *reinterpret_cast<const float4*>(Ar + s + 4);
+      bv[c] = *reinterpret_cast<const uint4*>(Br + s);
+      cv[c] = *reinterpret_cast<const uint4*>(Cr + s);
+    }
+  }
+  const float dt = valid ? ssu_dt(p, r) : 0.f;
+  const float xv = valid ? bf(p.x, r.row) : 0.f;
+  const float dtx = dt * xv;
+  float acc = 0.f;
+  if (valid) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const uint32_t su[4] = {sv[c].x, sv[c].y, sv[c].z, sv[c].w};
+      const uint32_t bu[4] = {bv[c].x, bv[c].y, bv[c].z, bv[c].w};
+      const uint32_t cu[4] = {cv[c].x, cv[c].y, cv[c].z, cv[c].w};
+      const float a8[8] = {av[2 * c].x, av[2 * c].y, av[2 * c].z, av[2 * c].w,
+                           av[2 * c + 1].x, av[2 * c + 1].y, av[2 * c + 1].z, av[2 * c + 1].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float n0 = fmaf(bf16lo(su[k]), expf(dt * a8[2 * k]), dtx * bf16lo(bu[k]));
+        const float n1 = fmaf(bf16hi(su[k]), expf(dt * a8[2 * k + 1]), dtx * bf16hi(bu[k]));
+        acc = fmaf(n0, bf16lo(cu[k]), acc);
+        acc = fmaf(n1, bf16hi(cu[k]), acc);
+        o[k] = pack_bf16x2(n0, n1);
+      }
+      *reinterpret_cast<uint4*>(st + 128 * c + 8 * l16) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (valid && l16 == 0) ssu_finish(p, r, acc, xv);
+}
+
+// Strided kernel (any d_state <= 256, any alignment): one warp per row,
+// lane l holds elements l, l + 32, ...
+__global__ void __launch_bounds__(256) selective_state_update_kernel(const SsuParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= static_cast<int64_t>(p.batch) * p.nh * p.hd) return;
+  const SsuRow r = ssu_row(p, row);
+  __nv_bfloat16* st = p.state + row * p.ds;
+  const float* Ar = p.A + r.hrow * p.ds;
+  const __nv_bfloat16* Br = p.Bm + r.bg * p.ds;
+  const __nv_bfloat16* Cr = p.Cm + r.bg * p.ds;
+  float sv[kMaxStatePerLane], av[kMaxStatePerLane], bv[kMaxStatePerLane], cv[kMaxStatePerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxStatePerLane; ++i) {
+    const int s = lane + 32 * i;
+    if (s < p.ds) {
+      sv[i] = __bfloat162float(st[s]);
+      av[i] = Ar[s];
+      bv[i] = __bfloat162float(Br[s]);
+      cv[i] = __bfloat162float(Cr[s]);
+    }
+  }
+  const float dt = ssu_dt(p, r);
   const float xv = bf(p.x, row);
   const float dtx = dt * xv;
-  __nv_bfloat16* st = p.state + row * p.ds;
-  const float* Ar = p.A + hrow * p.ds;
-  const __nv_bfloat16* Br = p.Bm + (static_cast<int64_t>(b) * p.ng + g) * p.ds;
-  const __nv_bfloat16* Cr = p.Cm + (static_cast<int64_t>(b) * p.ng + g) * p.ds;
   float acc = 0.f;
 #pragma unroll
   for (int i = 0; i < kMaxStatePerLane; ++i) {
     const int s = lane + 32 * i;
     if (s < p.ds) {
-      const float ns = fmaf(__bfloat162float(st[s]), expf(dt * Ar[s]), dtx * __bfloat162float(Br[s]));
-      const __nv_bfloat16 nb = __float2bfloat16_rn(ns);
-      st[s] = nb;
-      acc = fmaf(ns, __bfloat162float(Cr[s]), acc);
+      const float ns = fmaf(sv[i], expf(dt * av[i]), dtx * bv[i]);
+      st[s] = __float2bfloat16_rn(ns);
+      acc = fmaf(ns, cv[i], acc);
     }
   }
   acc = warp_sum(acc);
-  if (lane == 0) {
-    float out = acc;
-    if (p.D) out = fmaf(xv, bf(p.D, hrow), out);
-    if (p.z) out *= silu(bf(p.z, row));
-    p.y[row] = __float2bfloat16_rn(out);
-  }
+  if (lane == 0) ssu_finish(p, r, acc, xv);
 }
 
 // ---------------------------------------------------------------------------
@@ -340,8 +432,16 @@ int sn_selective_state_update(void* state, const void* x, const void* dt, const 
   p.ng = ngroups;
   p.softplus = dt_softplus ? 1 : 0;
   const int64_t rows = static_cast<int64_t>(batch) * nheads * headdim;
-  return sn::launch(sn::selective_state_update_kernel, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0,
-                    static_cast<cudaStream_t>(stream), false, p);
+  const bool vec = (dstate == 128 || dstate == 256) && sn::aligned16(state) && sn::aligned16(Bm) &&
+                   sn::aligned16(Cm) && sn::aligned16(A);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (vec) {
+    const dim3 grid(static_cast<unsigned>((rows + 15) / 16));  // 16 rows per 256-thread CTA
+    return dstate == 128 ? sn::launch(sn::selective_state_update_vec_kernel<1>, grid, dim3(256), 0, st, false, p)
+                         : sn::launch(sn::selective_state_update_vec_kernel<2>, grid, dim3(256), 0, st, false, p);
+  }
+  return sn::launch(sn::selective_state_update_kernel, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0, st,
+                    false, p);
 }
 
 int sn_rmsnorm_gated(const void* x, const void* weight, const void* bias, const void* z, void* y, int rows, int N,
