@@ -316,7 +316,8 @@ def _graph_us(fn, calls, reps=20):
 
 def bench_configs(hbm, with_cpu):
     """Configs 1, 3 (chains of 26 distinct in_proj weights with programmatic
-    dependent launch, as in the decode graph), config 4 (one head call per
+    dependent launch and each GEMV's next-weight L2 prefetch hint, as in the
+    decode graph), config 4 (one head call per
     graph replay) and config 5's CPU reference.  GB/s are algorithmic bytes."""
     from oracle import cpu_baseline as cb
     from sonata_b200.kernels import bmm as Bm
@@ -328,10 +329,11 @@ def bench_configs(hbm, with_cpu):
     Ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for _ in range(26)]
     x = torch.randn(1, K, device="cuda", generator=g).to(torch.bfloat16)
     y = torch.empty(1, N, device="cuda", dtype=torch.bfloat16)
-    us = _graph_us(lambda: [G.gemv(x, W, out=y, pdl=True) for W in Ws], 1) / 26
+    us = _graph_us(lambda: [G.gemv(x, W, out=y, pdl=True, next_weight=Ws[(i + 1) % 26]) for i, W in enumerate(Ws)],
+                   1) / 26
     byt = (N * K + K + N) * 2
     c1 = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1), "roofline_frac": round(byt / us / 1e3 / hbm, 4),
-          "bytes": byt, "workload": "in_proj 8512x2048 bf16, M=1, chain of 26 distinct weights (PDL)"}
+          "bytes": byt, "workload": "in_proj 8512x2048 bf16, M=1, chain of 26 distinct weights (PDL, next-weight hint)"}
     if with_cpu:
         torch.set_num_threads(thr)
         xc, Wc = x.cpu(), Ws[0].cpu()
@@ -342,10 +344,11 @@ def bench_configs(hbm, with_cpu):
     for kind in ("int8", "e4m3"):
         qws = [G.quantize_weight(W, kind) for W in Ws]
         yq = torch.empty(1, N, device="cuda", dtype=torch.float32)
-        us = _graph_us(lambda: [G.gemv_quantized(x, q, out=yq, pdl=True) for q in qws], 1) / 26
+        us = _graph_us(lambda: [G.gemv_quantized(x, q, out=yq, pdl=True, next_weight=qws[(i + 1) % 26])
+                                for i, q in enumerate(qws)], 1) / 26
         byt = N * K + N * 4 + K * 2 + N * 4
         c3 = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1), "roofline_frac": round(byt / us / 1e3 / hbm, 4),
-              "bytes": byt, "workload": f"in_proj {kind} codes + fp32 row scales, M=1, fp32 out, chain of 26 (PDL)"}
+              "bytes": byt, "workload": f"in_proj {kind} codes + fp32 row scales, M=1, fp32 out, chain of 26 (PDL, next-weight hint)"}
         if with_cpu:
             t = cb.time_quant_gemv(N, K, kind, thr)
             c3["cpu_baseline"] = {"us": round(t * 1e6, 1), "cores": thr, "kind": "port",

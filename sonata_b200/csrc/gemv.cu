@@ -1284,6 +1284,19 @@ int64_t prefetch_budget() {
   return v;
 }
 
+// At most this percentage of the next weight is prefetched: 25 (measured
+// against 35 / 50 / 100 on the config-2 chain, 0.919 -> 0.913 ms, and on
+// int8 / e4m3 in_proj chains, -2%; the 8 MB budget already is ~25% of a
+// bf16 in_proj); SONATA_GEMV_PREFETCH_PCT overrides (100: budget only).
+int prefetch_pct() {
+  static const int v = [] {
+    const char* e = getenv("SONATA_GEMV_PREFETCH_PCT");
+    const int pct = e ? atoi(e) : 25;
+    return std::max(0, std::min(pct, 100));
+  }();
+  return v;
+}
+
 int nd_of(int wk) { return wk == W_INT8 ? 3 : wk == W_E4M3 ? 2 : 1; }
 
 int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS, const void* x,
@@ -1340,7 +1353,8 @@ int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale
   if (next && next->W) {
     const int nesz = (next->wk == W_BF16) ? 2 : 1;
     const int64_t row_b = static_cast<int64_t>(next->K) * nesz;
-    const int64_t want = std::min(static_cast<int64_t>(next->N) * row_b, prefetch_budget());
+    const int64_t nbytes = static_cast<int64_t>(next->N) * row_b;
+    const int64_t want = std::min(std::min(nbytes, prefetch_budget()), nbytes / 100 * prefetch_pct());
     // a hint: weights a bulk prefetch cannot address (16-byte rules) are skipped
     if (want > 0 && aligned16(next->W) && (next->ldw * nesz) % 16 == 0 && row_b % 16 == 0 && row_b < (1 << 30)) {
       MmaGrid g;
