@@ -72,6 +72,7 @@ struct GemvParams {
   int64_t pf_ld;
   int pf_rows, pf_parts;
   uint32_t pf_row_bytes, pf_part_bytes;
+  int x_rot;    // x row copies start at a CTA-dependent 128-byte piece
   int pf_lead;  // issue once all but this many of the CTA's own tiles have landed (< 0: at once)
 };
 
@@ -721,6 +722,25 @@ __device__ __forceinline__ void prefetch_next_weights(const GemvParams& p) {
   }
 }
 
+// One x row that every CTA of the launch copies at the same moment (when
+// the dependency resolves): CTA c starts at 128-byte piece `rot` of the row
+// and wraps around, so the CTAs' requests spread over the L2 slices instead
+// of queuing on the same lines in the same order.  src, dst and bytes are
+// multiples of 16.  Used for the 8-bit kernels' x rows (int8 / e4m3 in_proj
+// chains -1.5% / -2%); the bf16 kernel keeps one copy per row (the second
+// copy cost it +0.8%, config 2 +0.7%).
+__device__ __forceinline__ void bulk_g2s_rot(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol,
+                                             uint32_t rot) {
+  const uint32_t pieces = bytes / 128;
+  const uint32_t off = (bytes % 128 == 0 && pieces > 1) ? (rot % pieces) * 128 : 0;
+  if (off == 0) {
+    bulk_g2s(dst, src, bytes, bar, pol);
+    return;
+  }
+  bulk_g2s(static_cast<uint8_t*>(dst) + off, static_cast<const uint8_t*>(src) + off, bytes - off, bar, pol);
+  bulk_g2s(dst, src, off, bar, pol);
+}
+
 template <int WK, int MT, int S>
 __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const GemvParams p, const MmaShape sh) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -836,7 +856,8 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
           const uint64_t pol = l2_policy_evict_normal();
           mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * p.K * 2);
           for (int m = 0; m < p.M; ++m)
-            bulk_g2s(const_cast<__nv_bfloat16*>(xraw) + m * p.K, xb + m * p.ldx, p.K * 2, xbar, pol);
+            bulk_g2s_rot(const_cast<__nv_bfloat16*>(xraw) + m * p.K, xb + m * p.ldx, p.K * 2, xbar, pol,
+                         p.x_rot ? blockIdx.x + m : 0);
         }
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) record_status(SN_ERR_TIMEOUT);
         const uint4* xr = reinterpret_cast<const uint4*>(xraw);
@@ -1275,6 +1296,15 @@ int prefetch_lead() {
   return v;
 }
 
+// Rotated x row copies (bulk_g2s_rot); SONATA_GEMV_X_ROT=0 turns them off.
+int x_rotate() {
+  static const int v = [] {
+    const char* e = getenv("SONATA_GEMV_X_ROT");
+    return e ? (atoi(e) != 0) : 1;
+  }();
+  return v;
+}
+
 int64_t prefetch_budget() {
   static const int64_t v = [] {
     const char* e = getenv("SONATA_GEMV_PREFETCH_MB");
@@ -1350,6 +1380,7 @@ int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale
   p.pf_rows = p.pf_parts = 0;
   p.pf_row_bytes = p.pf_part_bytes = 0;
   p.pf_lead = prefetch_lead();
+  p.x_rot = x_rotate();
   if (next && next->W) {
     const int nesz = (next->wk == W_BF16) ? 2 : 1;
     const int64_t row_b = static_cast<int64_t>(next->K) * nesz;
