@@ -722,6 +722,20 @@ __device__ __forceinline__ void prefetch_next_weights(const GemvParams& p) {
   }
 }
 
+// 16-byte x pieces an 8-bit kernel's staging thread may hold in registers
+// (then no shared-memory copy of x: K <= 1024 * kXRegs / MT).
+constexpr int kXRegs = 8;
+
+// 16-byte load cached in L2 only: x is written by the previous kernel, and
+// this SM's L1 may hold lines of the same buffer from an earlier launch.
+__device__ __forceinline__ uint4 ld_cg_v4(const void* ptr) {
+  uint4 r;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(ptr));
+  return r;
+}
+
 // One x row that every CTA of the launch copies at the same moment (when
 // the dependency resolves): CTA c starts at 128-byte piece `rot` of the row
 // and wraps around, so the CTAs' requests spread over the L2 slices instead
@@ -847,81 +861,121 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
         tc::fence_proxy_async_smem();
       }
     } else {
-      // x rows by bulk copy, then the B planes of x * 2^e_m: three int8 digits
-      // of rint(x * 2^e_m), or two e4m3 terms
+      // x rows, then the B planes of x * 2^e_m: three int8 digits of
+      // rint(x * 2^e_m), or two e4m3 terms.  When every 16-byte piece a
+      // staging thread needs fits in kXRegs registers, the pieces are loaded
+      // straight into registers (no staging copy in shared memory, which
+      // leaves room for one more ring slot); otherwise one bulk copy per row.
       if (warp >= 2) {
         const int xt = threadIdx.x - 64;  // 0..127
-        const __nv_bfloat16* xraw = reinterpret_cast<const __nv_bfloat16*>(smem + sh.xraw_off);
-        if (xt == 0) {
-          const uint64_t pol = l2_policy_evict_normal();
-          mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * p.K * 2);
-          for (int m = 0; m < p.M; ++m)
-            bulk_g2s_rot(const_cast<__nv_bfloat16*>(xraw) + m * p.K, xb + m * p.ldx, p.K * 2, xbar, pol,
-                         p.x_rot ? blockIdx.x + m : 0);
-        }
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) record_status(SN_ERR_TIMEOUT);
-        const uint4* xr = reinterpret_cast<const uint4*>(xraw);
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {  // max |x| (bit patterns of non-negative values order like them)
+        // max |x| of a piece (bit patterns of non-negative values order like them)
+        auto piece_max = [](uint4 v) {
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
           uint32_t mx = 0;
-          if (m < p.M) {
-            for (int c = xt; c < cpr; c += 128) {
-              const uint4 v = xr[m * cpr + c];
-              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-              for (int j = 0; j < 4; ++j) mx = max(mx, max(w[j] & 0x7FFFu, (w[j] >> 16) & 0x7FFFu));
-            }
-          }
+          for (int j = 0; j < 4; ++j) mx = max(mx, max(w[j] & 0x7FFFu, (w[j] >> 16) & 0x7FFFu));
+          return mx;
+        };
+        auto row_max = [&](int m, uint32_t mx) {
           mx = __reduce_max_sync(0xffffffffu, mx);
           if (lane == 0) atomicMax(xmax + m, mx);
-        }
-        named_bar_sync(2, 128);
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          // max|x| < 2^(E+1) with E = biased exponent - 127 (subnormal rows
-          // too: E = -127): scale by 2^e, e = 21 - E, as two exact
-          // power-of-two factors (e in [-107, 148])
+        };
+        // scale of row m: max|x| < 2^(E+1) with E = biased exponent - 127
+        // (subnormal rows too: E = -127): 2^e, e = 21 - E (int8) or 7 - E,
+        // as two exact power-of-two factors (e in [-107, 148])
+        auto row_scale = [&](int m, float& up1, float& up2) {
           const int ebits = static_cast<int>(xmax[m] >> 7);
           const int e = (WK == W_INT8 ? 21 : 7) - (ebits - 127);
-          const float up1 = __uint_as_float(static_cast<uint32_t>(127 + e / 2) << 23);
-          const float up2 = __uint_as_float(static_cast<uint32_t>(127 + (e - e / 2)) << 23);
+          up1 = __uint_as_float(static_cast<uint32_t>(127 + e / 2) << 23);
+          up2 = __uint_as_float(static_cast<uint32_t>(127 + (e - e / 2)) << 23);
           if (xt == 0) xexp[m] = (ebits == 255) ? INT_MIN : e;  // non-finite x row
-          for (int c = xt; c < cpr; c += 128) {
-            uint32_t dg[ND][2] = {};  // plane d of 8 elements
-            if (m < p.M) {
-              const uint4 v = xr[m * cpr + c];
-              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        };
+        // the ND planes of piece c of row m (v = 0 for padding rows)
+        auto emit = [&](int m, int c, uint4 v, float up1, float up2) {
+          uint32_t dg[ND][2] = {};  // plane d of 8 elements
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const uint32_t h = w[e >> 1];
-                const float xf = (e & 1) ? bf16hi(h) : bf16lo(h);
-                const float xs = (xf * up1) * up2;
-                uint32_t b[ND];
-                if constexpr (WK == W_INT8) {
-                  int X = __float2int_rn(xs);  // |X| < 2^22
-                  const int d0 = static_cast<int8_t>(X & 0xFF);
-                  X = (X - d0) >> 8;
-                  const int d1 = static_cast<int8_t>(X & 0xFF);
-                  const int d2 = (X - d1) >> 8;  // |d2| <= 64
-                  b[0] = static_cast<uint32_t>(d0) & 0xFFu;
-                  b[1] = static_cast<uint32_t>(d1) & 0xFFu;
-                  b[2] = static_cast<uint32_t>(d2) & 0xFFu;
-                } else {
-                  // |xs| < 2^8: no saturation; t1 + t2 reproduces xs to 2^-10
-                  const __nv_fp8_storage_t t1 = __nv_cvt_float_to_fp8(xs, __NV_SATFINITE, __NV_E4M3);
-                  const float r = xs - __half2float(__half(__nv_cvt_fp8_to_halfraw(t1, __NV_E4M3)));
-                  const __nv_fp8_storage_t t2 = __nv_cvt_float_to_fp8(r, __NV_SATFINITE, __NV_E4M3);
-                  b[0] = t1;
-                  b[1] = t2;
-                }
-#pragma unroll
-                for (int d = 0; d < ND; ++d) dg[d][e >> 2] |= b[d] << (8 * (e & 3));
-              }
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t h = w[e >> 1];
+            const float xf = (e & 1) ? bf16hi(h) : bf16lo(h);
+            const float xsc = (xf * up1) * up2;
+            uint32_t b[ND];
+            if constexpr (WK == W_INT8) {
+              int X = __float2int_rn(xsc);  // |X| < 2^22
+              const int d0 = static_cast<int8_t>(X & 0xFF);
+              X = (X - d0) >> 8;
+              const int d1 = static_cast<int8_t>(X & 0xFF);
+              const int d2 = (X - d1) >> 8;  // |d2| <= 64
+              b[0] = static_cast<uint32_t>(d0) & 0xFFu;
+              b[1] = static_cast<uint32_t>(d1) & 0xFFu;
+              b[2] = static_cast<uint32_t>(d2) & 0xFFu;
+            } else {
+              // |xsc| < 2^8: no saturation; t1 + t2 reproduces xsc to 2^-10
+              const __nv_fp8_storage_t t1 = __nv_cvt_float_to_fp8(xsc, __NV_SATFINITE, __NV_E4M3);
+              const float r = xsc - __half2float(__half(__nv_cvt_fp8_to_halfraw(t1, __NV_E4M3)));
+              const __nv_fp8_storage_t t2 = __nv_cvt_float_to_fp8(r, __NV_SATFINITE, __NV_E4M3);
+              b[0] = t1;
+              b[1] = t2;
             }
 #pragma unroll
-            for (int d = 0; d < ND; ++d)
-              *reinterpret_cast<uint2*>(xs + (static_cast<size_t>(d) * MT + m) * p.K + c * 8) =
-                  make_uint2(dg[d][0], dg[d][1]);
+            for (int d = 0; d < ND; ++d) dg[d][e >> 2] |= b[d] << (8 * (e & 3));
+          }
+#pragma unroll
+          for (int d = 0; d < ND; ++d)
+            *reinterpret_cast<uint2*>(xs + (static_cast<size_t>(d) * MT + m) * p.K + c * 8) =
+                make_uint2(dg[d][0], dg[d][1]);
+        };
+        if (sh.xraw_off == 0) {
+          constexpr int PPR = kXRegs / MT;  // pieces per row a thread holds (host: cpr <= 128 * PPR)
+          uint4 xv[MT][PPR];
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+#pragma unroll
+            for (int j = 0; j < PPR; ++j) {
+              const int c = xt + 128 * j;
+              xv[m][j] = (m < p.M && c < cpr) ? ld_cg_v4(xb + m * p.ldx + c * 8) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            uint32_t mx = 0;
+#pragma unroll
+            for (int j = 0; j < PPR; ++j) mx = max(mx, piece_max(xv[m][j]));
+            row_max(m, mx);
+          }
+          named_bar_sync(2, 128);
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            float up1, up2;
+            row_scale(m, up1, up2);
+#pragma unroll
+            for (int j = 0; j < PPR; ++j)
+              if (xt + 128 * j < cpr) emit(m, xt + 128 * j, xv[m][j], up1, up2);
+          }
+        } else {
+          const __nv_bfloat16* xraw = reinterpret_cast<const __nv_bfloat16*>(smem + sh.xraw_off);
+          if (xt == 0) {
+            const uint64_t pol = l2_policy_evict_normal();
+            mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * p.K * 2);
+            for (int m = 0; m < p.M; ++m)
+              bulk_g2s_rot(const_cast<__nv_bfloat16*>(xraw) + m * p.K, xb + m * p.ldx, p.K * 2, xbar, pol,
+                           p.x_rot ? blockIdx.x + m : 0);
+          }
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) record_status(SN_ERR_TIMEOUT);
+          const uint4* xr = reinterpret_cast<const uint4*>(xraw);
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            uint32_t mx = 0;
+            if (m < p.M)
+              for (int c = xt; c < cpr; c += 128) mx = max(mx, piece_max(xr[m * cpr + c]));
+            row_max(m, mx);
+          }
+          named_bar_sync(2, 128);
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            float up1, up2;
+            row_scale(m, up1, up2);
+            for (int c = xt; c < cpr; c += 128)
+              emit(m, c, m < p.M ? xr[m * cpr + c] : make_uint4(0, 0, 0, 0), up1, up2);
           }
         }
         tc::fence_proxy_async_smem();
@@ -1222,7 +1276,13 @@ int dispatch_mma(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
   const int ns_max = 16;
   sh.xs_off = 1024;  // barriers, TMEM address and x scales below
   sh.xraw_off = round_up_u32(sh.xs_off + static_cast<uint32_t>(MT * ND) * p.K * ESZ, 128);
-  sh.ring_off = (WK != W_BF16) ? round_up_u32(sh.xraw_off + static_cast<uint32_t>(MT) * p.K * 2, 128) : sh.xraw_off;
+  sh.ring_off = sh.xraw_off;
+  if (WK != W_BF16) {
+    if ((p.K >> 3) <= 128 * (kXRegs / MT))
+      sh.xraw_off = 0;  // x pieces staged in registers: no shared-memory copy
+    else
+      sh.ring_off = round_up_u32(sh.xraw_off + static_cast<uint32_t>(MT) * p.K * 2, 128);
+  }
   // shared memory: ~half an SM per CTA at one CTA per SM, ~72 KB (two slots)
   // at two or three (SONATA_GEMV_SMEM_KB overrides)
   const size_t budget = getenv("SONATA_GEMV_SMEM_KB") ? bulk_smem_budget() : cps == 1 ? 110 * 1024 : 72 * 1024;

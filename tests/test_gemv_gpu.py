@@ -145,7 +145,7 @@ def test_quantize_codes_bit_exact(G, kind):
 
 @pytest.mark.parametrize("kind", ["int8", "e4m3"])
 @pytest.mark.parametrize("M", [1, 2, 4])
-@pytest.mark.parametrize("NK", [(8512, 2048), (2048, 4096), (777, 1280), (1000, 1040), (64, 24)])
+@pytest.mark.parametrize("NK", [(8512, 2048), (2048, 4096), (512, 5632), (777, 1280), (1000, 1040), (64, 24)])
 def test_quantized_gemv_matches_dequant_oracle(G, kind, M, NK):
     N, K = NK
     x, W = make(N, K, M, seed=11)
