@@ -361,10 +361,12 @@ __global__ void __launch_bounds__(kNormThreads) layer_norm_kernel(const __nv_bfl
 }
 
 // Cluster size for a row of n elements: the fewest CTAs (1, 2, 4, 8) with at
-// most 2 elements a thread, 8 at most (then up to kNormPer).
+// most one element a thread, 8 at most (then up to kNormPer).  Measured
+// against two and four elements a thread: add + LayerNorm over 2 x 2048
+// 3.70 / 4.34 -> 3.60 us; gated RMSNorm over 2 x 4096 is at 8 CTAs either way.
 inline int norm_cluster(int n) {
   int cl = 1;
-  while (cl < 8 && n > cl * kNormThreads * 2) cl *= 2;
+  while (cl < 8 && n > cl * kNormThreads) cl *= 2;
   return cl;
 }
 
