@@ -458,16 +458,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int q = warp & 3;
     if (__all_sync(0xffffffffu, mbar_wait_bounded(done, 0))) {
       tc::fence_after_sync();
-      const int i = mt * 128 + q * 32 + lane;  // row within the chunk
-      float* row = p.out + ((((static_cast<int64_t>(b) * p.nch + c) * p.ng + g) * p.ch) + i) * p.ch + nt * 128;
-      for (int j = 0; j < 128; j += 16) {
-        float v[16];
-        tc::tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + j, v);
-        float4* dst = reinterpret_cast<float4*>(row + j);
-        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-        dst[2] = make_float4(v[8], v[9], v[10], v[11]);
-        dst[3] = make_float4(v[12], v[13], v[14], v[15]);
+      // Lane l holds row q * 32 + l of the tile.  Each 32 x 32 block goes
+      // through shared memory (the operand buffers are free once the MMAs
+      // are done; 36-float rows keep both passes free of bank conflicts) so
+      // that every store instruction writes four whole 128-byte row
+      // segments, not 32 pieces of 16 bytes in 32 different rows.
+      float* stage = reinterpret_cast<float*>(smem) + q * (32 * 36);
+      float* tile = p.out +
+                    ((((static_cast<int64_t>(b) * p.nch + c) * p.ng + g) * p.ch) + mt * 128 + q * 32) * p.ch +
+                    nt * 128;
+      for (int j = 0; j < 128; j += 32) {
+        float v[32];
+        tc::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + j, v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float4*>(stage + lane * 36 + 4 * k) =
+              make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int r = it * 4 + (lane >> 3);
+          *reinterpret_cast<float4*>(tile + static_cast<int64_t>(r) * p.ch + j + (lane & 7) * 4) =
+              *reinterpret_cast<const float4*>(stage + r * 36 + (lane & 7) * 4);
+        }
+        __syncwarp();
       }
     } else {
       record_status(SN_ERR_TIMEOUT);
