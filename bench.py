@@ -625,14 +625,16 @@ def run_case(args):
         algo = 9 * 2048 * 1025 * 2 + 9 * B * 2048 * 2 + 9 * B * 1025 * 4
     elif args.case == "ssd":
         from sonata_b200.kernels import bmm as Bm
-        (L,) = (shape + [4096])[:1]
-        C = torch.randn(1, L, 1, 128, device="cuda").to(torch.bfloat16)
-        Bt = torch.randn(1, L, 1, 128, device="cuda").to(torch.bfloat16)
-        nch = (L + 255) // 256
-        o = torch.empty(1, nch, 1, 256, 256, device="cuda")
-        run = lambda: Bm.launch_bmm(C, Bt, 1, L, 1, 128, 256, nch, o)
+        # --shape L, or BATCH x SEQLEN x NGROUPS x DSTATE x CHUNK
+        Bz, L, ng, ds, ch = (1, *(shape or [4096]), 1, 128, 256) if len(shape) <= 1 else \
+            (shape + [1, 4096, 1, 128, 256][len(shape):])[:5]
+        C = torch.randn(Bz, L, ng, ds, device="cuda").to(torch.bfloat16)
+        Bt = torch.randn(Bz, L, ng, ds, device="cuda").to(torch.bfloat16)
+        nch = (L + ch - 1) // ch
+        o = torch.empty(Bz, nch, ng, ch, ch, device="cuda")
+        run = lambda: Bm.launch_bmm(C, Bt, Bz, L, ng, ds, ch, nch, o)
         per = 1
-        algo = 2 * L * 128 * 2 + nch * 256 * 256 * 4
+        algo = 2 * Bz * L * ng * ds * 2 + o.numel() * 4
     else:
         raise SystemExit(f"unknown case {args.case}")
     for _ in range(args.warmup):
