@@ -740,9 +740,11 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* ptr) {
 // the dependency resolves): CTA c starts at 128-byte piece `rot` of the row
 // and wraps around, so the CTAs' requests spread over the L2 slices instead
 // of queuing on the same lines in the same order.  src, dst and bytes are
-// multiples of 16.  Used for the 8-bit kernels' x rows (int8 / e4m3 in_proj
-// chains -1.5% / -2%); the bf16 kernel keeps one copy per row (the second
-// copy cost it +0.8%, config 2 +0.7%).
+// multiples of 16.  Used where an 8-bit kernel stages x through shared
+// memory (K * M beyond the staging registers): measured when every 8-bit x
+// row went that way, int8 / e4m3 in_proj chains -1.5% / -2%.  The bf16
+// kernel keeps one copy per row (the second copy cost it +0.8%, config 2
+// +0.7%).
 __device__ __forceinline__ void bulk_g2s_rot(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol,
                                              uint32_t rot) {
   const uint32_t pieces = bytes / 128;

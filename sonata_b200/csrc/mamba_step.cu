@@ -83,7 +83,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return a | (b << 16);
 }
 
-// The row's scalars: dt after bias and softplus, x, D, SiLU(z) inputs.
+// Indices of one (batch, head, headdim) row into the [batch, nh, hd],
+// [nh, hd] and [batch, ng] tensors.
 struct SsuRow {
   int64_t row, hrow, bg;  // [batch, nh, hd], [nh, hd] and [batch, ng] indices
 };
