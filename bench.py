@@ -49,6 +49,8 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from sonata_b200 import shard  # noqa: E402
+
 METRIC = "decode GEMV HBM GB/s (% of 8 TB/s); DAC snake-conv µs per audio-sec"
 SHAPES = {"in_proj": (8512, 2048), "out_proj": (2048, 4096), "qkv": (3072, 2048), "o_proj": (2048, 2048),
           "fc1": (11264, 2048), "fc2": (2048, 5632)}
@@ -94,12 +96,7 @@ def barrier(world):
 
 
 def max_over_ranks(v, world):
-    if world == 1:
-        return v
-    import torch.distributed as dist
-    t = torch.tensor([v], device="cuda", dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return v if world == 1 else shard.max_over_ranks(v, device="cuda")
 
 
 # ---------------------------------------------------------------------------

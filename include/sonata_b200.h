@@ -35,6 +35,7 @@ extern "C" {
 #define SN_ERR_DEVICE (-5)           /* current device is not sm_100 */
 #define SN_ERR_TIMEOUT (-6)          /* a bounded device-side wait ran out */
 #define SN_ERR_SCRATCH_LIMIT (-7)    /* needs more scratch than the allocation-free entry point holds */
+#define SN_ERR_SCRATCH_ADDRESS (-8)  /* the allocation-free entry point could not look up its array's address */
 
 /* ---- dtype codes for outputs ---- */
 #define SN_DTYPE_BF16 0
@@ -127,6 +128,16 @@ int sn_quantize_rows_fp8e4m3(const void *W, int64_t ldw, int N, int K, uint8_t *
 int sn_device_status(int reset, void *stream);
 
 /*
+ * Failure-detection check: launches one thread that waits, with the same
+ * bounded mbarrier wait every kernel here uses, on a barrier nothing arrives
+ * on.  After limit_ns nanoseconds (1 us .. 1 s) the wait gives up, the kernel
+ * records SN_ERR_TIMEOUT and returns, so a following sn_device_status reports
+ * SN_ERR_TIMEOUT and the context stays usable.  No counterpart in the
+ * reference (its kernels have no device-side waits).
+ */
+int sn_diag_bounded_wait(uint64_t limit_ns, void *stream);
+
+/*
  * Multi-codebook logit head, BASELINE config 4 (no kernel exists in the
  * reference; it is the per-codebook bmm its decode step runs on the 9 heads):
  *   logits[cb, b, n] = sum_k hidden[cb, b, k] * W[cb, k, n]
@@ -201,6 +212,17 @@ int sn_snake_conv1d_pack(const float *W, int Cin, int Cout, int K, void *packed,
                          void *stream);
 
 /*
+ * Snake1d on its own, elementwise over x [B, C, T] (contiguous):
+ *   y[b, c, t] = x + sin(alpha[c] * x)^2 / (alpha[c] + eps)
+ * with the same device arithmetic as the fused kernels' activation (sin^2
+ * after a Cody-Waite reduction modulo pi, accurate for any |alpha * x|).
+ * y may equal x.  The Snake of kernels/fused_snake_conv.py:264-286
+ * (reference_snake_conv1d) and of transformers' Snake1d, which the reference's
+ * DAC decoder runs before each conv (docs/dac_architecture.md:46-51).
+ */
+int sn_snake1d(const float *x, const float *alpha, float *y, int B, int C, int64_t T, float eps, void *stream);
+
+/*
  * Fused Snake + ConvTranspose1d (the DacDecoderBlock's snake1 -> conv_t1):
  *   y[b, o, t] = bias[o] + sum over (i, k, j) with t = j*stride - padding + k of
  *                snake(x[b, i, j]) * W[i, o, k]
@@ -232,13 +254,24 @@ int sn_snake_conv_transpose1d_pack(const float *W, int Cin, int Cout, int K, int
  * packed weights go to a static device array of
  * SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH bytes (16 MiB, enough for the largest
  * DAC unit, Cin = Cout = 768, K = 7) that every GPU loading the library keeps
- * until the process exits.  Problems with Cin * Cout * K * 4 bytes of packed
- * weights above that limit return SN_ERR_SCRATCH_LIMIT.  The function itself
- * calls no cudaMalloc / cudaFree.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress, with that device current), so
- * make that first call before capturing any stream.  All calls share the one
- * array: calls that may overlap on the GPU (other streams, other threads) race
- * on it and must be ordered by the caller.
+ * until the process exits.
+ *
+ * Limit: only shapes that run on the tensor cores use the array (stride 1,
+ * K <= 7, (K-1)*dilation <= 72, Cin and Cout multiples of 16); among those,
+ * problems whose packed weights (Cin * Cout * K * 4 bytes) exceed the array
+ * return SN_ERR_SCRATCH_LIMIT.  Every other shape runs the per-output kernel,
+ * which reads W directly, needs no scratch and has no size limit.
+ *
+ * The function calls no cudaMalloc / cudaFree.  It looks the array's device
+ * address up (cudaGetSymbolAddress, with the caller's device current) on
+ * every call; SN_ERR_SCRATCH_ADDRESS means that lookup failed.  The first
+ * call into this library on a device (this one or any other entry point)
+ * loads the library's device code on that device, which reserves the 16 MiB
+ * and may block or synchronise: make it outside the real-time thread and
+ * before capturing any stream (or load eagerly with CUDA_MODULE_LOADING=EAGER).
+ * All calls share the one array and it keeps the last call's weights: calls
+ * that may overlap on the GPU (other streams, other threads) race on it and
+ * must be ordered by the caller.
  */
 #define SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH (16u * 1024u * 1024u)
 int sn_snake_conv1d_noalloc(const float *x, const float *alpha, const float *W, const float *bias, float *y,

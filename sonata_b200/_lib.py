@@ -59,6 +59,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_selective_state_update": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
     "sn_rmsnorm_gated": ([_P, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _I, _P], _I),
     "sn_layer_norm_fused": ([_P, _P, _I, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _I, _P], _I),
+    "sn_snake1d": ([_P, _P, _P, _I, _I, _I64, ctypes.c_float, _P], _I),
+    "sn_diag_bounded_wait": ([ctypes.c_uint64, _P], _I),
     "sn_snake_conv_transpose1d_pack": ([_P, _I, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
     "sn_snake_conv_transpose1d_output_length": ([_I64, _I, _I, _I], _I64),
     "sn_snake_conv_transpose1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _U, _P,

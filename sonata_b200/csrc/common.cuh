@@ -168,7 +168,8 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 static __device__ int g_tu_status;
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tu_status, 0, code); }
 
-inline int read_tu_status(bool reset, cudaStream_t st, int* out) {
+// static: each translation unit reads its own status word, never another unit's copy
+static inline int read_tu_status(bool reset, cudaStream_t st, int* out) {
   int v = 0;
   if (cudaMemcpyFromSymbolAsync(&v, g_tu_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess) {

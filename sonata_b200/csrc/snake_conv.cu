@@ -32,7 +32,6 @@
 #include <cstring>
 #include <cstdlib>
 #include <cstdint>
-#include <mutex>
 
 namespace sn {
 namespace {
@@ -227,6 +226,34 @@ __device__ __forceinline__ void sc_epilogue_tile(const ScParams& p, uint32_t bas
     sc_load_bias16<UP>(p, o0 + cc, c.bv);
     sc_emit16<UP>(p, b, t, o0 + cc, vv, c);
   }
+}
+
+// sin(y)^2 for the Snake activation, accurate for arguments of any size.
+// sin^2 has period pi, so y is first reduced to r = y - n*pi, n = rint(y/pi),
+// |r| <= pi/2, by Cody and Waite's method (W. J. Cody and W. Waite, Software
+// Manual for the Elementary Functions, 1980): pi is split into three fp32
+// parts PI_A + PI_B + PI_C (the fp32 value of pi, then the fp32 values of the
+// two successive remainders) and each n * part is subtracted with one FMA.
+// For n != 0, |y| >= pi/2 > 1, so y is a multiple of 2^-23 and n * PI_A of
+// 2^-21: the first difference is exact.  The hardware approximation __sinf
+// is then only evaluated on |r| <= pi/2, where its absolute error is about
+// 2^-21; applied to a large y directly its error grows with |y|.
+__device__ __forceinline__ float snake_sin2(float y) {
+  constexpr float kInvPi = 0x1.45f306p-2f;
+  constexpr float kPiA = 0x1.921fb6p+1f;
+  constexpr float kPiB = -0x1.777a5cp-24f;
+  constexpr float kPiC = -0x1.ee59dap-49f;
+  const float n = rintf(y * kInvPi);
+  float r = fmaf(-n, kPiA, y);
+  r = fmaf(-n, kPiB, r);
+  r = fmaf(-n, kPiC, r);
+  const float sv = __sinf(r);
+  return sv * sv;
+}
+
+// snake(v) = v + sin(alpha v)^2 / (alpha + eps), with inv = 1 / (alpha + eps)
+__device__ __forceinline__ float snake_value(float v, float alpha, float inv) {
+  return fmaf(snake_sin2(alpha * v), inv, v);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -439,10 +466,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               float s = v[it][e];
-              if (p.act == SN_ACT_SNAKE) {
-                const float sv = __sinf(al[e] * s);
-                s = fmaf(sv * sv, inv[e], s);  // snake(v); snake(0) == 0
-              }
+              if (p.act == SN_ACT_SNAKE) s = snake_value(s, al[e], inv[e]);  // snake(0) == 0
               hi[e] = __bfloat162float(__float2bfloat16_rn(s));
               lo[e] = s - hi[e];
             }
@@ -681,10 +705,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               float s = v[it][e];
-              if (p.act == SN_ACT_SNAKE) {
-                const float sv = __sinf(al[e] * s);
-                s = fmaf(sv * sv, inv[e], s);
-              }
+              if (p.act == SN_ACT_SNAKE) s = snake_value(s, al[e], inv[e]);
               hi[e] = __bfloat162float(__float2bfloat16_rn(s));
               lo[e] = s - hi[e];
             }
@@ -784,6 +805,35 @@ __device__ __forceinline__ float sc_act(int act, float v, float a, float inv) {
   if (act != SN_ACT_SNAKE) return v;
   const float sv = sinf(a * v);
   return fmaf(sv * sv, inv, v);
+}
+
+// Snake1d on its own (transformers' Snake1d, the activation each DAC
+// Snake -> conv edge fuses): y = snake(x) elementwise over [rows = B*C, T],
+// with the fused kernels' snake_value, so it also shows what their producers
+// compute.  Four consecutive times a thread (one 16-byte access when T % 4 == 0
+// and both pointers are 16-byte aligned).  y may be x.
+__global__ void snake1d_kernel(const float* x, const float* __restrict__ alpha, float* y, int64_t rows, int64_t T,
+                               int C, float eps, bool vec) {
+  const int64_t groups_per_row = (T + 3) / 4;
+  const int64_t total = rows * groups_per_row;
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < total;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = g / groups_per_row;
+    const int64_t t0 = (g - row * groups_per_row) * 4;
+    const float a = __ldg(alpha + row % C);
+    const float inv = 1.0f / (a + eps);
+    const int64_t base = row * T + t0;
+    if (vec) {
+      float4 v = *reinterpret_cast<const float4*>(x + base);
+      v.x = snake_value(v.x, a, inv);
+      v.y = snake_value(v.y, a, inv);
+      v.z = snake_value(v.z, a, inv);
+      v.w = snake_value(v.w, a, inv);
+      *reinterpret_cast<float4*>(y + base) = v;
+    } else {
+      for (int e = 0; e < 4 && t0 + e < T; ++e) y[base + e] = snake_value(x[base + e], a, inv);
+    }
+  }
 }
 
 // Fallback: one thread per output element, the reference's loop order.
@@ -898,7 +948,9 @@ int64_t sn_snake_conv1d_output_length(int64_t T, int K, int stride, int padding,
 }
 
 size_t sn_snake_conv1d_workspace_size(int Cin, int Cout, int K) {
-  return static_cast<size_t>(Cin) * ((Cout + 15) / 16 * 16) * K * 2 * sizeof(__nv_bfloat16);
+  if (Cin < 1 || Cout < 1 || K < 1) return 0;
+  const size_t cg = (static_cast<size_t>(Cout) + 15) / 16 * 16;  // 64-bit before the round-up
+  return static_cast<size_t>(Cin) * cg * static_cast<size_t>(K) * 2 * sizeof(__nv_bfloat16);
 }
 
 int sn_snake_conv1d(const float* x, const float* alpha, const float* W, const float* bias, float* y, int B, int Cin,
@@ -1082,6 +1134,14 @@ int sn_snake_conv1d_ex(const float* x, const float* alpha, const float* W, const
                     W, bias, residual, y, B, Cin, Cout, T, Tout, K, stride, padding, dilation, eps, act, post);
 }
 
+int sn_snake1d(const float* x, const float* alpha, float* y, int B, int C, int64_t T, float eps, void* stream) {
+  if (!x || !alpha || !y || B < 1 || C < 1 || T < 1) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t rows = static_cast<int64_t>(B) * C;
+  const bool vec = T % 4 == 0 && sn::aligned16(x) && sn::aligned16(y);
+  return sn::launch(sn::snake1d_kernel, dim3(sn::blocks_for(rows * ((T + 3) / 4), 16)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, x, alpha, y, rows, T, C, eps, vec);
+}
+
 int64_t sn_snake_conv_transpose1d_output_length(int64_t T, int K, int stride, int padding) {
   if (T < 1 || stride < 1 || K < 1 || padding < 0) return -1;
   return (T - 1) * stride - 2 * static_cast<int64_t>(padding) + K;
@@ -1140,39 +1200,39 @@ int sn_snake_conv_transpose1d(const float* x, const float* alpha, const float* W
 // in this file-scope device array instead of a caller-provided workspace; the
 // array exists once per GPU that loads the library, for the life of the
 // process.  Host code cannot use the array's name as a device address: the
-// address is looked up with cudaGetSymbolAddress, once per device, on the
-// first call made while that device is current.
+// address is looked up with cudaGetSymbolAddress on every call, with the
+// caller's device current.  The lookup is a host-side query once the module
+// is loaded, and looking it up each time keeps the address right after a
+// cudaDeviceReset re-creates the context (the array may then sit elsewhere).
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char g_snake_noalloc_scratch[SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH];
 
 static void* snake_noalloc_scratch() {
-  static std::mutex mu;
-  static void* addr[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_snake_noalloc_scratch) != cudaSuccess) {
     cudaGetLastError();
     return nullptr;
   }
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_snake_noalloc_scratch) != cudaSuccess) {
-      cudaGetLastError();
-      return nullptr;
-    }
-    addr[dev] = p;
-  }
-  return addr[dev];
+  return p;
 }
 
 int sn_snake_conv1d_noalloc(const float* x, const float* alpha, const float* W, const float* bias, float* y, int B,
                             int Cin, int Cout, int T, int K, int stride, int padding, int dilation, float eps,
                             void* stream) {
-  if (Cin < 1 || Cout < 1 || K < 1) return SN_ERR_INVALID_ARGUMENT;
+  if (Cin < 1 || Cout < 1 || K < 1 || T < 1 || stride < 1 || padding < 0 || dilation < 1)
+    return SN_ERR_INVALID_ARGUMENT;
+  const int64_t tout = sn_snake_conv1d_output_length(T, K, stride, padding, dilation);
+  if (tout < 1 || tout > INT32_MAX) return SN_ERR_INVALID_ARGUMENT;
+  // Only the tensor-core path packs weights into the scratch; every other
+  // shape runs the per-output kernel, which reads W directly and needs none.
+  const int Cg = (Cout + 15) / 16 * 16;
+  if (!sn::fast_path_ok(Cin, Cg, K, stride, dilation, static_cast<int>(tout)))
+    return sn_snake_conv1d(x, alpha, W, bias, y, B, Cin, Cout, T, K, stride, padding, dilation, eps, nullptr, 0,
+                           stream);
   if (sn_snake_conv1d_workspace_size(Cin, Cout, K) > SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH)
     return SN_ERR_SCRATCH_LIMIT;
   void* scratch = snake_noalloc_scratch();
-  if (!scratch) return SN_ERR_DEVICE;
+  if (!scratch) return SN_ERR_SCRATCH_ADDRESS;
   return sn_snake_conv1d(x, alpha, W, bias, y, B, Cin, Cout, T, K, stride, padding, dilation, eps, scratch,
                          SN_SNAKE_CONV1D_NOALLOC_MAX_SCRATCH, stream);
 }

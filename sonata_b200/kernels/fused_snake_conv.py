@@ -210,6 +210,28 @@ def fused_snake_conv_transpose1d(x: torch.Tensor, alpha: torch.Tensor, weight: t
     return out
 
 
+def snake1d(x: torch.Tensor, alpha: torch.Tensor, eps: float = 1e-9, out: torch.Tensor | None = None,
+            stream=None) -> torch.Tensor:
+    """Snake on its own, ``x + sin(alpha * x)**2 / (alpha + eps)`` per channel of
+    x [B, C, T] (fp32): the Snake of ``reference_snake_conv1d`` and of
+    transformers' ``Snake1d``, computed by ``sn_snake1d`` with the same device
+    arithmetic the fused kernels' producers use.  ``out`` may be ``x``."""
+    require_cuda("x", x, torch.float32, 3)
+    require_cuda("alpha", alpha, torch.float32)
+    batch_size, channels, length = x.shape
+    if alpha.numel() != channels:
+        raise ValueError("alpha must contain one value per input channel.")
+    x = x.contiguous()
+    alpha = alpha.contiguous().view(-1)
+    if out is None:
+        out = torch.empty_like(x)
+    elif tuple(out.shape) != tuple(x.shape) or not out.is_contiguous() or out.dtype != torch.float32:
+        raise ValueError("out has the wrong shape, dtype or is not contiguous")
+    _lib.check("sn_snake1d", _lib.lib().sn_snake1d(x.data_ptr(), alpha.data_ptr(), out.data_ptr(), batch_size,
+                                                   channels, length, float(eps), stream_handle(stream)))
+    return out
+
+
 def explicit_snake_conv1d(x, alpha, weight, bias=None, stride=1, padding=0, dilation=1, eps=1e-9):
     """Unfold + einsum formulation (fused_snake_conv.py:201-262)."""
     _, input_channels, _ = x.shape

@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference checkout is importable:
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH   (or SONATA_REFERENCE=PATH)
 
 It imports the reference's Python modules directly --
 ``kernels/fused_snake_conv.py`` (reference_snake_conv1d, explicit_snake_conv1d,
@@ -16,6 +16,7 @@ never runs this script: it only reads the committed fixtures.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -33,7 +34,8 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SONATA_REFERENCE"), required="SONATA_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (or set SONATA_REFERENCE)")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref / "kernels"))

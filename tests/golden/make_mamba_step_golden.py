@@ -7,7 +7,7 @@ scripts/validation_harness.py against causal_conv1d 1.6.2.post1 and mamba_ssm
 file's sha256 against the manifest, loads it with torch.load(weights_only=True)
 and stores every bf16 tensor as its uint16 bit pattern:
 
-    python tests/golden/make_mamba_step_golden.py [--reference PATH]
+    python tests/golden/make_mamba_step_golden.py --reference PATH   (or SONATA_REFERENCE=PATH)
 
 selective_state_update is listed in the manifest but its file is absent from
 the checkout, so it has no golden here.  The GPU box never runs this script.
@@ -15,6 +15,7 @@ the checkout, so it has no golden here.  The GPU box never runs this script.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import json
 from pathlib import Path
@@ -33,7 +34,8 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SONATA_REFERENCE"), required="SONATA_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (or set SONATA_REFERENCE)")
     args = ap.parse_args()
     gdir = Path(args.reference) / "tests" / "goldens" / "kernels"
     manifest = json.loads((gdir / "MANIFEST.json").read_text())

@@ -96,6 +96,46 @@ def test_no_bias_and_large_activations(S):
     assert O.cosine(y, truth) >= COS_MIN
 
 
+def test_snake_activation_accurate_at_large_arguments(S):
+    """The producers' sin^2 (Cody-Waite reduction modulo pi, then the hardware
+    sine on |r| <= pi/2) against float64 over |alpha x| from 1e-3 to 1e5: the
+    error stays at the fp32 rounding level instead of growing with |alpha x|
+    as a sine evaluated on the unreduced argument does."""
+    g = torch.Generator().manual_seed(5)
+    C, T = 16, 4096
+    mag = torch.logspace(-3, 5, T, dtype=torch.float64)
+    sign = torch.where(torch.rand(C, T, generator=g) < 0.5, -1.0, 1.0).double()
+    x = (mag[None, :] * sign * (1 + 0.1 * torch.rand(C, T, generator=g).double())).float()
+    alpha = (torch.rand(C, generator=g) + 0.5).float()
+    y = S.snake1d(x[None].cuda(), alpha.cuda())[0].cpu().double()
+    a = alpha.double()[:, None]
+    arg = (alpha[:, None] * x).double()  # the fp32 product both sides start from
+    truth = x.double() + torch.sin(arg) ** 2 / (a + 1e-9)
+    err = (y - truth).abs()
+    bound = 4e-6 + 2.0 ** -22 * x.double().abs()
+    assert (err <= bound).all(), (err.max().item(), (err / bound).max().item())
+    # in place gives the same bits
+    xc = x[None].cuda()
+    S.snake1d(xc, alpha.cuda(), out=xc)
+    assert torch.equal(xc[0].cpu().double(), y)
+
+
+def test_large_alpha_x_under_absolute_gate(S):
+    """|alpha x| up to a few thousand with the outputs at their usual size:
+    the north-star gate unrelaxed (max|err| <= 2e-3 absolute, cos >= 0.9999)."""
+    g = torch.Generator().manual_seed(21)
+    B, C, T, d = 1, 192, 900, 3
+    x = torch.randn(B, C, T, generator=g) * 2.0
+    alpha = torch.rand(C, generator=g) * 250 + 50
+    W = torch.randn(C, C, 7, generator=g) / math.sqrt(7 * C)
+    b = torch.randn(C, generator=g)
+    assert (alpha[None, :, None] * x).abs().max() > 1000
+    y = S.fused_snake_conv1d(x.cuda(), alpha.cuda(), W.cuda(), b.cuda(), padding=3 * d, dilation=d)
+    torch.cuda.synchronize()
+    truth = O.snake_conv1d_ref(x.numpy(), alpha.numpy(), W.numpy(), b.numpy(), padding=3 * d, dilation=d)
+    check(y.cpu().numpy(), truth)
+
+
 def test_full_size_stage_vs_torch_fp32(S):
     """BASELINE's largest stage at full length, checked against cuDNN fp32
     (TF32 off) -- the oracle is too slow at 441k samples x 96 channels."""

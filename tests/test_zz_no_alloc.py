@@ -8,7 +8,10 @@ caller workspace.  These tests check that it agrees with the regular entry
 point (the workspace-taking sn_snake_conv1d behind fused_snake_conv1d) within
 the same tolerance the other Snake+Conv1d tests use, on two calls in a row
 with different weights -- the shared array must carry the second call's
-weights, not the first's -- and that oversized problems are refused.
+weights, not the first's -- that a call leaves the device's free memory
+unchanged, that shapes which need no scratch (they run the per-output
+kernel) are served whatever their size, and that oversized problems are
+refused.
 
 This file is collected last on purpose (tests/test_zz_*): a failure here does
 not hide any other test in a run that stops at the first failure.
@@ -34,12 +37,18 @@ def _case(C, T, seed):
     return x, alpha, W, b
 
 
-def _noalloc(lib, x, alpha, W, b, y, d):
+def _noalloc(lib, x, alpha, W, b, y, d, stride=1):
     B, Cin, T = x.shape
     Cout, _, K = W.shape
     return lib.sn_snake_conv1d_noalloc(x.data_ptr(), alpha.data_ptr(), W.data_ptr(), b.data_ptr(), y.data_ptr(), B,
-                                       Cin, Cout, T, K, 1, 3 * d, d, ctypes.c_float(1e-9),
+                                       Cin, Cout, T, K, stride, 3 * d, d, ctypes.c_float(1e-9),
                                        torch.cuda.current_stream().cuda_stream)
+
+
+def _close(y, ref):
+    err = (y - ref).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(y.flatten().double(), ref.flatten().double(), dim=0).item()
+    return err <= MAX_ABS and cos >= COS_MIN, (err, cos)
 
 
 def test_noalloc_matches_regular_entry_point_twice(cuda_lib):
@@ -51,10 +60,38 @@ def test_noalloc_matches_regular_entry_point_twice(cuda_lib):
         ref = S.fused_snake_conv1d(x, alpha, W, b, padding=3 * d, dilation=d)
         torch.cuda.synchronize()
         assert torch.isfinite(y).all()
-        err = (y - ref).abs().max().item()
-        cos = torch.nn.functional.cosine_similarity(y.flatten().double(), ref.flatten().double(), dim=0).item()
-        assert err <= MAX_ABS and cos >= COS_MIN, (call, err, cos)
+        ok, info = _close(y, ref)
+        assert ok, (call, info)
     assert cuda_lib.sn_device_status(1, None) == 0
+
+
+def test_noalloc_leaves_device_memory_unchanged(cuda_lib):
+    # every buffer exists before the measurement; a warm-up call first (the
+    # first call into the library on a device may load its device code)
+    x, alpha, W, b = _case(768, 3000, seed=7)
+    y = torch.empty_like(x)
+    assert _noalloc(cuda_lib, x, alpha, W, b, y, 1) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for d in (3, 9):
+        assert _noalloc(cuda_lib, x, alpha, W, b, y, d) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+
+
+def test_noalloc_serves_shapes_without_scratch(cuda_lib):
+    # stride 2 runs the per-output kernel, which reads W itself: 1024 x 1024 x 7
+    # is beyond the static array but needs none of it
+    from sonata_b200.kernels import fused_snake_conv as S
+    x, alpha, W, b = _case(1024, 96, seed=11)
+    Tout = S.conv1d_output_length(96, 7, stride=2, padding=3, dilation=1)
+    y = torch.full((1, 1024, Tout), float("nan"), device="cuda")
+    assert _noalloc(cuda_lib, x, alpha, W, b, y, 1, stride=2) == 0
+    ref = S.fused_snake_conv1d(x, alpha, W, b, stride=2, padding=3, dilation=1)
+    torch.cuda.synchronize()
+    ok, info = _close(y, ref)
+    assert ok, info
 
 
 def test_noalloc_refuses_problems_beyond_its_scratch(cuda_lib):
