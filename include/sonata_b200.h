@@ -244,6 +244,49 @@ int sn_snake_conv_transpose1d_pack(const float *W, int Cin, int Cout, int K, int
                                    size_t packed_bytes, void *stream);
 
 /*
+ * Strided variants for a streaming (cached-convolution) decoder, whose
+ * per-layer inputs and outputs are windows of larger buffers: x, y and
+ * residual take a batch stride (*_bs) and a channel-row stride (*_ld), in
+ * elements, with time contiguous (ld >= the row's length; batches must not
+ * overlap).  y must not overlap x or residual.  Otherwise
+ * sn_snake_conv1d_strided is sn_snake_conv1d_ex.
+ * sn_snake_conv_transpose1d_strided writes samples [0, Ty) of the transposed
+ * convolution with the given padding, for any 1 <= Ty <= (T - 1) * stride -
+ * padding + K: a streaming decoder passes [previous input frame | new frames]
+ * with padding = stride (+ the layer's own padding on the first chunk) and Ty
+ * = the samples whose input frames have all arrived.  No counterpart in the
+ * reference, which vocodes a stream by re-decoding overlapping windows
+ * (scripts/streaming.py:191-238); these replace that re-decode with
+ * per-convolution left-history caches (docs/dac_profile.md:42,86).
+ */
+int sn_snake_conv1d_strided(const float *x, int64_t x_bs, int64_t x_ld, const float *alpha, const float *W,
+                            const float *bias, const float *residual, int64_t r_bs, int64_t r_ld, float *y,
+                            int64_t y_bs, int64_t y_ld, int B, int Cin, int Cout, int T, int K, int stride,
+                            int padding, int dilation, float eps, int act, int post, unsigned flags, void *workspace,
+                            size_t workspace_bytes, void *stream);
+int sn_snake_conv_transpose1d_strided(const float *x, int64_t x_bs, int64_t x_ld, const float *alpha, const float *W,
+                                      const float *bias, float *y, int64_t y_bs, int64_t y_ld, int B, int Cin,
+                                      int Cout, int T, int K, int stride, int padding, int Ty, float eps,
+                                      unsigned flags, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * History move of a streaming decoder, for up to SN_SHIFT_MAX_DESCS layer
+ * buffers in one launch: in every row (batch b, channel c) of entry i,
+ * samples [src, src + len) move to [0, len) (len <= SN_SHIFT_MAX_LEN;
+ * overlapping ranges are fine).  The table is read on the host and passed by
+ * value, so it may be reused or freed as soon as the call returns.
+ */
+#define SN_SHIFT_MAX_DESCS 48
+#define SN_SHIFT_MAX_LEN 64
+typedef struct sn_shift_desc {
+  float *buf;
+  int64_t batch_stride, row_stride; /* elements */
+  int batches, rows;
+  int src, len;
+} sn_shift_desc;
+int sn_stream_shift(const sn_shift_desc *descs, int n, void *stream);
+
+/*
  * Allocation-free Snake + Conv1d.  No counterpart in the reference.
  *
  * For callers that must not allocate device memory at all: a host that runs

@@ -59,6 +59,11 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_selective_state_update": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
     "sn_rmsnorm_gated": ([_P, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _I, _P], _I),
     "sn_layer_norm_fused": ([_P, _P, _I, _P, _P, _P, _P, _I, _I, _I, ctypes.c_float, _I, _P], _I),
+    "sn_snake_conv1d_strided": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _P, _I64, _I64, _I, _I, _I, _I, _I, _I,
+                                 _I, _I, ctypes.c_float, _I, _I, _U, _P, ctypes.c_size_t, _P], _I),
+    "sn_snake_conv_transpose1d_strided": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I, _I, _I, _I,
+                                           _I, ctypes.c_float, _U, _P, ctypes.c_size_t, _P], _I),
+    "sn_stream_shift": ([_P, _I, _P], _I),
     "sn_snake1d": ([_P, _P, _P, _I, _I, _I64, ctypes.c_float, _P], _I),
     "sn_diag_bounded_wait": ([ctypes.c_uint64, _P], _I),
     "sn_snake_conv_transpose1d_pack": ([_P, _I, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
@@ -66,6 +71,17 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_snake_conv_transpose1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _U, _P,
                                    ctypes.c_size_t, _P], _I),
 }
+
+
+
+class ShiftDesc(ctypes.Structure):
+    """sn_shift_desc of include/sonata_b200.h."""
+    _fields_ = [("buf", ctypes.c_void_p), ("batch_stride", ctypes.c_int64), ("row_stride", ctypes.c_int64),
+                ("batches", ctypes.c_int), ("rows", ctypes.c_int), ("src", ctypes.c_int), ("len", ctypes.c_int)]
+
+
+SN_SHIFT_MAX_DESCS = 48
+SN_SHIFT_MAX_LEN = 64
 
 _lib = None
 

@@ -67,6 +67,10 @@ struct ScParams {
   // [B, Cy, Ty].  up_s == 0: plain convolution, column o, row t of y[b, o, t].
   int up_s, up_p, Cy, Ty;
   int up_vec;          // widest vector store (1, 2 or 4 floats) the phase runs of y allow
+  // element strides of the batch and channel (row) dimensions; time is
+  // contiguous.  Whole tensors: x (Cin * T, T), y and res (Cy * Ty, Ty); a
+  // streaming decoder passes windows of larger per-layer buffers.
+  int64_t x_bs, x_ld, y_bs, y_ld, r_bs, r_ld;
 };
 
 // Pull a tile's residual (GEMM rows t0 .. t0 + 127, columns o0 .. o0 + nt - 1)
@@ -75,11 +79,11 @@ struct ScParams {
 // threads (et = 0 .. 32 * kScEpilogueWarps - 1).
 __device__ __forceinline__ void sc_prefetch_res(const ScParams& p, int b, int t0, int o0, int et) {
   if (!p.res || p.up_s != 0) return;
-  const float* rb = p.res + static_cast<int64_t>(b) * p.Cy * p.Tout;
+  const float* rb = p.res + static_cast<int64_t>(b) * p.r_bs;
   for (int l = et; l < p.nt * 4; l += 32 * kScEpilogueWarps) {
     const int o = o0 + (l >> 2), t = t0 + 32 * (l & 3);
     if (o < p.Cy && t < p.Tout)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(rb + static_cast<int64_t>(o) * p.Tout + t));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(rb + static_cast<int64_t>(o) * p.r_ld + t));
   }
 }
 
@@ -111,10 +115,10 @@ __device__ __forceinline__ void sc_load_res16(const ScParams& p, int b, int t, i
 #pragma unroll
   for (int e = 0; e < 16; ++e) rv[e] = 0.f;
   if (p.res && p.up_s == 0 && t < p.Tout) {
-    const float* rb = p.res + static_cast<int64_t>(b) * p.Cy * p.Tout;
+    const float* rb = p.res + static_cast<int64_t>(b) * p.r_bs;
 #pragma unroll
     for (int e = 0; e < 16; ++e)
-      if (o_base + e < p.Cy) rv[e] = __ldg(rb + static_cast<int64_t>(o_base + e) * p.Tout + t);
+      if (o_base + e < p.Cy) rv[e] = __ldg(rb + static_cast<int64_t>(o_base + e) * p.r_ld + t);
   }
 }
 
@@ -139,7 +143,7 @@ __device__ __forceinline__ void sc_emit16_phases(const ScParams& p, float* yb, i
       w[r] = vv[g * S + r] + c.bv[g * S + r];
       if (p.post == SN_POST_TANH) w[r] = tanhf(w[r]);
     }
-    float* dst = yb + static_cast<int64_t>(o) * p.Ty + ty0;
+    float* dst = yb + static_cast<int64_t>(o) * p.y_ld + ty0;
     if constexpr (S % 4 == 0) {
       if (inside && p.up_vec == 4) {
 #pragma unroll
@@ -165,18 +169,18 @@ __device__ __forceinline__ void sc_emit16(const ScParams& p, int b, int t, int o
                                           const ScChunk& c) {
   if (t >= p.Tout) return;
   if constexpr (!UP) {
-    float* yb = p.y + static_cast<int64_t>(b) * p.Cy * p.Tout;
+    float* yb = p.y + static_cast<int64_t>(b) * p.y_bs;
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int o = o_base + e;
       if (o < p.Cy) {
         float v = vv[e] + c.bv[e] + c.rv[e];
         if (p.post == SN_POST_TANH) v = tanhf(v);
-        yb[static_cast<int64_t>(o) * p.Tout + t] = v;
+        yb[static_cast<int64_t>(o) * p.y_ld + t] = v;
       }
     }
   } else {
-    float* yb = p.y + static_cast<int64_t>(b) * p.Cy * p.Ty;
+    float* yb = p.y + static_cast<int64_t>(b) * p.y_bs;
     switch (p.up_s) {  // the DAC strides; o_base is a multiple of 16
       case 2: sc_emit16_phases<2>(p, yb, t, o_base, vv, c); return;
       case 4: sc_emit16_phases<4>(p, yb, t, o_base, vv, c); return;
@@ -192,7 +196,7 @@ __device__ __forceinline__ void sc_emit16(const ScParams& p, int b, int t, int o
         if (ty >= 0 && ty < p.Ty) {
           float v = vv[e] + c.bv[e];
           if (p.post == SN_POST_TANH) v = tanhf(v);
-          yb[static_cast<int64_t>(o) * p.Ty + ty] = v;
+          yb[static_cast<int64_t>(o) * p.y_ld + ty] = v;
         }
       }
     }
@@ -405,7 +409,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
     for (int j = 0; j < my_tiles; ++j) {
       int b, t0, o0;
       tile_coords(j, b, t0, o0);
-      const float* xb = p.x + static_cast<int64_t>(b) * p.Cin * p.T;
+      const float* xb = p.x + static_cast<int64_t>(b) * p.x_bs;
       const int tin0 = t0 - p.pad;  // input time of activation row 0
       for (int c = 0; c < nchunks; ++c, ++g) {
         const int ab = g & 1;
@@ -424,13 +428,13 @@ __global__ void __launch_bounds__(kScThreads, 1)
             ni0 = pw * 8;
           }
           const bool more = (c + 1 < nchunks) || (j + 1 < my_tiles);
-          const float* nxb = p.x + static_cast<int64_t>(nb) * p.Cin * p.T;
+          const float* nxb = p.x + static_cast<int64_t>(nb) * p.x_bs;
 #pragma unroll
           for (int k = lane; k < 8 * kMaxRowIters; k += 32) {
             const int e = k & 7, it = k >> 3;
             const int tin = max(nt0 + 32 * it, 0);
             if (more && ni0 + e < p.Cin && 32 * it < p.rows && tin < p.T)
-              asm volatile("prefetch.global.L2 [%0];" ::"l"(nxb + static_cast<int64_t>(ni0 + e) * p.T + tin));
+              asm volatile("prefetch.global.L2 [%0];" ::"l"(nxb + static_cast<int64_t>(ni0 + e) * p.x_ld + tin));
           }
         }
         // issue every x load of this chunk before the first use (memory-level
@@ -443,7 +447,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
           const bool in_t = r < p.rows && tin >= 0 && tin < p.T;
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.T + tin) : 0.f;
+            v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.x_ld + tin) : 0.f;
         }
         float al[8], inv[8];
 #pragma unroll
@@ -669,7 +673,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
     for (int j = 0; j < my_tiles; ++j) {
       int b, t0, o0;
       tile_coords(j, b, t0, o0);
-      const float* xb = p.x + static_cast<int64_t>(b) * p.Cin * p.T;
+      const float* xb = p.x + static_cast<int64_t>(b) * p.x_bs;
       const int tin0 = t0 - p.pad;
       for (int c = 0; c < nchunks; ++c, ++g) {
         const int ab = g & 1;
@@ -682,7 +686,7 @@ __global__ void __launch_bounds__(kScThreads, 1)
           const bool in_t = r < p.rows && tin >= 0 && tin < p.T;
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.T + tin) : 0.f;
+            v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.x_ld + tin) : 0.f;
         }
         float al[8], inv[8];
 #pragma unroll
@@ -836,12 +840,49 @@ __global__ void snake1d_kernel(const float* x, const float* __restrict__ alpha, 
   }
 }
 
+// Batch and row (channel) strides, in elements, of the fallback kernels'
+// x, y and residual tensors; time is contiguous.
+struct ScStrides {
+  int64_t x_bs, x_ld, y_bs, y_ld, r_bs, r_ld;
+};
+
+// The history move of a streaming decoder: for each table entry, every row
+// (batch b, channel c) keeps samples [src, src + len) of its buffer row by
+// moving them to [0, len).  One warp per row loads the kept samples into
+// registers before storing any, so overlapping ranges move correctly.
+struct ShiftTable {
+  sn_shift_desc d[SN_SHIFT_MAX_DESCS];
+  int64_t first_row[SN_SHIFT_MAX_DESCS];
+  int64_t total_rows;
+  int n;
+};
+
+__global__ void stream_shift_kernel(const __grid_constant__ ShiftTable tab) {
+  static_assert(SN_SHIFT_MAX_LEN <= 64, "two samples a lane");
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); row < tab.total_rows;
+       row += warps) {
+    int i = 0;
+    while (i + 1 < tab.n && tab.first_row[i + 1] <= row) ++i;
+    const sn_shift_desc& d = tab.d[i];
+    const int64_t r = row - tab.first_row[i];
+    const int64_t b = r / d.rows, c = r - b * d.rows;
+    float* base = d.buf + b * d.batch_stride + c * d.row_stride;
+    const float v0 = lane < d.len ? base[d.src + lane] : 0.f;
+    const float v1 = lane + 32 < d.len ? base[d.src + lane + 32] : 0.f;
+    __syncwarp();
+    if (lane < d.len) base[lane] = v0;
+    if (lane + 32 < d.len) base[lane + 32] = v1;
+  }
+}
+
 // Fallback: one thread per output element, the reference's loop order.
 __global__ void snake_conv_simt_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
                                        const float* __restrict__ W, const float* __restrict__ bias,
                                        const float* __restrict__ res, float* __restrict__ y, int B, int Cin,
                                        int Cout, int T, int Tout, int K, int stride, int pad, int dil, float eps,
-                                       int act, int post) {
+                                       int act, int post, ScStrides ss) {
   const int64_t total = static_cast<int64_t>(B) * Cout * Tout;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -853,7 +894,7 @@ __global__ void snake_conv_simt_kernel(const float* __restrict__ x, const float*
     for (int i = 0; i < Cin; ++i) {
       const float a = act == SN_ACT_SNAKE ? alpha[i] : 0.f;
       const float inv = 1.0f / (a + eps);
-      const float* xr = x + (static_cast<int64_t>(b) * Cin + i) * T;
+      const float* xr = x + b * ss.x_bs + i * ss.x_ld;
       const float* wr = W + (static_cast<int64_t>(o) * Cin + i) * K;
       for (int k = 0; k < K; ++k) {
         const int ti = t * stride - pad + k * dil;
@@ -861,9 +902,9 @@ __global__ void snake_conv_simt_kernel(const float* __restrict__ x, const float*
         acc = fmaf(sc_act(act, xr[ti], a, inv), wr[k], acc);
       }
     }
-    if (res) acc += res[e];
+    if (res) acc += res[b * ss.r_bs + o * ss.r_ld + t];
     if (post == SN_POST_TANH) acc = tanhf(acc);
-    y[e] = acc;
+    y[b * ss.y_bs + o * ss.y_ld + t] = acc;
   }
 }
 
@@ -872,7 +913,7 @@ __global__ void snake_conv_simt_kernel(const float* __restrict__ x, const float*
 __global__ void snake_convt_simt_kernel(const float* __restrict__ x, const float* __restrict__ alpha,
                                         const float* __restrict__ W, const float* __restrict__ bias,
                                         float* __restrict__ y, int B, int Cin, int Cout, int T, int Tout, int K,
-                                        int stride, int pad, float eps) {
+                                        int stride, int pad, float eps, ScStrides ss) {
   const int64_t total = static_cast<int64_t>(B) * Cout * Tout;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -884,7 +925,7 @@ __global__ void snake_convt_simt_kernel(const float* __restrict__ x, const float
     for (int i = 0; i < Cin; ++i) {
       const float a = alpha[i];
       const float inv = 1.0f / (a + eps);
-      const float* xr = x + (static_cast<int64_t>(b) * Cin + i) * T;
+      const float* xr = x + b * ss.x_bs + i * ss.x_ld;
       const float* wr = W + (static_cast<int64_t>(i) * Cout + o) * K;
       for (int k = 0; k < K; ++k) {
         const int num = t + pad - k;  // j * stride
@@ -894,7 +935,7 @@ __global__ void snake_convt_simt_kernel(const float* __restrict__ x, const float
         acc = fmaf(sc_act(SN_ACT_SNAKE, xr[j], a, inv), wr[k], acc);
       }
     }
-    y[e] = acc;
+    y[b * ss.y_bs + o * ss.y_ld + t] = acc;
   }
 }
 
@@ -1089,10 +1130,22 @@ int sn_snake_conv_transpose1d_pack(const float* W, int Cin, int Cout, int K, int
                     stride);
 }
 
-int sn_snake_conv1d_ex(const float* x, const float* alpha, const float* W, const float* bias, const float* residual,
-                       float* y, int B, int Cin, int Cout, int T, int K, int stride, int padding, int dilation,
-                       float eps, int act, int post, unsigned flags, void* workspace, size_t workspace_bytes,
-                       void* stream) {
+}  // extern "C"
+
+namespace sn {
+namespace {
+
+// Row (channel) strides must keep rows apart: ld >= len, and batch strides
+// must keep batches apart.
+bool strides_ok(int64_t bs, int64_t ld, int B, int C, int64_t len) {
+  return ld >= len && (B == 1 || bs >= (static_cast<int64_t>(C) - 1) * ld + len) && bs >= 0;
+}
+
+int snake_conv1d_impl(const float* x, int64_t x_bs, int64_t x_ld, const float* alpha, const float* W,
+                      const float* bias, const float* residual, int64_t r_bs, int64_t r_ld, float* y, int64_t y_bs,
+                      int64_t y_ld, int B, int Cin, int Cout, int T, int K, int stride, int padding, int dilation,
+                      float eps, int act, int post, unsigned flags, void* workspace, size_t workspace_bytes,
+                      void* stream) {
   if (!x || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0 ||
       dilation < 1)
     return SN_ERR_INVALID_ARGUMENT;
@@ -1104,11 +1157,14 @@ int sn_snake_conv1d_ex(const float* x, const float* alpha, const float* W, const
   const int64_t tout64 = sn_snake_conv1d_output_length(T, K, stride, padding, dilation);
   if (tout64 < 1 || tout64 > (int64_t(1) << 31) - 1) return SN_ERR_INVALID_ARGUMENT;
   const int Tout = static_cast<int>(tout64);
+  if (!strides_ok(x_bs, x_ld, B, Cin, T) || !strides_ok(y_bs, y_ld, B, Cout, Tout) ||
+      (residual && !strides_ok(r_bs, r_ld, B, Cout, Tout)))
+    return SN_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int Cg = (Cout + 15) / 16 * 16;  // GEMM width: zero weight rows past Cout
-  if (sn::fast_path_ok(Cin, Cg, K, stride, dilation, Tout) && workspace &&
-      workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && sn::aligned16(workspace)) {
-    sn::ScParams p = sn::base_params(x, alpha, bias, y, B, Cin, eps);
+  if (fast_path_ok(Cin, Cg, K, stride, dilation, Tout) && workspace &&
+      workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && aligned16(workspace)) {
+    ScParams p = base_params(x, alpha, bias, y, B, Cin, eps);
     p.Cout = Cg;
     p.T = T;
     p.Tout = Tout;
@@ -1120,26 +1176,112 @@ int sn_snake_conv1d_ex(const float* x, const float* alpha, const float* W, const
     p.post = post;
     p.Cy = Cout;
     p.Ty = Tout;
+    p.x_bs = x_bs;
+    p.x_ld = x_ld;
+    p.y_bs = y_bs;
+    p.y_ld = y_ld;
+    p.r_bs = r_bs;
+    p.r_ld = r_ld;
     __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
-    const int rc = sn::snake_fast(p, Wp, st, [&] {
+    const int rc = snake_fast(p, Wp, st, [&] {
       if (prepacked) return static_cast<int>(SN_OK);
       const int64_t tot = static_cast<int64_t>(Cg) * Cin;
-      return sn::launch(sn::pack_weights_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0, st, false, W, Wp, Cout,
-                        Cin, K, Cg);
+      return launch(pack_weights_kernel, dim3(blocks_for(tot, 8)), dim3(256), 0, st, false, W, Wp, Cout, Cin, K,
+                    Cg);
     });
     if (rc != SN_ERR_UNSUPPORTED) return rc;
   }
   const int64_t total = static_cast<int64_t>(B) * Cout * Tout;
-  return sn::launch(sn::snake_conv_simt_kernel, dim3(sn::blocks_for(total, 32)), dim3(256), 0, st, false, x, alpha,
-                    W, bias, residual, y, B, Cin, Cout, T, Tout, K, stride, padding, dilation, eps, act, post);
+  const ScStrides ss = {x_bs, x_ld, y_bs, y_ld, r_bs, r_ld};
+  return launch(snake_conv_simt_kernel, dim3(blocks_for(total, 32)), dim3(256), 0, st, false, x, alpha, W, bias,
+                residual, y, B, Cin, Cout, T, Tout, K, stride, padding, dilation, eps, act, post, ss);
 }
 
-int sn_snake1d(const float* x, const float* alpha, float* y, int B, int C, int64_t T, float eps, void* stream) {
-  if (!x || !alpha || !y || B < 1 || C < 1 || T < 1) return SN_ERR_INVALID_ARGUMENT;
-  const int64_t rows = static_cast<int64_t>(B) * C;
-  const bool vec = T % 4 == 0 && sn::aligned16(x) && sn::aligned16(y);
-  return sn::launch(sn::snake1d_kernel, dim3(sn::blocks_for(rows * ((T + 3) / 4), 16)), dim3(256), 0,
-                    static_cast<cudaStream_t>(stream), false, x, alpha, y, rows, T, C, eps, vec);
+// Transposed convolution writing output samples [0, Ty) of the full
+// ConvTranspose1d (whose own length would be (T - 1) * stride - 2 * padding + K):
+// Ty may be shorter (a streaming decoder emits only the samples whose inputs
+// have all arrived) or longer up to (T - 1) * stride - padding + K.
+int snake_convt_impl(const float* x, int64_t x_bs, int64_t x_ld, const float* alpha, const float* W,
+                     const float* bias, float* y, int64_t y_bs, int64_t y_ld, int B, int Cin, int Cout, int T, int K,
+                     int stride, int padding, int Ty, float eps, unsigned flags, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (!x || !alpha || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0 ||
+      Ty < 1)
+    return SN_ERR_INVALID_ARGUMENT;
+  if (flags & ~SN_FLAG_PREPACKED) return SN_ERR_INVALID_ARGUMENT;
+  if (static_cast<int64_t>(Ty) > (static_cast<int64_t>(T) - 1) * stride - padding + K) return SN_ERR_INVALID_ARGUMENT;
+  if (!strides_ok(x_bs, x_ld, B, Cin, T) || !strides_ok(y_bs, y_ld, B, Cout, Ty)) return SN_ERR_INVALID_ARGUMENT;
+  const bool prepacked = (flags & SN_FLAG_PREPACKED) != 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // polyphase GEMM: m = K / s taps per phase over rows q in [0, T + m - 1);
+  // row q holds output samples s * q + r - padding, so rows past the one that
+  // holds sample Ty - 1 are not computed
+  const int m = (K % stride == 0) ? K / stride : 0;
+  const int64_t gcols = static_cast<int64_t>(Cout) * stride;
+  const int64_t rows = std::min<int64_t>(static_cast<int64_t>(T) + m - 1,
+                                         (static_cast<int64_t>(Ty) - 1 + padding) / stride + 1);
+  if (m >= 1 && gcols <= INT32_MAX && rows <= INT32_MAX &&
+      fast_path_ok(Cin, static_cast<int>(gcols), m, 1, 1, static_cast<int>(rows)) && workspace &&
+      workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && aligned16(workspace)) {
+    ScParams p = base_params(x, alpha, bias, y, B, Cin, eps);
+    p.Cout = static_cast<int>(gcols);
+    p.T = T;
+    p.Tout = static_cast<int>(rows);
+    p.K = m;
+    p.pad = m - 1;
+    p.dil = 1;
+    p.up_s = stride;
+    p.up_p = padding;
+    p.Cy = Cout;
+    p.Ty = Ty;
+    p.x_bs = x_bs;
+    p.x_ld = x_ld;
+    p.y_bs = y_bs;
+    p.y_ld = y_ld;
+    // phase runs start at stride * q - padding: vector stores when that and
+    // every row start keep 16 (8) byte alignment
+    const uintptr_t ya = reinterpret_cast<uintptr_t>(y);
+    p.up_vec = (stride % 4 == 0 && padding % 4 == 0 && y_ld % 4 == 0 && y_bs % 4 == 0 && ya % 16 == 0)   ? 4
+               : (stride % 2 == 0 && padding % 2 == 0 && y_ld % 2 == 0 && y_bs % 2 == 0 && ya % 8 == 0) ? 2
+                                                                                                        : 1;
+    __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
+    const int rc = snake_fast(p, Wp, st, [&] {
+      if (prepacked) return static_cast<int>(SN_OK);
+      const int64_t tot = static_cast<int64_t>(Cin) * Cout;
+      return launch(pack_weights_t_kernel, dim3(blocks_for(tot, 8)), dim3(256), 0, st, false, W, Wp, Cin, Cout, K,
+                    stride);
+    });
+    if (rc != SN_ERR_UNSUPPORTED) return rc;
+  }
+  const int64_t total = static_cast<int64_t>(B) * Cout * Ty;
+  const ScStrides ss = {x_bs, x_ld, y_bs, y_ld, 0, 0};
+  return launch(snake_convt_simt_kernel, dim3(blocks_for(total, 32)), dim3(256), 0, st, false, x, alpha, W, bias, y,
+                B, Cin, Cout, T, Ty, K, stride, padding, eps, ss);
+}
+
+}  // namespace
+}  // namespace sn
+
+extern "C" {
+
+int sn_snake_conv1d_ex(const float* x, const float* alpha, const float* W, const float* bias, const float* residual,
+                       float* y, int B, int Cin, int Cout, int T, int K, int stride, int padding, int dilation,
+                       float eps, int act, int post, unsigned flags, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  const int64_t tout = sn_snake_conv1d_output_length(T, K, stride, padding, dilation);
+  if (tout < 1 || T < 1 || Cin < 1 || Cout < 1) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t xb = static_cast<int64_t>(Cin) * T, yb = static_cast<int64_t>(Cout) * tout;
+  return sn::snake_conv1d_impl(x, xb, T, alpha, W, bias, residual, yb, tout, y, yb, tout, B, Cin, Cout, T, K, stride,
+                               padding, dilation, eps, act, post, flags, workspace, workspace_bytes, stream);
+}
+
+int sn_snake_conv1d_strided(const float* x, int64_t x_bs, int64_t x_ld, const float* alpha, const float* W,
+                            const float* bias, const float* residual, int64_t r_bs, int64_t r_ld, float* y,
+                            int64_t y_bs, int64_t y_ld, int B, int Cin, int Cout, int T, int K, int stride,
+                            int padding, int dilation, float eps, int act, int post, unsigned flags, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  return sn::snake_conv1d_impl(x, x_bs, x_ld, alpha, W, bias, residual, r_bs, r_ld, y, y_bs, y_ld, B, Cin, Cout, T, K,
+                               stride, padding, dilation, eps, act, post, flags, workspace, workspace_bytes, stream);
 }
 
 int64_t sn_snake_conv_transpose1d_output_length(int64_t T, int K, int stride, int padding) {
@@ -1150,49 +1292,49 @@ int64_t sn_snake_conv_transpose1d_output_length(int64_t T, int K, int stride, in
 int sn_snake_conv_transpose1d(const float* x, const float* alpha, const float* W, const float* bias, float* y, int B,
                               int Cin, int Cout, int T, int K, int stride, int padding, float eps, unsigned flags,
                               void* workspace, size_t workspace_bytes, void* stream) {
-  if (!x || !alpha || !W || !y || B < 1 || Cin < 1 || Cout < 1 || T < 1 || K < 1 || stride < 1 || padding < 0)
-    return SN_ERR_INVALID_ARGUMENT;
-  if (flags & ~SN_FLAG_PREPACKED) return SN_ERR_INVALID_ARGUMENT;
-  const bool prepacked = (flags & SN_FLAG_PREPACKED) != 0;
   const int64_t ty64 = sn_snake_conv_transpose1d_output_length(T, K, stride, padding);
-  if (ty64 < 1 || ty64 > (int64_t(1) << 31) - 1) return SN_ERR_INVALID_ARGUMENT;
-  const int Ty = static_cast<int>(ty64);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // polyphase GEMM: m = K / s taps per phase over rows q in [0, T + m - 1)
-  const int m = (K % stride == 0) ? K / stride : 0;
-  const int64_t gcols = static_cast<int64_t>(Cout) * stride;
-  if (m >= 1 && gcols <= INT32_MAX && static_cast<int64_t>(T) + m - 1 <= INT32_MAX &&
-      sn::fast_path_ok(Cin, static_cast<int>(gcols), m, 1, 1, T + m - 1) && workspace &&
-      workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && sn::aligned16(workspace)) {
-    sn::ScParams p = sn::base_params(x, alpha, bias, y, B, Cin, eps);
-    p.Cout = static_cast<int>(gcols);
-    p.T = T;
-    p.Tout = T + m - 1;
-    p.K = m;
-    p.pad = m - 1;
-    p.dil = 1;
-    p.up_s = stride;
-    p.up_p = padding;
-    p.Cy = Cout;
-    p.Ty = Ty;
-    // phase runs start at stride * q - padding: vector stores when that, Ty
-    // and y keep 16 (8) byte alignment
-    const uintptr_t ya = reinterpret_cast<uintptr_t>(y);
-    p.up_vec = (stride % 4 == 0 && padding % 4 == 0 && Ty % 4 == 0 && ya % 16 == 0)   ? 4
-               : (stride % 2 == 0 && padding % 2 == 0 && Ty % 2 == 0 && ya % 8 == 0) ? 2
-                                                                                       : 1;
-    __nv_bfloat16* Wp = static_cast<__nv_bfloat16*>(workspace);
-    const int rc = sn::snake_fast(p, Wp, st, [&] {
-      if (prepacked) return static_cast<int>(SN_OK);
-      const int64_t tot = static_cast<int64_t>(Cin) * Cout;
-      return sn::launch(sn::pack_weights_t_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0, st, false, W, Wp, Cin,
-                        Cout, K, stride);
-    });
-    if (rc != SN_ERR_UNSUPPORTED) return rc;
+  if (ty64 < 1 || ty64 > (int64_t(1) << 31) - 1 || Cin < 1 || Cout < 1) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t xb = static_cast<int64_t>(Cin) * T, yb = static_cast<int64_t>(Cout) * ty64;
+  return sn::snake_convt_impl(x, xb, T, alpha, W, bias, y, yb, ty64, B, Cin, Cout, T, K, stride, padding,
+                              static_cast<int>(ty64), eps, flags, workspace, workspace_bytes, stream);
+}
+
+int sn_snake_conv_transpose1d_strided(const float* x, int64_t x_bs, int64_t x_ld, const float* alpha, const float* W,
+                                      const float* bias, float* y, int64_t y_bs, int64_t y_ld, int B, int Cin,
+                                      int Cout, int T, int K, int stride, int padding, int Ty, float eps,
+                                      unsigned flags, void* workspace, size_t workspace_bytes, void* stream) {
+  return sn::snake_convt_impl(x, x_bs, x_ld, alpha, W, bias, y, y_bs, y_ld, B, Cin, Cout, T, K, stride, padding, Ty,
+                              eps, flags, workspace, workspace_bytes, stream);
+}
+
+int sn_snake1d(const float* x, const float* alpha, float* y, int B, int C, int64_t T, float eps, void* stream) {
+  if (!x || !alpha || !y || B < 1 || C < 1 || T < 1) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t rows = static_cast<int64_t>(B) * C;
+  const bool vec = T % 4 == 0 && sn::aligned16(x) && sn::aligned16(y);
+  return sn::launch(sn::snake1d_kernel, dim3(sn::blocks_for(rows * ((T + 3) / 4), 16)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, x, alpha, y, rows, T, C, eps, vec);
+}
+
+int sn_stream_shift(const sn_shift_desc* descs, int n, void* stream) {
+  if (!descs || n < 1 || n > SN_SHIFT_MAX_DESCS) return SN_ERR_INVALID_ARGUMENT;
+  sn::ShiftTable tab = {};
+  int64_t rows = 0;
+  for (int i = 0; i < n; ++i) {
+    const sn_shift_desc& d = descs[i];
+    if (!d.buf || d.batches < 1 || d.rows < 1 || d.src < 0 || d.len < 0 || d.len > SN_SHIFT_MAX_LEN ||
+        d.row_stride < static_cast<int64_t>(d.src) + d.len ||
+        (d.batches > 1 && d.batch_stride < static_cast<int64_t>(d.rows) * d.row_stride))
+      return SN_ERR_INVALID_ARGUMENT;
+    tab.d[i] = d;
+    tab.first_row[i] = rows;
+    rows += static_cast<int64_t>(d.batches) * d.rows;
   }
-  const int64_t total = static_cast<int64_t>(B) * Cout * Ty;
-  return sn::launch(sn::snake_convt_simt_kernel, dim3(sn::blocks_for(total, 32)), dim3(256), 0, st, false, x, alpha,
-                    W, bias, y, B, Cin, Cout, T, Ty, K, stride, padding, eps);
+  tab.n = n;
+  tab.total_rows = rows;
+  const int warps_per_block = 8;
+  const int64_t blocks = std::min<int64_t>((rows + warps_per_block - 1) / warps_per_block, 148 * 16);
+  return sn::launch(sn::stream_shift_kernel, dim3(static_cast<unsigned>(std::max<int64_t>(blocks, 1))),
+                    dim3(32 * warps_per_block), 0, static_cast<cudaStream_t>(stream), false, tab);
 }
 
 // ---------------------------------------------------------------------------
