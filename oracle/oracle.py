@@ -426,6 +426,93 @@ def selective_state_update_ref(state, x, dt, A, B, C, D=None, z=None, dt_bias=No
     return y, st
 
 
+def bf16_round(v) -> np.ndarray:
+    """Round to the nearest bf16 value (ties to even), returned as float64."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(v, np.float32))).astype(np.float64)
+
+
+def rotary_ref(x, pos: int, base: float = 10000.0):
+    """Non-interleaved rotary embedding over the last dimension (the halves
+    rotate by angle pos / base**(2i / D)), mamba_ssm MHA's decode rotary."""
+    x = np.asarray(x, np.float64)
+    D = x.shape[-1]
+    inv = 1.0 / (base ** (np.arange(0, D, 2, dtype=np.float64) / D))
+    c, s = np.cos(pos * inv), np.sin(pos * inv)
+    x1, x2 = x[..., :D // 2], x[..., D // 2:]
+    return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1)
+
+
+def gqa_attention_ref(q, k, v):
+    """One query per head over a cache: q [b, hq, d], k / v [b, hk, L, d],
+    query head h reads KV head h // (hq / hk); softmax(q.k / sqrt(d)).v."""
+    q, k, v = (np.asarray(t, np.float64) for t in (q, k, v))
+    hq, hk = q.shape[1], k.shape[1]
+    k = np.repeat(k, hq // hk, axis=1)
+    v = np.repeat(v, hq // hk, axis=1)
+    sc = np.einsum("bhd,bhld->bhl", q, k) / np.sqrt(q.shape[-1])
+    sc = np.exp(sc - sc.max(axis=-1, keepdims=True))
+    sc /= sc.sum(axis=-1, keepdims=True)
+    return np.einsum("bhl,bhld->bhd", sc, v)
+
+
+def zonos_decode_step_ref(p: dict, hidden, cfg: dict) -> np.ndarray:
+    """One Zonos-hybrid decode token (mamba_ssm Block / Mamba2.step / MHA
+    decode / GatedMLP, the layout of the reference's docs/architecture.md:
+    5-30, 138-236) restated with the float64 op restatements above, rounding
+    to bf16 wherever the bf16 model stores a tensor.  p: per-layer numpy
+    arrays and states (``L{i}.*``), ``norm_f_w`` / ``norm_f_b``, ``head_W``
+    [ncb, d, vocab]; cfg: d_inner, d_state, nheads, headdim, conv_dim,
+    num_heads, num_heads_kv, head_dim, attn_layer_idx, n_layer, pos, eps.
+    Returns fp64 logits [ncb, batch, vocab]; states in p are not modified."""
+    r = bf16_round
+    eps = cfg["eps"]
+    h = r(hidden)
+    res = None
+    b = h.shape[0]
+    di, ds, nh, hdim = cfg["d_inner"], cfg["d_state"], cfg["nheads"], cfg["headdim"]
+    for i in range(cfg["n_layer"]):
+        L = lambda k: p[f"L{i}.{k}"]
+        out, hres = layer_norm_fn_ref(h, L("norm_w"), L("norm_b"), res, eps)
+        h, res = r(out), r(hres)
+        if i in cfg["attn_layer_idx"]:
+            hq, hk, hd = cfg["num_heads"], cfg["num_heads_kv"], cfg["head_dim"]
+            qkv = r(h @ L("in_proj").T)
+            q = r(rotary_ref(qkv[:, :hq * hd].reshape(b, hq, hd), cfg["pos"]))
+            k = r(rotary_ref(qkv[:, hq * hd:(hq + hk) * hd].reshape(b, hk, hd), cfg["pos"]))
+            v = qkv[:, (hq + hk) * hd:].reshape(b, hk, hd)
+            pos = cfg["pos"]
+            kc = L("k_cache")[:, :, :pos + 1].copy()
+            vc = L("v_cache")[:, :, :pos + 1].copy()
+            kc[:, :, pos] = k
+            vc[:, :, pos] = v
+            o = r(gqa_attention_ref(q, kc, vc)).reshape(b, hq * hd)
+            h = r(o @ L("out_proj").T)
+            out, hres = layer_norm_fn_ref(h, L("norm2_w"), L("norm2_b"), res, eps)
+            h, res = r(out), r(hres)
+            f = r(h @ L("fc1").T)
+            d = f.shape[1] // 2
+            y = r(f[:, :d] * r(_silu(f[:, d:])))
+            h = r(y @ L("fc2").T)
+        else:
+            zx = r(h @ L("in_proj").T)
+            cd = cfg["conv_dim"]
+            z, xBC, dt = zx[:, :di], zx[:, di:di + cd], zx[:, di + cd:]
+            y, _ = causal_conv1d_update_ref(xBC, L("conv_state"), L("conv_w"), L("conv_b"), "silu")
+            xBC = r(y)
+            x = xBC[:, :di].reshape(b, nh, hdim)
+            Bm = xBC[:, di:di + ds].reshape(b, 1, ds)
+            Cm = xBC[:, di + ds:].reshape(b, 1, ds)
+            dt_e = np.repeat(dt[:, :, None], hdim, axis=2)
+            y, _ = selective_state_update_ref(L("ssm_state"), x, dt_e, L("A"), Bm, Cm, D=L("D_e"), z=None,
+                                              dt_bias=L("dt_bias_e"), dt_softplus=True)
+            y = r(y).reshape(b, di)
+            y = r(rmsnorm_gated_ref(y, L("norm_mix_w"), None, z, eps, di, norm_before_gate=False))
+            h = r(y @ L("out_proj").T)
+    out, _ = layer_norm_fn_ref(h, p["norm_f_w"], p["norm_f_b"], res, eps)
+    hf = r(out)
+    return np.einsum("bk,ckn->cbn", hf, np.asarray(p["head_W"], np.float64))
+
+
 def cosine(a: np.ndarray, b: np.ndarray) -> float:
     a = np.asarray(a, np.float64).ravel()
     b = np.asarray(b, np.float64).ravel()

@@ -149,6 +149,24 @@ class DacDecoder:
         return f * batch
 
 
+def decoder_bytes(dec: "DacDecoder", T0: int, batch: int = 1) -> int:
+    """Algorithmic HBM bytes of one forward: every launch reads its fp32
+    input (and residual) and writes its fp32 output once, and reads its
+    packed weights (bf16 hi + lo, 4 bytes per weight) once."""
+    cfg = dec.config
+    C = cfg["decoder_hidden_size"]
+    T = T0
+    elems = cfg["hidden_size"] * T + C * T  # stem in, out
+    for i, s in enumerate(cfg["upsampling_ratios"]):
+        cin, cout = C // 2 ** i, C // 2 ** (i + 1)
+        elems += cin * T + cout * T * s  # ConvTranspose in, out
+        T *= s
+        elems += 3 * 5 * cout * T  # per unit: k7 in, out; k1 in, residual, out
+    elems += (C // 2 ** len(cfg["upsampling_ratios"])) * T + T  # output conv in, out
+    weights = sum(v.numel() for k, v in dec.p.items() if k.endswith("weight"))
+    return 4 * batch * elems + 4 * weights
+
+
 def dac_residual_unit(x: torch.Tensor, alpha1, w1, b1, alpha2, w2, b2, dilation: int, stream=None) -> torch.Tensor:
     """x + conv2(snake2(conv1(snake1(x)))) (transformers DacResidualUnit):
     two launches, the residual add fused into the second's epilogue."""
@@ -178,6 +196,7 @@ def bench_dac_decoder(warmup: int = 2, reps: int = 3, frames: int = 862, seed: i
     hop = math.prod(cfg["upsampling_ratios"])
     seconds = frames * hop / 44100.0
     flops = dec.flops(frames)
+    nbytes = decoder_bytes(dec, frames)
     if not torch.isfinite(audio).all():
         raise RuntimeError("DAC decoder produced non-finite audio")
     return {
@@ -188,6 +207,9 @@ def bench_dac_decoder(warmup: int = 2, reps: int = 3, frames: int = 862, seed: i
         "audio_seconds": round(seconds, 3),
         "realtime_factor": round(seconds / (us * 1e-6), 1),
         "useful_tflops": round(flops / (us * 1e-6) / 1e12, 1),
+        "mma_tflops": round(3 * flops / (us * 1e-6) / 1e12, 1),
+        "bytes": nbytes,
+        "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
         "workload": "full 44.1 kHz DAC decoder (transformers DacDecoder layout): stem conv 1024->1536 k7, 4 blocks of "
                     "Snake+ConvTranspose1d (strides 8,8,4,2) and 3 residual units (Snake+Conv1d k7 d=1,3,9, "
                     "Snake+Conv1d k1 + residual), Snake+Conv1d 96->1 k7 + tanh; synthetic weights, fp32 in/out",

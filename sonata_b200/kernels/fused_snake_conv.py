@@ -315,6 +315,47 @@ def stream_flops(streams=1):
     return sum(2 * C * C * 7 * T * len(DAC_DILATIONS) for C, T in DAC_STAGES) * streams
 
 
+def stream_bytes(streams=1):
+    """Algorithmic HBM bytes of the 12 units: fp32 x read and y written per
+    stream, fp32 weights read once per unit."""
+    return sum((8 * C * T * streams + 4 * 7 * C * C) * len(DAC_DILATIONS) for C, T in DAC_STAGES)
+
+
+def bench_snake_then_cudnn(warmup=1, reps=2, streams=1):
+    """The baseline the reference judged its fused kernel against
+    (kernels/bench_snake_conv.py:27-58): Snake as torch elementwise ops, then
+    cuDNN fp32 Conv1d (reference_snake_conv1d on the GPU), TF32 off, over the
+    same 12 units; microseconds per second of audio."""
+    units = []
+    for si, (C, T) in enumerate(DAC_STAGES):
+        units.append(dac_stage_inputs(C, T, streams=streams, seed=si))
+    prev = (torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32)
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        def one_pass():
+            for x, alpha, W, b in units:
+                for d in DAC_DILATIONS:
+                    reference_snake_conv1d(x, alpha, W, b, padding=3 * d, dilation=d)
+
+        for _ in range(warmup):
+            one_pass()
+        torch.cuda.synchronize()
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            one_pass()
+        e.record()
+        torch.cuda.synchronize()
+    finally:
+        torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32 = prev
+    us = a.elapsed_time(e) * 1e3 / reps
+    return {"us_per_audio_second": round(us / (AUDIO_SECONDS * streams), 2), "us_per_pass": round(us, 1),
+            "useful_tflops": round(stream_flops(streams) / (us * 1e-6) / 1e12, 1),
+            "what": "Snake as torch ops then cuDNN fp32 Conv1d (TF32 off), the reference's own GPU baseline "
+                    "(kernels/bench_snake_conv.py), same 12 units"}
+
+
 def bench_dac_stream(warmup=2, reps=3, streams=1):
     """Microseconds per second of audio for `streams` independent streams.
 
@@ -351,6 +392,8 @@ def bench_dac_stream(warmup=2, reps=3, streams=1):
         "realtime_factor": round(AUDIO_SECONDS * streams / (us * 1e-6), 1),
         "useful_tflops": round(flops / (us * 1e-6) / 1e12, 1),
         "mma_tflops": round(3 * flops / (us * 1e-6) / 1e12, 1),
+        "bytes": stream_bytes(streams),
+        "gbs": round(stream_bytes(streams) / (us * 1e-6) / 1e9, 1),
         "workload": "BASELINE config 5: stages (768,6896) (384,55168) (192,220672) (96,441344) x dilations 1,3,9, "
                     "k=7 'same', fp32 in/out, bf16x3 split-precision tcgen05",
         "launches_per_pass": 2 * len(DAC_STAGES) * len(DAC_DILATIONS),

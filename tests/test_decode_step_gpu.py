@@ -1,0 +1,139 @@
+"""A Zonos-hybrid decode step through the patched Linears, against the oracle.
+
+SyntheticZonos has the Zonos backbone's module names and shapes; after
+``patch_zonos_projections(model, include_attn=True)`` (the reference's
+drop-in call) one token runs the repository's GEMV, Mamba2-op and codebook
+head kernels with the attention, rotary and SwiGLU torch ops between them.
+The logits are compared with the float64 op restatements chained on the CPU
+(oracle.zonos_decode_step_ref, bf16 rounding wherever the model stores bf16);
+the CUDA-graph replay of the step must equal the eager step bit for bit and
+must recompute when the input changes (the reference's empty-graph tripwire,
+kernels/bench_decode.py:114-121).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def _model(n_layer=6, attn=(0, 4), batch=2, seed=5):
+    from sonata_b200.kernels import decode_step as DS
+    cfg = DS.ZonosBackboneConfig(n_layer=n_layer, attn_layer_idx=list(attn))
+    m = DS.SyntheticZonos(cfg, batch=batch, context=40, max_seqlen=64, seed=seed)
+    g = torch.Generator(device="cuda").manual_seed(seed + 100)
+    for blk in m.backbone.layers:  # non-trivial recurrent state
+        if not blk.is_attn:
+            blk.mixer.conv_state.copy_(torch.randn(blk.mixer.conv_state.shape, device="cuda", generator=g))
+            blk.mixer.ssm_state.copy_(0.5 * torch.randn(blk.mixer.ssm_state.shape, device="cuda", generator=g))
+    return m
+
+
+def _snapshot(m):
+    p, st = {}, {}
+    for i, blk in enumerate(m.backbone.layers):
+        pre = f"L{i}."
+        p[pre + "norm_w"], p[pre + "norm_b"] = _np(blk.norm_w), _np(blk.norm_b)
+        p[pre + "in_proj"], p[pre + "out_proj"] = _np(blk.mixer.in_proj.weight), _np(blk.mixer.out_proj.weight)
+        if blk.is_attn:
+            p[pre + "norm2_w"], p[pre + "norm2_b"] = _np(blk.norm2_w), _np(blk.norm2_b)
+            p[pre + "fc1"], p[pre + "fc2"] = _np(blk.mlp.fc1.weight), _np(blk.mlp.fc2.weight)
+            p[pre + "k_cache"], p[pre + "v_cache"] = _np(blk.mixer.k_cache), _np(blk.mixer.v_cache)
+            st[i] = (blk.mixer.k_cache.clone(), blk.mixer.v_cache.clone())
+        else:
+            mx = blk.mixer
+            p[pre + "conv_w"], p[pre + "conv_b"] = _np(mx.conv_w), _np(mx.conv_b)
+            p[pre + "conv_state"], p[pre + "ssm_state"] = _np(mx.conv_state), _np(mx.ssm_state)
+            p[pre + "A"], p[pre + "D_e"], p[pre + "dt_bias_e"] = _np(mx.A), _np(mx.D_e), _np(mx.dt_bias_e)
+            p[pre + "norm_mix_w"] = _np(mx.norm_w)
+            st[i] = (mx.conv_state.clone(), mx.ssm_state.clone())
+    p["norm_f_w"], p["norm_f_b"] = _np(m.backbone.norm_f_w), _np(m.backbone.norm_f_b)
+    p["head_W"] = _np(m.head_W)
+    return p, st
+
+
+def _restore(m, st):
+    for i, blk in enumerate(m.backbone.layers):
+        a, b = st[i]
+        if blk.is_attn:
+            blk.mixer.k_cache.copy_(a)
+            blk.mixer.v_cache.copy_(b)
+        else:
+            blk.mixer.conv_state.copy_(a)
+            blk.mixer.ssm_state.copy_(b)
+
+
+def _cfg(m):
+    c = m.cfg
+    return {"d_inner": c.d_inner, "d_state": c.d_state, "nheads": c.nheads, "headdim": c.headdim,
+            "conv_dim": c.d_inner + 2 * c.ngroups * c.d_state, "num_heads": c.num_heads,
+            "num_heads_kv": c.num_heads_kv, "head_dim": c.head_dim, "attn_layer_idx": list(c.attn_layer_idx),
+            "n_layer": c.n_layer, "pos": m.pos, "eps": c.norm_epsilon}
+
+
+@pytest.fixture(scope="module")
+def patched():
+    from sonata_b200.kernels.patch import patch_zonos_projections
+    m = _model()
+    p, st = _snapshot(m)
+    n = patch_zonos_projections(m, include_attn=True)
+    assert n == 2 * 6 + 2 * 2
+    x = torch.randn(2, 2048, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9)).to(torch.bfloat16)
+    return m, p, st, x
+
+
+def test_step_matches_oracle_chain(patched):
+    m, p, st, x = patched
+    _restore(m, st)
+    with torch.no_grad():
+        logits = m.step(x)
+    torch.cuda.synchronize()
+    truth = O.zonos_decode_step_ref(p, _np(x), _cfg(m))
+    got = logits.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert O.rel_err_inf(got, truth) <= 5e-2, O.rel_err_inf(got, truth)
+    assert O.cosine(got, truth) >= 0.999
+
+
+def test_graph_replay_equals_eager_and_recomputes(patched):
+    m, p, st, x = patched
+    _restore(m, st)
+    with torch.no_grad():
+        eager = m.step(x).clone()
+    _restore(m, st)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.no_grad(), torch.cuda.stream(s):
+        m.step(x)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    _restore(m, st)
+    with torch.no_grad(), torch.cuda.graph(g):
+        out = m.step(x)
+    _restore(m, st)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    before = out.clone()
+    _restore(m, st)
+    x2 = x.clone()
+    x.mul_(-1)
+    g.replay()
+    torch.cuda.synchronize()
+    x.copy_(x2)
+    assert not torch.equal(out, before)
+    del g
+
+
+def test_full_46_layer_step_runs_in_a_graph(cuda_lib):
+    from sonata_b200.kernels import decode_step as DS
+    r = DS.bench_decode_step(steps=3, warmup=1)
+    assert r["patched_linears"] == 34 * 2 + 12 * 4
+    assert r["value"] > 0 and r["us_cublas_linear"] > 0
+    assert cuda_lib.sn_device_status(1, None) == 0
