@@ -400,10 +400,16 @@ def bench_configs(hbm, with_cpu):
     for B in (1, 8, 64, 256):
         h = torch.randn(9, B, 2048, device="cuda", generator=gh).to(torch.bfloat16)
         o = torch.empty(9, B, 1025, device="cuda")
-        us = _graph_us(lambda: head(h, out=o), 1)
+        # as in a decode step: each call launched behind the kernel before it
+        # (programmatic dependent launch), 20 calls per graph; and alone
+        us = _graph_us(lambda: head(h, out=o, pdl=True), 20)
+        us_iso = _graph_us(lambda: head(h, out=o), 1)
         byt = 9 * 2048 * 1025 * 2 + 9 * B * 2048 * 2 + 9 * B * 1025 * 4
         c4 = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1), "roofline_frac": round(byt / us / 1e3 / hbm, 4),
-              "bytes": byt, "tflops": round(2 * 9 * B * 2048 * 1025 / us / 1e6, 1)}
+              "bytes": byt, "tflops": round(2 * 9 * B * 2048 * 1025 / us / 1e6, 1),
+              "us_isolated": round(us_iso, 2), "roofline_frac_isolated": round(byt / us_iso / 1e3 / hbm, 4),
+              "timing": "us: chain of 20 calls with programmatic dependent launch (decode-step setting); "
+                        "us_isolated: one call per graph replay"}
         if with_cpu:
             t = cb.time_head_bmm(B, thr)
             c4["cpu_baseline"] = {"us": round(t * 1e6, 1), "cores": thr, "kind": "port",

@@ -144,7 +144,10 @@ int sn_diag_bounded_wait(uint64_t limit_ns, void *stream);
  * sn_codebook_head_pack transposes W [ncb, K, N] (bf16) once into Wt
  * [ncb, N, K]; sn_codebook_head_bmm reads hidden [ncb, B, K] (bf16,
  * contiguous) and Wt, and writes fp32 logits [ncb, B, N].  B <= 4 runs the
- * decode GEMV, B >= 5 the tcgen05 contraction (K a multiple of 64).
+ * decode GEMV, B >= 5 the tcgen05 contraction (K a multiple of 64).  flags:
+ * 0 or SN_FLAG_PDL (programmatic dependent launch: the head starts and
+ * streams its first weights while the previous kernel on the stream is still
+ * running, and reads hidden / writes logits only after it has finished).
  */
 int sn_codebook_head_pack(const void *W, int ncb, int K, int N, void *Wt, void *stream);
 int sn_codebook_head_bmm(const void *hidden, const void *Wt, float *logits, int ncb, int B, int K, int N,

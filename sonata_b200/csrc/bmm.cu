@@ -21,6 +21,7 @@
 #include "tc.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace sn {
 int gemv_any(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS, const void* x,
@@ -174,6 +175,7 @@ struct HeadSkParams {
   int stages;
   uint32_t stage_bytes, a_bytes;
   uint32_t recv_off, bar_off;    // recv: [bt / 2 columns][128 rows] fp32
+  int alias_recv;                // one tile per cluster: recv lies over the (then idle) stage ring
 };
 
 __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
@@ -223,22 +225,45 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
+  pdl_launch_dependents();
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer: K half `rank` of each tile ----------------
+    auto load_w = [&](uint8_t* a, int kb, int rt, int cb, uint64_t* bar) {
+      tc::tma_load_3d(a, &mapW, kb * 64, rt * 128, cb, bar);
+    };
     int it = 0;
     bool ok = true;
+    // weights are frozen: the first ring's weight boxes go out before the
+    // previous kernel (programmatic dependent launch) has finished; hidden,
+    // which it may produce, only after griddepcontrol.wait
+    const int pre = min(ns, (p.ntiles > cluster ? (p.ntiles - 1 - cluster) / nclusters + 1 : 0) * kb_half);
+    {
+      int t = cluster, j = 0;
+      for (int q = 0; q < pre; ++q) {
+        const int rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);
+        mbar_arrive_expect_tx(full + q, p.stage_bytes);
+        load_w(smem + q * p.stage_bytes, kb0 + j, rt, cb, full + q);
+        if (++j == kb_half) {
+          j = 0;
+          t += nclusters;
+        }
+      }
+    }
+    pdl_wait();
     for (int t = cluster; t < p.ntiles && ok; t += nclusters) {
       const int bti = t % p.nbt, rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);
       for (int j = 0; j < kb_half; ++j, ++it) {
         const int s = it % ns, k = it / ns;
-        if (k > 0 && !mbar_wait_bounded(empty + s, (k - 1) & 1)) {
-          record_status(SN_ERR_TIMEOUT);
-          ok = false;
-          break;
-        }
         uint8_t* a = smem + s * p.stage_bytes;
-        mbar_arrive_expect_tx(full + s, p.stage_bytes);
-        tc::tma_load_3d(a, &mapW, (kb0 + j) * 64, rt * 128, cb, full + s);
+        if (it >= pre) {
+          if (k > 0 && !mbar_wait_bounded(empty + s, (k - 1) & 1)) {
+            record_status(SN_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + s, p.stage_bytes);
+          load_w(a, kb0 + j, rt, cb, full + s);
+        }
         tc::tma_load_3d(a + p.a_bytes, &mapH, (kb0 + j) * 64, bti * p.bt, cb, full + s);
       }
     }
@@ -273,6 +298,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       tc::mma_commit(tfull);
     }
   } else if (warp >= 2) {
+    pdl_wait();  // hidden and the logits buffer belong to the previous kernel until here
     // ---- rows past the last full tile (row 1024 of the head): CUDA-core dot
     // products, done while this CTA's MMAs run; all loads of a dot issued first
     {
@@ -321,8 +347,16 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     for (int t = cluster; t < p.ntiles; t += nclusters, ++j) {
       const int bti = t % p.nbt, rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);
       bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(tfull, j & 1));
-      // the peer's recv buffer is free once it has read the previous tile's
-      if (ok && j > 0) ok = __all_sync(0xffffffffu, tc::mbar_wait_cluster_bounded(rempty, (j - 1) & 1));
+      if (p.alias_recv) {
+        // recv lies over the stage ring: my ring is idle once my MMAs are done,
+        // and the peer's once it says so
+        tc::fence_before_sync();
+        tc::mbar_arrive_remote(peer_rempty);
+        if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait_cluster_bounded(rempty, 0));
+      } else if (ok && j > 0) {
+        // the peer's recv buffer is free once it has read the previous tile's
+        ok = __all_sync(0xffffffffu, tc::mbar_wait_cluster_bounded(rempty, (j - 1) & 1));
+      }
       if (!ok) {
         record_status(SN_ERR_TIMEOUT);
         break;
@@ -352,7 +386,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           if (b < p.B) ob[static_cast<int64_t>(b) * p.N] = y;
         }
       }
-      tc::mbar_arrive_remote(peer_rempty);  // my recv may be refilled
+      if (!p.alias_recv) tc::mbar_arrive_remote(peer_rempty);  // my recv may be refilled
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty);
@@ -525,7 +559,8 @@ int tu_status_bmm(bool reset, cudaStream_t st, int* out) { return read_tu_status
 
 // Codebook head for B >= 5 with K split over CTA pairs; SN_ERR_UNSUPPORTED when
 // the cluster launch or the shared-memory plan does not fit.
-int head_splitk(const void* hidden, const void* Wt, float* logits, int ncb, int B, int K, int N, cudaStream_t st) {
+int head_splitk(const void* hidden, const void* Wt, float* logits, int ncb, int B, int K, int N, bool pdl,
+                cudaStream_t st) {
   HeadSkParams p;
   p.out = logits;
   p.hidden = static_cast<const __nv_bfloat16*>(hidden);
@@ -542,12 +577,38 @@ int head_splitk(const void* hidden, const void* Wt, float* logits, int ncb, int 
   p.stage_bytes = p.a_bytes + static_cast<uint32_t>(p.bt) * 64 * 2;
   const uint32_t recv_bytes = static_cast<uint32_t>(p.bt / 2) * 128 * 4;
   const size_t cap = 227 * 1024 - 1024 - 256;  // opt-in maximum less the alignment slack and the barriers
-  int stages = static_cast<int>(std::min<size_t>(kSkStagesMax, (cap - recv_bytes) / p.stage_bytes));
+  // A ring of at most ~110 KB leaves room for the next kernel's CTA beside
+  // this one (programmatic dependent launch overlaps its start and first
+  // weight loads with this kernel's tail; measured in a chain of calls with
+  // 2..8 stages: B = 8 11.7 -> 10.2 us, B = 64 12.9 -> 11.3 us).  Where that
+  // leaves fewer than three stages (B = 256: 48 KB stages) the ring takes up
+  // to the whole shared memory instead (2 stages measured 18.2 us, 3..4
+  // 17.6 us).  With one tile per cluster the exchange buffer lies over the
+  // idle ring.
+  const size_t coresident = 110 * 1024 - 1024 - 256;
+  const int clusters = std::max(1, sm_count() / 2);
+  p.alias_recv = p.ntiles <= clusters;
+  static const int stages_env = [] {  // SONATA_HEAD_STAGES caps the ring (2..8)
+    const char* e = getenv("SONATA_HEAD_STAGES");
+    const int v = e ? atoi(e) : 0;
+    return (v >= 2 && v <= kSkStagesMax) ? v : 0;
+  }();
+  const size_t extra = p.alias_recv ? 0 : recv_bytes;
+  int stages;
+  if (stages_env) {
+    stages = stages_env;
+  } else if (coresident > extra && (coresident - extra) / p.stage_bytes >= 3) {
+    stages = static_cast<int>(std::min<size_t>(kSkStagesMax, (coresident - extra) / p.stage_bytes));
+  } else {
+    stages = static_cast<int>(std::min<size_t>(kSkStagesMax, (cap - extra) / p.stage_bytes));
+  }
   stages = std::min(stages, K / 128);
-  if (stages < 2) return SN_ERR_UNSUPPORTED;
+  if (p.alias_recv)
+    while (static_cast<size_t>(stages) * p.stage_bytes < recv_bytes) ++stages;
+  if (stages < 2 || static_cast<size_t>(stages) * p.stage_bytes + extra > cap) return SN_ERR_UNSUPPORTED;
   p.stages = stages;
-  p.recv_off = static_cast<uint32_t>(stages) * p.stage_bytes;
-  p.bar_off = p.recv_off + recv_bytes;
+  p.recv_off = p.alias_recv ? 0 : static_cast<uint32_t>(stages) * p.stage_bytes;
+  p.bar_off = p.alias_recv ? static_cast<uint32_t>(stages) * p.stage_bytes : p.recv_off + recv_bytes;
   const size_t smem = 1024 + p.bar_off + 8 * (2 * stages + 4) + 16;
   CUtensorMap mapW, mapH;
   const uint64_t dW[3] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint64_t>(ncb)};
@@ -563,19 +624,20 @@ int head_splitk(const void* hidden, const void* Wt, float* logits, int ncb, int 
     cudaGetLastError();
     return SN_ERR_UNSUPPORTED;
   }
-  const int clusters = std::max(1, sm_count() / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
   cfg.blockDim = dim3(kSkThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, head_splitk_kernel, mapW, mapH, p) != cudaSuccess) {
     cudaGetLastError();
     return SN_ERR_LAUNCH;
@@ -596,6 +658,7 @@ int sn_codebook_head_pack(const void* W, int ncb, int K, int N, void* Wt, void* 
 int sn_codebook_head_bmm(const void* hidden, const void* Wt, float* logits, int ncb, int B, int K, int N,
                          unsigned flags, void* stream) {
   if (!hidden || !Wt || !logits || ncb < 1 || B < 1 || K < 1 || N < 1) return SN_ERR_INVALID_ARGUMENT;
+  if (flags & ~SN_FLAG_PDL) return SN_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool tc_ok = (K % 64 == 0) && sn::aligned16(hidden) && sn::aligned16(Wt);
   if (B <= 4 || !tc_ok) {
@@ -611,7 +674,7 @@ int sn_codebook_head_bmm(const void* hidden, const void* Wt, float* logits, int 
     return SN_OK;
   }
   if (K % 128 == 0 && N >= 128) {
-    const int rc = sn::head_splitk(hidden, Wt, logits, ncb, B, K, N, st);
+    const int rc = sn::head_splitk(hidden, Wt, logits, ncb, B, K, N, (flags & SN_FLAG_PDL) != 0, st);
     if (rc != SN_ERR_UNSUPPORTED) return rc;
   }
   sn::HeadParams p;

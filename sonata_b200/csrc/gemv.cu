@@ -812,6 +812,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
     // ---------------- producer: weights only, so no griddepcontrol.wait ----
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
+      if (p.pf != nullptr && p.pf_lead <= -2) prefetch_next_weights(p);  // before this CTA's own copies
       int t = 0;
       for (; t < ntiles; ++t) {
         const int s = t % ns, k = t / ns;
@@ -834,7 +835,7 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
       }
       if (t < ntiles) {  // error path: let the copies in flight land before exit
         for (int j = (t > ns ? t - ns : 0); j < t; ++j) mbar_wait_bounded(full + j % ns, (j / ns) & 1);
-      } else if (p.pf != nullptr) {
+      } else if (p.pf != nullptr && p.pf_lead > -2) {
         // once this CTA's own reads are (nearly) all served: wait until tile
         // ntiles - 1 - lead has landed (lead < ns, so its slot was not reused)
         const int lead = min(p.pf_lead, ns - 1);
@@ -1347,8 +1348,9 @@ struct GemvNext {
 // while a launch drains and the next one starts (measured best of 4..48 MB
 // on the config-2 chain; SONATA_GEMV_PREFETCH_MB overrides, 0 disables).
 // When a CTA issues the prefetch: once all but this many of its own tiles
-// have landed (0: the last one; < 0: as soon as its last copy is issued,
-// which competes with its own reads and measured slower).
+// have landed (0: the last one; -1: as soon as its last copy is issued,
+// which competes with its own reads and measured slower; -2: at the start,
+// before its own copies).
 // SONATA_GEMV_PREFETCH_LEAD overrides.
 int prefetch_lead() {
   static const int v = [] {

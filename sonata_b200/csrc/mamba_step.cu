@@ -8,7 +8,11 @@
 // `layer_norm_fn`.  All arithmetic in fp32, outputs rounded once to bf16, as
 // those kernels do.  Decode shapes are tiny (a few K elements per row, batch
 // 1-2), so each op is one launch sized to the rows it has and bounded by
-// launch latency and one HBM round trip, not bandwidth.
+// launch latency and one HBM round trip, not bandwidth.  Each kernel starts
+// with griddepcontrol.launch_dependents: the projection GEMV that follows it
+// in a decode step (launched with programmatic dependent launch) may then
+// start streaming its frozen weights while the op runs; it reads the op's
+// output only after griddepcontrol.wait.
 #include "common.cuh"
 
 #include <climits>
@@ -32,6 +36,7 @@ __global__ void __launch_bounds__(256) causal_conv1d_update_kernel(const __nv_bf
                                                                    const __nv_bfloat16* __restrict__ bias,
                                                                    __nv_bfloat16* __restrict__ y, int B, int D,
                                                                    int W, int act) {
+  pdl_launch_dependents();  // a following programmatic-dependent GEMV may start its weight stream
   const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (e >= static_cast<int64_t>(B) * D) return;
   const int d = static_cast<int>(e % D);
@@ -116,6 +121,7 @@ __device__ __forceinline__ float ssu_dt(const SsuParams& p, const SsuRow& r) {
 // shapes) at this kernel's register count.
 template <int NCH>
 __global__ void __launch_bounds__(256) selective_state_update_vec_kernel(const SsuParams p) {
+  pdl_launch_dependents();
   const int l16 = threadIdx.x & 15;
   const int64_t rows = static_cast<int64_t>(p.batch) * p.nh * p.hd;
   const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 4;
@@ -170,6 +176,7 @@ __global__ void __launch_bounds__(256) selective_state_update_vec_kernel(const S
 // Strided kernel (any d_state <= 256, any alignment): one warp per row,
 // lane l holds elements l, l + 32, ...
 __global__ void __launch_bounds__(256) selective_state_update_kernel(const SsuParams p) {
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= static_cast<int64_t>(p.batch) * p.nh * p.hd) return;
@@ -269,6 +276,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_gated_kernel(const __nv_
                                                                      const __nv_bfloat16* __restrict__ z,
                                                                      __nv_bfloat16* __restrict__ y, int N, int G,
                                                                      float eps, int norm_before_gate) {
+  pdl_launch_dependents();
   __shared__ float red[16];
   __shared__ float part[2];
   const int rank = CL == 1 ? 0 : static_cast<int>(cluster_rank());
@@ -313,6 +321,7 @@ __global__ void __launch_bounds__(kNormThreads) layer_norm_kernel(const __nv_bfl
                                                                   __nv_bfloat16* __restrict__ out,
                                                                   void* __restrict__ residual_out, int rout_f32,
                                                                   int N, float eps, int rms) {
+  pdl_launch_dependents();
   __shared__ float red[16];
   __shared__ float part[2];
   const int rank = CL == 1 ? 0 : static_cast<int>(cluster_rank());

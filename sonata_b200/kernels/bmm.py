@@ -17,7 +17,7 @@ Drop-in for the reference's kernels/bmm.py:
 
 Addition (no reference kernel): the multi-codebook logit
 head ``logits[cb, b, n] = sum_k hidden[cb, b, k] * W[cb, k, n]`` --
-``CodebookHead(W)`` packs the [ncb, K, N] weight once, ``head(hidden)`` or
+``CodebookHead(W)`` packs the [ncb, K, N] weight once, ``head(hidden, pdl=...)`` or
 ``codebook_head_bmm(hidden, W)`` returns fp32 [ncb, B, N].
 """
 from __future__ import annotations

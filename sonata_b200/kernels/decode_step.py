@@ -265,7 +265,7 @@ class SyntheticZonos(torch.nn.Module):
                 h = blk.mixer.step(h)
         h = MS.layer_norm_fn(h, self.backbone.norm_f_w, self.backbone.norm_f_b, residual=residual, eps=eps)
         hid = h.unsqueeze(0).expand(cfg.n_codebooks, *h.shape).contiguous()
-        return self.head(hid)
+        return self.head(hid, pdl=True)
 
 
 def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: int = 0) -> dict:
