@@ -369,6 +369,33 @@ int sn_layer_norm_fused(const void *x, const void *residual, int residual_f32, c
                         const void *bias, void *out, void *residual_out, int residual_out_f32, int rows, int N,
                         float eps, int is_rms_norm, void *stream);
 
+/*
+ * Decode-step glue of the Zonos hybrid (no counterpart kernels in the
+ * reference, where torch slices, broadcasts and elementwise ops run between
+ * the library calls; each of these is one launch in place of several).
+ *
+ * sn_mamba2_split_conv: from the Mamba2 in_proj output zxbcdt [batch, ld]
+ * (= [z (d_inner) | xBC (d_inner + 2 ngroups d_state) | dt (nheads)], ld >=
+ * that width) writes z [batch, d_inner]; causal_conv1d_update with SiLU of
+ * xBC (conv_state [batch, conv_dim, d_conv] updated in place, weight
+ * [conv_dim, d_conv], bias or NULL) split into x [batch, d_inner], B and C
+ * [batch, ngroups * d_state]; and dt broadcast over headdim [batch, nheads,
+ * headdim] (nheads * headdim == d_inner).  Same values as the separate
+ * sn_causal_conv1d_update on the contiguous slices.
+ * sn_rotary_kv_append: qkv [batch, (nheads + 2 nheads_kv) head_dim] -> q
+ * [batch, nheads, head_dim] with non-interleaved rotary (cos / sin fp32
+ * [head_dim / 2] of the position), k rotated and v written at position pos
+ * of k_cache / v_cache [batch, nheads_kv, max_seqlen, head_dim].
+ * sn_swiglu: h [batch, 2d] -> y [batch, d] = h[:, :d] * SiLU(h[:, d:]).
+ * All bf16 and contiguous.
+ */
+int sn_mamba2_split_conv(const void *zxbcdt, int64_t ld, void *conv_state, const void *conv_weight,
+                         const void *conv_bias, void *z, void *x, void *B, void *C, void *dt, int batch, int d_inner,
+                         int ngroups, int d_state, int nheads, int headdim, int d_conv, void *stream);
+int sn_rotary_kv_append(const void *qkv, void *q, void *k_cache, void *v_cache, const float *cos, const float *sin,
+                        int batch, int nheads, int nheads_kv, int head_dim, int max_seqlen, int pos, void *stream);
+int sn_swiglu(const void *h, void *y, int batch, int d, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,6 +64,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_snake_conv_transpose1d_strided": ([_P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I, _I, _I, _I,
                                            _I, ctypes.c_float, _U, _P, ctypes.c_size_t, _P], _I),
     "sn_stream_shift": ([_P, _I, _P], _I),
+    "sn_mamba2_split_conv": ([_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
+    "sn_rotary_kv_append": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
+    "sn_swiglu": ([_P, _P, _I, _I, _P], _I),
     "sn_snake1d": ([_P, _P, _P, _I, _I, _I64, ctypes.c_float, _P], _I),
     "sn_diag_bounded_wait": ([ctypes.c_uint64, _P], _I),
     "sn_snake_conv_transpose1d_pack": ([_P, _I, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),

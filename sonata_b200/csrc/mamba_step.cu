@@ -30,21 +30,15 @@ __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 // ---------------------------------------------------------------------------
 constexpr int kMaxConvWidth = 8;
 
-__global__ void __launch_bounds__(256) causal_conv1d_update_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                   __nv_bfloat16* __restrict__ state,
-                                                                   const __nv_bfloat16* __restrict__ w,
-                                                                   const __nv_bfloat16* __restrict__ bias,
-                                                                   __nv_bfloat16* __restrict__ y, int B, int D,
-                                                                   int W, int act) {
-  pdl_launch_dependents();  // a following programmatic-dependent GEMV may start its weight stream
-  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (e >= static_cast<int64_t>(B) * D) return;
-  const int d = static_cast<int>(e % D);
-  __nv_bfloat16* st = state + e * W;
+// One channel d of causal_conv1d_update: st (W values) shifts one step left
+// and takes xv as its newest value; returns act(sum_w st[w] * w[d, w] + bias).
+__device__ __forceinline__ __nv_bfloat16 conv_update_channel(__nv_bfloat16 xv, __nv_bfloat16* st,
+                                                             const __nv_bfloat16* __restrict__ w,
+                                                             const __nv_bfloat16* __restrict__ bias, int d, int W,
+                                                             int act) {
   float s[kMaxConvWidth];
 #pragma unroll
   for (int k = 0; k < kMaxConvWidth; ++k) s[k] = (k + 1 < W) ? __bfloat162float(st[k + 1]) : 0.f;
-  const __nv_bfloat16 xv = x[e];
   float acc = bias ? bf(bias, d) : 0.f;
 #pragma unroll
   for (int k = 0; k < kMaxConvWidth; ++k) {
@@ -55,7 +49,20 @@ __global__ void __launch_bounds__(256) causal_conv1d_update_kernel(const __nv_bf
   for (int k = 0; k < kMaxConvWidth; ++k)
     if (k + 1 < W) st[k] = __float2bfloat16_rn(s[k]);  // exact: bf16 values moved one slot
   st[W - 1] = xv;
-  y[e] = __float2bfloat16_rn(act ? silu(acc) : acc);
+  return __float2bfloat16_rn(act ? silu(acc) : acc);
+}
+
+__global__ void __launch_bounds__(256) causal_conv1d_update_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                   __nv_bfloat16* __restrict__ state,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   const __nv_bfloat16* __restrict__ bias,
+                                                                   __nv_bfloat16* __restrict__ y, int B, int D,
+                                                                   int W, int act) {
+  pdl_launch_dependents();  // a following programmatic-dependent GEMV may start its weight stream
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e >= static_cast<int64_t>(B) * D) return;
+  const int d = static_cast<int>(e % D);
+  y[e] = conv_update_channel(x[e], state + e * W, w, bias, d, W, act);
 }
 
 // ---------------------------------------------------------------------------
@@ -400,6 +407,108 @@ int launch_cluster(Kern kern, int clusters, int cl, cudaStream_t st, Args... arg
   return SN_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Decode-step glue, fused so that a Zonos decode step launches one kernel
+// where torch would launch several (slices made contiguous, broadcasts,
+// elementwise products):
+//
+// mamba2_split_conv: the in_proj output zxbcdt [b, ld] = [z | xBC | dt] of a
+//   Mamba2 step -> z [b, di] (copy), causal_conv1d_update + SiLU of xBC (state
+//   updated in place) written as x [b, di], B [b, ng*ds], C [b, ng*ds], and
+//   dt broadcast over headdim [b, nh, hd] -- the inputs of
+//   selective_state_update and the gated RMSNorm, each contiguous.
+// rotary_kv_append: the qkv projection [b, (hq + 2 hk) hd] -> q rotated
+//   [b, hq, hd]; k rotated and v written at position pos of the KV caches
+//   [b, hk, max_seqlen, hd].  Non-interleaved rotary (halves rotate), fp32
+//   arithmetic with the products and the difference / sum rounded separately
+//   (no fused multiply-add: the same values as the torch expression).
+// swiglu: h [b, 2d] -> h[:, :d] * SiLU(h[:, d:]) [b, d], SiLU rounded to
+//   bf16 before the product (torch's bf16 ops).
+// ---------------------------------------------------------------------------
+struct SplitConvParams {
+  const __nv_bfloat16* zx;  // [b, ld]
+  int64_t ld;
+  __nv_bfloat16* conv_state;  // [b, conv_dim, W]
+  const __nv_bfloat16* w;     // [conv_dim, W]
+  const __nv_bfloat16* bias;  // [conv_dim] or null
+  __nv_bfloat16 *z, *x, *Bm, *Cm, *dt;
+  int batch, di, gds, nh, hd, W;
+};
+
+__global__ void __launch_bounds__(256) mamba2_split_conv_kernel(const SplitConvParams p) {
+  pdl_launch_dependents();
+  const int conv_dim = p.di + 2 * p.gds;
+  const int per_b = conv_dim + p.di + p.nh * p.hd;  // conv channels, z copy, dt broadcast
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e >= static_cast<int64_t>(p.batch) * per_b) return;
+  const int b = static_cast<int>(e / per_b);
+  int i = static_cast<int>(e % per_b);
+  const __nv_bfloat16* row = p.zx + b * p.ld;
+  if (i < conv_dim) {
+    const __nv_bfloat16 v = conv_update_channel(row[p.di + i], p.conv_state + (static_cast<int64_t>(b) * conv_dim + i) * p.W,
+                                                p.w, p.bias, i, p.W, 1);
+    if (i < p.di)
+      p.x[static_cast<int64_t>(b) * p.di + i] = v;
+    else if (i < p.di + p.gds)
+      p.Bm[static_cast<int64_t>(b) * p.gds + i - p.di] = v;
+    else
+      p.Cm[static_cast<int64_t>(b) * p.gds + i - p.di - p.gds] = v;
+    return;
+  }
+  i -= conv_dim;
+  if (i < p.di) {
+    p.z[static_cast<int64_t>(b) * p.di + i] = row[i];
+    return;
+  }
+  i -= p.di;  // dt broadcast: head i / hd
+  p.dt[static_cast<int64_t>(b) * p.nh * p.hd + i] = row[p.di + conv_dim + i / p.hd];
+}
+
+struct RotaryParams {
+  const __nv_bfloat16* qkv;  // [b, (hq + 2 hk) hd]
+  __nv_bfloat16* q;          // [b, hq, hd]
+  __nv_bfloat16 *kc, *vc;    // [b, hk, S, hd]
+  const float *cos, *sin;    // [hd / 2]
+  int batch, hq, hk, hd, S, pos;
+};
+
+__global__ void __launch_bounds__(256) rotary_kv_append_kernel(const RotaryParams p) {
+  pdl_launch_dependents();
+  const int h2 = p.hd / 2;
+  const int heads = p.hq + 2 * p.hk;
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;  // (b, head, j < h2)
+  if (e >= static_cast<int64_t>(p.batch) * heads * h2) return;
+  const int j = static_cast<int>(e % h2);
+  const int head = static_cast<int>((e / h2) % heads);
+  const int b = static_cast<int>(e / (static_cast<int64_t>(h2) * heads));
+  const __nv_bfloat16* src = p.qkv + (static_cast<int64_t>(b) * heads + head) * p.hd;
+  const float x1 = __bfloat162float(src[j]), x2 = __bfloat162float(src[j + h2]);
+  if (head >= p.hq + p.hk) {  // v: copied into the cache
+    __nv_bfloat16* dst = p.vc + ((static_cast<int64_t>(b) * p.hk + head - p.hq - p.hk) * p.S + p.pos) * p.hd;
+    dst[j] = src[j];
+    dst[j + h2] = src[j + h2];
+    return;
+  }
+  const float c = p.cos[j], s = p.sin[j];
+  const float r1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+  const float r2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+  __nv_bfloat16* dst = head < p.hq ? p.q + (static_cast<int64_t>(b) * p.hq + head) * p.hd
+                                   : p.kc + ((static_cast<int64_t>(b) * p.hk + head - p.hq) * p.S + p.pos) * p.hd;
+  dst[j] = __float2bfloat16_rn(r1);
+  dst[j + h2] = __float2bfloat16_rn(r2);
+}
+
+__global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ y,
+                                                     int batch, int d) {
+  pdl_launch_dependents();
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e >= static_cast<int64_t>(batch) * d) return;
+  const int64_t b = e / d, i = e % d;
+  const float g = __bfloat162float(h[b * 2 * d + d + i]);
+  const float sg = __bfloat162float(__float2bfloat16_rn(silu(g)));
+  y[e] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(h[b * 2 * d + i]), sg));
+}
+
 }  // namespace
 
 }  // namespace sn
@@ -496,6 +605,68 @@ int sn_layer_norm_fused(const void* x, const void* residual, int residual_f32, c
     case 4: return args(sn::layer_norm_kernel<4>);
     default: return args(sn::layer_norm_kernel<8>);
   }
+}
+
+int sn_mamba2_split_conv(const void* zxbcdt, int64_t ld, void* conv_state, const void* conv_weight,
+                         const void* conv_bias, void* z, void* x, void* B, void* C, void* dt, int batch, int d_inner,
+                         int ngroups, int d_state, int nheads, int headdim, int d_conv, void* stream) {
+  if (!zxbcdt || !conv_state || !conv_weight || !z || !x || !B || !C || !dt || batch < 1 || d_inner < 1 ||
+      ngroups < 1 || d_state < 1 || nheads < 1 || headdim < 1 || d_conv < 1 || d_conv > sn::kMaxConvWidth)
+    return SN_ERR_INVALID_ARGUMENT;
+  if (static_cast<int64_t>(nheads) * headdim != d_inner) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t gds = static_cast<int64_t>(ngroups) * d_state;
+  if (ld < 2 * d_inner + 2 * gds + nheads) return SN_ERR_INVALID_ARGUMENT;
+  sn::SplitConvParams p;
+  p.zx = static_cast<const __nv_bfloat16*>(zxbcdt);
+  p.ld = ld;
+  p.conv_state = static_cast<__nv_bfloat16*>(conv_state);
+  p.w = static_cast<const __nv_bfloat16*>(conv_weight);
+  p.bias = static_cast<const __nv_bfloat16*>(conv_bias);
+  p.z = static_cast<__nv_bfloat16*>(z);
+  p.x = static_cast<__nv_bfloat16*>(x);
+  p.Bm = static_cast<__nv_bfloat16*>(B);
+  p.Cm = static_cast<__nv_bfloat16*>(C);
+  p.dt = static_cast<__nv_bfloat16*>(dt);
+  p.batch = batch;
+  p.di = d_inner;
+  p.gds = static_cast<int>(gds);
+  p.nh = nheads;
+  p.hd = headdim;
+  p.W = d_conv;
+  const int64_t n = static_cast<int64_t>(batch) * (2 * d_inner + 2 * gds + static_cast<int64_t>(nheads) * headdim);
+  return sn::launch(sn::mamba2_split_conv_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, p);
+}
+
+int sn_rotary_kv_append(const void* qkv, void* q, void* k_cache, void* v_cache, const float* cos, const float* sin,
+                        int batch, int nheads, int nheads_kv, int head_dim, int max_seqlen, int pos, void* stream) {
+  if (!qkv || !q || !k_cache || !v_cache || !cos || !sin || batch < 1 || nheads < 1 || nheads_kv < 1 ||
+      head_dim < 2 || head_dim % 2 != 0 || max_seqlen < 1 || pos < 0 || pos >= max_seqlen)
+    return SN_ERR_INVALID_ARGUMENT;
+  sn::RotaryParams p;
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.q = static_cast<__nv_bfloat16*>(q);
+  p.kc = static_cast<__nv_bfloat16*>(k_cache);
+  p.vc = static_cast<__nv_bfloat16*>(v_cache);
+  p.cos = cos;
+  p.sin = sin;
+  p.batch = batch;
+  p.hq = nheads;
+  p.hk = nheads_kv;
+  p.hd = head_dim;
+  p.S = max_seqlen;
+  p.pos = pos;
+  const int64_t n = static_cast<int64_t>(batch) * (nheads + 2 * nheads_kv) * (head_dim / 2);
+  return sn::launch(sn::rotary_kv_append_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, p);
+}
+
+int sn_swiglu(const void* h, void* y, int batch, int d, void* stream) {
+  if (!h || !y || batch < 1 || d < 1) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t n = static_cast<int64_t>(batch) * d;
+  return sn::launch(sn::swiglu_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), false, static_cast<const __nv_bfloat16*>(h),
+                    static_cast<__nv_bfloat16*>(y), batch, d);
 }
 
 }  // extern "C"

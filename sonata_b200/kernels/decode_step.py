@@ -97,11 +97,19 @@ class Mamba2Mixer(torch.nn.Module):
         self.conv_state = torch.zeros(batch, self.conv_dim, cfg.d_conv, device=dev, dtype=_BF16)
         self.ssm_state = torch.zeros(batch, cfg.nheads, cfg.headdim, cfg.d_state, device=dev, dtype=_BF16)
 
-    def step(self, u: torch.Tensor) -> torch.Tensor:
+    def step(self, u: torch.Tensor, fused_glue: bool = True) -> torch.Tensor:
         cfg = self.cfg
         b = u.shape[0]
         di, ds, nh = cfg.d_inner, cfg.d_state, cfg.nheads
         zxbcdt = self.in_proj(u)
+        if fused_glue:
+            z, x, Bm, Cm, dt_e = MS.mamba2_split_conv(zxbcdt, self.conv_state, self.conv_w, self.conv_b, di,
+                                                      cfg.ngroups, ds, nh)
+            y = MS.selective_state_update(self.ssm_state, x, dt_e, self.A, Bm, Cm, D=self.D_e, z=None,
+                                          dt_bias=self.dt_bias_e, dt_softplus=True)
+            y = MS.rmsnorm_fn(y.view(b, di), self.norm_w, None, z=z, eps=cfg.norm_epsilon,
+                              group_size=di // cfg.ngroups, norm_before_gate=False)
+            return self.out_proj(y)
         z = zxbcdt[:, :di].contiguous()
         xBC = zxbcdt[:, di:di + self.conv_dim].contiguous()
         dt = zxbcdt[:, di + self.conv_dim:]
@@ -155,11 +163,16 @@ class AttnMixer(torch.nn.Module):
         self.v_cache[:, :, :prefix] = torch.randn(batch, cfg.num_heads_kv, prefix, cfg.head_dim, device=device,
                                                   generator=g).to(_BF16)
 
-    def step(self, u: torch.Tensor, pos: int, cos, sin) -> torch.Tensor:
+    def step(self, u: torch.Tensor, pos: int, cos, sin, fused_glue: bool = True) -> torch.Tensor:
         cfg = self.cfg
         b = u.shape[0]
         hq, hk, hd = cfg.num_heads, cfg.num_heads_kv, cfg.head_dim
         qkv = self.in_proj(u)
+        if fused_glue:
+            q = MS.rotary_kv_append(qkv, self.k_cache, self.v_cache, cos, sin, hq, pos)
+            o = F.scaled_dot_product_attention(q, self.k_cache[:, :, :pos + 1], self.v_cache[:, :, :pos + 1],
+                                               enable_gqa=True)
+            return self.out_proj(o.reshape(b, hq * hd))
         q = apply_rotary(qkv[:, :hq * hd].view(b, hq, 1, hd), cos, sin)
         k = apply_rotary(qkv[:, hq * hd:(hq + hk) * hd].view(b, hk, 1, hd), cos, sin)
         v = qkv[:, (hq + hk) * hd:].view(b, hk, 1, hd)
@@ -180,7 +193,9 @@ class GatedMLP(torch.nn.Module):
             self.fc1.weight.copy_(torch.randn(*self.fc1.weight.shape, device=device, generator=g) * 0.02)
             self.fc2.weight.copy_(torch.randn(*self.fc2.weight.shape, device=device, generator=g) * 0.02)
 
-    def forward(self, u):
+    def forward(self, u, fused_glue: bool = True):
+        if fused_glue:
+            return self.fc2(MS.swiglu(self.fc1(u)))
         y, gate = self.fc1(u).chunk(2, dim=-1)
         return self.fc2(y * F.silu(gate))
 
@@ -219,6 +234,7 @@ class SyntheticZonos(torch.nn.Module):
                  max_seqlen: int = 1024, device="cuda", seed: int = 0):
         super().__init__()
         self.cfg = cfg or ZonosBackboneConfig()
+        self.fused_glue = True  # False: the glue between the kernels as plain torch ops
         g = torch.Generator(device=device).manual_seed(seed)
         self.backbone = _Backbone(self.cfg, device, g)
         self.batch = batch
@@ -255,14 +271,15 @@ class SyntheticZonos(torch.nn.Module):
         eps = cfg.norm_epsilon
         residual = None
         h = hidden
+        fg = self.fused_glue
         for blk in self.backbone.layers:
             h, residual = MS.layer_norm_fn(h, blk.norm_w, blk.norm_b, residual=residual, eps=eps, prenorm=True)
             if blk.is_attn:
-                h = blk.mixer.step(h, self.pos, self.cos, self.sin)
+                h = blk.mixer.step(h, self.pos, self.cos, self.sin, fused_glue=fg)
                 h, residual = MS.layer_norm_fn(h, blk.norm2_w, blk.norm2_b, residual=residual, eps=eps, prenorm=True)
-                h = blk.mlp(h)
+                h = blk.mlp(h, fused_glue=fg)
             else:
-                h = blk.mixer.step(h)
+                h = blk.mixer.step(h, fused_glue=fg)
         h = MS.layer_norm_fn(h, self.backbone.norm_f_w, self.backbone.norm_f_b, residual=residual, eps=eps)
         hid = h.unsqueeze(0).expand(cfg.n_codebooks, *h.shape).contiguous()
         return self.head(hid, pdl=True)
@@ -275,7 +292,9 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
     model: the GEMV kernel with programmatic dependent launch and the
     next-weight L2 prefetch (``patch_zonos_projections(include_attn=True)``),
     the GEMV kernel without the prefetch chain, and the unpatched nn.Linear
-    (cuBLAS).  A replay after changing the input must change the logits
+    (cuBLAS); and the first variant with the glue between the kernels as
+    plain torch ops (slices made contiguous, rotary, SwiGLU) instead of the
+    fused glue kernels.  A replay after changing the input must change the logits
     (the empty-graph tripwire of bench_decode.py:114-121)."""
     from .patch import patch_zonos_projections, unpatch_linear
     model = SyntheticZonos(batch=batch, seed=seed)
@@ -309,6 +328,11 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
 
     res = {}
     n = patch_zonos_projections(model, include_attn=True, prefetch_chain=True)
+    model.fused_glue = False
+    g, out = capture()
+    res["torch_glue"] = timed(g)
+    del g
+    model.fused_glue = True
     g, out = capture()
     res["gemv_pdl_prefetch"] = timed(g)
     before = out.clone()
@@ -333,7 +357,10 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
     us = res["gemv_pdl_prefetch"]
     cfg = model.cfg
     n_attn = len(cfg.attn_layer_idx)
-    launches_other = (cfg.n_layer - n_attn) * 7 + n_attn * 12 + 3
+    # with the fused glue: per Mamba2 block add+LayerNorm, split+conv, SSU,
+    # gated RMSNorm; per attention block add+LayerNorm, rotary+cache, SDPA,
+    # add+LayerNorm, SwiGLU; then the final norm and the head's input copy
+    launches_other = (cfg.n_layer - n_attn) * 4 + n_attn * 5 + 2
     return {
         "metric": "synthetic Zonos-hybrid decode step µs (46 layers, CUDA graph)",
         "value": round(us, 1),
@@ -342,14 +369,15 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
         "weight_bytes": wbytes,
         "weight_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
         "us_gemv_without_prefetch_chain": round(res["gemv_pdl"], 1),
+        "us_torch_glue": round(res["torch_glue"], 1),
         "us_cublas_linear": round(res["cublas"], 1),
         "patched_linears": n,
         "tokens_per_s": round(1e6 / us, 1),
         "frame_budget_frac": round(us / 11610.0, 4),
         "workload": f"46 layers ({cfg.n_layer - n_attn} Mamba2, {n_attn} attention + gated MLP), d_model 2048, batch "
                     f"{batch}, KV context {model.pos}, synthetic weights; per token: add+LayerNorm, Mamba2 step "
-                    "(in_proj GEMV, causal_conv1d_update, selective_state_update, gated RMSNorm, out_proj GEMV) or "
-                    "attention (qkv GEMV, rotary, SDPA over the cache, o_proj GEMV, add+LayerNorm, fc1 GEMV, "
-                    "SwiGLU, fc2 GEMV), final norm, 9 codebook heads",
+                    "(in_proj GEMV, split + causal_conv1d_update, selective_state_update, gated RMSNorm, out_proj "
+                    "GEMV) or attention (qkv GEMV, rotary + KV append, SDPA over the cache, o_proj GEMV, "
+                    "add+LayerNorm, fc1 GEMV, SwiGLU, fc2 GEMV), final norm, 9 codebook heads",
         "non_gemv_launches_approx": launches_other,
     }

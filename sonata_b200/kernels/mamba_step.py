@@ -130,6 +130,61 @@ def layer_norm_fn(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | No
     return (out, rout) if prenorm else out
 
 
+def mamba2_split_conv(zxbcdt: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor, bias, d_inner: int,
+                      ngroups: int, d_state: int, nheads: int, stream=None):
+    """The Mamba2 step between in_proj and selective_state_update in one
+    launch: zxbcdt [b, >= width] (row stride taken from the tensor) ->
+    (z [b, d_inner], x [b, nheads, headdim], B [b, ngroups, d_state],
+    C [b, ngroups, d_state], dt [b, nheads, headdim]); conv_state updated in
+    place (causal_conv1d_update with SiLU on xBC)."""
+    require_cuda("zxbcdt", zxbcdt, _BF16, 2)
+    if zxbcdt.stride(1) != 1:
+        raise ValueError("zxbcdt must be contiguous along its last dimension")
+    b = zxbcdt.shape[0]
+    hd = d_inner // nheads
+    conv_dim = d_inner + 2 * ngroups * d_state
+    _bf16("conv_state", conv_state, (b, conv_dim, conv_state.shape[-1]))
+    _bf16("weight", weight, (conv_dim, conv_state.shape[-1]))
+    if bias is not None:
+        _bf16("bias", bias, (conv_dim,))
+    dev = zxbcdt.device
+    z = torch.empty(b, d_inner, device=dev, dtype=_BF16)
+    x = torch.empty(b, nheads, hd, device=dev, dtype=_BF16)
+    Bm = torch.empty(b, ngroups, d_state, device=dev, dtype=_BF16)
+    Cm = torch.empty(b, ngroups, d_state, device=dev, dtype=_BF16)
+    dt = torch.empty(b, nheads, hd, device=dev, dtype=_BF16)
+    call("sn_mamba2_split_conv", zxbcdt.data_ptr(), zxbcdt.stride(0) if b > 1 else zxbcdt.shape[1],
+         conv_state.data_ptr(), weight.data_ptr(), _ptr(bias), z.data_ptr(), x.data_ptr(), Bm.data_ptr(),
+         Cm.data_ptr(), dt.data_ptr(), b, d_inner, ngroups, d_state, nheads, hd, conv_state.shape[-1],
+         stream_handle(stream))
+    return z, x, Bm, Cm, dt
+
+
+def rotary_kv_append(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, cos: torch.Tensor,
+                     sin: torch.Tensor, nheads: int, pos: int, stream=None) -> torch.Tensor:
+    """q with rotary [b, nheads, 1, head_dim]; k (rotated) and v written at
+    position pos of the caches [b, nheads_kv, max_seqlen, head_dim]."""
+    _bf16("qkv", qkv)
+    b, hk, S, hd = k_cache.shape
+    _bf16("k_cache", k_cache)
+    _bf16("v_cache", v_cache, (b, hk, S, hd))
+    require_cuda("cos", cos, torch.float32)
+    require_cuda("sin", sin, torch.float32)
+    q = torch.empty(b, nheads, 1, hd, device=qkv.device, dtype=_BF16)
+    call("sn_rotary_kv_append", qkv.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), cos.data_ptr(),
+         sin.data_ptr(), b, nheads, hk, hd, S, pos, stream_handle(stream))
+    return q
+
+
+def swiglu(h: torch.Tensor, stream=None) -> torch.Tensor:
+    """h [b, 2d] -> h[:, :d] * SiLU(h[:, d:])."""
+    _bf16("h", h)
+    b, d2 = h.shape
+    y = torch.empty(b, d2 // 2, device=h.device, dtype=_BF16)
+    call("sn_swiglu", h.data_ptr(), y.data_ptr(), b, d2 // 2, stream_handle(stream))
+    return y
+
+
 def bench_step_ops(reps: int = 10, calls: int = 20, seed: int = 0) -> dict:
     """Microseconds per call of the four decode-step ops at the Zonos shapes of
     the reference's goldens (validation_harness.py:18-36: batch 2, d_inner

@@ -88,11 +88,14 @@ def patched():
     return m, p, st, x
 
 
-def test_step_matches_oracle_chain(patched):
+@pytest.mark.parametrize("fused_glue", [True, False])
+def test_step_matches_oracle_chain(patched, fused_glue):
     m, p, st, x = patched
     _restore(m, st)
+    m.fused_glue = fused_glue
     with torch.no_grad():
         logits = m.step(x)
+    m.fused_glue = True
     torch.cuda.synchronize()
     truth = O.zonos_decode_step_ref(p, _np(x), _cfg(m))
     got = logits.cpu().numpy()
@@ -137,3 +140,42 @@ def test_full_46_layer_step_runs_in_a_graph(cuda_lib):
     assert r["patched_linears"] == 34 * 2 + 12 * 4
     assert r["value"] > 0 and r["us_cublas_linear"] > 0
     assert cuda_lib.sn_device_status(1, None) == 0
+
+
+def test_glue_kernels_match_torch_glue():
+    """The fused glue kernels against the torch ops they replace: the split +
+    conv and the rotary bit for bit, SwiGLU within one bf16 rounding."""
+    from sonata_b200.kernels import decode_step as DS
+    from sonata_b200.kernels import mamba_step as MS
+    g = torch.Generator(device="cuda").manual_seed(3)
+    b, di, ds, nh, W = 2, 4096, 128, 64, 4
+    cd = di + 2 * ds
+    zx = torch.randn(b, 2 * di + 2 * ds + nh, device="cuda", generator=g).to(torch.bfloat16)
+    st = torch.randn(b, cd, W, device="cuda", generator=g).to(torch.bfloat16)
+    w = torch.randn(cd, W, device="cuda", generator=g).to(torch.bfloat16)
+    bias = torch.randn(cd, device="cuda", generator=g).to(torch.bfloat16)
+    st2 = st.clone()
+    z, x, Bm, Cm, dt = MS.mamba2_split_conv(zx, st, w, bias, di, 1, ds, nh)
+    xbc = MS.causal_conv1d_update(zx[:, di:di + cd].contiguous(), st2, w, bias, "silu")
+    assert torch.equal(st, st2)
+    assert torch.equal(z, zx[:, :di]) and torch.equal(x.view(b, di), xbc[:, :di])
+    assert torch.equal(Bm.view(b, ds), xbc[:, di:di + ds]) and torch.equal(Cm.view(b, ds), xbc[:, di + ds:])
+    assert torch.equal(dt, zx[:, di + cd:, None].expand(b, nh, di // nh))
+
+    hq, hk, hd, S, pos = 16, 4, 128, 64, 37
+    qkv = torch.randn(b, (hq + 2 * hk) * hd, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(b, hk, S, hd, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(b, hk, S, hd, device="cuda", generator=g).to(torch.bfloat16)
+    kc2, vc2 = kc.clone(), vc.clone()
+    cos, sin = DS.rotary_cos_sin(pos, hd, "cuda")
+    q = MS.rotary_kv_append(qkv, kc, vc, cos, sin, hq, pos)
+    q_ref = DS.apply_rotary(qkv[:, :hq * hd].view(b, hq, 1, hd), cos, sin)
+    kc2[:, :, pos:pos + 1] = DS.apply_rotary(qkv[:, hq * hd:(hq + hk) * hd].view(b, hk, 1, hd), cos, sin)
+    vc2[:, :, pos:pos + 1] = qkv[:, (hq + hk) * hd:].view(b, hk, 1, hd)
+    assert torch.equal(q, q_ref) and torch.equal(kc, kc2) and torch.equal(vc, vc2)
+
+    h = torch.randn(b, 2 * 8192, device="cuda", generator=g).to(torch.bfloat16)
+    y = MS.swiglu(h)
+    ref = h[:, :8192] * torch.nn.functional.silu(h[:, 8192:])
+    ulp = (ref.float().abs() * 2.0 ** -7).clamp_min(1e-30)
+    assert ((y.float() - ref.float()).abs() <= ulp).all()
