@@ -661,7 +661,8 @@ def run_ours(args):
         from sonata_b200.kernels import fused_snake_conv as fsc
         snake["snake_then_cudnn_fp32"] = fsc.bench_snake_then_cudnn()
         dac = with_snake_roofline(bench_dac_decoder(), hbm, tf_sust)
-        stream_dac = bench_streaming_dac()
+        if not args.skip_streaming:
+            stream_dac = bench_streaming_dac()
     if rank == 0 and not args.skip_decode_step:
         from sonata_b200.kernels import decode_step
         decode = decode_step.bench_decode_step(steps=max(5, args.steps), warmup=args.warmup)
@@ -897,6 +898,7 @@ def main():
     ap.add_argument("--skip-configs", action="store_true", help="skip the per-config (1, 3, 4, 5) lines")
     ap.add_argument("--skip-sharded", action="store_true", help="skip the stream-sharded config 4 / 5 sections")
     ap.add_argument("--skip-decode-step", action="store_true", help="skip the synthetic Zonos decode step")
+    ap.add_argument("--skip-streaming", action="store_true", help="skip the streaming DAC decoder")
     ap.add_argument("--case", choices=["gemv", "snake", "head", "ssd"], default=None,
                     help="run one kernel on one shape (profiling / microbenchmark)")
     ap.add_argument("--shape", default="", help="e.g. 8512x2048x1 (gemv N x K x M), 384x55168x3 (snake C x T x d)")
