@@ -106,6 +106,32 @@ int sn_gemv_ex(int w_kind, const void *W, int64_t ldw, const float *scale, const
                int next_kind, const void *next_W, int64_t next_ldw, int next_N, int next_K);
 
 /*
+ * bf16 GEMV with the normalisation before it fused into the x staging (the
+ * Zonos decode step's gated RMSNorm -> out_proj and add + LayerNorm ->
+ * in_proj / qkv / fc1; no counterpart in the reference, where the norm is a
+ * separate kernel).  Every CTA normalises the x rows it stages:
+ *   SN_NORM_RMS_GATED: x' = (x * SiLU(aux)) / rms(x * SiLU(aux)) * norm_w
+ *                      (aux = z, may be NULL: no gate; the whole row is one
+ *                      group), as sn_rmsnorm_gated with norm_before_gate 0;
+ *   SN_NORM_ADD_LAYER: h = x + aux (aux = residual or NULL),
+ *                      x' = LayerNorm(h) * norm_w (+ norm_b), and
+ *                      residual_out (or NULL) = h in bf16, as
+ *                      sn_layer_norm_fused with bf16 residuals;
+ * then y = x' W^T as sn_gemv_ex (next-weight hint as there).  x, aux,
+ * residual_out: contiguous bf16 [M, K], 16-byte aligned; M <= 4, K a
+ * multiple of 1024 up to 4096; SN_ERR_UNSUPPORTED for shapes the tensor-core
+ * kernel does not take (the caller then runs the two kernels).  The row sums
+ * are taken in another order than the standalone norm kernels', so x' may
+ * differ from theirs by one bf16 rounding step.
+ */
+#define SN_NORM_RMS_GATED 1
+#define SN_NORM_ADD_LAYER 2
+int sn_gemv_bf16_norm(int norm_kind, const void *W, int64_t ldw, const void *x, const void *aux, const void *norm_w,
+                      const void *norm_b, void *residual_out, float eps, void *y, int64_t ldy, int M, int N, int K,
+                      int y_dtype, unsigned flags, void *stream, int next_kind, const void *next_W,
+                      int64_t next_ldw, int next_N, int next_K);
+
+/*
  * Per-output-channel weight quantisation on the device (bit-identical to
  * scripts/fake_quant.py:37-40 for int8):
  *   scale[n] = max(max_k |W[n, k]|, 1e-8) / 127   (int8)   or / 448 (e4m3)

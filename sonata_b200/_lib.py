@@ -22,6 +22,8 @@ SN_FLAG_PREPACKED = 2
 SN_WEIGHT_BF16 = 0
 SN_WEIGHT_INT8 = 1
 SN_WEIGHT_E4M3 = 2
+SN_NORM_RMS_GATED = 1
+SN_NORM_ADD_LAYER = 2
 SN_ACT_SNAKE = 0
 SN_ACT_NONE = 1
 SN_ACT_SILU = 2
@@ -41,6 +43,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_gemv_int8": ([_P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
     "sn_gemv_fp8e4m3": ([_P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P], _I),
     "sn_gemv_ex": ([_I, _P, _I64, _P, _P, _I64, _P, _I64, _I, _I, _I, _I, _U, _P, _I, _P, _I64, _I, _I], _I),
+    "sn_gemv_bf16_norm": ([_I, _P, _I64, _P, _P, _P, _P, _P, ctypes.c_float, _P, _I64, _I, _I, _I, _I, _U, _P, _I, _P,
+                           _I64, _I, _I], _I),
     "sn_quantize_rows_int8": ([_P, _I64, _I, _I, _P, _I64, _P, _P], _I),
     "sn_quantize_rows_fp8e4m3": ([_P, _I64, _I, _I, _P, _I64, _P, _P], _I),
     "sn_device_status": ([_I, _P], _I),

@@ -74,6 +74,14 @@ struct GemvParams {
   uint32_t pf_row_bytes, pf_part_bytes;
   int x_rot;    // x row copies start at a CTA-dependent 128-byte piece
   int pf_lead;  // issue once all but this many of the CTA's own tiles have landed (< 0: at once)
+  // Normalisation fused into the x staging of the bf16 tensor-core GEMV
+  // (sn_gemv_bf16_norm): every CTA normalises the x rows it stages.
+  int xn;                       // 0 none, SN_NORM_RMS_GATED, SN_NORM_ADD_LAYER
+  const __nv_bfloat16* xn_aux;  // gate z (RMS) or residual (LayerNorm, may be null), [M][K] row stride ldx
+  const __nv_bfloat16* xn_w;    // norm weight [K]
+  const __nv_bfloat16* xn_b;    // LayerNorm bias [K] or null
+  __nv_bfloat16* xn_rout;       // LayerNorm: x + residual [M][K] (row stride ldx), written by CTA (0, 0), or null
+  float xn_eps;
 };
 
 constexpr int kWarps = 8;
@@ -757,6 +765,115 @@ __device__ __forceinline__ void bulk_g2s_rot(void* dst, const void* src, uint32_
   bulk_g2s(dst, src, off, bar, pol);
 }
 
+// Fused normalisation of the bf16 GEMV's x rows (the decode step's gated
+// RMSNorm before out_proj and add + LayerNorm before in_proj / qkv / fc1):
+// the 128 staging threads of every CTA load the row(s) (16-byte pieces from
+// L2), reduce over the row through shared memory and write the normalised
+// bf16 row where the plain kernel's bulk copy would have put x.  Same
+// arithmetic as rmsnorm_gated_kernel / layer_norm_kernel (fp32, one bf16
+// rounding); only the order of the row sums differs.  K % 1024 == 0,
+// K <= 4096 (host-checked).
+template <int MT>
+__device__ __forceinline__ void stage_x_norm(const GemvParams& p, const __nv_bfloat16* xb, uint8_t* xs, float* red) {
+  constexpr int kMaxPieces = 4;  // 16-byte pieces a thread holds per row (K <= 4096)
+  const int xt = threadIdx.x - 64;  // 0..127 (warps 2-5)
+  const int wq = xt >> 5, ln = xt & 31;
+  const int np = p.K / 1024;       // pieces per thread
+  const bool writer = p.xn_rout != nullptr && blockIdx.x == 0 && blockIdx.y == 0;
+  auto block_sum = [&](float v) {
+    v = warp_sum(v);
+    if (ln == 0) red[wq] = v;
+    named_bar_sync(3, 128);
+    const float t = red[0] + red[1] + red[2] + red[3];
+    named_bar_sync(3, 128);  // red reusable
+    return t;
+  };
+  for (int m = 0; m < MT; ++m) {
+    uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<size_t>(m) * p.K * 2);
+    if (m >= p.M) {
+      for (int c = xt; c < p.K / 8; c += 128) dst[c] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    float t[kMaxPieces][8];
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxPieces; ++j) {
+      if (j >= np) break;
+      const int c = xt + 128 * j;
+      const uint4 xv = ld_cg_v4(xb + m * p.ldx + c * 8);
+      uint4 av = make_uint4(0, 0, 0, 0);
+      if (p.xn_aux) av = ld_cg_v4(p.xn_aux + m * p.ldx + c * 8);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, aw[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xf = (e & 1) ? bf16hi(xw[e >> 1]) : bf16lo(xw[e >> 1]);
+        const float af = (e & 1) ? bf16hi(aw[e >> 1]) : bf16lo(aw[e >> 1]);
+        float v;
+        if (p.xn == SN_NORM_RMS_GATED) {
+          v = p.xn_aux ? xf * (af / (1.0f + expf(-af))) : xf;
+          acc = fmaf(v, v, acc);
+        } else {
+          v = xf + af;
+          acc += v;
+        }
+        t[j][e] = v;
+      }
+      if (writer) {
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(t[j][2 * q]));
+          const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(t[j][2 * q + 1]));
+          o[q] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4*>(p.xn_rout + m * p.ldx + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    float mean = 0.f, r;
+    if (p.xn == SN_NORM_RMS_GATED) {
+      r = rsqrtf(block_sum(acc) / p.K + p.xn_eps);
+    } else {
+      mean = block_sum(acc) / p.K;
+      float sq = 0.f;
+#pragma unroll
+      for (int j = 0; j < kMaxPieces; ++j) {
+        if (j >= np) break;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = t[j][e] - mean;
+          sq = fmaf(d, d, sq);
+        }
+      }
+      r = rsqrtf(block_sum(sq) / p.K + p.xn_eps);
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxPieces; ++j) {
+      if (j >= np) break;
+      const int c = xt + 128 * j;
+      const uint4 wv = *reinterpret_cast<const uint4*>(p.xn_w + c * 8);
+      uint4 bv = make_uint4(0, 0, 0, 0);
+      if (p.xn_b) bv = *reinterpret_cast<const uint4*>(p.xn_b + c * 8);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float f[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int e = 2 * q + h;
+          const float wf = h ? bf16hi(ww[q]) : bf16lo(ww[q]);
+          float o1 = (p.xn == SN_NORM_RMS_GATED) ? t[j][e] * r * wf : (t[j][e] - mean) * r * wf;
+          if (p.xn_b) o1 += h ? bf16hi(bw[q]) : bf16lo(bw[q]);
+          f[h] = o1;
+        }
+        o[q] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(f[0]))) |
+               (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(f[1]))) << 16);
+      }
+      dst[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 template <int WK, int MT, int S>
 __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const GemvParams p, const MmaShape sh) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -850,8 +967,16 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
     pdl_wait();  // x and y belong to the previous kernel from here on
     const int cpr = p.K >> 3;  // 16-byte pieces of a bf16 x row
     if constexpr (WK == W_BF16) {
-      // x rows by bulk copy (one L2 round trip); padding rows zeroed meanwhile
-      if (warp == 1) {
+      if (p.xn != 0) {
+        // x rows normalised by the staging warps; one arrival completes xbar
+        if (warp >= 2) {
+          stage_x_norm<MT>(p, xb, xs, reinterpret_cast<float*>(smem + 768));
+          tc::fence_proxy_async_smem();
+          named_bar_sync(3, 128);
+          if (threadIdx.x == 64) mbar_arrive(xbar);
+        }
+      } else if (warp == 1) {
+        // x rows by bulk copy (one L2 round trip); padding rows zeroed meanwhile
         if (lane == 0) {
           const uint64_t pol = l2_policy_evict_normal();
           mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(p.M) * row_bytes);
@@ -1393,9 +1518,17 @@ int prefetch_pct() {
 
 int nd_of(int wk) { return wk == W_INT8 ? 3 : wk == W_E4M3 ? 2 : 1; }
 
+// Normalisation fused into the x staging (sn_gemv_bf16_norm).
+struct GemvNorm {
+  int kind;  // SN_NORM_*
+  const void *aux, *w, *b;
+  void* rout;
+  float eps;
+};
+
 int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS, const void* x,
               int64_t ldx, int64_t sx, void* y, int64_t ldy, int64_t sy, int M, int N, int K, int batch,
-              int y_dtype, unsigned flags, cudaStream_t st, const GemvNext* next);
+              int y_dtype, unsigned flags, cudaStream_t st, const GemvNext* next, const GemvNorm* norm = nullptr);
 }  // namespace
 
 // Shared by the C entry points and the codebook-head BMM (batch > 1).
@@ -1409,7 +1542,7 @@ int gemv_any(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale,
 namespace {
 int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale, int64_t sS, const void* x,
               int64_t ldx, int64_t sx, void* y, int64_t ldy, int64_t sy, int M, int N, int K, int batch,
-              int y_dtype, unsigned flags, cudaStream_t st, const GemvNext* next) {
+              int y_dtype, unsigned flags, cudaStream_t st, const GemvNext* next, const GemvNorm* norm) {
   if (!W || !x || !y) return SN_ERR_INVALID_ARGUMENT;
   if (wk != W_BF16 && !scale) return SN_ERR_INVALID_ARGUMENT;
   if (next && next->W &&
@@ -1445,6 +1578,26 @@ int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale
   p.pf_row_bytes = p.pf_part_bytes = 0;
   p.pf_lead = prefetch_lead();
   p.x_rot = x_rotate();
+  p.xn = 0;
+  p.xn_aux = p.xn_w = p.xn_b = nullptr;
+  p.xn_rout = nullptr;
+  p.xn_eps = 0.f;
+  if (norm) {
+    // the tensor-core bf16 kernel's staging threads normalise the rows: 16-byte
+    // pieces, K a multiple of 1024 up to 4096, one weight (batch 1)
+    if (norm->kind != SN_NORM_RMS_GATED && norm->kind != SN_NORM_ADD_LAYER) return SN_ERR_INVALID_ARGUMENT;
+    if (!norm->w) return SN_ERR_INVALID_ARGUMENT;
+    if (wk != W_BF16 || batch != 1 || K % 1024 != 0 || K > 4096) return SN_ERR_UNSUPPORTED;
+    if (!p.x_vec || !aligned16(norm->w) || (norm->aux && !aligned16(norm->aux)) || (norm->b && !aligned16(norm->b)) ||
+        (norm->rout && !aligned16(norm->rout)))
+      return SN_ERR_MISALIGNED;
+    p.xn = norm->kind;
+    p.xn_aux = static_cast<const __nv_bfloat16*>(norm->aux);
+    p.xn_w = static_cast<const __nv_bfloat16*>(norm->w);
+    p.xn_b = static_cast<const __nv_bfloat16*>(norm->b);
+    p.xn_rout = static_cast<__nv_bfloat16*>(norm->rout);
+    p.xn_eps = norm->eps;
+  }
   if (next && next->W) {
     const int nesz = (next->wk == W_BF16) ? 2 : 1;
     const int64_t row_b = static_cast<int64_t>(next->K) * nesz;
@@ -1466,6 +1619,14 @@ int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale
   const size_t smem = (size_t)MT * p.Kp * sizeof(float);
   if (smem > 200 * 1024) return SN_ERR_UNSUPPORTED;  // x must fit in shared memory
   const bool pdl = (flags & SN_FLAG_PDL) != 0;
+  if (p.xn != 0) {  // only the tensor-core bf16 kernel implements the fused normalisation
+    if (!wvec) return SN_ERR_UNSUPPORTED;
+    switch (MT) {
+      case 1: return dispatch_mma<W_BF16, 1>(p, batch, st, pdl);
+      case 2: return dispatch_mma<W_BF16, 2>(p, batch, st, pdl);
+      default: return dispatch_mma<W_BF16, 4>(p, batch, st, pdl);
+    }
+  }
 #define SN_DISPATCH(WKV)                                                   \
   switch (MT) {                                                            \
     case 1: return dispatch_mt<WKV, 1>(p, batch, smem, st, pdl, wvec);     \
@@ -1547,6 +1708,17 @@ int sn_gemv_ex(int w_kind, const void* W, int64_t ldw, const float* scale, const
   const sn::GemvNext nx{next_kind, next_W, next_ldw, next_N, next_K};
   return sn::gemv_impl(w_kind, W, ldw, 0, w_kind == SN_WEIGHT_BF16 ? nullptr : scale, 0, x, ldx, 0, y, ldy, 0,
                        M, N, K, 1, y_dtype, flags, static_cast<cudaStream_t>(stream), next_W ? &nx : nullptr);
+}
+
+int sn_gemv_bf16_norm(int norm_kind, const void* W, int64_t ldw, const void* x, const void* aux, const void* norm_w,
+                      const void* norm_b, void* residual_out, float eps, void* y, int64_t ldy, int M, int N, int K,
+                      int y_dtype, unsigned flags, void* stream, int next_kind, const void* next_W,
+                      int64_t next_ldw, int next_N, int next_K) {
+  if (M > 4) return SN_ERR_INVALID_ARGUMENT;
+  const sn::GemvNext nx{next_kind, next_W, next_ldw, next_N, next_K};
+  const sn::GemvNorm nm{norm_kind, aux, norm_w, norm_b, residual_out, eps};
+  return sn::gemv_impl(SN_WEIGHT_BF16, W, ldw, 0, nullptr, 0, x, K, 0, y, ldy, 0, M, N, K, 1, y_dtype, flags,
+                       static_cast<cudaStream_t>(stream), next_W ? &nx : nullptr, &nm);
 }
 
 static int quantize_rows(bool e4m3, const void* W, int64_t ldw, int N, int K, void* q, int64_t ldq, float* scale,

@@ -33,6 +33,7 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn.functional as F
 
+from . import gemv as G
 from . import mamba_step as MS
 from .bmm import CodebookHead
 
@@ -96,6 +97,22 @@ class Mamba2Mixer(torch.nn.Module):
         dev = self.conv_w.device
         self.conv_state = torch.zeros(batch, self.conv_dim, cfg.d_conv, device=dev, dtype=_BF16)
         self.ssm_state = torch.zeros(batch, cfg.nheads, cfg.headdim, cfg.d_state, device=dev, dtype=_BF16)
+
+    def step_fused_norms(self, h: torch.Tensor, residual, norm_w, norm_b):
+        """The block's add + LayerNorm fused into in_proj and the gated RMSNorm
+        fused into out_proj (sn_gemv_bf16_norm): returns (out, residual)."""
+        cfg = self.cfg
+        b = h.shape[0]
+        di, ds, nh = cfg.d_inner, cfg.d_state, cfg.nheads
+        zxbcdt, residual = G.gemv_add_layernorm(h, residual, norm_w, norm_b, self.in_proj.weight,
+                                                cfg.norm_epsilon, link=self.in_proj)
+        z, x, Bm, Cm, dt_e = MS.mamba2_split_conv(zxbcdt, self.conv_state, self.conv_w, self.conv_b, di,
+                                                  cfg.ngroups, ds, nh)
+        y = MS.selective_state_update(self.ssm_state, x, dt_e, self.A, Bm, Cm, D=self.D_e, z=None,
+                                      dt_bias=self.dt_bias_e, dt_softplus=True)
+        out = G.gemv_rmsnorm_gated(y.view(b, di), z, self.norm_w, self.out_proj.weight, cfg.norm_epsilon,
+                                   link=self.out_proj)
+        return out, residual
 
     def step(self, u: torch.Tensor, fused_glue: bool = True) -> torch.Tensor:
         cfg = self.cfg
@@ -163,6 +180,18 @@ class AttnMixer(torch.nn.Module):
         self.v_cache[:, :, :prefix] = torch.randn(batch, cfg.num_heads_kv, prefix, cfg.head_dim, device=device,
                                                   generator=g).to(_BF16)
 
+    def step_fused_norms(self, h, residual, norm_w, norm_b, pos: int, cos, sin):
+        """add + LayerNorm fused into the qkv projection; returns (out, residual)."""
+        cfg = self.cfg
+        b = h.shape[0]
+        hq, hd = cfg.num_heads, cfg.head_dim
+        qkv, residual = G.gemv_add_layernorm(h, residual, norm_w, norm_b, self.in_proj.weight, cfg.norm_epsilon,
+                                             link=self.in_proj)
+        q = MS.rotary_kv_append(qkv, self.k_cache, self.v_cache, cos, sin, hq, pos)
+        o = F.scaled_dot_product_attention(q, self.k_cache[:, :, :pos + 1], self.v_cache[:, :, :pos + 1],
+                                           enable_gqa=True)
+        return self.out_proj(o.reshape(b, hq * hd)), residual
+
     def step(self, u: torch.Tensor, pos: int, cos, sin, fused_glue: bool = True) -> torch.Tensor:
         cfg = self.cfg
         b = u.shape[0]
@@ -192,6 +221,11 @@ class GatedMLP(torch.nn.Module):
         with torch.no_grad():
             self.fc1.weight.copy_(torch.randn(*self.fc1.weight.shape, device=device, generator=g) * 0.02)
             self.fc2.weight.copy_(torch.randn(*self.fc2.weight.shape, device=device, generator=g) * 0.02)
+
+    def forward_fused_norm(self, h, residual, norm_w, norm_b, eps):
+        """add + LayerNorm fused into fc1; returns (out, residual)."""
+        y, residual = G.gemv_add_layernorm(h, residual, norm_w, norm_b, self.fc1.weight, eps, link=self.fc1)
+        return self.fc2(MS.swiglu(y)), residual
 
     def forward(self, u, fused_glue: bool = True):
         if fused_glue:
@@ -235,6 +269,9 @@ class SyntheticZonos(torch.nn.Module):
         super().__init__()
         self.cfg = cfg or ZonosBackboneConfig()
         self.fused_glue = True  # False: the glue between the kernels as plain torch ops
+        # norms fused into the next GEMV's x staging (needs fused_glue and
+        # patched projections: patch_zonos_projections)
+        self.fused_norms = False
         g = torch.Generator(device=device).manual_seed(seed)
         self.backbone = _Backbone(self.cfg, device, g)
         self.batch = batch
@@ -272,6 +309,17 @@ class SyntheticZonos(torch.nn.Module):
         residual = None
         h = hidden
         fg = self.fused_glue
+        if fg and self.fused_norms:
+            for blk in self.backbone.layers:
+                if blk.is_attn:
+                    h, residual = blk.mixer.step_fused_norms(h, residual, blk.norm_w, blk.norm_b, self.pos, self.cos,
+                                                             self.sin)
+                    h, residual = blk.mlp.forward_fused_norm(h, residual, blk.norm2_w, blk.norm2_b, eps)
+                else:
+                    h, residual = blk.mixer.step_fused_norms(h, residual, blk.norm_w, blk.norm_b)
+            h = MS.layer_norm_fn(h, self.backbone.norm_f_w, self.backbone.norm_f_b, residual=residual, eps=eps)
+            hid = h.unsqueeze(0).expand(cfg.n_codebooks, *h.shape).contiguous()
+            return self.head(hid, pdl=True)
         for blk in self.backbone.layers:
             h, residual = MS.layer_norm_fn(h, blk.norm_w, blk.norm_b, residual=residual, eps=eps, prenorm=True)
             if blk.is_attn:
@@ -334,6 +382,10 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
     del g
     model.fused_glue = True
     g, out = capture()
+    res["gemv_unfused_norms"] = timed(g)
+    del g
+    model.fused_norms = True
+    g, out = capture()
     res["gemv_pdl_prefetch"] = timed(g)
     before = out.clone()
     x.mul_(-1.0)
@@ -348,6 +400,7 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
             m._gemv_next = None
     g, out = capture()
     res["gemv_pdl"] = timed(g)
+    model.fused_norms = False
     del g
     for m in model.projections():
         unpatch_linear(m)
@@ -357,10 +410,10 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
     us = res["gemv_pdl_prefetch"]
     cfg = model.cfg
     n_attn = len(cfg.attn_layer_idx)
-    # with the fused glue: per Mamba2 block add+LayerNorm, split+conv, SSU,
-    # gated RMSNorm; per attention block add+LayerNorm, rotary+cache, SDPA,
-    # add+LayerNorm, SwiGLU; then the final norm and the head's input copy
-    launches_other = (cfg.n_layer - n_attn) * 4 + n_attn * 5 + 2
+    # with the fused glue and norms: per Mamba2 block split+conv and SSU; per
+    # attention block rotary+cache, SDPA and SwiGLU; then the final norm and
+    # the head's input copy
+    launches_other = (cfg.n_layer - n_attn) * 2 + n_attn * 3 + 2
     return {
         "metric": "synthetic Zonos-hybrid decode step µs (46 layers, CUDA graph)",
         "value": round(us, 1),
@@ -370,6 +423,7 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
         "weight_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
         "us_gemv_without_prefetch_chain": round(res["gemv_pdl"], 1),
         "us_torch_glue": round(res["torch_glue"], 1),
+        "us_norms_as_kernels": round(res["gemv_unfused_norms"], 1),
         "us_cublas_linear": round(res["cublas"], 1),
         "patched_linears": n,
         "tokens_per_s": round(1e6 / us, 1),

@@ -93,6 +93,60 @@ def gemv(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor | None = None, out_
     return out
 
 
+def _linear_next(lin) -> tuple:
+    """sn_gemv_ex's next-weight arguments from a patched Linear's chain link
+    (kernels.patch.link_decode_chain), or none."""
+    nxt = getattr(lin, "_gemv_next", None) if lin is not None else None
+    return nxt[0] if nxt is not None else (_lib.SN_WEIGHT_BF16, None, 0, 0, 0)
+
+
+def _gemv_norm(kind, x, aux, norm_w, norm_b, W, eps, residual_out, out, pdl, stream, link):
+    M, N, K = _check_gemv(x, W)
+    for name, t in (("aux", aux), ("residual_out", residual_out)):
+        if t is not None:
+            require_cuda(name, t, _BF16, 2)
+            if tuple(t.shape) != (M, K) or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous bf16 [{M}, {K}] tensor")
+    for name, t in (("norm_w", norm_w), ("norm_b", norm_b)):
+        if t is not None:
+            require_cuda(name, t, _BF16)
+            if t.numel() != K or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous bf16 [{K}] tensor")
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous")
+    if out is None:
+        out = torch.empty(M, N, device=x.device, dtype=_BF16)
+    call("sn_gemv_bf16_norm", kind, W.data_ptr(), row_major("W", W), x.data_ptr(),
+         aux.data_ptr() if aux is not None else None, norm_w.data_ptr(),
+         norm_b.data_ptr() if norm_b is not None else None,
+         residual_out.data_ptr() if residual_out is not None else None, float(eps), out.data_ptr(), N, M, N, K,
+         _lib.SN_DTYPE_BF16, _lib.SN_FLAG_PDL if pdl else 0, stream_handle(stream), *_linear_next(link))
+    return out
+
+
+def gemv_rmsnorm_gated(x: torch.Tensor, z: torch.Tensor | None, norm_w: torch.Tensor, W: torch.Tensor,
+                       eps: float = 1e-5, out=None, pdl: bool = True, stream=None, link=None) -> torch.Tensor:
+    """``rmsnorm_fn(x, norm_w, None, z, eps, norm_before_gate=False)`` (one
+    group over the row) followed by ``x' @ W.T``, the norm done inside the
+    GEMV's x staging (``sn_gemv_bf16_norm``): one launch for the Mamba2 step's
+    gated RMSNorm -> out_proj.  ``link``: a patched Linear whose next-weight
+    hint to use."""
+    return _gemv_norm(_lib.SN_NORM_RMS_GATED, x, z, norm_w, None, W, eps, None, out, pdl, stream, link)
+
+
+def gemv_add_layernorm(x: torch.Tensor, residual: torch.Tensor | None, norm_w: torch.Tensor,
+                       norm_b: torch.Tensor | None, W: torch.Tensor, eps: float = 1e-5, out=None,
+                       pdl: bool = True, stream=None, link=None):
+    """``layer_norm_fn(x, norm_w, norm_b, residual, eps, prenorm=True)``
+    followed by ``x' @ W.T`` in one launch: returns (y, residual_out) with
+    residual_out = x + residual (bf16), as the block entry of a Zonos decode
+    step feeds in_proj / qkv / fc1."""
+    M, K = x.shape
+    rout = torch.empty(M, K, device=x.device, dtype=_BF16)
+    y = _gemv_norm(_lib.SN_NORM_ADD_LAYER, x, residual, norm_w, norm_b, W, eps, rout, out, pdl, stream, link)
+    return y, rout
+
+
 def _launcher(y, x, W, M, N, K, stream):
     if tuple(x.shape) != (M, K) or tuple(W.shape) != (N, K) or tuple(y.shape) != (M, N):
         raise ValueError("shapes of y, x, W disagree with M, N, K")

@@ -88,14 +88,14 @@ def patched():
     return m, p, st, x
 
 
-@pytest.mark.parametrize("fused_glue", [True, False])
-def test_step_matches_oracle_chain(patched, fused_glue):
+@pytest.mark.parametrize("fused_glue,fused_norms", [(True, True), (True, False), (False, False)])
+def test_step_matches_oracle_chain(patched, fused_glue, fused_norms):
     m, p, st, x = patched
     _restore(m, st)
-    m.fused_glue = fused_glue
+    m.fused_glue, m.fused_norms = fused_glue, fused_norms
     with torch.no_grad():
         logits = m.step(x)
-    m.fused_glue = True
+    m.fused_glue, m.fused_norms = True, False
     torch.cuda.synchronize()
     truth = O.zonos_decode_step_ref(p, _np(x), _cfg(m))
     got = logits.cpu().numpy()
@@ -179,3 +179,34 @@ def test_glue_kernels_match_torch_glue():
     ref = h[:, :8192] * torch.nn.functional.silu(h[:, 8192:])
     ulp = (ref.float().abs() * 2.0 ** -7).clamp_min(1e-30)
     assert ((y.float() - ref.float()).abs() <= ulp).all()
+
+
+@pytest.mark.parametrize("M", [1, 2])
+def test_norm_fused_gemv_matches_norm_then_gemv(M):
+    """The norms fused into the GEMV's x staging against the standalone norm
+    kernel followed by the GEMV: the residual sum bit for bit, the outputs
+    within the decode-step tolerance (the row sums run in another order, so
+    x' may differ by one bf16 rounding)."""
+    from sonata_b200.kernels import gemv as G
+    from sonata_b200.kernels import mamba_step as MS
+    g = torch.Generator(device="cuda").manual_seed(30 + M)
+    r = lambda *s, sc=1.0: (torch.randn(*s, device="cuda", generator=g) * sc).to(torch.bfloat16)
+    # gated RMSNorm -> out_proj (K = 4096)
+    y, z, w = r(M, 4096), r(M, 4096), r(4096, sc=0.5)
+    W = r(2048, 4096, sc=0.02)
+    got = G.gemv_rmsnorm_gated(y, z, w, W, 1e-5)
+    ref = G.gemv(MS.rmsnorm_fn(y, w, None, z=z, eps=1e-5, group_size=4096, norm_before_gate=False), W)
+    torch.cuda.synchronize()
+    err = (got.float() - ref.float()).abs().max().item()
+    assert err <= 2e-2 * ref.float().abs().max().item(), err
+    # add + LayerNorm -> in_proj (K = 2048), with and without a residual
+    for with_res in (True, False):
+        h, res, w2, b2 = r(M, 2048), r(M, 2048), r(2048, sc=0.5), r(2048, sc=0.1)
+        W2 = r(8512, 2048, sc=0.02)
+        got, rout = G.gemv_add_layernorm(h, res if with_res else None, w2, b2, W2, 1e-5)
+        xn, rref = MS.layer_norm_fn(h, w2, b2, residual=res if with_res else None, eps=1e-5, prenorm=True)
+        ref = G.gemv(xn, W2)
+        torch.cuda.synchronize()
+        assert torch.equal(rout, rref)
+        err = (got.float() - ref.float()).abs().max().item()
+        assert err <= 2e-2 * ref.float().abs().max().item(), (with_res, err)
