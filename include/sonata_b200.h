@@ -132,6 +132,56 @@ int sn_gemv_bf16_norm(int norm_kind, const void *W, int64_t ldw, const void *x, 
                       int64_t next_ldw, int next_N, int next_K);
 
 /*
+ * GEMV chain: a list of bf16 decode GEMVs y_j = x_j W_j^T (e.g. the per-token
+ * projection set of a Zonos-hybrid decode step) run by ONE persistent
+ * launch instead of one launch per GEMV.  Every CTA streams the jobs' weight
+ * rows in order through one ring, so HBM keeps reading the next job's
+ * weights while the current job finishes; only a job's x waits, inside the
+ * kernel, for the job named by `dep` (an earlier job, or -1: x is ready when
+ * the launch starts).  dep = j - 1 for every job gives the ordering of
+ * back-to-back launches on one stream.  Results are bit-identical to
+ * sn_gemv_bf16 on the same job (same tensor-core partition and order).
+ * Same role as a CUDA graph of patched nn.Linear calls (kernels/patch.py:54-66,
+ * kernels/bench_gemv_graph.py:30-63); no counterpart in the reference.
+ *
+ * Job: W bf16 [N, ldw], x bf16 [M, ldx], y [M, ldy] in y_dtype; W and x
+ * 16-byte aligned, ldw and ldx multiples of 8; K within the tensor-core
+ * GEMV's rules (K * 2 a multiple of 512).  M (1 or 2) is common to the chain.
+ * No job may write a weight or another job's y, nor x of a job that does not
+ * wait for it (through its dep, its dep's dep, ...); x and y of a job must
+ * not overlap.  Violations: SN_ERR_INVALID_ARGUMENT.
+ *
+ * sn_gemv_chain_plan validates the jobs on the host, writes the device job
+ * table and zeroed completion counters into `workspace` (device memory of
+ * sn_gemv_chain_workspace_size(njobs) bytes, 16-byte aligned) and fills
+ * *info; it synchronises `stream` (set-up, not for capture).
+ * sn_gemv_chain_launch enqueues the chain (capturable; flags 0 or
+ * SN_FLAG_PDL).  One launch per workspace at a time: the counters live there.
+ */
+typedef struct sn_gemv_job {
+  const void *W;
+  const void *x;
+  void *y;
+  int64_t ldw, ldx, ldy; /* elements */
+  int N, K;
+  int dep;     /* earlier job whose outputs x waits for, -1: none */
+  int y_dtype; /* SN_DTYPE_BF16 or SN_DTYPE_F32 */
+} sn_gemv_job;
+
+typedef struct sn_gemv_chain_info { /* filled by sn_gemv_chain_plan */
+  int njobs, M;
+  int ctas_per_sm;
+  uint32_t tile_bytes_max;       /* largest weight tile (16 / S whole rows) */
+  uint32_t ring_bytes, xbuf_bytes; /* shared-memory weight ring, one x buffer */
+  uint64_t workspace_bytes;
+} sn_gemv_chain_info;
+
+size_t sn_gemv_chain_workspace_size(int njobs);
+int sn_gemv_chain_plan(const sn_gemv_job *jobs, int njobs, int M, void *workspace, size_t workspace_bytes,
+                       sn_gemv_chain_info *info, void *stream);
+int sn_gemv_chain_launch(const sn_gemv_chain_info *info, void *workspace, unsigned flags, void *stream);
+
+/*
  * Per-output-channel weight quantisation on the device (bit-identical to
  * scripts/fake_quant.py:37-40 for int8):
  *   scale[n] = max(max_k |W[n, k]|, 1e-8) / 127   (int8)   or / 448 (e4m3)

@@ -75,6 +75,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_diag_bounded_wait": ([ctypes.c_uint64, _P], _I),
     "sn_snake_conv_transpose1d_pack": ([_P, _I, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
     "sn_snake_conv_transpose1d_output_length": ([_I64, _I, _I, _I], _I64),
+    "sn_gemv_chain_workspace_size": ([_I], ctypes.c_size_t),
+    "sn_gemv_chain_plan": ([_P, _I, _I, _P, ctypes.c_size_t, _P, _P], _I),
+    "sn_gemv_chain_launch": ([_P, _P, _U, _P], _I),
     "sn_snake_conv_transpose1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _U, _P,
                                    ctypes.c_size_t, _P], _I),
 }
@@ -85,6 +88,20 @@ class ShiftDesc(ctypes.Structure):
     """sn_shift_desc of include/sonata_b200.h."""
     _fields_ = [("buf", ctypes.c_void_p), ("batch_stride", ctypes.c_int64), ("row_stride", ctypes.c_int64),
                 ("batches", ctypes.c_int), ("rows", ctypes.c_int), ("src", ctypes.c_int), ("len", ctypes.c_int)]
+
+
+class GemvJob(ctypes.Structure):
+    """sn_gemv_job of include/sonata_b200.h."""
+    _fields_ = [("W", ctypes.c_void_p), ("x", ctypes.c_void_p), ("y", ctypes.c_void_p), ("ldw", ctypes.c_int64),
+                ("ldx", ctypes.c_int64), ("ldy", ctypes.c_int64), ("N", ctypes.c_int), ("K", ctypes.c_int),
+                ("dep", ctypes.c_int), ("y_dtype", ctypes.c_int)]
+
+
+class GemvChainInfo(ctypes.Structure):
+    """sn_gemv_chain_info of include/sonata_b200.h."""
+    _fields_ = [("njobs", ctypes.c_int), ("M", ctypes.c_int), ("ctas_per_sm", ctypes.c_int),
+                ("tile_bytes_max", ctypes.c_uint32), ("ring_bytes", ctypes.c_uint32), ("xbuf_bytes", ctypes.c_uint32),
+                ("workspace_bytes", ctypes.c_uint64)]
 
 
 SN_SHIFT_MAX_DESCS = 48

@@ -37,6 +37,7 @@
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 namespace sn {
 namespace {
@@ -1679,6 +1680,408 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16*
 }
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// GEMV chain: a list of bf16 decode GEMVs (the per-token projection set of a
+// decode step) streamed by ONE persistent launch.
+//
+// Between two launches of the per-call kernel HBM idles for the kernel
+// boundary (~2.2 us per GEMV on B200: the previous grid drains, the next one's
+// griddepcontrol.wait returns, x lands, the first MMAs issue), which is what
+// holds the 156-GEMV set of a Zonos step below the copy roofline.  Weights are
+// frozen, so nothing stops a CTA from streaming the next GEMV's rows into its
+// ring while the current GEMV finishes: here every CTA walks the jobs in
+// order with the same ring, TMEM accumulators and epilogue as the per-call
+// kernel, and only the x of a job waits, in the kernel, for the job that
+// produces it.
+//
+// Ordering between jobs: job j names `dep`, an earlier job whose completion
+// its x waits for (-1: x is ready when the launch starts).  Every CTA's
+// epilogue, after storing its rows of job j, releases one count on job j's
+// completion counter (gpu scope); a job's x loader acquires its dep's counter
+// at grid size before it copies x (then a proxy fence, since the copy is a
+// bulk copy).  dep = j - 1 for every job is the order of back-to-back
+// launches on one stream.  The last CTA to leave zeroes the counters for the
+// next launch.  All CTAs are co-resident (cooperative launch), and every wait
+// is bounded.
+//
+// Warps: 0 weight producer (frozen weights, no wait), 1 TMEM owner and MMA
+// issuer, 2..5 epilogue (TMEM lane quarter = warp % 4), 6 x loader.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct ChainJob {  // device copy of one job (64 bytes)
+  const uint8_t* W;
+  const __nv_bfloat16* x;
+  void* y;
+  int64_t ldw_bytes;
+  int ldx, ldy;  // elements
+  int N, K;
+  int dep;
+  int S;  // row segments (2 or 4): 16 / S rows per tile
+  int flags;  // kJobF32 (fp32 y), kJobSignal (a later job waits for this one)
+  uint32_t tile_bytes;
+};
+static_assert(sizeof(ChainJob) == 64, "ChainJob is 64 bytes");
+
+constexpr int kChainThreads = 224;
+constexpr int kChainAcc = 8;             // TMEM accumulators (a power of two)
+constexpr int kJobF32 = 1, kJobSignal = 2;
+constexpr int kChainTiles = 16;          // weight tiles in flight at most (mbarrier pairs)
+constexpr int kChainXBufs = 2;           // x buffers: x copies run up to this many jobs ahead (4: no faster)
+constexpr int kChainCounterStride = 32;  // one 128-byte line per completion counter
+
+struct ChainParams {
+  const ChainJob* jobs;
+  unsigned* counters;  // [njobs] completions, one line each, then the exit ticket
+  int njobs, M;
+  uint32_t ring_bytes;   // weight ring (>= every job's tile_bytes)
+  uint32_t xbuf_bytes;   // one x buffer: MT rows of the longest K
+  uint32_t xs_off, ring_off;
+  uint32_t tcols;
+  uint32_t copy_bytes;  // largest bulk copy of a weight tile (0: one copy per tile)
+};
+
+__device__ __forceinline__ ChainJob load_job(const ChainJob* jobs, int j) {
+  union {
+    uint4 v[4];
+    ChainJob job;
+  } u;
+  const uint4* src = reinterpret_cast<const uint4*>(jobs + j);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) u.v[i] = __ldg(src + i);
+  return u.job;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Named barrier that also returns the OR of `v` over the participating threads.
+__device__ __forceinline__ bool named_bar_or(int id, int threads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Bounded wait until *c >= target (one second, as every mbarrier wait here).
+__device__ __forceinline__ bool wait_counter(const unsigned* c, unsigned target) {
+  if (ld_acquire_gpu(c) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_gpu(c) < target) {
+    if (globaltimer_ns() - t0 > 1000000000ull) return false;
+    __nanosleep(32);
+  }
+  return true;
+}
+
+// Rows [r0, r1) of a job with N rows owned by CTA c of G.
+__device__ __forceinline__ void cta_rows(int N, int c, int G, int& r0, int& r1) {
+  r0 = static_cast<int>(static_cast<int64_t>(N) * c / G);
+  r1 = static_cast<int>(static_cast<int64_t>(N) * (c + 1) / G);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const ChainParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kChainTiles], tile t uses t % kChainTiles
+  uint64_t* empty = full + kChainTiles;
+  uint64_t* tfull = empty + kChainTiles;
+  uint64_t* tempty = tfull + kChainAcc;
+  uint64_t* xfull = tempty + kChainAcc;
+  uint64_t* xfree = xfull + kChainXBufs;
+  uint64_t* done = xfree + kChainXBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint32_t* tbeg = tmem_slot + 1;  // producer only: ring range of the tiles in flight
+  uint32_t* tend = tbeg + kChainTiles;
+  uint8_t* xs = smem + p.xs_off;
+  uint8_t* ring = smem + p.ring_off;
+  constexpr uint32_t kAccStride = 32 * MT;  // TMEM columns per accumulator (N of an S = 4 job)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kChainTiles; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < kChainAcc; ++b) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, 4);
+    }
+    for (int b = 0; b < kChainXBufs; ++b) {
+      mbar_init(xfull + b, 1);
+      mbar_init(xfree + b, 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, p.tcols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- producer: every job's weight rows, in job order ------
+    // The ring is a byte ring: tile t (tile_bytes of its job) goes right
+    // after tile t - 1, or at 0 when it would pass the end, so tiles of
+    // different jobs pack without padding; before it is written, the oldest
+    // tiles it overlaps (and any beyond kChainTiles in flight) must have
+    // been consumed.
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int t = 0, tail = 0;
+      uint32_t off = 0;
+      bool ok = true;
+      ChainJob job = load_job(p.jobs, 0), nxt;
+      for (int j = 0; j < p.njobs && ok; ++j, job = nxt) {
+        nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));  // in flight while job j runs
+        if (job.tile_bytes > p.ring_bytes) {  // workspace and plan do not match
+          record_status(SN_ERR_INVALID_ARGUMENT);
+          ok = false;
+          break;
+        }
+        const int R = 16 / job.S;
+        const uint32_t row_bytes = static_cast<uint32_t>(job.K) * 2;
+        int r0, r1;
+        cta_rows(job.N, c, G, r0, r1);
+        for (int first = r0; first < r1; first += R, ++t) {
+          if (off + job.tile_bytes > p.ring_bytes) off = 0;
+          const uint32_t end = off + job.tile_bytes;
+          // the youngest tile in flight that the new one overlaps (tiles are
+          // consumed in order, so its release implies every older one's)
+          int need = t - kChainTiles;  // the mbarrier pair is reused
+          for (int v = max(tail, 0); v < t; ++v) {
+            const int q = v % kChainTiles;
+            if (tend[q] > off && tbeg[q] < end) need = max(need, v);
+          }
+          if (need >= tail) {
+            if (!mbar_wait_bounded(empty + need % kChainTiles, (need / kChainTiles) & 1)) {
+              record_status(SN_ERR_TIMEOUT);
+              ok = false;
+              break;
+            }
+            tail = need + 1;
+          }
+          const int q = t % kChainTiles;
+          tbeg[q] = off;
+          tend[q] = end;
+          const int cnt = min(R, r1 - first);
+          uint8_t* dst = ring + off;
+          mbar_arrive_expect_tx(full + q, static_cast<uint32_t>(cnt) * row_bytes);
+          if (job.ldw_bytes == static_cast<int64_t>(row_bytes)) {
+            const uint8_t* src = job.W + static_cast<int64_t>(first) * job.ldw_bytes;
+            const uint32_t bytes = static_cast<uint32_t>(cnt) * row_bytes;
+            const uint32_t piece = p.copy_bytes ? p.copy_bytes : bytes;
+            for (uint32_t o = 0; o < bytes; o += piece)
+              bulk_g2s(dst + o, src + o, min(piece, bytes - o), full + q, pol);
+          } else {
+            for (int r = 0; r < cnt; ++r)
+              bulk_g2s(dst + static_cast<size_t>(r) * row_bytes, job.W + static_cast<int64_t>(first + r) * job.ldw_bytes,
+                       row_bytes, full + q, pol);
+          }
+          off = end;
+        }
+      }
+      if (!ok) {
+        // let the copies in flight land before the CTA exits
+        for (int v = (t > kChainTiles ? t - kChainTiles : 0); v < t; ++v)
+          mbar_wait_bounded(full + v % kChainTiles, (v / kChainTiles) & 1);
+      }
+    }
+  } else if (warp == 6) {
+    // ---------------- x loader: waits for each job's producer --------------
+    if (lane == 0) {
+      pdl_wait();  // the first jobs' x and the counters belong to earlier kernels
+      const uint64_t pol = l2_policy_evict_normal();
+      int u = 0;
+      ChainJob job = load_job(p.jobs, 0), nxt;
+      for (int j = 0; j < p.njobs; ++j, job = nxt) {
+        nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
+        int r0, r1;
+        cta_rows(job.N, c, G, r0, r1);
+        if (r0 == r1) continue;
+        const int b = u % kChainXBufs;
+        const uint32_t row_bytes = static_cast<uint32_t>(job.K) * 2;
+        if (static_cast<uint32_t>(p.M) * row_bytes > p.xbuf_bytes) {
+          record_status(SN_ERR_INVALID_ARGUMENT);
+          break;
+        }
+        if ((u >= kChainXBufs && !mbar_wait_bounded(xfree + b, ((u / kChainXBufs) - 1) & 1)) ||
+            (job.dep >= 0 && !wait_counter(p.counters + static_cast<size_t>(job.dep) * kChainCounterStride,
+                                           static_cast<unsigned>(G)))) {
+          record_status(SN_ERR_TIMEOUT);
+          break;
+        }
+        if (job.dep >= 0) fence_proxy_async_global();  // acquired generic writes -> the bulk copy below
+        uint8_t* dst = xs + static_cast<size_t>(b) * p.xbuf_bytes;
+        mbar_arrive_expect_tx(xfull + b, static_cast<uint32_t>(p.M) * row_bytes);
+        for (int m = 0; m < p.M; ++m)
+          bulk_g2s(dst + static_cast<size_t>(m) * row_bytes, job.x + static_cast<int64_t>(m) * job.ldx, row_bytes,
+                   xfull + b, pol);
+        ++u;
+      }
+      // the last copies have landed before the CTA can exit (the MMA issuer
+      // waits for them too unless it stopped early)
+      for (int v = (u > kChainXBufs ? u - kChainXBufs : 0); v < u; ++v)
+        mbar_wait_bounded(xfull + v % kChainXBufs, (v / kChainXBufs) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int t = 0, u = 0;
+      uint32_t off = 0;  // the producer's placement rule, replayed
+      bool ok = true;
+      ChainJob job = load_job(p.jobs, 0), nxt;
+      for (int j = 0; j < p.njobs && ok; ++j, job = nxt) {
+        nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
+        int r0, r1;
+        cta_rows(job.N, c, G, r0, r1);
+        if (r0 == r1) continue;
+        const int b = u % kChainXBufs;
+        if (!mbar_wait_bounded(xfull + b, (u / kChainXBufs) & 1)) {
+          record_status(SN_ERR_TIMEOUT);
+          break;
+        }
+        const int R = 16 / job.S;
+        const uint32_t L = static_cast<uint32_t>(job.K) * 2 / job.S;  // segment bytes
+        const uint32_t nk = L / 256;
+        const uint32_t idesc = tc::idesc_bf16_f32(128, 8 * job.S * MT);
+        const uint64_t db0 = tc::smem_desc_noswz(xs + static_cast<size_t>(b) * p.xbuf_bytes, 128, L);
+        for (int first = r0; first < r1; first += R, ++t) {
+          if (off + job.tile_bytes > p.ring_bytes) off = 0;
+          const int q = t % kChainTiles, a = t & (kChainAcc - 1);
+          if (!mbar_wait_bounded(full + q, (t / kChainTiles) & 1) ||
+              (t >= kChainAcc && !mbar_wait_bounded(tempty + a, ((t / kChainAcc) - 1) & 1))) {
+            record_status(SN_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint64_t da0 = tc::smem_desc_noswz(ring + off, 128, L);
+          const uint32_t d = tmem + static_cast<uint32_t>(a) * kAccStride;
+          for (uint32_t k = 0; k < nk; ++k) tc::mma_bf16(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+          tc::mma_commit(empty + q);
+          tc::mma_commit(tfull + a);
+          off += job.tile_bytes;
+        }
+        tc::mma_commit(xfree + b);  // x buffer b is free once these MMAs retire
+        ++u;
+      }
+      // every MMA issued has retired before TMEM is released
+      tc::mma_commit(done);
+      if (!mbar_wait_bounded(done, 0)) record_status(SN_ERR_TIMEOUT);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    pdl_wait();  // y and the counters belong to earlier kernels until here
+    const int q = warp & 3;
+    const int i = q * 32 + lane;  // A row = TMEM lane
+    int t = 0;
+    bool ok = true;
+    ChainJob job = load_job(p.jobs, 0), nxt;
+    for (int j = 0; j < p.njobs; ++j, job = nxt) {
+      nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
+      int r0, r1;
+      cta_rows(job.N, c, G, r0, r1);
+      const int R = 16 / job.S;
+      const int Gs = 8 * job.S;  // TMEM lanes (and columns) per weight row
+      const int r = i / Gs;      // weight row inside the tile
+      for (int first = r0; ok && first < r1; first += R, ++t) {
+        const int a = t & (kChainAcc - 1);
+        const int cnt = min(R, r1 - first);
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(tfull + a, (t / kChainAcc) & 1))) {
+          record_status(SN_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a) * kAccStride;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float v = job.S == 2 ? diag_entry<2>(taddr + m * Gs, lane) : diag_entry<4>(taddr + m * Gs, lane);
+          for (int o = Gs / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if ((lane & (Gs - 1)) == 0 && r < cnt && m < p.M) {
+            const int64_t off = static_cast<int64_t>(m) * job.ldy + first + r;
+            if (job.flags & kJobF32)
+              static_cast<float*>(job.y)[off] = v;
+            else
+              static_cast<__nv_bfloat16*>(job.y)[off] = __float2bfloat16_rn(v);
+          }
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty + a);
+      }
+      // the four epilogue warps agree on whether to go on (a warp whose wait
+      // ran out skipped its remaining tiles); then, if a later job waits for
+      // job j, one count on its completion: this CTA's rows are stored (the
+      // barrier orders the four warps' stores before the release)
+      // (a warp that stopped skips the tiles of the jobs without a barrier
+      // and leaves at the next one, with the others)
+      if (job.flags & kJobSignal) {
+        if (named_bar_or(2, 128, !ok)) break;
+        if (threadIdx.x == 64) red_release_gpu_add(p.counters + static_cast<size_t>(j) * kChainCounterStride, 1u);
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, p.tcols);
+  if (threadIdx.x == 0) {
+    // the last CTA to leave zeroes the counters for the next launch (every
+    // other CTA has finished all its waits and counts before taking a ticket)
+    unsigned* ticket = p.counters + static_cast<size_t>(p.njobs) * kChainCounterStride;
+    __threadfence();
+    if (atomicAdd(ticket, 1u) == static_cast<unsigned>(G) - 1) {
+      __threadfence();
+      for (int j = 0; j < p.njobs; ++j) p.counters[static_cast<size_t>(j) * kChainCounterStride] = 0;
+      *ticket = 0;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace
+
+namespace {
+
+constexpr int kChainMaxJobs = 4096;
+
+size_t chain_table_bytes(int njobs) { return (static_cast<size_t>(njobs) * sizeof(ChainJob) + 127) / 128 * 128; }
+size_t chain_workspace_bytes(int njobs) {
+  return chain_table_bytes(njobs) + static_cast<size_t>(njobs + 1) * kChainCounterStride * sizeof(unsigned);
+}
+
+// Dynamic shared memory of one chain CTA: one CTA per SM (a second one would
+// halve the ring, and config-2 shapes need two 44 KB tiles plus x in each).
+constexpr size_t kChainSmem = 232448;
+
+struct ByteRange {
+  uintptr_t lo, hi;  // [lo, hi)
+};
+ByteRange rows_range(const void* p, int rows, int64_t ld, int64_t len, int esz) {
+  const uintptr_t lo = reinterpret_cast<uintptr_t>(p);
+  return {lo, lo + static_cast<uintptr_t>(((rows - 1) * ld + len) * esz)};
+}
+bool overlap(const ByteRange& a, const ByteRange& b) { return a.lo < b.hi && b.lo < a.hi; }
+
+}  // namespace
+
 }  // namespace sn
 
 extern "C" {
@@ -1739,6 +2142,155 @@ int sn_quantize_rows_int8(const void* W, int64_t ldw, int N, int K, int8_t* q, i
 int sn_quantize_rows_fp8e4m3(const void* W, int64_t ldw, int N, int K, uint8_t* q, int64_t ldq, float* scale,
                              void* stream) {
   return quantize_rows(true, W, ldw, N, K, q, ldq, scale, stream);
+}
+
+
+size_t sn_gemv_chain_workspace_size(int njobs) {
+  if (njobs < 1 || njobs > sn::kChainMaxJobs) return 0;
+  return sn::chain_workspace_bytes(njobs);
+}
+
+int sn_gemv_chain_plan(const sn_gemv_job* jobs, int njobs, int M, void* workspace, size_t workspace_bytes,
+                       sn_gemv_chain_info* info, void* stream) {
+  using namespace sn;
+  if (!jobs || !workspace || !info || njobs < 1 || njobs > kChainMaxJobs || M < 1 || M > 2)
+    return SN_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < chain_workspace_bytes(njobs)) return SN_ERR_INVALID_ARGUMENT;
+  if (!aligned16(workspace)) return SN_ERR_MISALIGNED;
+  const int MT = M;
+  std::vector<ChainJob> dev(static_cast<size_t>(njobs));
+  std::vector<ByteRange> xr(njobs), yr(njobs), wr(njobs);
+  uint32_t tile_max = 0;
+  int kmax = 0;
+  for (int j = 0; j < njobs; ++j) {
+    const sn_gemv_job& a = jobs[j];
+    if (!a.W || !a.x || !a.y || a.N < 1 || a.K < 1 || a.ldw < a.K || a.ldx < a.K || a.ldy < a.N)
+      return SN_ERR_INVALID_ARGUMENT;
+    if (a.dep < -1 || a.dep >= j) return SN_ERR_INVALID_ARGUMENT;
+    if (a.y_dtype != SN_DTYPE_BF16 && a.y_dtype != SN_DTYPE_F32) return SN_ERR_INVALID_ARGUMENT;
+    if (!aligned16(a.W) || !aligned16(a.x) || (a.ldw * 2) % 16 != 0 || (a.ldx * 2) % 16 != 0)
+      return SN_ERR_MISALIGNED;
+    const int S = mma_segments(a.K, 2, MT, 1);
+    if (S == 0 || a.ldx > INT_MAX || a.ldy > INT_MAX) return SN_ERR_UNSUPPORTED;
+    const int64_t tile = static_cast<int64_t>(16 / S) * a.K * 2;
+    if (tile > 128 * 1024) return SN_ERR_UNSUPPORTED;
+    ChainJob& d = dev[j];
+    d.W = static_cast<const uint8_t*>(a.W);
+    d.x = static_cast<const __nv_bfloat16*>(a.x);
+    d.y = a.y;
+    d.ldw_bytes = a.ldw * 2;
+    d.ldx = static_cast<int>(a.ldx);
+    d.ldy = static_cast<int>(a.ldy);
+    d.N = a.N;
+    d.K = a.K;
+    d.dep = a.dep;
+    d.S = S;
+    d.flags = (a.y_dtype == SN_DTYPE_F32) ? kJobF32 : 0;
+    d.tile_bytes = static_cast<uint32_t>(tile);
+    tile_max = std::max(tile_max, d.tile_bytes);
+    kmax = std::max(kmax, a.K);
+    xr[j] = rows_range(a.x, M, a.ldx, a.K, 2);
+    yr[j] = rows_range(a.y, M, a.ldy, a.N, a.y_dtype == SN_DTYPE_F32 ? 4 : 2);
+    wr[j] = rows_range(a.W, a.N, a.ldw, a.K, 2);
+  }
+  for (int j = 0; j < njobs; ++j)
+    if (jobs[j].dep >= 0) dev[jobs[j].dep].flags |= kJobSignal;
+  // Buffers: no job writes a weight or another job's output, and a job's x
+  // may be written only by a job it waits for (its dep, its dep's dep, ...).
+  for (int j = 0; j < njobs; ++j) {
+    for (int i = 0; i < njobs; ++i) {
+      if (overlap(yr[i], wr[j])) return SN_ERR_INVALID_ARGUMENT;
+      if (i != j && overlap(yr[i], yr[j])) return SN_ERR_INVALID_ARGUMENT;
+      if (!overlap(yr[i], xr[j])) continue;
+      bool waits = false;
+      for (int d = jobs[j].dep; d >= 0 && !waits; d = jobs[d].dep) waits = (d == i);
+      if (!waits) return SN_ERR_INVALID_ARGUMENT;
+    }
+  }
+  const uint32_t xbuf = round_up_u32(static_cast<uint32_t>(MT * kmax * 2), 128);
+  const uint32_t ring_off = round_up_u32(1024 + kChainXBufs * xbuf, 1024);
+  const size_t budget = kChainSmem;
+  if (budget < ring_off + 2 * static_cast<size_t>(tile_max)) return SN_ERR_UNSUPPORTED;  // two tiles in flight at least
+  uint32_t ring_bytes = static_cast<uint32_t>((budget - ring_off) / 1024 * 1024);
+  if (const char* e = getenv("SONATA_CHAIN_RING_KB")) {  // measurement override (smaller rings only)
+    const uint32_t kb = static_cast<uint32_t>(atoi(e));
+    if (kb * 1024 >= 2 * tile_max && kb * 1024 < ring_bytes) ring_bytes = kb * 1024;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (cudaMemcpyAsync(ws, dev.data(), dev.size() * sizeof(ChainJob), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemsetAsync(ws + chain_table_bytes(njobs), 0,
+                      static_cast<size_t>(njobs + 1) * kChainCounterStride * sizeof(unsigned), st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_LAUNCH;
+  }
+  info->njobs = njobs;
+  info->M = M;
+  info->ctas_per_sm = 1;
+  info->tile_bytes_max = tile_max;
+  info->ring_bytes = ring_bytes;
+  info->xbuf_bytes = xbuf;
+  info->workspace_bytes = chain_workspace_bytes(njobs);
+  return SN_OK;
+}
+
+int sn_gemv_chain_launch(const sn_gemv_chain_info* info, void* workspace, unsigned flags, void* stream) {
+  using namespace sn;
+  if (!info || !workspace) return SN_ERR_INVALID_ARGUMENT;
+  const int njobs = info->njobs, M = info->M;
+  if (njobs < 1 || njobs > kChainMaxJobs || M < 1 || M > 2 || info->ctas_per_sm != 1 || info->tile_bytes_max == 0 ||
+      info->tile_bytes_max % 16 != 0 || info->ring_bytes % 1024 != 0 || info->ring_bytes < 2 * info->tile_bytes_max ||
+      info->xbuf_bytes % 128 != 0 || info->workspace_bytes != chain_workspace_bytes(njobs))
+    return SN_ERR_INVALID_ARGUMENT;
+  if ((flags & ~SN_FLAG_PDL) != 0) return SN_ERR_INVALID_ARGUMENT;
+  ChainParams p;
+  p.jobs = static_cast<const ChainJob*>(workspace);
+  p.counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) + chain_table_bytes(njobs));
+  p.njobs = njobs;
+  p.M = M;
+  p.ring_bytes = info->ring_bytes;
+  p.xbuf_bytes = info->xbuf_bytes;
+  p.xs_off = 1024;
+  p.ring_off = round_up_u32(1024 + kChainXBufs * p.xbuf_bytes, 1024);
+  p.tcols = tc::tmem_cols_for(kChainAcc * 32 * M);
+  p.copy_bytes = 0;
+  if (const char* e = getenv("SONATA_CHAIN_COPY_KB")) p.copy_bytes = static_cast<uint32_t>(std::max(0, atoi(e))) * 1024;
+  const size_t smem = p.ring_off + static_cast<size_t>(p.ring_bytes);
+  if (smem > kChainSmem) return SN_ERR_INVALID_ARGUMENT;
+  const void* kern = M == 1 ? reinterpret_cast<const void*>(gemv_chain_kernel<1>)
+                            : reinterpret_cast<const void*>(gemv_chain_kernel<2>);
+  if (!ensure_smem(kern, smem)) return SN_ERR_UNSUPPORTED;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kChainThreads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_LAUNCH;
+  }
+  if (per_sm < 1) return SN_ERR_UNSUPPORTED;
+  // every CTA waits for others (job completions): all must be resident at
+  // once, which a cooperative launch guarantees
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(kChainThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  int na = 1;
+  if (flags & SN_FLAG_PDL) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = M == 1 ? cudaLaunchKernelEx(&cfg, gemv_chain_kernel<1>, p) : cudaLaunchKernelEx(&cfg, gemv_chain_kernel<2>, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_LAUNCH;
+  }
+  return SN_OK;
 }
 
 }  // extern "C"

@@ -24,6 +24,7 @@ scripts/fake_quant.py's simulation).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -91,6 +92,67 @@ def gemv(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor | None = None, out_
              row_major("x", x), out.data_ptr(), row_major("out", out), M, N, K, y_dtype, flags,
              stream_handle(stream), *_next_args(next_weight, x.device))
     return out
+
+
+class GemvChain:
+    """A list of bf16 decode GEMVs ``y_j = x_j @ W_j.T`` run by ONE persistent
+    launch (``sn_gemv_chain_*``), e.g. the per-token projection set of a
+    decode step.  Each CTA streams the jobs' weights in order through one
+    ring, so HBM reads the next job's weights while the current one finishes;
+    a job's x waits, inside the kernel, for the job named in ``deps``.
+
+    jobs: ``(W [N, K] bf16, x [M, K] bf16, y [M, N] bf16 or fp32)`` triples,
+    M (1 or 2) common to all.  deps: ``"serial"`` (job j waits for job j-1:
+    the order of back-to-back launches on one stream), ``"none"`` (every x is
+    ready when the launch starts) or a list of earlier job indices (-1: none).
+    The plan is validated and uploaded once; ``__call__`` only launches (CUDA
+    graph capturable).  Results equal ``gemv`` on each job bit for bit.
+    """
+
+    def __init__(self, jobs, deps="serial", device=None):
+        if not jobs:
+            raise ValueError("GemvChain needs at least one job")
+        n = len(jobs)
+        if deps == "serial":
+            deps = [j - 1 for j in range(n)]
+        elif deps == "none":
+            deps = [-1] * n
+        deps = [int(d) for d in deps]
+        if len(deps) != n:
+            raise ValueError("deps must name one dependency per job")
+        arr = (_lib.GemvJob * n)()
+        M = None
+        self._keep = []
+        for j, (W, x, y) in enumerate(jobs):
+            Mj, N, K = _check_gemv(x, W)
+            require_cuda("y", y, None, 2)
+            if y.shape != (Mj, N) or y.dtype not in (_BF16, torch.float32):
+                raise ValueError(f"job {j}: y must be [{Mj}, {N}] bf16 or fp32")
+            if M is None:
+                M = Mj
+            elif Mj != M:
+                raise ValueError("every job of a chain has the same M")
+            arr[j] = _lib.GemvJob(W.data_ptr(), x.data_ptr(), y.data_ptr(), row_major("W", W), row_major("x", x),
+                                  row_major("y", y), N, K, deps[j],
+                                  _lib.SN_DTYPE_F32 if y.dtype == torch.float32 else _lib.SN_DTYPE_BF16)
+            self._keep += [W, x, y]
+        if M > 2:
+            raise ValueError("a GEMV chain takes M <= 2")
+        dev = device if device is not None else jobs[0][0].device
+        nbytes = _lib.lib().sn_gemv_chain_workspace_size(n)
+        if nbytes == 0:
+            raise ValueError(f"{n} jobs: outside the chain's limits")
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.info = _lib.GemvChainInfo()
+        call("sn_gemv_chain_plan", ctypes.addressof(arr), n, M, self.workspace.data_ptr(), nbytes,
+             ctypes.byref(self.info), stream_handle(None))
+        self.njobs, self.M, self.deps = n, M, deps
+        self.outputs = [y for (_, _, y) in jobs]
+
+    def __call__(self, pdl: bool = False, stream=None):
+        call("sn_gemv_chain_launch", ctypes.byref(self.info), self.workspace.data_ptr(),
+             _lib.SN_FLAG_PDL if pdl else 0, stream_handle(stream))
+        return self.outputs
 
 
 def _linear_next(lin) -> tuple:

@@ -80,3 +80,45 @@ def test_product_raises_without_library(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "missing.so")
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.lib()
+
+
+def _job(W, x, y, N=64, K=256, dep=-1, ldw=None, ldx=None, ldy=None, y_dtype=0):
+    return _lib.GemvJob(W, x, y, ldw or K, ldx or K, ldy or N, N, K, dep, y_dtype)
+
+
+def test_gemv_chain_plan_rejects_bad_jobs_on_host(L):
+    """sn_gemv_chain_plan validates every job (shapes, alignment, dependency
+    order, buffer overlaps) before it touches the device: fake, never
+    dereferenced addresses are enough."""
+    assert L.sn_gemv_chain_workspace_size(0) == 0
+    assert L.sn_gemv_chain_workspace_size(4097) == 0
+    n = L.sn_gemv_chain_workspace_size(3)
+    assert n >= 3 * 64 + 4 * 128
+    ws = 1 << 40
+    info = _lib.GemvChainInfo()
+    W0, W1, X, Y0, Y1 = 1 << 30, 2 << 30, 3 << 30, 4 << 30, 5 << 30
+
+    def plan(jobs, M=1, wsb=n):
+        arr = (_lib.GemvJob * len(jobs))(*jobs)
+        return L.sn_gemv_chain_plan(ctypes.addressof(arr), len(jobs), M, ctypes.c_void_p(ws), wsb,
+                                    ctypes.byref(info), None)
+
+    good = [_job(W0, X, Y0), _job(W1, Y0, Y1, dep=0)]
+    assert plan(good, M=3) == -1                                    # M outside 1..2
+    assert plan(good, wsb=L.sn_gemv_chain_workspace_size(2) - 1) == -1  # workspace too small
+    assert plan([_job(W0, X, Y0), _job(W1, X, Y1, dep=1)]) == -1    # dep must name an earlier job
+    assert plan([_job(W0, X, Y0, y_dtype=5)]) == -1                 # output dtype
+    assert plan([_job(W0, X, Y0, ldw=128)]) == -1                   # row stride below K
+    assert plan([_job(W0 + 8, X, Y0)]) == -2                        # W not 16-byte aligned
+    assert plan([_job(W0, X, Y0, K=104)]) == -3                     # K outside the tensor-core rules
+    assert plan([_job(W0, X, Y0), _job(W1, Y0, Y1)]) == -1          # x written by a job it does not wait for
+    assert plan([_job(W0, X, Y0), _job(W1, X, Y0, dep=0)]) == -1    # two jobs writing one buffer
+    assert plan([_job(W0, X, W0 + 256)]) == -1                      # an output over a weight
+    assert plan([_job(W0, X, X)]) == -1                             # x and y of one job overlap
+    # a transitive dependency is enough: job 2 reads job 0's output through 1
+    chain3 = [_job(W0, X, Y0), _job(W1, X, Y1, dep=0), _job(W1 + (1 << 20), Y0, 6 << 30, dep=1)]
+    import torch
+    if not torch.cuda.is_available():  # valid jobs reach the device copy, which fails without a GPU
+        assert plan(chain3, wsb=L.sn_gemv_chain_workspace_size(3)) == -4
+    launch_info = _lib.GemvChainInfo(0, 1, 1, 2, 4096, 512, 0)
+    assert L.sn_gemv_chain_launch(ctypes.byref(launch_info), ctypes.c_void_p(ws), 0, None) == -1
