@@ -8,9 +8,13 @@ Headline workload: the full per-token decode GEMV set of a
 out_proj [2048, 4096], attention qkv [3072, 2048] and o_proj [2048, 2048],
 SwiGLU fc1 [11264, 2048] and fc2 [2048, 5632] -- 156 distinct bf16 weights,
 3.69 GB per step (far larger than the 126 MB L2, so no flush is needed).
-They run as 156 patched ``nn.Linear`` modules (``sonata_b200.kernels.patch``,
-the reference's drop-in) captured in one CUDA graph, the way Zonos captures
-its decode step.  A step is one replay of that graph.
+The 156 GEMVs have independent inputs; they run as ONE GEMV-chain launch
+(``kernels.gemv.GemvChain``: every SM streams the jobs' weights through one
+ring, so HBM is not idle across GEMV boundaries), captured in a CUDA graph.
+A step is one replay of that graph.  Reported beside it: the same set as 156
+patched ``nn.Linear`` modules (``sonata_b200.kernels.patch``, the
+reference's drop-in) in one graph, and the chain with every GEMV ordered
+after the previous one.
 
 * ``value``: weight+activation bytes streamed per second with x and W
   resident in HBM (CUDA events around K replays, max over ranks).
@@ -18,7 +22,7 @@ its decode step.  A step is one replay of that graph.
   vectors from pinned host memory, replays the graph and reads the 156 outputs
   back, inside the timed region; two buffers and graphs alternate so that the
   copies of one step overlap the compute of its neighbours.
-* ``roofline``: the GEMV kernel's achieved GB/s against the measured HBM copy
+* ``roofline``: the chain kernel's achieved GB/s against the measured HBM copy
   bandwidth in MEASURED_PEAKS.json.
 * ``cpu_baseline``: the reference's CPU path (torch ``F.linear`` in bf16, see
   oracle/cpu_baseline.py) on the host cores, rank 0 at N=1 only.
@@ -56,10 +60,11 @@ SHAPES = {"in_proj": (8512, 2048), "out_proj": (2048, 4096), "qkv": (3072, 2048)
           "fc1": (11264, 2048), "fc2": (2048, 5632)}
 LAYERS = 26
 NOMINAL_HBM_GBS = 8000.0
-# Per-launch DRAM traffic of the GEMV kernel from one ncu capture of in_proj
-# (profiles/gemv_mma_kernel_in_proj.md): dram__bytes_read.sum + write.sum.
-NCU_TRAFFIC_IN_PROJ = 34_893_568 + 0
-IN_PROJ_ALGO_BYTES = (8512 * 2048 + 2048 + 8512) * 2
+# DRAM traffic of one GEMV-chain launch over 4 layers (24 GEMVs) from one ncu
+# capture (profiles/gemv_chain_kernel_4layers.md): dram__bytes_read.sum +
+# dram__bytes_write.sum, and the algorithmic bytes of that launch.
+NCU_TRAFFIC_CHAIN = 567_520_000 + 3_737_088
+NCU_CHAIN_ALGO_BYTES = 4 * sum((N * K + K + N) * 2 for (N, K) in SHAPES.values())
 
 
 def peaks():
@@ -203,6 +208,42 @@ def capture_step(layers, xs):
                 outs.append(L[name](X[name]))
         torch.cat([o.view(-1) for o in outs], out=y_all)
     return g, outs, y_all
+
+
+def x_views(x_flat):
+    """The 156 input vectors as [1, K] views of one flat buffer, per layer."""
+    xs, off = [], 0
+    for _ in range(LAYERS):
+        X = {}
+        for name, (N, K) in SHAPES.items():
+            X[name] = x_flat[off:off + K].view(1, K)
+            off += K
+        xs.append(X)
+    return xs
+
+
+def capture_chain(layers, xs, deps):
+    """The 156 GEMVs as ONE GEMV-chain launch (kernels.gemv.GemvChain), its
+    outputs [1, N] views of one flat buffer, captured in a CUDA graph;
+    returns (graph, chain, flat outputs)."""
+    from sonata_b200.kernels.gemv import GemvChain
+    total_n = LAYERS * sum(N for (N, K) in SHAPES.values())
+    y_all = torch.empty(total_n, device="cuda", dtype=torch.bfloat16)
+    jobs, off = [], 0
+    for L, X in zip(layers, xs):
+        for name, (N, K) in SHAPES.items():
+            jobs.append((L[name].weight, X[name], y_all[off:off + N].view(1, N)))
+            off += N
+    chain = GemvChain(jobs, deps=deps)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chain()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain()
+    return g, chain, y_all
 
 
 def time_e2e_pipelined(graphs, x_bufs, y_bufs, x_host, y_hosts, steps, warmup, world):
@@ -574,6 +615,9 @@ def summary_of(line, hbm):
     the line (readers of a truncated log see them)."""
     s = {"config2_GBs": line["value"], "config2_frac": line["roofline"]["frac"],
          "config2_e2e_GBs": line["e2e"]["value"]}
+    if line.get("config2_patched_linears"):
+        s["config2_patched_linears_frac"] = line["config2_patched_linears"]["roofline_frac"]
+        s["config2_chain_serial_frac"] = line["config2_chain_serial"]["roofline_frac"]
     if line.get("config2_cublas_same_graph"):
         s["config2_cublas_ms"] = line["config2_cublas_same_graph"]["ms_per_step"]
     if line.get("config2_per_shape_chains"):
@@ -614,9 +658,11 @@ def run_ours(args):
     world, rank, local = dist_setup(args.gpus)
     hbm, tf_burst, tf_sust, peak_kind = peaks()
     layers, xs, x_flat = build_stack(seed=1234 + rank)
-    g, outs, y_all = capture_step(layers, xs)
+    # headline: the 156 GEMVs as one GEMV-chain launch; the set's inputs are
+    # independent (every x drawn on its own), so no job waits for another
+    g, chain, y_all = capture_chain(layers, xs, deps="none")
     sb = step_bytes()
-    launches_per_step = LAYERS * len(SHAPES)
+    launches_per_step = 1
 
     sampler = ClockSampler(list(range(world)) if world > 1 else [local]) if rank == 0 else None
     if sampler:
@@ -628,18 +674,11 @@ def run_ours(args):
     ms_per_step = t_max / args.steps * 1e3
     value = world * sb * args.steps / t_max / 1e9
 
-    # e2e: host buffers, every step's copies inside the timed region
-    # (double-buffered: a second graph reads a second input buffer)
+    # e2e through GemvChain with host buffers, every step's copies inside the
+    # timed region (double-buffered: a second chain reads a second input buffer)
     x_host = x_flat.cpu().pin_memory()
     x_flat2 = torch.empty_like(x_flat)
-    xs2, off = [], 0
-    for _ in range(LAYERS):
-        X = {}
-        for name, (N, K) in SHAPES.items():
-            X[name] = x_flat2[off:off + K].view(1, K)
-            off += K
-        xs2.append(X)
-    g2, _, y_all2 = capture_step(layers, xs2)
+    g2, chain2, y_all2 = capture_chain(layers, x_views(x_flat2), deps="none")
     y_hosts = [torch.empty(y_all.shape, dtype=y_all.dtype).pin_memory() for _ in range(2)]
     h2d = x_host.numel() * x_host.element_size()
     d2h = y_hosts[0].numel() * y_hosts[0].element_size()
@@ -651,14 +690,37 @@ def run_ours(args):
     ref_y = y_all if ((e2e_steps - 1) & 1) == 0 else y_all2
     if not torch.equal(y_hosts[(e2e_steps - 1) & 1], ref_y.cpu()):
         raise RuntimeError("e2e: the host copy of the outputs differs from the device result")
-    del g2
+    del g2, chain2
 
-    # sanity: the replay really computed (non-empty graph tripwire)
-    y0 = outs[0].float()
-    ref0 = torch.nn.functional.linear(xs[0]["in_proj"], layers[0]["in_proj"].weight).float()
+    # sanity: the replay really computed (non-empty graph tripwire), and
+    # equals the patched-Linear path bit for bit
+    torch.cuda.synchronize()
+    y0 = y_all[:SHAPES["in_proj"][0]].float()
+    ref0 = torch.nn.functional.linear(xs[0]["in_proj"], layers[0]["in_proj"].weight).float().view(-1)
     rel = (y0 - ref0).abs().max().item() / max(ref0.abs().max().item(), 1e-12)
     if rel > 2e-2:
-        raise RuntimeError(f"graph replay output does not match F.linear (rel err {rel:.3e})")
+        raise RuntimeError(f"chain replay output does not match F.linear (rel err {rel:.3e})")
+
+    # the drop-in path: 156 patched nn.Linear launches in one graph (PDL and
+    # the next-weight hint), and the chain with every job ordered after the
+    # previous one (a dependent decode chain's ordering)
+    gp, outs, y_lin = capture_step(layers, xs)
+    tp = max_over_ranks(time_replays(gp, args.steps, args.warmup, world), world)
+    if not torch.equal(y_lin, y_all):
+        raise RuntimeError("patched-Linear graph and GEMV chain disagree")
+    del gp
+    gs, chain_s, _ = capture_chain(layers, xs, deps="serial")
+    ts = max_over_ranks(time_replays(gs, args.steps, args.warmup, world), world)
+    del gs, chain_s
+
+    def set_line(tt, what):
+        ms = tt / args.steps * 1e3
+        gbs = sb / (ms * 1e-3) / 1e9
+        return {"ms_per_step": round(ms, 4), "gbs": round(gbs, 1), "roofline_frac": round(gbs / hbm, 4),
+                "what": what}
+    patched = set_line(tp, "156 patched nn.Linear (sn_gemv_ex) in one CUDA graph, PDL + next-weight L2 hint")
+    serial = set_line(ts, "the GEMV chain with job j waiting for job j-1 (dep = j-1, the order of a dependent "
+                          "decode chain)")
 
     snake = None
     dac = None
@@ -706,7 +768,7 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    achieved = sb / (t / args.steps) / 1e9  # per launch: (bytes/156) / (time/156)
+    achieved = sb / (t / args.steps) / 1e9  # one chain launch per step: its bytes / its duration
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -724,9 +786,12 @@ def run_ours(args):
         "config": {
             "workload": "BASELINE config 2: 26 layers x 6 decode GEMVs (in_proj 8512x2048, out_proj 2048x4096, "
                         "qkv 3072x2048, o_proj 2048x2048, fc1 11264x2048, fc2 2048x5632), batch 1, bf16 weights, "
-                        "fp32 accumulate, patched nn.Linear in one CUDA graph with programmatic dependent launch, "
-                        "each GEMV prefetching the start of the next one's weight into L2 (link_decode_chain)",
-            "gemvs_per_step": launches_per_step,
+                        "fp32 accumulate; the 156 GEMVs (independent inputs) as one GEMV-chain launch "
+                        "(kernels.gemv.GemvChain, sn_gemv_chain_*) in a CUDA graph; the patched-nn.Linear graph and "
+                        "the dependency-ordered chain are reported beside it (config2_patched_linears, "
+                        "config2_chain_serial)",
+            "gemvs_per_step": LAYERS * len(SHAPES),
+            "kernel_launches_per_step": launches_per_step,
             "bytes_per_step_per_gpu": sb,
             "l2": "inputs larger than L2: 3.69 GB of distinct weights per step vs 126 MB L2",
             "parallelism": f"replicas x{world} (no collective on the data path)",
@@ -738,17 +803,20 @@ def run_ours(args):
             "unit": "GB/s",
             "frac": round(achieved / hbm, 4),
             "peak_kind": f"{peak_kind} HBM copy bandwidth",
-            "traffic": round(NCU_TRAFFIC_IN_PROJ / IN_PROJ_ALGO_BYTES * sb / launches_per_step),
-            "traffic_note": "ncu dram bytes per in_proj launch scaled to the average launch",
+            "traffic": round(NCU_TRAFFIC_CHAIN / NCU_CHAIN_ALGO_BYTES * sb),
+            "traffic_note": "ncu dram bytes of one chain launch over 4 layers (24 GEMVs), scaled to 26 layers "
+                            "(profiles/gemv_chain_kernel_4layers.md)",
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "note": "every step copies its 156 inputs from pinned host memory and its gathered outputs back; "
-                        "double-buffered, so a step's copies overlap its neighbours' compute"},
+                "note": "through GemvChain: every step copies its 156 inputs from pinned host memory and its 156 "
+                        "outputs back; double-buffered, so a step's copies overlap its neighbours' compute"},
         "gpu_launches": world * launches_per_step * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+    line["config2_patched_linears"] = patched
+    line["config2_chain_serial"] = serial
     if chains is not None:
         line["config2_per_shape_chains"] = chains
         line["config2_cublas_same_graph"] = cublas

@@ -1738,7 +1738,6 @@ struct ChainParams {
   uint32_t xbuf_bytes;   // one x buffer: MT rows of the longest K
   uint32_t xs_off, ring_off;
   uint32_t tcols;
-  uint32_t copy_bytes;  // largest bulk copy of a weight tile (0: one copy per tile)
 };
 
 __device__ __forceinline__ ChainJob load_job(const ChainJob* jobs, int j) {
@@ -1882,11 +1881,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
           uint8_t* dst = ring + off;
           mbar_arrive_expect_tx(full + q, static_cast<uint32_t>(cnt) * row_bytes);
           if (job.ldw_bytes == static_cast<int64_t>(row_bytes)) {
-            const uint8_t* src = job.W + static_cast<int64_t>(first) * job.ldw_bytes;
-            const uint32_t bytes = static_cast<uint32_t>(cnt) * row_bytes;
-            const uint32_t piece = p.copy_bytes ? p.copy_bytes : bytes;
-            for (uint32_t o = 0; o < bytes; o += piece)
-              bulk_g2s(dst + o, src + o, min(piece, bytes - o), full + q, pol);
+            bulk_g2s(dst, job.W + static_cast<int64_t>(first) * job.ldw_bytes, static_cast<uint32_t>(cnt) * row_bytes,
+                     full + q, pol);
           } else {
             for (int r = 0; r < cnt; ++r)
               bulk_g2s(dst + static_cast<size_t>(r) * row_bytes, job.W + static_cast<int64_t>(first + r) * job.ldw_bytes,
@@ -2211,11 +2207,7 @@ int sn_gemv_chain_plan(const sn_gemv_job* jobs, int njobs, int M, void* workspac
   const uint32_t ring_off = round_up_u32(1024 + kChainXBufs * xbuf, 1024);
   const size_t budget = kChainSmem;
   if (budget < ring_off + 2 * static_cast<size_t>(tile_max)) return SN_ERR_UNSUPPORTED;  // two tiles in flight at least
-  uint32_t ring_bytes = static_cast<uint32_t>((budget - ring_off) / 1024 * 1024);
-  if (const char* e = getenv("SONATA_CHAIN_RING_KB")) {  // measurement override (smaller rings only)
-    const uint32_t kb = static_cast<uint32_t>(atoi(e));
-    if (kb * 1024 >= 2 * tile_max && kb * 1024 < ring_bytes) ring_bytes = kb * 1024;
-  }
+  const uint32_t ring_bytes = static_cast<uint32_t>((budget - ring_off) / 1024 * 1024);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (cudaMemcpyAsync(ws, dev.data(), dev.size() * sizeof(ChainJob), cudaMemcpyHostToDevice, st) != cudaSuccess ||
@@ -2254,8 +2246,6 @@ int sn_gemv_chain_launch(const sn_gemv_chain_info* info, void* workspace, unsign
   p.xs_off = 1024;
   p.ring_off = round_up_u32(1024 + kChainXBufs * p.xbuf_bytes, 1024);
   p.tcols = tc::tmem_cols_for(kChainAcc * 32 * M);
-  p.copy_bytes = 0;
-  if (const char* e = getenv("SONATA_CHAIN_COPY_KB")) p.copy_bytes = static_cast<uint32_t>(std::max(0, atoi(e))) * 1024;
   const size_t smem = p.ring_off + static_cast<size_t>(p.ring_bytes);
   if (smem > kChainSmem) return SN_ERR_INVALID_ARGUMENT;
   const void* kern = M == 1 ? reinterpret_cast<const void*>(gemv_chain_kernel<1>)
