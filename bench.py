@@ -395,10 +395,11 @@ def _graph_us(fn, calls, reps=20):
 
 
 def bench_configs(hbm, with_cpu):
-    """Configs 1, 3 (chains of 26 distinct in_proj weights with programmatic
-    dependent launch and each GEMV's next-weight L2 prefetch hint, as in the
-    decode graph), config 4 (one head call per
-    graph replay) and config 5's CPU reference.  GB/s are algorithmic bytes."""
+    """Configs 1, 3 (26 distinct in_proj weights: as one GEMV-chain launch,
+    and as 26 launches with programmatic dependent launch and each GEMV's
+    next-weight L2 prefetch hint, as in the decode graph), config 4 (a chain
+    of head calls, and one call per graph replay) and config 5's CPU
+    reference.  GB/s are algorithmic bytes."""
     from oracle import cpu_baseline as cb
     from sonata_b200.kernels import bmm as Bm
     from sonata_b200.kernels import gemv as G
@@ -409,11 +410,17 @@ def bench_configs(hbm, with_cpu):
     Ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for _ in range(26)]
     x = torch.randn(1, K, device="cuda", generator=g).to(torch.bfloat16)
     y = torch.empty(1, N, device="cuda", dtype=torch.bfloat16)
-    us = _graph_us(lambda: [G.gemv(x, W, out=y, pdl=True, next_weight=Ws[(i + 1) % 26]) for i, W in enumerate(Ws)],
-                   1) / 26
+    us_call = _graph_us(lambda: [G.gemv(x, W, out=y, pdl=True, next_weight=Ws[(i + 1) % 26])
+                                 for i, W in enumerate(Ws)], 1) / 26
+    ys = [torch.empty(1, N, device="cuda", dtype=torch.bfloat16) for _ in range(26)]
+    ch = G.GemvChain([(W, x, yy) for W, yy in zip(Ws, ys)], deps="none")
+    us = _graph_us(ch, 1) / 26
     byt = (N * K + K + N) * 2
     c1 = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1), "roofline_frac": round(byt / us / 1e3 / hbm, 4),
-          "bytes": byt, "workload": "in_proj 8512x2048 bf16, M=1, chain of 26 distinct weights (PDL, next-weight hint)"}
+          "bytes": byt, "us_per_call": round(us_call, 2), "roofline_frac_per_call": round(byt / us_call / 1e3 / hbm, 4),
+          "workload": "in_proj 8512x2048 bf16, M=1, 26 distinct weights: us = per GEMV of one GemvChain launch; "
+                      "us_per_call = per launch of 26 gemv calls in a graph (PDL, next-weight hint)"}
+    del ch, ys
     if with_cpu:
         torch.set_num_threads(thr)
         xc, Wc = x.cpu(), Ws[0].cpu()
@@ -424,11 +431,19 @@ def bench_configs(hbm, with_cpu):
     for kind in ("int8", "e4m3"):
         qws = [G.quantize_weight(W, kind) for W in Ws]
         yq = torch.empty(1, N, device="cuda", dtype=torch.float32)
-        us = _graph_us(lambda: [G.gemv_quantized(x, q, out=yq, pdl=True, next_weight=qws[(i + 1) % 26])
-                                for i, q in enumerate(qws)], 1) / 26
+        us_call = _graph_us(lambda: [G.gemv_quantized(x, q, out=yq, pdl=True, next_weight=qws[(i + 1) % 26])
+                                     for i, q in enumerate(qws)], 1) / 26
+        yqs = [torch.empty(1, N, device="cuda", dtype=torch.float32) for _ in range(26)]
+        ch = G.GemvChain([(q, x, yy) for q, yy in zip(qws, yqs)], deps="none")
+        us = _graph_us(ch, 1) / 26
         byt = N * K + N * 4 + K * 2 + N * 4
         c3 = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1), "roofline_frac": round(byt / us / 1e3 / hbm, 4),
-              "bytes": byt, "workload": f"in_proj {kind} codes + fp32 row scales, M=1, fp32 out, chain of 26 (PDL, next-weight hint)"}
+              "bytes": byt, "us_per_call": round(us_call, 2),
+              "roofline_frac_per_call": round(byt / us_call / 1e3 / hbm, 4),
+              "workload": f"in_proj {kind} codes + fp32 row scales, M=1, fp32 out, 26 distinct weights: us = per "
+                          "GEMV of one GemvChain launch; us_per_call = per launch of 26 gemv_quantized calls in a "
+                          "graph (PDL, next-weight hint)"}
+        del ch, yqs
         if with_cpu:
             t = cb.time_quant_gemv(N, K, kind, thr)
             c3["cpu_baseline"] = {"us": round(t * 1e6, 1), "cores": thr, "kind": "port",

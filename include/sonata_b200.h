@@ -144,9 +144,12 @@ int sn_gemv_bf16_norm(int norm_kind, const void *W, int64_t ldw, const void *x, 
  * Same role as a CUDA graph of patched nn.Linear calls (kernels/patch.py:54-66,
  * kernels/bench_gemv_graph.py:30-63); no counterpart in the reference.
  *
- * Job: W bf16 [N, ldw], x bf16 [M, ldx], y [M, ldy] in y_dtype; W and x
- * 16-byte aligned, ldw and ldx multiples of 8; K within the tensor-core
- * GEMV's rules (K * 2 a multiple of 512).  M (1 or 2) is common to the chain.
+ * Every job of a chain has the same weight kind w_kind (SN_WEIGHT_*): bf16,
+ * or the fused-dequant int8 / e4m3 codes with per-row scales (same
+ * arithmetic as sn_gemv_int8 / sn_gemv_fp8e4m3).  Job: W [N, ldw], x bf16
+ * [M, ldx], y [M, ldy] in y_dtype; W and x 16-byte aligned, row strides of
+ * 16 bytes; K within the tensor-core GEMV's rules (K * element size a
+ * multiple of 512).  M (1 or 2) is common to the chain.
  * No job may write a weight or another job's y, nor x of a job that does not
  * wait for it (through its dep, its dep's dep, ...); x and y of a job must
  * not overlap.  Violations: SN_ERR_INVALID_ARGUMENT.
@@ -159,9 +162,10 @@ int sn_gemv_bf16_norm(int norm_kind, const void *W, int64_t ldw, const void *x, 
  * SN_FLAG_PDL).  One launch per workspace at a time: the counters live there.
  */
 typedef struct sn_gemv_job {
-  const void *W;
-  const void *x;
-  void *y;
+  const void *W;       /* bf16 [N, ldw], or 8-bit codes [N, ldw] (sn_quantize_rows_*) */
+  const void *x;       /* bf16 [M, ldx] */
+  void *y;             /* [M, ldy] in y_dtype */
+  const float *scale;  /* 8-bit kinds: per-row scales [N]; ignored for bf16 */
   int64_t ldw, ldx, ldy; /* elements */
   int N, K;
   int dep;     /* earlier job whose outputs x waits for, -1: none */
@@ -170,15 +174,19 @@ typedef struct sn_gemv_job {
 
 typedef struct sn_gemv_chain_info { /* filled by sn_gemv_chain_plan */
   int njobs, M;
-  int ctas_per_sm;
+  int w_kind;                    /* SN_WEIGHT_* of every job */
+  int x_buffers;                 /* x staging buffers (x is staged this many jobs ahead) */
   uint32_t tile_bytes_max;       /* largest weight tile (16 / S whole rows) */
   uint32_t ring_bytes, xbuf_bytes; /* shared-memory weight ring, one x buffer */
+  uint32_t accumulators;         /* TMEM accumulators */
+  uint32_t accumulator_cols;     /* TMEM columns per accumulator */
+  uint32_t reserved;
   uint64_t workspace_bytes;
 } sn_gemv_chain_info;
 
 size_t sn_gemv_chain_workspace_size(int njobs);
-int sn_gemv_chain_plan(const sn_gemv_job *jobs, int njobs, int M, void *workspace, size_t workspace_bytes,
-                       sn_gemv_chain_info *info, void *stream);
+int sn_gemv_chain_plan(int w_kind, const sn_gemv_job *jobs, int njobs, int M, void *workspace,
+                       size_t workspace_bytes, sn_gemv_chain_info *info, void *stream);
 int sn_gemv_chain_launch(const sn_gemv_chain_info *info, void *workspace, unsigned flags, void *stream);
 
 /*

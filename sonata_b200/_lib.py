@@ -76,7 +76,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sn_snake_conv_transpose1d_pack": ([_P, _I, _I, _I, _I, _P, ctypes.c_size_t, _P], _I),
     "sn_snake_conv_transpose1d_output_length": ([_I64, _I, _I, _I], _I64),
     "sn_gemv_chain_workspace_size": ([_I], ctypes.c_size_t),
-    "sn_gemv_chain_plan": ([_P, _I, _I, _P, ctypes.c_size_t, _P, _P], _I),
+    "sn_gemv_chain_plan": ([_I, _P, _I, _I, _P, ctypes.c_size_t, _P, _P], _I),
     "sn_gemv_chain_launch": ([_P, _P, _U, _P], _I),
     "sn_snake_conv_transpose1d": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, _U, _P,
                                    ctypes.c_size_t, _P], _I),
@@ -92,15 +92,16 @@ class ShiftDesc(ctypes.Structure):
 
 class GemvJob(ctypes.Structure):
     """sn_gemv_job of include/sonata_b200.h."""
-    _fields_ = [("W", ctypes.c_void_p), ("x", ctypes.c_void_p), ("y", ctypes.c_void_p), ("ldw", ctypes.c_int64),
-                ("ldx", ctypes.c_int64), ("ldy", ctypes.c_int64), ("N", ctypes.c_int), ("K", ctypes.c_int),
-                ("dep", ctypes.c_int), ("y_dtype", ctypes.c_int)]
+    _fields_ = [("W", ctypes.c_void_p), ("x", ctypes.c_void_p), ("y", ctypes.c_void_p), ("scale", ctypes.c_void_p),
+                ("ldw", ctypes.c_int64), ("ldx", ctypes.c_int64), ("ldy", ctypes.c_int64), ("N", ctypes.c_int),
+                ("K", ctypes.c_int), ("dep", ctypes.c_int), ("y_dtype", ctypes.c_int)]
 
 
 class GemvChainInfo(ctypes.Structure):
     """sn_gemv_chain_info of include/sonata_b200.h."""
-    _fields_ = [("njobs", ctypes.c_int), ("M", ctypes.c_int), ("ctas_per_sm", ctypes.c_int),
+    _fields_ = [("njobs", ctypes.c_int), ("M", ctypes.c_int), ("w_kind", ctypes.c_int), ("x_buffers", ctypes.c_int),
                 ("tile_bytes_max", ctypes.c_uint32), ("ring_bytes", ctypes.c_uint32), ("xbuf_bytes", ctypes.c_uint32),
+                ("accumulators", ctypes.c_uint32), ("accumulator_cols", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
                 ("workspace_bytes", ctypes.c_uint64)]
 
 

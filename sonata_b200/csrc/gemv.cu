@@ -708,6 +708,32 @@ __device__ __forceinline__ float diag_entry(uint32_t taddr, int lane) {
   }
 }
 
+// This lane's diagonal entries of ND blocks of 8S TMEM columns (one per B
+// plane, starting at ta[d]), with the ND loads in flight together and one wait.
+template <int S, int ND>
+__device__ __forceinline__ void diag_entries(const uint32_t (&ta)[ND], int lane, float (&out)[ND]) {
+  constexpr int W = 8 * S;
+  uint32_t r[ND][W];
+#pragma unroll
+  for (int d = 0; d < ND; ++d) {
+    if constexpr (S == 2)
+      tc::tmem_ld16_async(ta[d], r[d]);
+    else
+      tc::tmem_ld32_async(ta[d], r[d]);
+  }
+  tc::tmem_wait_ld();
+#pragma unroll
+  for (int d = 0; d < ND; ++d) {
+    float t[W];
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      tc::tmem_reg_fence(r[d][i]);
+      t[i] = __uint_as_float(r[d][i]);
+    }
+    out[d] = pick<W>(t, lane & (W - 1));
+  }
+}
+
 // The next GEMV's weights are frozen too: while this kernel's last weight
 // copies are in flight, HBM reads the first bytes of every CTA range of the
 // next launch into L2, so that the next kernel's first ring fills hit L2 and
@@ -764,6 +790,83 @@ __device__ __forceinline__ void bulk_g2s_rot(void* dst, const void* src, uint32_
   }
   bulk_g2s(static_cast<uint8_t*>(dst) + off, static_cast<const uint8_t*>(src) + off, bytes - off, bar, pol);
   bulk_g2s(dst, src, off, bar, pol);
+}
+
+// ---- x staging of the 8-bit kinds (shared by gemv_mma_kernel's staging
+// threads and the chain's x loader) ----
+// max |x| of a 16-byte bf16 piece, as a bit pattern (non-negative bf16 values
+// order like their patterns)
+__device__ __forceinline__ uint32_t x8_piece_max(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t mx = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) mx = max(mx, max(w[j] & 0x7FFFu, (w[j] >> 16) & 0x7FFFu));
+  return mx;
+}
+// Scale of an x row with max |x| pattern mx: max|x| < 2^(E+1), E = biased
+// exponent - 127 (subnormal rows too: E = -127); 2^e with e = 21 - E (int8)
+// or 7 - E (e4m3), returned as two exact power-of-two factors (e in
+// [-107, 148]); INT_MIN for a row holding inf or NaN.
+template <int WK>
+__device__ __forceinline__ int x8_row_scale(uint32_t mx, float& up1, float& up2) {
+  const int ebits = static_cast<int>(mx >> 7);
+  const int e = (WK == W_INT8 ? 21 : 7) - (ebits - 127);
+  up1 = __uint_as_float(static_cast<uint32_t>(127 + e / 2) << 23);
+  up2 = __uint_as_float(static_cast<uint32_t>(127 + (e - e / 2)) << 23);
+  return (ebits == 255) ? INT_MIN : e;
+}
+// The ND B-operand planes of 16-byte piece c of x row m (planes[(d * MT + m)
+// * K + 8c ...]): three signed base-256 digits of rint(x * 2^e) (int8), or
+// the two e4m3 terms t1 = rn(x 2^e), t2 = rn(x 2^e - t1).
+template <int WK, int MT>
+__device__ __forceinline__ void x8_emit(uint8_t* planes, int K, int m, int c, uint4 v, float up1, float up2) {
+  constexpr int ND = (WK == W_INT8) ? 3 : 2;
+  uint32_t dg[ND][2] = {};
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t h = w[e >> 1];
+    const float xf = (e & 1) ? bf16hi(h) : bf16lo(h);
+    const float xsc = (xf * up1) * up2;
+    uint32_t b[ND];
+    if constexpr (WK == W_INT8) {
+      int X = __float2int_rn(xsc);  // |X| < 2^22
+      const int d0 = static_cast<int8_t>(X & 0xFF);
+      X = (X - d0) >> 8;
+      const int d1 = static_cast<int8_t>(X & 0xFF);
+      const int d2 = (X - d1) >> 8;  // |d2| <= 64
+      b[0] = static_cast<uint32_t>(d0) & 0xFFu;
+      b[1] = static_cast<uint32_t>(d1) & 0xFFu;
+      b[2] = static_cast<uint32_t>(d2) & 0xFFu;
+    } else {
+      // |xsc| < 2^8: no saturation; t1 + t2 reproduces xsc to 2^-10
+      const __nv_fp8_storage_t t1 = __nv_cvt_float_to_fp8(xsc, __NV_SATFINITE, __NV_E4M3);
+      const float r = xsc - __half2float(__half(__nv_cvt_fp8_to_halfraw(t1, __NV_E4M3)));
+      const __nv_fp8_storage_t t2 = __nv_cvt_float_to_fp8(r, __NV_SATFINITE, __NV_E4M3);
+      b[0] = t1;
+      b[1] = t2;
+    }
+#pragma unroll
+    for (int d = 0; d < ND; ++d) dg[d][e >> 2] |= b[d] << (8 * (e & 3));
+  }
+#pragma unroll
+  for (int d = 0; d < ND; ++d)
+    *reinterpret_cast<uint2*>(planes + (static_cast<size_t>(d) * MT + m) * K + c * 8) = make_uint2(dg[d][0], dg[d][1]);
+}
+// x_m . w of an 8-bit row from its TMEM sums: int8 -- the three digit sums
+// combined exactly in 64 bits, times 2^-e in double, rounded once to fp32;
+// e4m3 -- the fp32 sum (v[0]) times 2^-e.  NaN when x row m was non-finite.
+template <int WK, int ND>
+__device__ __forceinline__ float x8_dot(const int (&v)[ND], int e) {
+  if (e == INT_MIN) return __int_as_float(0x7FC00000);
+  const double inv = __longlong_as_double(static_cast<long long>(1023 - e) << 52);
+  if constexpr (WK == W_INT8) {
+    const long long acc = static_cast<long long>(v[0]) + (static_cast<long long>(v[1]) << 8) +
+                          (static_cast<long long>(v[2]) << 16);
+    return static_cast<float>(static_cast<double>(acc) * inv);
+  } else {
+    return static_cast<float>(static_cast<double>(__int_as_float(v[0])) * inv);
+  }
 }
 
 // Fused normalisation of the bf16 GEMV's x rows (the decode step's gated
@@ -997,63 +1100,16 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
       // leaves room for one more ring slot); otherwise one bulk copy per row.
       if (warp >= 2) {
         const int xt = threadIdx.x - 64;  // 0..127
-        // max |x| of a piece (bit patterns of non-negative values order like them)
-        auto piece_max = [](uint4 v) {
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-          uint32_t mx = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) mx = max(mx, max(w[j] & 0x7FFFu, (w[j] >> 16) & 0x7FFFu));
-          return mx;
-        };
         auto row_max = [&](int m, uint32_t mx) {
           mx = __reduce_max_sync(0xffffffffu, mx);
           if (lane == 0) atomicMax(xmax + m, mx);
         };
-        // scale of row m: max|x| < 2^(E+1) with E = biased exponent - 127
-        // (subnormal rows too: E = -127): 2^e, e = 21 - E (int8) or 7 - E,
-        // as two exact power-of-two factors (e in [-107, 148])
         auto row_scale = [&](int m, float& up1, float& up2) {
-          const int ebits = static_cast<int>(xmax[m] >> 7);
-          const int e = (WK == W_INT8 ? 21 : 7) - (ebits - 127);
-          up1 = __uint_as_float(static_cast<uint32_t>(127 + e / 2) << 23);
-          up2 = __uint_as_float(static_cast<uint32_t>(127 + (e - e / 2)) << 23);
-          if (xt == 0) xexp[m] = (ebits == 255) ? INT_MIN : e;  // non-finite x row
+          const int e = x8_row_scale<WK>(xmax[m], up1, up2);
+          if (xt == 0) xexp[m] = e;
         };
-        // the ND planes of piece c of row m (v = 0 for padding rows)
-        auto emit = [&](int m, int c, uint4 v, float up1, float up2) {
-          uint32_t dg[ND][2] = {};  // plane d of 8 elements
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const uint32_t h = w[e >> 1];
-            const float xf = (e & 1) ? bf16hi(h) : bf16lo(h);
-            const float xsc = (xf * up1) * up2;
-            uint32_t b[ND];
-            if constexpr (WK == W_INT8) {
-              int X = __float2int_rn(xsc);  // |X| < 2^22
-              const int d0 = static_cast<int8_t>(X & 0xFF);
-              X = (X - d0) >> 8;
-              const int d1 = static_cast<int8_t>(X & 0xFF);
-              const int d2 = (X - d1) >> 8;  // |d2| <= 64
-              b[0] = static_cast<uint32_t>(d0) & 0xFFu;
-              b[1] = static_cast<uint32_t>(d1) & 0xFFu;
-              b[2] = static_cast<uint32_t>(d2) & 0xFFu;
-            } else {
-              // |xsc| < 2^8: no saturation; t1 + t2 reproduces xsc to 2^-10
-              const __nv_fp8_storage_t t1 = __nv_cvt_float_to_fp8(xsc, __NV_SATFINITE, __NV_E4M3);
-              const float r = xsc - __half2float(__half(__nv_cvt_fp8_to_halfraw(t1, __NV_E4M3)));
-              const __nv_fp8_storage_t t2 = __nv_cvt_float_to_fp8(r, __NV_SATFINITE, __NV_E4M3);
-              b[0] = t1;
-              b[1] = t2;
-            }
-#pragma unroll
-            for (int d = 0; d < ND; ++d) dg[d][e >> 2] |= b[d] << (8 * (e & 3));
-          }
-#pragma unroll
-          for (int d = 0; d < ND; ++d)
-            *reinterpret_cast<uint2*>(xs + (static_cast<size_t>(d) * MT + m) * p.K + c * 8) =
-                make_uint2(dg[d][0], dg[d][1]);
-        };
+        auto emit = [&](int m, int c, uint4 v, float up1, float up2) { x8_emit<WK, MT>(xs, p.K, m, c, v, up1, up2); };
+        auto piece_max = [](uint4 v) { return x8_piece_max(v); };
         if (sh.xraw_off == 0) {
           constexpr int PPR = kXRegs / MT;  // pieces per row a thread holds (host: cpr <= 128 * PPR)
           uint4 xv[MT][PPR];
@@ -1709,10 +1765,11 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16*
 // ---------------------------------------------------------------------------
 namespace {
 
-struct ChainJob {  // device copy of one job (64 bytes)
+struct ChainJob {  // device copy of one job (80 bytes)
   const uint8_t* W;
   const __nv_bfloat16* x;
   void* y;
+  const float* scale;  // 8-bit kinds: per-row scales
   int64_t ldw_bytes;
   int ldx, ldy;  // elements
   int N, K;
@@ -1720,14 +1777,16 @@ struct ChainJob {  // device copy of one job (64 bytes)
   int S;  // row segments (2 or 4): 16 / S rows per tile
   int flags;  // kJobF32 (fp32 y), kJobSignal (a later job waits for this one)
   uint32_t tile_bytes;
+  int pad;
 };
-static_assert(sizeof(ChainJob) == 64, "ChainJob is 64 bytes");
+static_assert(sizeof(ChainJob) == 80, "ChainJob is 80 bytes");
 
 constexpr int kChainThreads = 224;
 constexpr int kChainAcc = 8;             // TMEM accumulators (a power of two)
 constexpr int kJobF32 = 1, kJobSignal = 2;
 constexpr int kChainTiles = 16;          // weight tiles in flight at most (mbarrier pairs)
-constexpr int kChainXBufs = 2;           // x buffers: x copies run up to this many jobs ahead (4: no faster)
+constexpr int kChainXBufs = 4;           // x buffers at most: x staging runs this many jobs ahead
+constexpr int kChainExps = 16;           // 8-bit x exponents in flight (> x buffers + accumulators)
 constexpr int kChainCounterStride = 32;  // one 128-byte line per completion counter
 
 struct ChainParams {
@@ -1738,16 +1797,19 @@ struct ChainParams {
   uint32_t xbuf_bytes;   // one x buffer: MT rows of the longest K
   uint32_t xs_off, ring_off;
   uint32_t tcols;
+  int nxb_log2;       // x buffers in use: 2 or 4 (log2 1 or 2)
+  int nacc_log2;      // TMEM accumulators in use: 2, 4 or 8
+  uint32_t acc_cols;  // TMEM columns per accumulator: the largest MMA N of the chain
 };
 
 __device__ __forceinline__ ChainJob load_job(const ChainJob* jobs, int j) {
   union {
-    uint4 v[4];
+    uint4 v[5];
     ChainJob job;
   } u;
   const uint4* src = reinterpret_cast<const uint4*>(jobs + j);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) u.v[i] = __ldg(src + i);
+  for (int i = 0; i < 5; ++i) u.v[i] = __ldg(src + i);
   return u.job;
 }
 
@@ -1784,14 +1846,17 @@ __device__ __forceinline__ bool wait_counter(const unsigned* c, unsigned target)
 }
 
 // Rows [r0, r1) of a job with N rows owned by CTA c of G.
+// (32-bit: the plan keeps N below 2^24, so N * (c + 1) < 2^32)
 __device__ __forceinline__ void cta_rows(int N, int c, int G, int& r0, int& r1) {
-  r0 = static_cast<int>(static_cast<int64_t>(N) * c / G);
-  r1 = static_cast<int>(static_cast<int64_t>(N) * (c + 1) / G);
+  r0 = static_cast<int>(static_cast<uint32_t>(N) * static_cast<uint32_t>(c) / static_cast<uint32_t>(G));
+  r1 = static_cast<int>(static_cast<uint32_t>(N) * static_cast<uint32_t>(c + 1) / static_cast<uint32_t>(G));
 }
 
-template <int MT>
+template <int WK, int MT>
 __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const ChainParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int ESZ = WT<WK>::ESZ;
+  constexpr int ND = (WK == W_INT8) ? 3 : (WK == W_E4M3) ? 2 : 1;  // B planes per x row
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kChainTiles], tile t uses t % kChainTiles
   uint64_t* empty = full + kChainTiles;
   uint64_t* tfull = empty + kChainTiles;
@@ -1799,12 +1864,17 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
   uint64_t* xfull = tempty + kChainAcc;
   uint64_t* xfree = xfull + kChainXBufs;
   uint64_t* done = xfree + kChainXBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* eready = done + 1;  // 8-bit: [kChainExps], the exponents of x use u are in xexp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(eready + kChainExps);
   uint32_t* tbeg = tmem_slot + 1;  // producer only: ring range of the tiles in flight
   uint32_t* tend = tbeg + kChainTiles;
+  int* xexp = reinterpret_cast<int*>(tend + kChainTiles);  // 8-bit: [use % kChainExps][m] e (x row m scaled by 2^e)
   uint8_t* xs = smem + p.xs_off;
   uint8_t* ring = smem + p.ring_off;
-  constexpr uint32_t kAccStride = 32 * MT;  // TMEM columns per accumulator (N of an S = 4 job)
+  // accumulators: a power of two, so masks and shifts (not divisions) in the hot loops
+  const int nacc = 1 << p.nacc_log2, nl = p.nacc_log2;
+  const uint32_t acc_cols = p.acc_cols;
+  const int nxb = 1 << p.nxb_log2, xl = p.nxb_log2;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
@@ -1823,6 +1893,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
       mbar_init(xfree + b, 1);
     }
     mbar_init(done, 1);
+    for (int k = 0; k < kChainExps; ++k) mbar_init(eready + k, 1);
     fence_barrier_init();
   }
   if (warp == 1) tc::tmem_alloc(tmem_slot, p.tcols);
@@ -1853,7 +1924,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
           break;
         }
         const int R = 16 / job.S;
-        const uint32_t row_bytes = static_cast<uint32_t>(job.K) * 2;
+        const uint32_t row_bytes = static_cast<uint32_t>(job.K) * ESZ;
         int r0, r1;
         cta_rows(job.N, c, G, r0, r1);
         for (int first = r0; first < r1; first += R, ++t) {
@@ -1899,41 +1970,69 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
     }
   } else if (warp == 6) {
     // ---------------- x loader: waits for each job's producer --------------
-    if (lane == 0) {
-      pdl_wait();  // the first jobs' x and the counters belong to earlier kernels
-      const uint64_t pol = l2_policy_evict_normal();
-      int u = 0;
-      ChainJob job = load_job(p.jobs, 0), nxt;
-      for (int j = 0; j < p.njobs; ++j, job = nxt) {
-        nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
-        int r0, r1;
-        cta_rows(job.N, c, G, r0, r1);
-        if (r0 == r1) continue;
-        const int b = u % kChainXBufs;
-        const uint32_t row_bytes = static_cast<uint32_t>(job.K) * 2;
-        if (static_cast<uint32_t>(p.M) * row_bytes > p.xbuf_bytes) {
-          record_status(SN_ERR_INVALID_ARGUMENT);
-          break;
-        }
-        if ((u >= kChainXBufs && !mbar_wait_bounded(xfree + b, ((u / kChainXBufs) - 1) & 1)) ||
-            (job.dep >= 0 && !wait_counter(p.counters + static_cast<size_t>(job.dep) * kChainCounterStride,
-                                           static_cast<unsigned>(G)))) {
-          record_status(SN_ERR_TIMEOUT);
-          break;
-        }
-        if (job.dep >= 0) fence_proxy_async_global();  // acquired generic writes -> the bulk copy below
-        uint8_t* dst = xs + static_cast<size_t>(b) * p.xbuf_bytes;
-        mbar_arrive_expect_tx(xfull + b, static_cast<uint32_t>(p.M) * row_bytes);
-        for (int m = 0; m < p.M; ++m)
-          bulk_g2s(dst + static_cast<size_t>(m) * row_bytes, job.x + static_cast<int64_t>(m) * job.ldx, row_bytes,
-                   xfull + b, pol);
-        ++u;
+    pdl_wait();  // the first jobs' x and the counters belong to earlier kernels
+    int u = 0;
+    ChainJob job = load_job(p.jobs, 0), nxt;
+    for (int j = 0; j < p.njobs; ++j, job = nxt) {
+      nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
+      int r0, r1;
+      cta_rows(job.N, c, G, r0, r1);
+      if (r0 == r1) continue;
+      const int b = u & (nxb - 1);
+      const uint32_t row_bytes = static_cast<uint32_t>(job.K) * ESZ;  // x row bytes in the B operand
+      if (static_cast<uint32_t>(MT * ND) * row_bytes > p.xbuf_bytes) {
+        if (lane == 0) record_status(SN_ERR_INVALID_ARGUMENT);
+        break;
       }
-      // the last copies have landed before the CTA can exit (the MMA issuer
-      // waits for them too unless it stopped early)
-      for (int v = (u > kChainXBufs ? u - kChainXBufs : 0); v < u; ++v)
-        mbar_wait_bounded(xfull + v % kChainXBufs, (v / kChainXBufs) & 1);
+      bool w = u < nxb || mbar_wait_bounded(xfree + b, ((u >> xl) - 1) & 1);
+      // every lane that reads x acquires its producer's completion itself
+      if (w && job.dep >= 0 && (WK != W_BF16 || lane == 0))
+        w = wait_counter(p.counters + static_cast<size_t>(job.dep) * kChainCounterStride, static_cast<unsigned>(G));
+      if (!__all_sync(0xffffffffu, w)) {
+        if (lane == 0) record_status(SN_ERR_TIMEOUT);
+        break;
+      }
+      uint8_t* dst = xs + static_cast<size_t>(b) * p.xbuf_bytes;
+      if constexpr (WK == W_BF16) {
+        // x rows by bulk copy, completing xfull[b]
+        if (lane == 0) {
+          if (job.dep >= 0) fence_proxy_async_global();  // acquired generic writes -> the bulk copy below
+          mbar_arrive_expect_tx(xfull + b, static_cast<uint32_t>(p.M) * row_bytes);
+          for (int m = 0; m < p.M; ++m)
+            bulk_g2s(dst + static_cast<size_t>(m) * row_bytes, job.x + static_cast<int64_t>(m) * job.ldx, row_bytes,
+                     xfull + b, l2_policy_evict_normal());
+        }
+      } else {
+        // the B planes of x * 2^e_m (8-bit kinds), by the whole warp: the row
+        // maximum, then the digits / terms of every element
+        const int cpr = job.K / 8;  // 16-byte pieces of a bf16 x row
+        for (int m = 0; m < MT; ++m) {
+          int e = 0;
+          float up1 = 0.f, up2 = 0.f;
+          const __nv_bfloat16* xrow = job.x + static_cast<int64_t>(m) * job.ldx;
+          if (m < p.M) {
+            uint32_t mx = 0;
+            for (int cc = lane; cc < cpr; cc += 32) mx = max(mx, x8_piece_max(ld_cg_v4(xrow + cc * 8)));
+            mx = __reduce_max_sync(0xffffffffu, mx);
+            e = x8_row_scale<WK>(mx, up1, up2);
+          }
+          for (int cc = lane; cc < cpr; cc += 32)
+            x8_emit<WK, MT>(dst, job.K, m, cc, m < p.M ? ld_cg_v4(xrow + cc * 8) : make_uint4(0, 0, 0, 0), up1, up2);
+          if (lane == 0) xexp[(u % kChainExps) * MT + m] = e;
+        }
+        tc::fence_proxy_async_smem();  // the plane stores -> the tensor core's reads
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(xfull + b);
+          mbar_arrive(eready + u % kChainExps);  // the exponents -> the epilogue
+        }
+      }
+      ++u;
     }
+    // the last bulk copies have landed before the CTA can exit (the MMA
+    // issuer waits for them too unless it stopped early)
+    if (WK == W_BF16 && lane == 0)
+      for (int v = (u > nxb ? u - nxb : 0); v < u; ++v) mbar_wait_bounded(xfull + (v & (nxb - 1)), (v >> xl) & 1);
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -1946,29 +2045,39 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
         int r0, r1;
         cta_rows(job.N, c, G, r0, r1);
         if (r0 == r1) continue;
-        const int b = u % kChainXBufs;
-        if (!mbar_wait_bounded(xfull + b, (u / kChainXBufs) & 1)) {
+        const int b = u & (nxb - 1);
+        if (!mbar_wait_bounded(xfull + b, (u >> xl) & 1)) {
           record_status(SN_ERR_TIMEOUT);
           break;
         }
         const int R = 16 / job.S;
-        const uint32_t L = static_cast<uint32_t>(job.K) * 2 / job.S;  // segment bytes
-        const uint32_t nk = L / 256;
-        const uint32_t idesc = tc::idesc_bf16_f32(128, 8 * job.S * MT);
+        const uint32_t L = static_cast<uint32_t>(job.K) * ESZ / job.S;  // segment bytes
+        const uint32_t nk = L / 256;                                      // MMAs per tile
+        const int n = 8 * job.S * MT * ND;
+        const uint32_t idesc = (WK == W_INT8)   ? tc::idesc_s8_s32(128, n)
+                               : (WK == W_E4M3) ? tc::idesc_e4m3_f32(128, n)
+                                                : tc::idesc_bf16_f32(128, n);
         const uint64_t db0 = tc::smem_desc_noswz(xs + static_cast<size_t>(b) * p.xbuf_bytes, 128, L);
         for (int first = r0; first < r1; first += R, ++t) {
           if (off + job.tile_bytes > p.ring_bytes) off = 0;
-          const int q = t % kChainTiles, a = t & (kChainAcc - 1);
+          const int q = t % kChainTiles, a = t & (nacc - 1);
           if (!mbar_wait_bounded(full + q, (t / kChainTiles) & 1) ||
-              (t >= kChainAcc && !mbar_wait_bounded(tempty + a, ((t / kChainAcc) - 1) & 1))) {
+              (t >= nacc && !mbar_wait_bounded(tempty + a, ((t >> nl) - 1) & 1))) {
             record_status(SN_ERR_TIMEOUT);
             ok = false;
             break;
           }
           tc::fence_after_sync();
           const uint64_t da0 = tc::smem_desc_noswz(ring + off, 128, L);
-          const uint32_t d = tmem + static_cast<uint32_t>(a) * kAccStride;
-          for (uint32_t k = 0; k < nk; ++k) tc::mma_bf16(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+          const uint32_t d = tmem + static_cast<uint32_t>(a) * acc_cols;
+          for (uint32_t k = 0; k < nk; ++k) {  // 256 bytes of every segment per MMA
+            if constexpr (WK == W_INT8)
+              tc::mma_s8(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+            else if constexpr (WK == W_E4M3)
+              tc::mma_e4m3(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+            else
+              tc::mma_bf16(d, da0 + 16 * k, db0 + 16 * k, idesc, k != 0);
+          }
           tc::mma_commit(empty + q);
           tc::mma_commit(tfull + a);
           off += job.tile_bytes;
@@ -1986,7 +2095,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
     pdl_wait();  // y and the counters belong to earlier kernels until here
     const int q = warp & 3;
     const int i = q * 32 + lane;  // A row = TMEM lane
-    int t = 0;
+    int t = 0, u = 0;
     bool ok = true;
     ChainJob job = load_job(p.jobs, 0), nxt;
     for (int j = 0; j < p.njobs; ++j, job = nxt) {
@@ -1996,20 +2105,62 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
       const int R = 16 / job.S;
       const int Gs = 8 * job.S;  // TMEM lanes (and columns) per weight row
       const int r = i / Gs;      // weight row inside the tile
+      int e[MT];                 // 8-bit: x row m was scaled by 2^e[m]
+#pragma unroll
+      for (int m = 0; m < MT; ++m) e[m] = 0;
+      if (WK != W_BF16 && r0 < r1 && ok) {
+        ok = mbar_wait_bounded(eready + u % kChainExps, (u / kChainExps) & 1);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) e[m] = xexp[(u % kChainExps) * MT + m];
+        if (!ok) record_status(SN_ERR_TIMEOUT);
+      }
+      if (r0 < r1) ++u;
       for (int first = r0; ok && first < r1; first += R, ++t) {
-        const int a = t & (kChainAcc - 1);
+        const int a = t & (nacc - 1);
         const int cnt = min(R, r1 - first);
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(tfull + a, (t / kChainAcc) & 1))) {
+        // the row scale (frozen weights) is in flight while the MMAs finish
+        const float rs = (WK != W_BF16 && r < cnt) ? __ldg(job.scale + first + r) : 0.f;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(tfull + a, (t >> nl) & 1))) {
           record_status(SN_ERR_TIMEOUT);
           ok = false;
           break;
         }
         tc::fence_after_sync();
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a) * kAccStride;
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a) * acc_cols;
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          float v = job.S == 2 ? diag_entry<2>(taddr + m * Gs, lane) : diag_entry<4>(taddr + m * Gs, lane);
-          for (int o = Gs / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          float v;
+          if constexpr (WK == W_BF16) {
+            v = job.S == 2 ? diag_entry<2>(taddr + m * Gs, lane) : diag_entry<4>(taddr + m * Gs, lane);
+            for (int o = Gs / 2; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          } else {
+            // same arithmetic and order as gemv_mma_kernel's epilogue
+            int d32[ND];
+            uint32_t ta[ND];
+            float de[ND];
+#pragma unroll
+            for (int d = 0; d < ND; ++d) ta[d] = taddr + (d * MT + m) * Gs;
+            if (job.S == 2)
+              diag_entries<2, ND>(ta, lane, de);
+            else
+              diag_entries<4, ND>(ta, lane, de);
+            if constexpr (WK == W_INT8) {
+#pragma unroll
+              for (int d = 0; d < ND; ++d) {  // exact s32 digit sums
+                int iv = __float_as_int(de[d]);
+                for (int o = Gs / 2; o >= 1; o >>= 1) iv += __shfl_xor_sync(0xffffffffu, iv, o);
+                d32[d] = iv;
+              }
+            } else {
+              float f = 0.f;  // the two e4m3 terms' products, summed per lane first
+#pragma unroll
+              for (int d = 0; d < ND; ++d) f += de[d];
+              for (int o = Gs / 2; o >= 1; o >>= 1) f += __shfl_xor_sync(0xffffffffu, f, o);
+#pragma unroll
+              for (int d = 0; d < ND; ++d) d32[d] = __float_as_int(f);
+            }
+            v = x8_dot<WK, ND>(d32, e[m]) * rs;
+          }
           if ((lane & (Gs - 1)) == 0 && r < cnt && m < p.M) {
             const int64_t off = static_cast<int64_t>(m) * job.ldy + first + r;
             if (job.flags & kJobF32)
@@ -2034,7 +2185,6 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
       }
     }
   }
-
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 1) tc::tmem_dealloc(tmem, p.tcols);
@@ -2076,6 +2226,43 @@ ByteRange rows_range(const void* p, int rows, int64_t ld, int64_t len, int esz) 
 }
 bool overlap(const ByteRange& a, const ByteRange& b) { return a.lo < b.hi && b.lo < a.hi; }
 
+}  // namespace
+
+namespace {
+template <int WK, int MT>
+int chain_launch(const ChainParams& p, size_t smem, unsigned flags, cudaStream_t stream) {
+  auto kern = gemv_chain_kernel<WK, MT>;
+  if (!ensure_smem(reinterpret_cast<const void*>(kern), smem)) return SN_ERR_UNSUPPORTED;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kChainThreads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_LAUNCH;
+  }
+  if (per_sm < 1) return SN_ERR_UNSUPPORTED;
+  // every CTA waits for others (job completions): all must be resident at
+  // once, which a cooperative launch guarantees
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(kChainThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  int na = 1;
+  if (flags & SN_FLAG_PDL) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) {
+    cudaGetLastError();
+    return SN_ERR_LAUNCH;
+  }
+  return SN_OK;
+}
 }  // namespace
 
 }  // namespace sn
@@ -2146,14 +2333,17 @@ size_t sn_gemv_chain_workspace_size(int njobs) {
   return sn::chain_workspace_bytes(njobs);
 }
 
-int sn_gemv_chain_plan(const sn_gemv_job* jobs, int njobs, int M, void* workspace, size_t workspace_bytes,
-                       sn_gemv_chain_info* info, void* stream) {
+int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, void* workspace,
+                       size_t workspace_bytes, sn_gemv_chain_info* info, void* stream) {
   using namespace sn;
   if (!jobs || !workspace || !info || njobs < 1 || njobs > kChainMaxJobs || M < 1 || M > 2)
     return SN_ERR_INVALID_ARGUMENT;
+  if (w_kind < SN_WEIGHT_BF16 || w_kind > SN_WEIGHT_E4M3) return SN_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < chain_workspace_bytes(njobs)) return SN_ERR_INVALID_ARGUMENT;
   if (!aligned16(workspace)) return SN_ERR_MISALIGNED;
   const int MT = M;
+  const int esz = (w_kind == SN_WEIGHT_BF16) ? 2 : 1;
+  const int nd = nd_of(w_kind);
   std::vector<ChainJob> dev(static_cast<size_t>(njobs));
   std::vector<ByteRange> xr(njobs), yr(njobs), wr(njobs);
   uint32_t tile_max = 0;
@@ -2162,19 +2352,22 @@ int sn_gemv_chain_plan(const sn_gemv_job* jobs, int njobs, int M, void* workspac
     const sn_gemv_job& a = jobs[j];
     if (!a.W || !a.x || !a.y || a.N < 1 || a.K < 1 || a.ldw < a.K || a.ldx < a.K || a.ldy < a.N)
       return SN_ERR_INVALID_ARGUMENT;
+    if (a.N >= (1 << 24)) return SN_ERR_UNSUPPORTED;  // the kernel splits rows in 32-bit arithmetic
+    if (esz == 1 && !a.scale) return SN_ERR_INVALID_ARGUMENT;
     if (a.dep < -1 || a.dep >= j) return SN_ERR_INVALID_ARGUMENT;
     if (a.y_dtype != SN_DTYPE_BF16 && a.y_dtype != SN_DTYPE_F32) return SN_ERR_INVALID_ARGUMENT;
-    if (!aligned16(a.W) || !aligned16(a.x) || (a.ldw * 2) % 16 != 0 || (a.ldx * 2) % 16 != 0)
+    if (!aligned16(a.W) || !aligned16(a.x) || (a.ldw * esz) % 16 != 0 || (a.ldx * 2) % 16 != 0)
       return SN_ERR_MISALIGNED;
-    const int S = mma_segments(a.K, 2, MT, 1);
+    const int S = mma_segments(a.K, esz, MT, nd);
     if (S == 0 || a.ldx > INT_MAX || a.ldy > INT_MAX) return SN_ERR_UNSUPPORTED;
-    const int64_t tile = static_cast<int64_t>(16 / S) * a.K * 2;
+    const int64_t tile = static_cast<int64_t>(16 / S) * a.K * esz;
     if (tile > 128 * 1024) return SN_ERR_UNSUPPORTED;
     ChainJob& d = dev[j];
     d.W = static_cast<const uint8_t*>(a.W);
     d.x = static_cast<const __nv_bfloat16*>(a.x);
     d.y = a.y;
-    d.ldw_bytes = a.ldw * 2;
+    d.scale = esz == 1 ? a.scale : nullptr;
+    d.ldw_bytes = a.ldw * esz;
     d.ldx = static_cast<int>(a.ldx);
     d.ldy = static_cast<int>(a.ldy);
     d.N = a.N;
@@ -2183,11 +2376,12 @@ int sn_gemv_chain_plan(const sn_gemv_job* jobs, int njobs, int M, void* workspac
     d.S = S;
     d.flags = (a.y_dtype == SN_DTYPE_F32) ? kJobF32 : 0;
     d.tile_bytes = static_cast<uint32_t>(tile);
+    d.pad = 0;
     tile_max = std::max(tile_max, d.tile_bytes);
     kmax = std::max(kmax, a.K);
     xr[j] = rows_range(a.x, M, a.ldx, a.K, 2);
     yr[j] = rows_range(a.y, M, a.ldy, a.N, a.y_dtype == SN_DTYPE_F32 ? 4 : 2);
-    wr[j] = rows_range(a.W, a.N, a.ldw, a.K, 2);
+    wr[j] = rows_range(a.W, a.N, a.ldw, a.K, esz);
   }
   for (int j = 0; j < njobs; ++j)
     if (jobs[j].dep >= 0) dev[jobs[j].dep].flags |= kJobSignal;
@@ -2203,11 +2397,24 @@ int sn_gemv_chain_plan(const sn_gemv_job* jobs, int njobs, int M, void* workspac
       if (!waits) return SN_ERR_INVALID_ARGUMENT;
     }
   }
-  const uint32_t xbuf = round_up_u32(static_cast<uint32_t>(MT * kmax * 2), 128);
-  const uint32_t ring_off = round_up_u32(1024 + kChainXBufs * xbuf, 1024);
-  const size_t budget = kChainSmem;
-  if (budget < ring_off + 2 * static_cast<size_t>(tile_max)) return SN_ERR_UNSUPPORTED;  // two tiles in flight at least
-  const uint32_t ring_bytes = static_cast<uint32_t>((budget - ring_off) / 1024 * 1024);
+  // one x buffer: the B operand of MT rows of the longest K (bf16 rows, or
+  // the nd 8-bit planes of each row)
+  const uint32_t xbuf = round_up_u32(static_cast<uint32_t>(MT * kmax * (esz == 2 ? 2 : nd)), 128);
+  // x buffers: up to kChainXBufs while the ring keeps two tiles and 96 KB
+  // (deeper rings measured no faster), at least two
+  const size_t ring_min = std::max<size_t>(2 * static_cast<size_t>(tile_max), 96 * 1024);
+  int nxb = kChainXBufs;  // 4 or 2 (a power of two: masks in the kernel)
+  if (kChainSmem < round_up_u32(1024 + nxb * xbuf, 1024) + ring_min) nxb = 2;
+  const uint32_t ring_off = round_up_u32(1024 + nxb * xbuf, 1024);
+  if (kChainSmem < ring_off + 2 * static_cast<size_t>(tile_max)) return SN_ERR_UNSUPPORTED;  // two tiles in flight
+  const uint32_t ring_bytes = static_cast<uint32_t>((kChainSmem - ring_off) / 1024 * 1024);
+  // TMEM accumulators: as many (up to kChainAcc, a power of two) as 512 columns hold
+  // TMEM accumulators: as many (a power of two up to kChainAcc) as 512
+  // columns hold at the chain's largest MMA N
+  uint32_t acc_cols = 0;
+  for (int j = 0; j < njobs; ++j) acc_cols = std::max(acc_cols, static_cast<uint32_t>(8 * dev[j].S * MT * nd));
+  int nacc = kChainAcc;
+  while (nacc > 2 && nacc * acc_cols > 512) nacc /= 2;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (cudaMemcpyAsync(ws, dev.data(), dev.size() * sizeof(ChainJob), cudaMemcpyHostToDevice, st) != cudaSuccess ||
@@ -2219,21 +2426,31 @@ int sn_gemv_chain_plan(const sn_gemv_job* jobs, int njobs, int M, void* workspac
   }
   info->njobs = njobs;
   info->M = M;
-  info->ctas_per_sm = 1;
+  info->w_kind = w_kind;
+  info->x_buffers = nxb;
   info->tile_bytes_max = tile_max;
   info->ring_bytes = ring_bytes;
   info->xbuf_bytes = xbuf;
+  info->accumulators = static_cast<uint32_t>(nacc);
+  info->accumulator_cols = acc_cols;
   info->workspace_bytes = chain_workspace_bytes(njobs);
   return SN_OK;
 }
 
+
 int sn_gemv_chain_launch(const sn_gemv_chain_info* info, void* workspace, unsigned flags, void* stream) {
   using namespace sn;
   if (!info || !workspace) return SN_ERR_INVALID_ARGUMENT;
-  const int njobs = info->njobs, M = info->M;
-  if (njobs < 1 || njobs > kChainMaxJobs || M < 1 || M > 2 || info->ctas_per_sm != 1 || info->tile_bytes_max == 0 ||
-      info->tile_bytes_max % 16 != 0 || info->ring_bytes % 1024 != 0 || info->ring_bytes < 2 * info->tile_bytes_max ||
-      info->xbuf_bytes % 128 != 0 || info->workspace_bytes != chain_workspace_bytes(njobs))
+  const int njobs = info->njobs, M = info->M, wk = info->w_kind;
+  const int nd = (wk >= SN_WEIGHT_BF16 && wk <= SN_WEIGHT_E4M3) ? nd_of(wk) : 0;
+  if (njobs < 1 || njobs > kChainMaxJobs || M < 1 || M > 2 || nd == 0 || info->x_buffers < 2 ||
+      info->x_buffers > kChainXBufs || (info->x_buffers & (info->x_buffers - 1)) != 0 ||
+      (info->accumulators != 2 && info->accumulators != 4 && info->accumulators != 8) ||
+      info->accumulator_cols == 0 || info->accumulator_cols % 16 != 0 || info->accumulator_cols > 256 ||
+      info->accumulators * info->accumulator_cols > 512 ||
+      info->tile_bytes_max == 0 || info->tile_bytes_max % 16 != 0 || info->ring_bytes % 1024 != 0 ||
+      info->ring_bytes < 2 * info->tile_bytes_max || info->xbuf_bytes % 128 != 0 ||
+      info->workspace_bytes != chain_workspace_bytes(njobs))
     return SN_ERR_INVALID_ARGUMENT;
   if ((flags & ~SN_FLAG_PDL) != 0) return SN_ERR_INVALID_ARGUMENT;
   ChainParams p;
@@ -2243,44 +2460,23 @@ int sn_gemv_chain_launch(const sn_gemv_chain_info* info, void* workspace, unsign
   p.M = M;
   p.ring_bytes = info->ring_bytes;
   p.xbuf_bytes = info->xbuf_bytes;
+  p.nxb_log2 = info->x_buffers == 4 ? 2 : 1;
   p.xs_off = 1024;
-  p.ring_off = round_up_u32(1024 + kChainXBufs * p.xbuf_bytes, 1024);
-  p.tcols = tc::tmem_cols_for(kChainAcc * 32 * M);
+  p.ring_off = round_up_u32(1024 + info->x_buffers * p.xbuf_bytes, 1024);
+  p.nacc_log2 = info->accumulators == 8 ? 3 : info->accumulators == 4 ? 2 : 1;
+  p.acc_cols = info->accumulator_cols;
+  p.tcols = tc::tmem_cols_for(info->accumulators * info->accumulator_cols);
   const size_t smem = p.ring_off + static_cast<size_t>(p.ring_bytes);
   if (smem > kChainSmem) return SN_ERR_INVALID_ARGUMENT;
-  const void* kern = M == 1 ? reinterpret_cast<const void*>(gemv_chain_kernel<1>)
-                            : reinterpret_cast<const void*>(gemv_chain_kernel<2>);
-  if (!ensure_smem(kern, smem)) return SN_ERR_UNSUPPORTED;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kChainThreads, smem) != cudaSuccess) {
-    cudaGetLastError();
-    return SN_ERR_LAUNCH;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (wk * 2 + (M - 1)) {
+    case SN_WEIGHT_BF16 * 2: return chain_launch<W_BF16, 1>(p, smem, flags, st);
+    case SN_WEIGHT_BF16 * 2 + 1: return chain_launch<W_BF16, 2>(p, smem, flags, st);
+    case SN_WEIGHT_INT8 * 2: return chain_launch<W_INT8, 1>(p, smem, flags, st);
+    case SN_WEIGHT_INT8 * 2 + 1: return chain_launch<W_INT8, 2>(p, smem, flags, st);
+    case SN_WEIGHT_E4M3 * 2: return chain_launch<W_E4M3, 1>(p, smem, flags, st);
+    default: return chain_launch<W_E4M3, 2>(p, smem, flags, st);
   }
-  if (per_sm < 1) return SN_ERR_UNSUPPORTED;
-  // every CTA waits for others (job completions): all must be resident at
-  // once, which a cooperative launch guarantees
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sm_count());
-  cfg.blockDim = dim3(kChainThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  int na = 1;
-  if (flags & SN_FLAG_PDL) {
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    na = 2;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  cudaError_t e = M == 1 ? cudaLaunchKernelEx(&cfg, gemv_chain_kernel<1>, p) : cudaLaunchKernelEx(&cfg, gemv_chain_kernel<2>, p);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return SN_ERR_LAUNCH;
-  }
-  return SN_OK;
 }
 
 }  // extern "C"

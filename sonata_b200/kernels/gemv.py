@@ -95,18 +95,21 @@ def gemv(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor | None = None, out_
 
 
 class GemvChain:
-    """A list of bf16 decode GEMVs ``y_j = x_j @ W_j.T`` run by ONE persistent
+    """A list of decode GEMVs ``y_j = x_j @ W_j.T`` run by ONE persistent
     launch (``sn_gemv_chain_*``), e.g. the per-token projection set of a
     decode step.  Each CTA streams the jobs' weights in order through one
     ring, so HBM reads the next job's weights while the current one finishes;
     a job's x waits, inside the kernel, for the job named in ``deps``.
 
-    jobs: ``(W [N, K] bf16, x [M, K] bf16, y [M, N] bf16 or fp32)`` triples,
-    M (1 or 2) common to all.  deps: ``"serial"`` (job j waits for job j-1:
-    the order of back-to-back launches on one stream), ``"none"`` (every x is
-    ready when the launch starts) or a list of earlier job indices (-1: none).
-    The plan is validated and uploaded once; ``__call__`` only launches (CUDA
-    graph capturable).  Results equal ``gemv`` on each job bit for bit.
+    jobs: ``(W, x [M, K] bf16, y [M, N] bf16 or fp32)`` triples, M (1 or 2)
+    common to all; W is a bf16 [N, K] weight or, for every job alike, a
+    ``QuantizedWeight`` of one kind (the fused-dequant int8 / e4m3 GEMV).
+    deps: ``"serial"`` (job j waits for job j-1: the order of back-to-back
+    launches on one stream), ``"none"`` (every x is ready when the launch
+    starts) or a list of earlier job indices (-1: none).  The plan is
+    validated and uploaded once; ``__call__`` only launches (CUDA graph
+    capturable).  Results equal ``gemv`` / ``gemv_quantized`` on each job bit
+    for bit.
     """
 
     def __init__(self, jobs, deps="serial", device=None):
@@ -120,11 +123,25 @@ class GemvChain:
         deps = [int(d) for d in deps]
         if len(deps) != n:
             raise ValueError("deps must name one dependency per job")
+        kinds = {(w.kind if isinstance(w, QuantizedWeight) else "bf16") for (w, _, _) in jobs}
+        if len(kinds) != 1:
+            raise ValueError(f"every job of a chain has the same weight kind, got {sorted(kinds)}")
+        kind = kinds.pop()
+        w_kind = {"bf16": _lib.SN_WEIGHT_BF16, "int8": _lib.SN_WEIGHT_INT8, "e4m3": _lib.SN_WEIGHT_E4M3}[kind]
         arr = (_lib.GemvJob * n)()
         M = None
         self._keep = []
         for j, (W, x, y) in enumerate(jobs):
-            Mj, N, K = _check_gemv(x, W)
+            if kind == "bf16":
+                Mj, N, K = _check_gemv(x, W)
+                codes, scale = W, None
+            else:
+                require_cuda("x", x, _BF16, 2)
+                codes, scale = W.q, W.scale
+                Mj, K = x.shape
+                N = codes.shape[0]
+                if codes.shape[1] != K or scale.shape != (N,) or scale.dtype != torch.float32:
+                    raise ValueError(f"job {j}: quantised weight does not match x")
             require_cuda("y", y, None, 2)
             if y.shape != (Mj, N) or y.dtype not in (_BF16, torch.float32):
                 raise ValueError(f"job {j}: y must be [{Mj}, {N}] bf16 or fp32")
@@ -132,21 +149,22 @@ class GemvChain:
                 M = Mj
             elif Mj != M:
                 raise ValueError("every job of a chain has the same M")
-            arr[j] = _lib.GemvJob(W.data_ptr(), x.data_ptr(), y.data_ptr(), row_major("W", W), row_major("x", x),
-                                  row_major("y", y), N, K, deps[j],
+            arr[j] = _lib.GemvJob(codes.data_ptr(), x.data_ptr(), y.data_ptr(),
+                                  scale.data_ptr() if scale is not None else None, row_major("W", codes),
+                                  row_major("x", x), row_major("y", y), N, K, deps[j],
                                   _lib.SN_DTYPE_F32 if y.dtype == torch.float32 else _lib.SN_DTYPE_BF16)
-            self._keep += [W, x, y]
-        if M > 2:
+            self._keep += [codes, x, y] + ([scale] if scale is not None else [])
+        if not 1 <= M <= 2:
             raise ValueError("a GEMV chain takes M <= 2")
-        dev = device if device is not None else jobs[0][0].device
+        dev = device if device is not None else jobs[0][1].device
         nbytes = _lib.lib().sn_gemv_chain_workspace_size(n)
         if nbytes == 0:
             raise ValueError(f"{n} jobs: outside the chain's limits")
         self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         self.info = _lib.GemvChainInfo()
-        call("sn_gemv_chain_plan", ctypes.addressof(arr), n, M, self.workspace.data_ptr(), nbytes,
+        call("sn_gemv_chain_plan", w_kind, ctypes.addressof(arr), n, M, self.workspace.data_ptr(), nbytes,
              ctypes.byref(self.info), stream_handle(None))
-        self.njobs, self.M, self.deps = n, M, deps
+        self.njobs, self.M, self.deps, self.kind = n, M, deps, kind
         self.outputs = [y for (_, _, y) in jobs]
 
     def __call__(self, pdl: bool = False, stream=None):

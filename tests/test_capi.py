@@ -82,8 +82,8 @@ def test_product_raises_without_library(monkeypatch, tmp_path):
         _lib.lib()
 
 
-def _job(W, x, y, N=64, K=256, dep=-1, ldw=None, ldx=None, ldy=None, y_dtype=0):
-    return _lib.GemvJob(W, x, y, ldw or K, ldx or K, ldy or N, N, K, dep, y_dtype)
+def _job(W, x, y, N=64, K=256, dep=-1, ldw=None, ldx=None, ldy=None, y_dtype=0, scale=None):
+    return _lib.GemvJob(W, x, y, scale, ldw or K, ldx or K, ldy or N, N, K, dep, y_dtype)
 
 
 def test_gemv_chain_plan_rejects_bad_jobs_on_host(L):
@@ -98,13 +98,15 @@ def test_gemv_chain_plan_rejects_bad_jobs_on_host(L):
     info = _lib.GemvChainInfo()
     W0, W1, X, Y0, Y1 = 1 << 30, 2 << 30, 3 << 30, 4 << 30, 5 << 30
 
-    def plan(jobs, M=1, wsb=n):
+    def plan(jobs, M=1, wsb=n, kind=0):
         arr = (_lib.GemvJob * len(jobs))(*jobs)
-        return L.sn_gemv_chain_plan(ctypes.addressof(arr), len(jobs), M, ctypes.c_void_p(ws), wsb,
+        return L.sn_gemv_chain_plan(kind, ctypes.addressof(arr), len(jobs), M, ctypes.c_void_p(ws), wsb,
                                     ctypes.byref(info), None)
 
     good = [_job(W0, X, Y0), _job(W1, Y0, Y1, dep=0)]
     assert plan(good, M=3) == -1                                    # M outside 1..2
+    assert plan(good, kind=3) == -1                                 # weight kind
+    assert plan(good, kind=1) == -1                                 # 8-bit codes without row scales
     assert plan(good, wsb=L.sn_gemv_chain_workspace_size(2) - 1) == -1  # workspace too small
     assert plan([_job(W0, X, Y0), _job(W1, X, Y1, dep=1)]) == -1    # dep must name an earlier job
     assert plan([_job(W0, X, Y0, y_dtype=5)]) == -1                 # output dtype
@@ -120,5 +122,5 @@ def test_gemv_chain_plan_rejects_bad_jobs_on_host(L):
     import torch
     if not torch.cuda.is_available():  # valid jobs reach the device copy, which fails without a GPU
         assert plan(chain3, wsb=L.sn_gemv_chain_workspace_size(3)) == -4
-    launch_info = _lib.GemvChainInfo(0, 1, 1, 2, 4096, 512, 0)
+    launch_info = _lib.GemvChainInfo(0, 1, 0, 2, 4096, 8192, 512, 8, 16, 0, 0)
     assert L.sn_gemv_chain_launch(ctypes.byref(launch_info), ctypes.c_void_p(ws), 0, None) == -1

@@ -150,3 +150,48 @@ def test_plan_rejects_unordered_buffers(G):
         G.GemvChain([(Ws[0], xs[0], ys[0]), (Ws[0], xs[0], ys[0])], deps="serial")
     with pytest.raises(SonataError):  # an output over one of the chain's weights
         G.GemvChain([(Ws[0], xs[0], Ws[0].view(-1)[:4096].view(1, 4096))], deps="none")
+
+
+@pytest.mark.parametrize("kind", ["int8", "e4m3"])
+@pytest.mark.parametrize("M", [1, 2])
+def test_quantized_chain_matches_per_call(G, cuda_lib, kind, M):
+    """8-bit weights (fused dequant): the chain equals gemv_quantized on every
+    job bit for bit, and the dequantise-then-matmul oracle within 1e-3."""
+    shapes = [(N, K) for (_, N, K) in CONFIG2]
+    Ws = _weights(shapes, 51 + M)
+    qws = [G.quantize_weight(W, kind) for W in Ws]
+    g = torch.Generator(device="cuda").manual_seed(52)
+    xs = [torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16) for (N, K) in shapes]
+    xs[1][0, 5] = 300.0  # one large activation
+    ys = [torch.full((M, N), float("nan"), device="cuda", dtype=torch.float32) for (N, K) in shapes]
+    chain = G.GemvChain(list(zip(qws, xs, ys)), deps="none")
+    chain()
+    torch.cuda.synchronize()
+    assert cuda_lib.sn_device_status(1, None) == 0
+    for qw, x, y in zip(qws, xs, ys):
+        assert torch.equal(y, G.gemv_quantized(x, qw, out_dtype=torch.float32))
+    for j in (0, 1, 5):
+        truth = O.dequant_gemv_ref(bits(xs[j]), qws[j].q.cpu().numpy(), qws[j].scale.cpu().numpy(), kind)
+        assert O.rel_err_inf(ys[j].cpu().numpy(), truth) <= 1e-3
+
+
+@pytest.mark.parametrize("kind", ["int8", "e4m3"])
+def test_quantized_dependent_chain_and_nonfinite_rows(G, cuda_lib, kind):
+    Ws, xs, ys = _dependent_chain(G, 2, 61)
+    qws = [G.quantize_weight(W, kind) for W in Ws]
+    with torch.no_grad():
+        xs[0][1, 3] = float("inf")  # row 1 of the first x is non-finite: NaN outputs on that row
+    chain = G.GemvChain(list(zip(qws, xs, ys)), deps="serial")
+    chain()
+    torch.cuda.synchronize()
+    assert cuda_lib.sn_device_status(1, None) == 0
+    got = [y.clone() for y in ys]
+    for y in ys:
+        y.zero_()
+    for qw, x, y in zip(qws, xs, ys):
+        G.gemv_quantized(x, qw, out=y)
+    torch.cuda.synchronize()
+    for a, b in zip(got, ys):
+        assert torch.equal(a, b) or (torch.isnan(a) == torch.isnan(b)).all() and torch.equal(
+            torch.nan_to_num(a), torch.nan_to_num(b))
+    assert torch.isnan(got[0][1]).all() and torch.isfinite(got[0][0]).all()
