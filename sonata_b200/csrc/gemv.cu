@@ -1932,8 +1932,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
           const uint32_t end = off + job.tile_bytes;
           // the youngest tile in flight that the new one overlaps (tiles are
           // consumed in order, so its release implies every older one's)
+          // (tiles before t - kChainTiles were released before their pairs
+          // were reused, so at most kChainTiles entries are scanned)
           int need = t - kChainTiles;  // the mbarrier pair is reused
-          for (int v = max(tail, 0); v < t; ++v) {
+          for (int v = max(tail, t - kChainTiles); v < t; ++v) {
             const int q = v % kChainTiles;
             if (tend[q] > off && tbeg[q] < end) need = max(need, v);
           }
