@@ -63,7 +63,7 @@ NOMINAL_HBM_GBS = 8000.0
 # DRAM traffic of one GEMV-chain launch over 4 layers (24 GEMVs) from one ncu
 # capture (profiles/gemv_chain_kernel_4layers.md): dram__bytes_read.sum +
 # dram__bytes_write.sum, and the algorithmic bytes of that launch.
-NCU_TRAFFIC_CHAIN = 567_520_000 + 3_737_088
+NCU_TRAFFIC_CHAIN = 567_478_784 + 3_615_744
 NCU_CHAIN_ALGO_BYTES = 4 * sum((N * K + K + N) * 2 for (N, K) in SHAPES.values())
 
 
