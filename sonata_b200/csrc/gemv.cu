@@ -716,7 +716,9 @@ __device__ __forceinline__ void diag_entries(const uint32_t (&ta)[ND], int lane,
   uint32_t r[ND][W];
 #pragma unroll
   for (int d = 0; d < ND; ++d) {
-    if constexpr (S == 2)
+    if constexpr (S == 1)
+      tc::tmem_ld8_async(ta[d], r[d]);
+    else if constexpr (S == 2)
       tc::tmem_ld16_async(ta[d], r[d]);
     else
       tc::tmem_ld32_async(ta[d], r[d]);
@@ -1761,7 +1763,8 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16*
 // is bounded.
 //
 // Warps: 0 weight producer (frozen weights, no wait), 1 TMEM owner and MMA
-// issuer, 2..5 epilogue (TMEM lane quarter = warp % 4), 6 x loader.
+// issuer, 2..5 epilogue (TMEM lane quarter = warp % 4), 6 x loader (and 7,
+// for the 8-bit kinds, whose x staging computes digit planes).
 // ---------------------------------------------------------------------------
 namespace {
 
@@ -1777,11 +1780,12 @@ struct ChainJob {  // device copy of one job (80 bytes)
   int S;  // row segments (2 or 4): 16 / S rows per tile
   int flags;  // kJobF32 (fp32 y), kJobSignal (a later job waits for this one)
   uint32_t tile_bytes;
-  int pad;
+  int n;  // MMA N: 8 * S * MT * planes, rounded up to 16
 };
 static_assert(sizeof(ChainJob) == 80, "ChainJob is 80 bytes");
 
-constexpr int kChainThreads = 224;
+constexpr int kChainThreads = 256;
+constexpr int kXPieces = 16;  // 16-byte x pieces an 8-bit x staging lane holds (rows up to K = 4096)
 constexpr int kChainAcc = 8;             // TMEM accumulators (a power of two)
 constexpr int kJobF32 = 1, kJobSignal = 2;
 constexpr int kChainTiles = 16;          // weight tiles in flight at most (mbarrier pairs)
@@ -1970,16 +1974,24 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
           mbar_wait_bounded(full + v % kChainTiles, (v / kChainTiles) & 1);
       }
     }
-  } else if (warp == 6) {
-    // ---------------- x loader: waits for each job's producer --------------
+  } else if (warp == 6 || warp == 7) {
+    // ---------------- x loaders: wait for each job's producer --------------
+    // bf16: warp 6 alone (one bulk copy per row); 8-bit: warps 6 and 7 take
+    // alternate jobs (a warp's row maximum and planes take ~3 us at K = 2048)
+    constexpr int kXWarps = (WK == W_BF16) ? 1 : 2;
+    const int xw = warp - 6;
     pdl_wait();  // the first jobs' x and the counters belong to earlier kernels
     int u = 0;
     ChainJob job = load_job(p.jobs, 0), nxt;
-    for (int j = 0; j < p.njobs; ++j, job = nxt) {
+    for (int j = 0; j < p.njobs && xw < kXWarps; ++j, job = nxt) {
       nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
       int r0, r1;
       cta_rows(job.N, c, G, r0, r1);
       if (r0 == r1) continue;
+      if (u % kXWarps != xw) {  // the other warp's job
+        ++u;
+        continue;
+      }
       const int b = u & (nxb - 1);
       const uint32_t row_bytes = static_cast<uint32_t>(job.K) * ESZ;  // x row bytes in the B operand
       if (static_cast<uint32_t>(MT * ND) * row_bytes > p.xbuf_bytes) {
@@ -2012,14 +2024,35 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
           int e = 0;
           float up1 = 0.f, up2 = 0.f;
           const __nv_bfloat16* xrow = job.x + static_cast<int64_t>(m) * job.ldx;
-          if (m < p.M) {
+          if (cpr <= 32 * kXPieces) {
+            // rows up to 32 kXPieces pieces: one load of each piece, held in
+            // registers between the maximum and the planes
+            uint4 v[kXPieces];
             uint32_t mx = 0;
-            for (int cc = lane; cc < cpr; cc += 32) mx = max(mx, x8_piece_max(ld_cg_v4(xrow + cc * 8)));
+#pragma unroll
+            for (int i = 0; i < kXPieces; ++i) {
+              const int cc = lane + 32 * i;
+              v[i] = (m < p.M && cc < cpr) ? ld_cg_v4(xrow + cc * 8) : make_uint4(0, 0, 0, 0);
+              mx = max(mx, x8_piece_max(v[i]));
+            }
             mx = __reduce_max_sync(0xffffffffu, mx);
             e = x8_row_scale<WK>(mx, up1, up2);
+#pragma unroll
+            for (int i = 0; i < kXPieces; ++i) {
+              const int cc = lane + 32 * i;
+              if (cc < cpr) x8_emit<WK, MT>(dst, job.K, m, cc, v[i], up1, up2);
+            }
+          } else {
+            if (m < p.M) {
+              uint32_t mx = 0;
+              for (int cc = lane; cc < cpr; cc += 32) mx = max(mx, x8_piece_max(ld_cg_v4(xrow + cc * 8)));
+              mx = __reduce_max_sync(0xffffffffu, mx);
+              e = x8_row_scale<WK>(mx, up1, up2);
+            }
+            for (int cc = lane; cc < cpr; cc += 32)
+              x8_emit<WK, MT>(dst, job.K, m, cc, m < p.M ? ld_cg_v4(xrow + cc * 8) : make_uint4(0, 0, 0, 0), up1,
+                              up2);
           }
-          for (int cc = lane; cc < cpr; cc += 32)
-            x8_emit<WK, MT>(dst, job.K, m, cc, m < p.M ? ld_cg_v4(xrow + cc * 8) : make_uint4(0, 0, 0, 0), up1, up2);
           if (lane == 0) xexp[(u % kChainExps) * MT + m] = e;
         }
         tc::fence_proxy_async_smem();  // the plane stores -> the tensor core's reads
@@ -2033,7 +2066,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
     }
     // the last bulk copies have landed before the CTA can exit (the MMA
     // issuer waits for them too unless it stopped early)
-    if (WK == W_BF16 && lane == 0)
+    if (WK == W_BF16 && xw == 0 && lane == 0)
       for (int v = (u > nxb ? u - nxb : 0); v < u; ++v) mbar_wait_bounded(xfull + (v & (nxb - 1)), (v >> xl) & 1);
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -2055,7 +2088,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
         const int R = 16 / job.S;
         const uint32_t L = static_cast<uint32_t>(job.K) * ESZ / job.S;  // segment bytes
         const uint32_t nk = L / 256;                                      // MMAs per tile
-        const int n = 8 * job.S * MT * ND;
+        const int n = job.n;
         const uint32_t idesc = (WK == W_INT8)   ? tc::idesc_s8_s32(128, n)
                                : (WK == W_E4M3) ? tc::idesc_e4m3_f32(128, n)
                                                 : tc::idesc_bf16_f32(128, n);
@@ -2142,7 +2175,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
             float de[ND];
 #pragma unroll
             for (int d = 0; d < ND; ++d) ta[d] = taddr + (d * MT + m) * Gs;
-            if (job.S == 2)
+            if (job.S == 1)
+              diag_entries<1, ND>(ta, lane, de);
+            else if (job.S == 2)
               diag_entries<2, ND>(ta, lane, de);
             else
               diag_entries<4, ND>(ta, lane, de);
@@ -2348,8 +2383,7 @@ int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, vo
   const int nd = nd_of(w_kind);
   std::vector<ChainJob> dev(static_cast<size_t>(njobs));
   std::vector<ByteRange> xr(njobs), yr(njobs), wr(njobs);
-  uint32_t tile_max = 0;
-  int kmax = 0;
+  uint32_t tile_max = 0, xbuf_need = 0;
   for (int j = 0; j < njobs; ++j) {
     const sn_gemv_job& a = jobs[j];
     if (!a.W || !a.x || !a.y || a.N < 1 || a.K < 1 || a.ldw < a.K || a.ldx < a.K || a.ldy < a.N)
@@ -2360,8 +2394,13 @@ int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, vo
     if (a.y_dtype != SN_DTYPE_BF16 && a.y_dtype != SN_DTYPE_F32) return SN_ERR_INVALID_ARGUMENT;
     if (!aligned16(a.W) || !aligned16(a.x) || (a.ldw * esz) % 16 != 0 || (a.ldx * 2) % 16 != 0)
       return SN_ERR_MISALIGNED;
-    const int S = mma_segments(a.K, esz, MT, nd);
+    int S = mma_segments(a.K, esz, MT, nd);
+    // 8-bit: one segment per row where it fits, so a tile is 16 whole rows
+    // (32 KB at K = 2048) and the per-tile costs are paid half as often
+    if (esz == 1 && a.K % 256 == 0 && 16 * a.K <= 64 * 1024) S = 1;
     if (S == 0 || a.ldx > INT_MAX || a.ldy > INT_MAX) return SN_ERR_UNSUPPORTED;
+    const int n = (8 * S * MT * nd + 15) / 16 * 16;  // MMA N (M = 128 takes multiples of 16)
+    if (n > 256) return SN_ERR_UNSUPPORTED;
     const int64_t tile = static_cast<int64_t>(16 / S) * a.K * esz;
     if (tile > 128 * 1024) return SN_ERR_UNSUPPORTED;
     ChainJob& d = dev[j];
@@ -2378,9 +2417,10 @@ int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, vo
     d.S = S;
     d.flags = (a.y_dtype == SN_DTYPE_F32) ? kJobF32 : 0;
     d.tile_bytes = static_cast<uint32_t>(tile);
-    d.pad = 0;
+    d.n = n;
+    // the B operand spans n / 8 groups of L = K esz / S bytes
+    xbuf_need = std::max<uint32_t>(xbuf_need, static_cast<uint32_t>(n / 8) * static_cast<uint32_t>(a.K * esz / S));
     tile_max = std::max(tile_max, d.tile_bytes);
-    kmax = std::max(kmax, a.K);
     xr[j] = rows_range(a.x, M, a.ldx, a.K, 2);
     yr[j] = rows_range(a.y, M, a.ldy, a.N, a.y_dtype == SN_DTYPE_F32 ? 4 : 2);
     wr[j] = rows_range(a.W, a.N, a.ldw, a.K, esz);
@@ -2399,9 +2439,10 @@ int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, vo
       if (!waits) return SN_ERR_INVALID_ARGUMENT;
     }
   }
-  // one x buffer: the B operand of MT rows of the longest K (bf16 rows, or
-  // the nd 8-bit planes of each row)
-  const uint32_t xbuf = round_up_u32(static_cast<uint32_t>(MT * kmax * (esz == 2 ? 2 : nd)), 128);
+  // one x buffer: the largest B operand of the chain (MT bf16 rows, or the
+  // nd 8-bit planes of each row; an int8 N rounded up to 16 reads one more
+  // plane's bytes, unused)
+  const uint32_t xbuf = round_up_u32(xbuf_need, 128);
   // x buffers: up to kChainXBufs while the ring keeps two tiles and 96 KB
   // (deeper rings measured no faster), at least two
   const size_t ring_min = std::max<size_t>(2 * static_cast<size_t>(tile_max), 96 * 1024);
@@ -2414,7 +2455,7 @@ int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, vo
   // TMEM accumulators: as many (a power of two up to kChainAcc) as 512
   // columns hold at the chain's largest MMA N
   uint32_t acc_cols = 0;
-  for (int j = 0; j < njobs; ++j) acc_cols = std::max(acc_cols, static_cast<uint32_t>(8 * dev[j].S * MT * nd));
+  for (int j = 0; j < njobs; ++j) acc_cols = std::max(acc_cols, static_cast<uint32_t>(dev[j].n));
   int nacc = kChainAcc;
   while (nacc > 2 && nacc * acc_cols > 512) nacc /= 2;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -155,8 +155,10 @@ def test_plan_rejects_unordered_buffers(G):
 @pytest.mark.parametrize("kind", ["int8", "e4m3"])
 @pytest.mark.parametrize("M", [1, 2])
 def test_quantized_chain_matches_per_call(G, cuda_lib, kind, M):
-    """8-bit weights (fused dequant): the chain equals gemv_quantized on every
-    job bit for bit, and the dequantise-then-matmul oracle within 1e-3."""
+    """8-bit weights (fused dequant): the chain takes whole rows as one
+    segment (32 KB tiles); int8 equals gemv_quantized bit for bit (exact
+    integer sums), e4m3 within fp32 summation order (1e-5 of ||y||_inf); both
+    the dequantise-then-matmul oracle within 1e-3."""
     shapes = [(N, K) for (_, N, K) in CONFIG2]
     Ws = _weights(shapes, 51 + M)
     qws = [G.quantize_weight(W, kind) for W in Ws]
@@ -169,7 +171,11 @@ def test_quantized_chain_matches_per_call(G, cuda_lib, kind, M):
     torch.cuda.synchronize()
     assert cuda_lib.sn_device_status(1, None) == 0
     for qw, x, y in zip(qws, xs, ys):
-        assert torch.equal(y, G.gemv_quantized(x, qw, out_dtype=torch.float32))
+        ref = G.gemv_quantized(x, qw, out_dtype=torch.float32)
+        if kind == "int8":  # exact integer sums either way
+            assert torch.equal(y, ref)
+        else:  # one fp32 accumulator per row here, two segment partials per call
+            assert (y - ref).abs().max().item() <= 1e-5 * ref.abs().max().item()
     for j in (0, 1, 5):
         truth = O.dequant_gemv_ref(bits(xs[j]), qws[j].q.cpu().numpy(), qws[j].scale.cpu().numpy(), kind)
         assert O.rel_err_inf(ys[j].cpu().numpy(), truth) <= 1e-3
@@ -192,6 +198,10 @@ def test_quantized_dependent_chain_and_nonfinite_rows(G, cuda_lib, kind):
         G.gemv_quantized(x, qw, out=y)
     torch.cuda.synchronize()
     for a, b in zip(got, ys):
-        assert torch.equal(a, b) or (torch.isnan(a) == torch.isnan(b)).all() and torch.equal(
-            torch.nan_to_num(a), torch.nan_to_num(b))
+        assert (torch.isnan(a) == torch.isnan(b)).all()
+        fa, fb = torch.nan_to_num(a).float(), torch.nan_to_num(b).float()
+        if kind == "int8":
+            assert torch.equal(fa, fb)
+        else:  # fp32 summation order, then one bf16 rounding per job
+            assert (fa - fb).abs().max().item() <= 2e-2 * fb.abs().max().item()
     assert torch.isnan(got[0][1]).all() and torch.isfinite(got[0][0]).all()
