@@ -180,7 +180,7 @@ typedef struct sn_gemv_chain_info { /* filled by sn_gemv_chain_plan */
   uint32_t ring_bytes, xbuf_bytes; /* shared-memory weight ring, one x buffer */
   uint32_t accumulators;         /* TMEM accumulators */
   uint32_t accumulator_cols;     /* TMEM columns per accumulator */
-  uint32_t reserved;
+  uint32_t grid;                 /* CTAs (one per SM of the planning device) */
   uint64_t workspace_bytes;
 } sn_gemv_chain_info;
 

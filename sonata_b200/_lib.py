@@ -101,7 +101,7 @@ class GemvChainInfo(ctypes.Structure):
     """sn_gemv_chain_info of include/sonata_b200.h."""
     _fields_ = [("njobs", ctypes.c_int), ("M", ctypes.c_int), ("w_kind", ctypes.c_int), ("x_buffers", ctypes.c_int),
                 ("tile_bytes_max", ctypes.c_uint32), ("ring_bytes", ctypes.c_uint32), ("xbuf_bytes", ctypes.c_uint32),
-                ("accumulators", ctypes.c_uint32), ("accumulator_cols", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+                ("accumulators", ctypes.c_uint32), ("accumulator_cols", ctypes.c_uint32), ("grid", ctypes.c_uint32),
                 ("workspace_bytes", ctypes.c_uint64)]
 
 

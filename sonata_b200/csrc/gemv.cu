@@ -1768,7 +1768,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16*
 // ---------------------------------------------------------------------------
 namespace {
 
-struct ChainJob {  // device copy of one job (80 bytes)
+struct ChainJob {  // device copy of one job (96 bytes)
   const uint8_t* W;
   const __nv_bfloat16* x;
   void* y;
@@ -1777,12 +1777,15 @@ struct ChainJob {  // device copy of one job (80 bytes)
   int ldx, ldy;  // elements
   int N, K;
   int dep;
-  int S;  // row segments (2 or 4): 16 / S rows per tile
+  int S;      // row segments (1, 2 or 4): 16 / S rows per tile
   int flags;  // kJobF32 (fp32 y), kJobSignal (a later job waits for this one)
   uint32_t tile_bytes;
-  int n;  // MMA N: 8 * S * MT * planes, rounded up to 16
+  int n;      // MMA N: 8 * S * MT * planes, rounded up to 16
+  int sl;     // log2 S
+  int q, rem; // rows per CTA: q, one more for the first rem CTAs (no division in the kernel)
+  int pad[2];
 };
-static_assert(sizeof(ChainJob) == 80, "ChainJob is 80 bytes");
+static_assert(sizeof(ChainJob) == 96, "ChainJob is 96 bytes");
 
 constexpr int kChainThreads = 256;
 constexpr int kXPieces = 16;  // 16-byte x pieces an 8-bit x staging lane holds (rows up to K = 4096)
@@ -1806,14 +1809,26 @@ struct ChainParams {
   uint32_t acc_cols;  // TMEM columns per accumulator: the largest MMA N of the chain
 };
 
+// The job table is read-only for the launch.  The loads are volatile so that
+// the compiler issues them where they stand (a role loads job j + 1 when it
+// starts job j) instead of sinking them to their first use at the job
+// boundary, where their latency (~0.5 us under a full HBM stream) stalled
+// every role once per job.
+__device__ __forceinline__ uint4 ld_nc_v4_early(const void* ptr) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(ptr));
+  return r;
+}
 __device__ __forceinline__ ChainJob load_job(const ChainJob* jobs, int j) {
   union {
-    uint4 v[5];
+    uint4 v[6];
     ChainJob job;
   } u;
   const uint4* src = reinterpret_cast<const uint4*>(jobs + j);
 #pragma unroll
-  for (int i = 0; i < 5; ++i) u.v[i] = __ldg(src + i);
+  for (int i = 0; i < 6; ++i) u.v[i] = ld_nc_v4_early(src + i);
   return u.job;
 }
 
@@ -1850,10 +1865,12 @@ __device__ __forceinline__ bool wait_counter(const unsigned* c, unsigned target)
 }
 
 // Rows [r0, r1) of a job with N rows owned by CTA c of G.
-// (32-bit: the plan keeps N below 2^24, so N * (c + 1) < 2^32)
-__device__ __forceinline__ void cta_rows(int N, int c, int G, int& r0, int& r1) {
-  r0 = static_cast<int>(static_cast<uint32_t>(N) * static_cast<uint32_t>(c) / static_cast<uint32_t>(G));
-  r1 = static_cast<int>(static_cast<uint32_t>(N) * static_cast<uint32_t>(c + 1) / static_cast<uint32_t>(G));
+// (no division: a job's q and rem come from the plan, whose grid the launch
+// uses; integer divisions by run-time values cost the single-threaded roles
+// ~0.1 us each at every job boundary)
+__device__ __forceinline__ void cta_rows(const ChainJob& job, int c, int& r0, int& r1) {
+  r0 = c * job.q + min(c, job.rem);
+  r1 = r0 + job.q + (c < job.rem ? 1 : 0);
 }
 
 template <int WK, int MT>
@@ -1927,10 +1944,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
           ok = false;
           break;
         }
-        const int R = 16 / job.S;
+        const int R = 16 >> job.sl;
         const uint32_t row_bytes = static_cast<uint32_t>(job.K) * ESZ;
         int r0, r1;
-        cta_rows(job.N, c, G, r0, r1);
+        cta_rows(job, c, r0, r1);
         for (int first = r0; first < r1; first += R, ++t) {
           if (off + job.tile_bytes > p.ring_bytes) off = 0;
           const uint32_t end = off + job.tile_bytes;
@@ -1986,7 +2003,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
     for (int j = 0; j < p.njobs && xw < kXWarps; ++j, job = nxt) {
       nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
       int r0, r1;
-      cta_rows(job.N, c, G, r0, r1);
+      cta_rows(job, c, r0, r1);
       if (r0 == r1) continue;
       if (u % kXWarps != xw) {  // the other warp's job
         ++u;
@@ -2078,15 +2095,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
       for (int j = 0; j < p.njobs && ok; ++j, job = nxt) {
         nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
         int r0, r1;
-        cta_rows(job.N, c, G, r0, r1);
+        cta_rows(job, c, r0, r1);
         if (r0 == r1) continue;
         const int b = u & (nxb - 1);
         if (!mbar_wait_bounded(xfull + b, (u >> xl) & 1)) {
           record_status(SN_ERR_TIMEOUT);
           break;
         }
-        const int R = 16 / job.S;
-        const uint32_t L = static_cast<uint32_t>(job.K) * ESZ / job.S;  // segment bytes
+        const int R = 16 >> job.sl;
+        const uint32_t L = (static_cast<uint32_t>(job.K) * ESZ) >> job.sl;  // segment bytes
         const uint32_t nk = L / 256;                                      // MMAs per tile
         const int n = job.n;
         const uint32_t idesc = (WK == W_INT8)   ? tc::idesc_s8_s32(128, n)
@@ -2136,9 +2153,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const Chai
     for (int j = 0; j < p.njobs; ++j, job = nxt) {
       nxt = load_job(p.jobs, min(j + 1, p.njobs - 1));
       int r0, r1;
-      cta_rows(job.N, c, G, r0, r1);
-      const int R = 16 / job.S;
-      const int Gs = 8 * job.S;  // TMEM lanes (and columns) per weight row
+      cta_rows(job, c, r0, r1);
+      const int R = 16 >> job.sl;
+      const int Gs = 8 << job.sl;  // TMEM lanes (and columns) per weight row
       const int r = i / Gs;      // weight row inside the tile
       int e[MT];                 // 8-bit: x row m was scaled by 2^e[m]
 #pragma unroll
@@ -2267,7 +2284,7 @@ bool overlap(const ByteRange& a, const ByteRange& b) { return a.lo < b.hi && b.l
 
 namespace {
 template <int WK, int MT>
-int chain_launch(const ChainParams& p, size_t smem, unsigned flags, cudaStream_t stream) {
+int chain_launch(const ChainParams& p, int grid, size_t smem, unsigned flags, cudaStream_t stream) {
   auto kern = gemv_chain_kernel<WK, MT>;
   if (!ensure_smem(reinterpret_cast<const void*>(kern), smem)) return SN_ERR_UNSUPPORTED;
   int per_sm = 0;
@@ -2279,7 +2296,7 @@ int chain_launch(const ChainParams& p, size_t smem, unsigned flags, cudaStream_t
   // every CTA waits for others (job completions): all must be resident at
   // once, which a cooperative launch guarantees
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sm_count());
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kChainThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -2382,6 +2399,7 @@ int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, vo
   const int esz = (w_kind == SN_WEIGHT_BF16) ? 2 : 1;
   const int nd = nd_of(w_kind);
   std::vector<ChainJob> dev(static_cast<size_t>(njobs));
+  const int grid = sm_count();  // one CTA per SM; the jobs' row split is for this grid
   std::vector<ByteRange> xr(njobs), yr(njobs), wr(njobs);
   uint32_t tile_max = 0, xbuf_need = 0;
   for (int j = 0; j < njobs; ++j) {
@@ -2418,6 +2436,10 @@ int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, vo
     d.flags = (a.y_dtype == SN_DTYPE_F32) ? kJobF32 : 0;
     d.tile_bytes = static_cast<uint32_t>(tile);
     d.n = n;
+    d.sl = S == 1 ? 0 : S == 2 ? 1 : 2;
+    d.q = a.N / grid;
+    d.rem = a.N % grid;
+    d.pad[0] = d.pad[1] = 0;
     // the B operand spans n / 8 groups of L = K esz / S bytes
     xbuf_need = std::max<uint32_t>(xbuf_need, static_cast<uint32_t>(n / 8) * static_cast<uint32_t>(a.K * esz / S));
     tile_max = std::max(tile_max, d.tile_bytes);
@@ -2476,6 +2498,7 @@ int sn_gemv_chain_plan(int w_kind, const sn_gemv_job* jobs, int njobs, int M, vo
   info->xbuf_bytes = xbuf;
   info->accumulators = static_cast<uint32_t>(nacc);
   info->accumulator_cols = acc_cols;
+  info->grid = static_cast<uint32_t>(grid);
   info->workspace_bytes = chain_workspace_bytes(njobs);
   return SN_OK;
 }
@@ -2511,14 +2534,17 @@ int sn_gemv_chain_launch(const sn_gemv_chain_info* info, void* workspace, unsign
   p.tcols = tc::tmem_cols_for(info->accumulators * info->accumulator_cols);
   const size_t smem = p.ring_off + static_cast<size_t>(p.ring_bytes);
   if (smem > kChainSmem) return SN_ERR_INVALID_ARGUMENT;
+  // the plan split the rows for its device's SM count: one CTA per SM
+  const int grid = static_cast<int>(info->grid);
+  if (grid < 1 || grid > sm_count()) return SN_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (wk * 2 + (M - 1)) {
-    case SN_WEIGHT_BF16 * 2: return chain_launch<W_BF16, 1>(p, smem, flags, st);
-    case SN_WEIGHT_BF16 * 2 + 1: return chain_launch<W_BF16, 2>(p, smem, flags, st);
-    case SN_WEIGHT_INT8 * 2: return chain_launch<W_INT8, 1>(p, smem, flags, st);
-    case SN_WEIGHT_INT8 * 2 + 1: return chain_launch<W_INT8, 2>(p, smem, flags, st);
-    case SN_WEIGHT_E4M3 * 2: return chain_launch<W_E4M3, 1>(p, smem, flags, st);
-    default: return chain_launch<W_E4M3, 2>(p, smem, flags, st);
+    case SN_WEIGHT_BF16 * 2: return chain_launch<W_BF16, 1>(p, grid, smem, flags, st);
+    case SN_WEIGHT_BF16 * 2 + 1: return chain_launch<W_BF16, 2>(p, grid, smem, flags, st);
+    case SN_WEIGHT_INT8 * 2: return chain_launch<W_INT8, 1>(p, grid, smem, flags, st);
+    case SN_WEIGHT_INT8 * 2 + 1: return chain_launch<W_INT8, 2>(p, grid, smem, flags, st);
+    case SN_WEIGHT_E4M3 * 2: return chain_launch<W_E4M3, 1>(p, grid, smem, flags, st);
+    default: return chain_launch<W_E4M3, 2>(p, grid, smem, flags, st);
   }
 }
 
