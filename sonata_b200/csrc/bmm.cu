@@ -250,10 +250,10 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       }
     }
     pdl_wait();
+    int s = 0, k = 0;  // stage of `it` (it mod ns) and its round (it / ns), kept without divisions
     for (int t = cluster; t < p.ntiles && ok; t += nclusters) {
       const int bti = t % p.nbt, rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);
-      for (int j = 0; j < kb_half; ++j, ++it) {
-        const int s = it % ns, k = it / ns;
+      for (int j = 0; j < kb_half; ++j, ++it, k += (++s == ns), s = (s == ns) ? 0 : s) {
         uint8_t* a = smem + s * p.stage_bytes;
         if (it >= pre) {
           if (k > 0 && !mbar_wait_bounded(empty + s, (k - 1) & 1)) {
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = tc::idesc_bf16_f32(128, p.bt);
-    int it = 0, j = 0;
+    int it = 0, j = 0, s = 0, ph = 0;  // stage it mod ns and its phase, kept without divisions
     bool ok = true;
     for (int t = cluster; t < p.ntiles && ok; t += nclusters, ++j) {
       if (j > 0 && !mbar_wait_bounded(tempty, (j - 1) & 1)) {
@@ -281,9 +281,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         break;
       }
       tc::fence_after_sync();
-      for (int kb = 0; kb < kb_half; ++kb, ++it) {
-        const int s = it % ns;
-        if (!mbar_wait_bounded(full + s, (it / ns) & 1)) {
+      for (int kb = 0; kb < kb_half; ++kb, ++it, ph ^= (++s == ns), s = (s == ns) ? 0 : s) {
+        if (!mbar_wait_bounded(full + s, ph)) {
           record_status(SN_ERR_TIMEOUT);
           ok = false;
           break;
@@ -303,13 +302,13 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     // products, done while this CTA's MMAs run; all loads of a dot issued first
     {
       const int nx = p.N - p.nrt * 128;
-      const int64_t items = static_cast<int64_t>(p.ncb) * p.B * nx;
+      const int items = p.ncb * p.B * nx;  // < 2^31 (host-checked shapes)
       const int gw = blockIdx.x * 4 + (warp - 2), nw = gridDim.x * 4;
       const int nck = p.K / 8;  // 16-byte chunks per row
-      for (int64_t e = gw; e < items; e += nw) {
-        const int x = static_cast<int>(e % nx);
-        const int b = static_cast<int>((e / nx) % p.B);
-        const int cb = static_cast<int>(e / (static_cast<int64_t>(nx) * p.B));
+      for (int e = gw; e < items; e += nw) {
+        const int x = e % nx;
+        const int b = (e / nx) % p.B;
+        const int cb = e / (nx * p.B);
         const int n = p.nrt * 128 + x;
         const uint4* hr = reinterpret_cast<const uint4*>(p.hidden + (static_cast<int64_t>(cb) * p.B + b) * p.K);
         const uint4* wr = reinterpret_cast<const uint4*>(p.Wt + (static_cast<int64_t>(cb) * p.N + n) * p.K);
@@ -561,6 +560,8 @@ int tu_status_bmm(bool reset, cudaStream_t st, int* out) { return read_tu_status
 // the cluster launch or the shared-memory plan does not fit.
 int head_splitk(const void* hidden, const void* Wt, float* logits, int ncb, int B, int K, int N, bool pdl,
                 cudaStream_t st) {
+  // the kernel's CUDA-core tail indexes ncb * B * (N mod 128) items in int
+  if (static_cast<int64_t>(ncb) * B * 128 >= (int64_t(1) << 31)) return SN_ERR_UNSUPPORTED;
   HeadSkParams p;
   p.out = logits;
   p.hidden = static_cast<const __nv_bfloat16*>(hidden);

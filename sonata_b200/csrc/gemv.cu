@@ -72,6 +72,7 @@ struct GemvParams {
   const uint8_t* pf;
   int64_t pf_ld;
   int pf_rows, pf_parts;
+  int pf_q, pf_rem;  // the next launch's rows per CTA: pf_q, one more for its first pf_rem CTAs
   uint32_t pf_row_bytes, pf_part_bytes;
   int x_rot;    // x row copies start at a CTA-dependent 128-byte piece
   int pf_lead;  // issue once all but this many of the CTA's own tiles have landed (< 0: at once)
@@ -677,6 +678,7 @@ struct MmaShape {
   uint32_t xraw_off;   // int8: byte offset of x as copied (bf16 [MT][K])
   uint32_t ring_off;   // byte offset of slot 0
   uint32_t tcols;      // TMEM columns allocated
+  int q, rem;          // rows per CTA: q, one more for the first rem CTAs of grid.x
 };
 
 // v[idx] for a lane-dependent idx without local-memory indexing.
@@ -745,8 +747,9 @@ __device__ __forceinline__ void prefetch_next_weights(const GemvParams& p) {
   constexpr uint32_t kPiece = 32 * 1024;
   const int nblk = static_cast<int>(gridDim.x * gridDim.y);
   for (int j = static_cast<int>(blockIdx.y * gridDim.x + blockIdx.x); j < p.pf_parts; j += nblk) {
-    const int64_t a = static_cast<int64_t>(p.pf_rows) * j / p.pf_parts;
-    const int64_t b = static_cast<int64_t>(p.pf_rows) * (j + 1) / p.pf_parts;
+    // the next launch's CTA j owns rows [a, b) (its division-free split)
+    const int64_t a = static_cast<int64_t>(j) * p.pf_q + min(j, p.pf_rem);
+    const int64_t b = a + p.pf_q + (j < p.pf_rem ? 1 : 0);
     const int64_t bytes = min(static_cast<int64_t>(p.pf_part_bytes), (b - a) * p.pf_row_bytes);
     if (p.pf_ld == static_cast<int64_t>(p.pf_row_bytes)) {
       const uint8_t* src = p.pf + a * p.pf_ld;
@@ -1006,8 +1009,11 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
   const __nv_bfloat16* xb = p.x + static_cast<int64_t>(blockIdx.y) * p.sx;
   void* yb = reinterpret_cast<uint8_t*>(p.y) + static_cast<int64_t>(blockIdx.y) * p.sy * (p.y_f32 ? 4 : 2);
   const float* sb = (WK != W_BF16) ? p.scale + static_cast<int64_t>(blockIdx.y) * p.sS : nullptr;
-  const int r0 = static_cast<int>(static_cast<int64_t>(p.N) * blockIdx.x / gridDim.x);
-  const int r1 = static_cast<int>(static_cast<int64_t>(p.N) * (blockIdx.x + 1) / gridDim.x);
+  // rows of this CTA without a division (a run-time division costs the
+  // single-threaded producer and MMA issuer ~0.1 us each at launch)
+  const int bx = static_cast<int>(blockIdx.x);
+  const int r0 = bx * sh.q + min(bx, sh.rem);
+  const int r1 = r0 + sh.q + (bx < sh.rem ? 1 : 0);
   const int nrows = r1 - r0;
   const uint32_t row_bytes = static_cast<uint32_t>(p.K) * ESZ;
   const int ntiles = (nrows + R - 1) / R;
@@ -1036,9 +1042,8 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
       if (p.pf != nullptr && p.pf_lead <= -2) prefetch_next_weights(p);  // before this CTA's own copies
-      int t = 0;
-      for (; t < ntiles; ++t) {
-        const int s = t % ns, k = t / ns;
+      int t = 0, s = 0, k = 0;  // tile, its slot (t mod ns) and round (t / ns), kept incrementally
+      for (; t < ntiles; ++t, s = (s + 1 == ns) ? 0 : s + 1, k += (s == 0)) {
         if (k > 0 && !mbar_wait_bounded(empty + s, (k - 1) & 1)) {
           record_status(SN_ERR_TIMEOUT);
           break;
@@ -1185,9 +1190,9 @@ __global__ void __launch_bounds__(kMmaGemvThreads, 2) gemv_mma_kernel(const Gemv
         bool x_ok = true;
         if constexpr (WK == W_BF16) x_ok = mbar_wait_bounded(xbar, 0);
         if (!x_ok) record_status(SN_ERR_TIMEOUT);
-        for (int t = 0; t < ntiles && x_ok; ++t) {
-          const int s = t % ns, b = t & (nacc - 1);
-          if (!mbar_wait_bounded(full + s, (t / ns) & 1) ||
+        for (int t = 0, s = 0, ph = 0; t < ntiles && x_ok; ++t, s = (s + 1 == ns) ? 0 : s + 1, ph ^= (s == 0)) {
+          const int b = t & (nacc - 1);
+          if (!mbar_wait_bounded(full + s, ph) ||
               (t >= nacc && !mbar_wait_bounded(tempty + b, ((t >> sh.acc_log2) - 1) & 1))) {
             record_status(SN_ERR_TIMEOUT);
             break;
@@ -1457,6 +1462,8 @@ int dispatch_mma(const GemvParams& p, int batch, cudaStream_t st, bool pdl) {
   sh.N = 8 * S * MT * ND;
   sh.slot_bytes = static_cast<uint32_t>(R) * p.K * ESZ;
   sh.acc_log2 = g.acc_log2;
+  sh.q = p.N / grid;
+  sh.rem = p.N % grid;
   sh.tcols = tc::tmem_cols_for(sh.N << sh.acc_log2);
   const int rows_per_cta = (p.N + grid - 1) / grid;
   const int tiles_per_cta = (rows_per_cta + R - 1) / R;
@@ -1634,6 +1641,7 @@ int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale
   p.pf = nullptr;
   p.pf_ld = 0;
   p.pf_rows = p.pf_parts = 0;
+  p.pf_q = p.pf_rem = 0;
   p.pf_row_bytes = p.pf_part_bytes = 0;
   p.pf_lead = prefetch_lead();
   p.x_rot = x_rotate();
@@ -1670,6 +1678,8 @@ int gemv_impl(int wk, const void* W, int64_t ldw, int64_t sW, const float* scale
       p.pf_ld = next->ldw * nesz;
       p.pf_rows = next->N;
       p.pf_parts = parts;
+      p.pf_q = next->N / parts;
+      p.pf_rem = next->N % parts;
       p.pf_row_bytes = static_cast<uint32_t>(row_b);
       const int64_t per_part = ((want + parts - 1) / parts + 127) / 128 * 128;  // whole 128-byte lines
       p.pf_part_bytes = static_cast<uint32_t>(std::min<int64_t>(per_part, int64_t(1) << 30));
