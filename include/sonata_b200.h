@@ -139,8 +139,10 @@ int sn_gemv_bf16_norm(int norm_kind, const void *W, int64_t ldw, const void *x, 
  * weights while the current job finishes; only a job's x waits, inside the
  * kernel, for the job named by `dep` (an earlier job, or -1: x is ready when
  * the launch starts).  dep = j - 1 for every job gives the ordering of
- * back-to-back launches on one stream.  Results are bit-identical to
- * sn_gemv_bf16 on the same job (same tensor-core partition and order).
+ * back-to-back launches on one stream.  bf16 and int8 results are
+ * bit-identical to sn_gemv_bf16 / sn_gemv_int8 on the same job (same
+ * tensor-core arithmetic and order); e4m3 accumulates each row in one fp32
+ * accumulator, so it matches sn_gemv_fp8e4m3 within fp32 summation order.
  * Same role as a CUDA graph of patched nn.Linear calls (kernels/patch.py:54-66,
  * kernels/bench_gemv_graph.py:30-63); no counterpart in the reference.
  *
