@@ -63,7 +63,7 @@ NOMINAL_HBM_GBS = 8000.0
 # DRAM traffic of one GEMV-chain launch over 4 layers (24 GEMVs) from one ncu
 # capture (profiles/gemv_chain_kernel_4layers.md): dram__bytes_read.sum +
 # dram__bytes_write.sum, and the algorithmic bytes of that launch.
-NCU_TRAFFIC_CHAIN = 567_478_784 + 3_615_744
+NCU_TRAFFIC_CHAIN = 567_466_496 + 4_645_120
 NCU_CHAIN_ALGO_BYTES = 4 * sum((N * K + K + N) * 2 for (N, K) in SHAPES.values())
 
 
@@ -861,7 +861,7 @@ def run_case(args):
     """One hot-path kernel on one shape, timed with CUDA events (also the
     command behind every ncu capture summarised in profiles/)."""
     dist_setup(1)
-    shape = [int(v) for v in args.shape.split("x")] if args.shape else []
+    shape = [int(v) for v in args.shape.split("x")] if args.shape and args.shape[0].isdigit() else []
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     out = {"case": args.case, "shape": args.shape}
     if args.case == "gemv":
@@ -874,17 +874,27 @@ def run_case(args):
         per = len(Ws)
         algo = (N * K + M * K + M * N) * 2
     elif args.case == "chain":
-        # --shape LAYERS: the config-2 set over LAYERS layers as one GEMV-chain launch
+        # --shape LAYERS: the config-2 set over LAYERS layers as one GEMV-chain
+        # launch; --shape int8 | e4m3: the config-3 chain of 26 in_proj weights
         from sonata_b200.kernels import gemv as G
-        (nl,) = (shape + [4])[:1]
-        shapes = [(N, K) for _ in range(nl) for (N, K) in SHAPES.values()]
-        Ws = [(torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16) for (N, K) in shapes]
-        xs = [torch.randn(1, K, device="cuda").to(torch.bfloat16) for (N, K) in shapes]
-        ys = [torch.empty(1, N, device="cuda", dtype=torch.bfloat16) for (N, K) in shapes]
-        ch = G.GemvChain(list(zip(Ws, xs, ys)), deps="none")
+        if args.shape in ("int8", "e4m3"):
+            N, K = SHAPES["in_proj"]
+            qws = [G.quantize_weight((torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16), args.shape)
+                   for _ in range(26)]
+            x = torch.randn(1, K, device="cuda").to(torch.bfloat16)
+            ys = [torch.empty(1, N, device="cuda") for _ in range(26)]
+            ch = G.GemvChain([(q, x, y) for q, y in zip(qws, ys)], deps="none")
+            algo = 26 * (N * K + N * 4 + K * 2 + N * 4)
+        else:
+            nl = int(args.shape) if args.shape else 4
+            shapes = [(N, K) for _ in range(nl) for (N, K) in SHAPES.values()]
+            Ws = [(torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16) for (N, K) in shapes]
+            xs = [torch.randn(1, K, device="cuda").to(torch.bfloat16) for (N, K) in shapes]
+            ys = [torch.empty(1, N, device="cuda", dtype=torch.bfloat16) for (N, K) in shapes]
+            ch = G.GemvChain(list(zip(Ws, xs, ys)), deps="none")
+            algo = sum((N * K + K + N) * 2 for (N, K) in shapes)
         run = ch
         per = 1
-        algo = sum((N * K + K + N) * 2 for (N, K) in shapes)
     elif args.case == "snake":
         from sonata_b200.kernels import fused_snake_conv as S
         C, T, d = (shape + [384, 55168, 3][len(shape):])[:3]
