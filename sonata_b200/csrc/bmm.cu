@@ -239,13 +239,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     const int pre = min(ns, (p.ntiles > cluster ? (p.ntiles - 1 - cluster) / nclusters + 1 : 0) * kb_half);
     {
       int t = cluster, j = 0;
+      int rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);  // per tile, not per stage
       for (int q = 0; q < pre; ++q) {
-        const int rt = (t / p.nbt) % p.nrt, cb = t / (p.nbt * p.nrt);
         mbar_arrive_expect_tx(full + q, p.stage_bytes);
         load_w(smem + q * p.stage_bytes, kb0 + j, rt, cb, full + q);
         if (++j == kb_half) {
           j = 0;
           t += nclusters;
+          rt = (t / p.nbt) % p.nrt;
+          cb = t / (p.nbt * p.nrt);
         }
       }
     }
