@@ -66,6 +66,7 @@ struct ScParams {
   // o' = o * up_s + r, row q holds y[b, o, up_s * q + r - up_p]; y is
   // [B, Cy, Ty].  up_s == 0: plain convolution, column o, row t of y[b, o, t].
   int up_s, up_p, Cy, Ty;
+  int up_sh;  // log2(up_s) when up_s is a power of two (every DAC stride), else -1
   int up_vec;          // widest vector store (1, 2 or 4 floats) the phase runs of y allow
   // element strides of the batch and channel (row) dimensions; time is
   // contiguous.  Whole tensors: x (Cin * T, T), y and res (Cy * Ty, Ty); a
@@ -107,7 +108,9 @@ __device__ __forceinline__ void sc_load_bias16(const ScParams& p, int o_base, fl
   } else {
 #pragma unroll
     for (int e = 0; e < 16; ++e)
-      bv[e] = (p.bias && o_base + e < p.Cout) ? __ldg(p.bias + (o_base + e) / p.up_s) : 0.f;
+      bv[e] = (p.bias && o_base + e < p.Cout)
+                  ? __ldg(p.bias + (p.up_sh >= 0 ? (o_base + e) >> p.up_sh : (o_base + e) / p.up_s))
+                  : 0.f;
   }
 }
 
@@ -1102,6 +1105,7 @@ ScParams base_params(const float* x, const float* alpha, const float* bias, floa
   p.act = SN_ACT_SNAKE;
   p.post = SN_POST_NONE;
   p.up_s = p.up_p = 0;
+  p.up_sh = -1;
   p.up_vec = 1;
   return p;
 }
@@ -1240,6 +1244,7 @@ int snake_convt_impl(const float* x, int64_t x_bs, int64_t x_ld, const float* al
     p.pad = m - 1;
     p.dil = 1;
     p.up_s = stride;
+    p.up_sh = (stride & (stride - 1)) == 0 ? __builtin_ctz(static_cast<unsigned>(stride)) : -1;
     p.up_p = padding;
     p.Cy = Cout;
     p.Ty = Ty;
