@@ -236,4 +236,6 @@ def bench_step_ops(reps: int = 10, calls: int = 20, seed: int = 0) -> dict:
         us = a.elapsed_time(e) * 1e3 / (reps * calls)
         out[name] = {"us_per_call": round(us, 2), "bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
     return {"metric": "Mamba2 decode-step ops µs per call (CUDA graph)", "unit": "us", "ops": out,
-            "note": "latency-bound at decode shapes: each op moves 41 KB - 6.3 MB"}
+            "note": "latency-bound at decode shapes: each op moves 41 KB - 6.3 MB; the 20 calls of a replay reuse "
+                    "one set of tensors, so operands are L2 hits after the first call (in a decode step the SSU "
+                    "state would come from HBM)"}
