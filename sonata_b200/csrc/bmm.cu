@@ -661,6 +661,7 @@ int sn_codebook_head_pack(const void* W, int ncb, int K, int N, void* Wt, void* 
 int sn_codebook_head_bmm(const void* hidden, const void* Wt, float* logits, int ncb, int B, int K, int N,
                          unsigned flags, void* stream) {
   if (!hidden || !Wt || !logits || ncb < 1 || B < 1 || K < 1 || N < 1) return SN_ERR_INVALID_ARGUMENT;
+  if (B > INT32_MAX - 31) return SN_ERR_INVALID_ARGUMENT;  // stream tiles round B up in int
   if (flags & ~SN_FLAG_PDL) return SN_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool tc_ok = (K % 64 == 0) && sn::aligned16(hidden) && sn::aligned16(Wt);

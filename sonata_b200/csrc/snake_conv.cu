@@ -1124,6 +1124,7 @@ int sn_snake_conv1d_pack(const float* W, int Cin, int Cout, int K, void* packed,
   if (!W || !packed || Cin < 1 || Cout < 1 || K < 1) return SN_ERR_INVALID_ARGUMENT;
   if (packed_bytes < sn_snake_conv1d_workspace_size(Cin, Cout, K)) return SN_ERR_INVALID_ARGUMENT;
   if (!sn::aligned16(packed)) return SN_ERR_MISALIGNED;
+  if (Cout > INT32_MAX - 15) return SN_ERR_INVALID_ARGUMENT;  // the round-up to 16 below stays in int
   const int Cg = (Cout + 15) / 16 * 16;
   const int64_t tot = static_cast<int64_t>(Cg) * Cin;
   return sn::launch(sn::pack_weights_kernel, dim3(sn::blocks_for(tot, 8)), dim3(256), 0,
@@ -1174,6 +1175,7 @@ int snake_conv1d_impl(const float* x, int64_t x_bs, int64_t x_ld, const float* a
       (residual && !strides_ok(r_bs, r_ld, B, Cout, Tout)))
     return SN_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (Cout > INT32_MAX - 15) return SN_ERR_INVALID_ARGUMENT;  // the round-up to 16 below stays in int
   const int Cg = (Cout + 15) / 16 * 16;  // GEMM width: zero weight rows past Cout
   if (fast_path_ok(Cin, Cg, K, stride, dilation, Tout) && workspace &&
       workspace_bytes >= sn_snake_conv1d_workspace_size(Cin, Cout, K) && aligned16(workspace)) {
@@ -1381,6 +1383,7 @@ int sn_snake_conv1d_noalloc(const float* x, const float* alpha, const float* W, 
   if (tout < 1 || tout > INT32_MAX) return SN_ERR_INVALID_ARGUMENT;
   // Only the tensor-core path packs weights into the scratch; every other
   // shape runs the per-output kernel, which reads W directly and needs none.
+  if (Cout > INT32_MAX - 15) return SN_ERR_INVALID_ARGUMENT;  // the round-up to 16 below stays in int
   const int Cg = (Cout + 15) / 16 * 16;
   if (!sn::fast_path_ok(Cin, Cg, K, stride, dilation, static_cast<int>(tout)))
     return sn_snake_conv1d(x, alpha, W, bias, y, B, Cin, Cout, T, K, stride, padding, dilation, eps, nullptr, 0,

@@ -61,6 +61,10 @@ def test_gemv_rejects_bad_arguments_on_host(L):
     assert L.sn_snake_conv1d_pack(p, 16, 16, 7, p, 16, None) == -1
     assert L.sn_snake_conv_transpose1d_pack(p, 16, 16, 5, 2, p, 1 << 20, None) == -3
     assert L.sn_snake_conv_transpose1d_output_length(10, 16, 8, 4) == 80
+    # channel / stream counts whose round-up to the GEMM tile would overflow int
+    imax = 2**31 - 1
+    assert L.sn_snake_conv1d_noalloc(p, p, p, None, p, 1, 16, imax, 8, 1, 1, 0, 1, 1e-9, None) == -1
+    assert L.sn_codebook_head_bmm(p, p, p, 9, imax, 2048, 1025, 0, None) == -1
     # Mamba2 decode-step ops
     assert L.sn_causal_conv1d_update(None, p, p, None, p, 1, 8, 4, 2, None) == -1
     assert L.sn_causal_conv1d_update(p, p, p, None, p, 1, 8, 9, 2, None) == -1   # W > 8
