@@ -12,7 +12,10 @@
 // with griddepcontrol.launch_dependents: the projection GEMV that follows it
 // in a decode step (launched with programmatic dependent launch) may then
 // start streaming its frozen weights while the op runs; it reads the op's
-// output only after griddepcontrol.wait.
+// output only after griddepcontrol.wait.  The ops themselves are launched
+// the same way and execute griddepcontrol.wait before their first memory
+// access, so their launch and set-up overlap the tail of the kernel before
+// them (a GEMV that produced their input), whatever that kernel is.
 #include "common.cuh"
 
 #include <climits>
@@ -59,6 +62,7 @@ __global__ void __launch_bounds__(256) causal_conv1d_update_kernel(const __nv_bf
                                                                    __nv_bfloat16* __restrict__ y, int B, int D,
                                                                    int W, int act) {
   pdl_launch_dependents();  // a following programmatic-dependent GEMV may start its weight stream
+  pdl_wait();               // launched early (programmatic dependent launch): inputs from here on
   const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (e >= static_cast<int64_t>(B) * D) return;
   const int d = static_cast<int>(e % D);
@@ -87,6 +91,7 @@ struct SsuParams {
   const __nv_bfloat16* dt_bias;    // [nh, hd] or nullptr
   __nv_bfloat16* y;                // [batch, nh, hd]
   int batch, nh, hd, ds, ng, softplus;
+  int hpg;  // heads per group (nh / ng)
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -100,17 +105,29 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 struct SsuRow {
   int64_t row, hrow, bg;  // [batch, nh, hd], [nh, hd] and [batch, ng] indices
 };
+// Rows number fewer than 2^31 (host-checked), so the split is 32-bit.
 __device__ __forceinline__ SsuRow ssu_row(const SsuParams& p, int64_t row) {
-  const int dd = static_cast<int>(row % p.hd);
-  const int h = static_cast<int>((row / p.hd) % p.nh);
-  const int b = static_cast<int>(row / (static_cast<int64_t>(p.hd) * p.nh));
-  const int g = h / (p.nh / p.ng);
+  const int ri = static_cast<int>(row);
+  const int t = ri / p.hd;
+  const int dd = ri - t * p.hd;
+  const int b = t / p.nh;
+  const int h = t - b * p.nh;
+  const int g = h / p.hpg;
   return {row, static_cast<int64_t>(h) * p.hd + dd, static_cast<int64_t>(b) * p.ng + g};
 }
-__device__ __forceinline__ void ssu_finish(const SsuParams& p, const SsuRow& r, float acc, float xv) {
+// The D and z terms of a row, read before the state update so that their
+// loads overlap the others instead of following the reduction.
+struct SsuTail {
+  float d, z;
+};
+__device__ __forceinline__ SsuTail ssu_tail(const SsuParams& p, const SsuRow& r) {
+  return {p.D ? bf(p.D, r.hrow) : 0.f, p.z ? bf(p.z, r.row) : 0.f};
+}
+__device__ __forceinline__ void ssu_finish(const SsuParams& p, const SsuRow& r, float acc, float xv,
+                                           const SsuTail& tl) {
   float out = acc;
-  if (p.D) out = fmaf(xv, bf(p.D, r.hrow), out);
-  if (p.z) out *= silu(bf(p.z, r.row));
+  if (p.D) out = fmaf(xv, tl.d, out);
+  if (p.z) out *= silu(tl.z);
   p.y[r.row] = __float2bfloat16_rn(out);
 }
 __device__ __forceinline__ float ssu_dt(const SsuParams& p, const SsuRow& r) {
@@ -129,6 +146,7 @@ __device__ __forceinline__ float ssu_dt(const SsuParams& p, const SsuRow& r) {
 template <int NCH>
 __global__ void __launch_bounds__(256) selective_state_update_vec_kernel(const SsuParams p) {
   pdl_launch_dependents();
+  pdl_wait();
   const int l16 = threadIdx.x & 15;
   const int64_t rows = static_cast<int64_t>(p.batch) * p.nh * p.hd;
   const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 4;
@@ -151,6 +169,7 @@ __global__ void __launch_bounds__(256) selective_state_update_vec_kernel(const S
       cv[c] = *reinterpret_cast<const uint4*>(Cr + s);
     }
   }
+  const SsuTail tl = (valid && l16 == 0) ? ssu_tail(p, r) : SsuTail{0.f, 0.f};
   const float dt = valid ? ssu_dt(p, r) : 0.f;
   const float xv = valid ? bf(p.x, r.row) : 0.f;
   const float dtx = dt * xv;
@@ -177,13 +196,14 @@ __global__ void __launch_bounds__(256) selective_state_update_vec_kernel(const S
   }
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (valid && l16 == 0) ssu_finish(p, r, acc, xv);
+  if (valid && l16 == 0) ssu_finish(p, r, acc, xv, tl);
 }
 
 // Strided kernel (any d_state <= 256, any alignment): one warp per row,
 // lane l holds elements l, l + 32, ...
 __global__ void __launch_bounds__(256) selective_state_update_kernel(const SsuParams p) {
   pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= static_cast<int64_t>(p.batch) * p.nh * p.hd) return;
@@ -203,6 +223,7 @@ __global__ void __launch_bounds__(256) selective_state_update_kernel(const SsuPa
       cv[i] = __bfloat162float(Cr[s]);
     }
   }
+  const SsuTail tl = lane == 0 ? ssu_tail(p, r) : SsuTail{0.f, 0.f};
   const float dt = ssu_dt(p, r);
   const float xv = bf(p.x, row);
   const float dtx = dt * xv;
@@ -217,7 +238,7 @@ __global__ void __launch_bounds__(256) selective_state_update_kernel(const SsuPa
     }
   }
   acc = warp_sum(acc);
-  if (lane == 0) ssu_finish(p, r, acc, xv);
+  if (lane == 0) ssu_finish(p, r, acc, xv, tl);
 }
 
 // ---------------------------------------------------------------------------
@@ -284,6 +305,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_gated_kernel(const __nv_
                                                                      __nv_bfloat16* __restrict__ y, int N, int G,
                                                                      float eps, int norm_before_gate) {
   pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[16];
   __shared__ float part[2];
   const int rank = CL == 1 ? 0 : static_cast<int>(cluster_rank());
@@ -329,6 +351,7 @@ __global__ void __launch_bounds__(kNormThreads) layer_norm_kernel(const __nv_bfl
                                                                   void* __restrict__ residual_out, int rout_f32,
                                                                   int N, float eps, int rms) {
   pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[16];
   __shared__ float part[2];
   const int rank = CL == 1 ? 0 : static_cast<int>(cluster_rank());
@@ -393,13 +416,15 @@ int launch_cluster(Kern kern, int clusters, int cl, cudaStream_t st, Args... arg
   cfg.gridDim = dim3(static_cast<unsigned>(clusters * cl));
   cfg.blockDim = dim3(kNormThreads);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernels wait (griddepcontrol.wait)
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kern, args...) != cudaSuccess) {
     cudaGetLastError();
     return SN_ERR_LAUNCH;
@@ -437,6 +462,7 @@ struct SplitConvParams {
 
 __global__ void __launch_bounds__(256) mamba2_split_conv_kernel(const SplitConvParams p) {
   pdl_launch_dependents();
+  pdl_wait();
   const int conv_dim = p.di + 2 * p.gds;
   const int per_b = conv_dim + p.di + p.nh * p.hd;  // conv channels, z copy, dt broadcast
   const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -474,6 +500,7 @@ struct RotaryParams {
 
 __global__ void __launch_bounds__(256) rotary_kv_append_kernel(const RotaryParams p) {
   pdl_launch_dependents();
+  pdl_wait();
   const int h2 = p.hd / 2;
   const int heads = p.hq + 2 * p.hk;
   const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;  // (b, head, j < h2)
@@ -501,6 +528,7 @@ __global__ void __launch_bounds__(256) rotary_kv_append_kernel(const RotaryParam
 __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ y,
                                                      int batch, int d) {
   pdl_launch_dependents();
+  pdl_wait();
   const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (e >= static_cast<int64_t>(batch) * d) return;
   const int64_t b = e / d, i = e % d;
@@ -522,7 +550,7 @@ int sn_causal_conv1d_update(const void* x, void* conv_state, const void* weight,
   if (activation != SN_ACT_NONE && activation != SN_ACT_SILU) return SN_ERR_INVALID_ARGUMENT;
   const int64_t n = static_cast<int64_t>(B) * D;
   return sn::launch(sn::causal_conv1d_update_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
-                    static_cast<cudaStream_t>(stream), false, static_cast<const __nv_bfloat16*>(x),
+                    static_cast<cudaStream_t>(stream), true, static_cast<const __nv_bfloat16*>(x),
                     static_cast<__nv_bfloat16*>(conv_state), static_cast<const __nv_bfloat16*>(weight),
                     static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y), B, D, W,
                     activation == SN_ACT_SILU ? 1 : 0);
@@ -552,17 +580,19 @@ int sn_selective_state_update(void* state, const void* x, const void* dt, const 
   p.ds = dstate;
   p.ng = ngroups;
   p.softplus = dt_softplus ? 1 : 0;
+  p.hpg = nheads / ngroups;
   const int64_t rows = static_cast<int64_t>(batch) * nheads * headdim;
+  if (rows > INT32_MAX / 16) return SN_ERR_UNSUPPORTED;  // 32-bit row split, 16 lanes a row
   const bool vec = (dstate == 128 || dstate == 256) && sn::aligned16(state) && sn::aligned16(Bm) &&
                    sn::aligned16(Cm) && sn::aligned16(A);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (vec) {
     const dim3 grid(static_cast<unsigned>((rows + 15) / 16));  // 16 rows per 256-thread CTA
-    return dstate == 128 ? sn::launch(sn::selective_state_update_vec_kernel<1>, grid, dim3(256), 0, st, false, p)
-                         : sn::launch(sn::selective_state_update_vec_kernel<2>, grid, dim3(256), 0, st, false, p);
+    return dstate == 128 ? sn::launch(sn::selective_state_update_vec_kernel<1>, grid, dim3(256), 0, st, true, p)
+                         : sn::launch(sn::selective_state_update_vec_kernel<2>, grid, dim3(256), 0, st, true, p);
   }
   return sn::launch(sn::selective_state_update_kernel, dim3(static_cast<unsigned>((rows + 7) / 8)), dim3(256), 0, st,
-                    false, p);
+                    true, p);
 }
 
 int sn_rmsnorm_gated(const void* x, const void* weight, const void* bias, const void* z, void* y, int rows, int N,
@@ -635,7 +665,7 @@ int sn_mamba2_split_conv(const void* zxbcdt, int64_t ld, void* conv_state, const
   p.W = d_conv;
   const int64_t n = static_cast<int64_t>(batch) * (2 * d_inner + 2 * gds + static_cast<int64_t>(nheads) * headdim);
   return sn::launch(sn::mamba2_split_conv_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
-                    static_cast<cudaStream_t>(stream), false, p);
+                    static_cast<cudaStream_t>(stream), true, p);
 }
 
 int sn_rotary_kv_append(const void* qkv, void* q, void* k_cache, void* v_cache, const float* cos, const float* sin,
@@ -658,14 +688,14 @@ int sn_rotary_kv_append(const void* qkv, void* q, void* k_cache, void* v_cache, 
   p.pos = pos;
   const int64_t n = static_cast<int64_t>(batch) * (nheads + 2 * nheads_kv) * (head_dim / 2);
   return sn::launch(sn::rotary_kv_append_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
-                    static_cast<cudaStream_t>(stream), false, p);
+                    static_cast<cudaStream_t>(stream), true, p);
 }
 
 int sn_swiglu(const void* h, void* y, int batch, int d, void* stream) {
   if (!h || !y || batch < 1 || d < 1) return SN_ERR_INVALID_ARGUMENT;
   const int64_t n = static_cast<int64_t>(batch) * d;
   return sn::launch(sn::swiglu_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
-                    static_cast<cudaStream_t>(stream), false, static_cast<const __nv_bfloat16*>(h),
+                    static_cast<cudaStream_t>(stream), true, static_cast<const __nv_bfloat16*>(h),
                     static_cast<__nv_bfloat16*>(y), batch, d);
 }
 
