@@ -414,7 +414,11 @@ int sn_snake_conv1d_noalloc(const float *x, const float *alpha, const float *W, 
  * Mamba2 decode-step ops (bf16 tensors, fp32 arithmetic, bf16 outputs), the
  * semantics of the libraries the reference's frozen goldens were made with
  * (scripts/validation_harness.py:39,58-115,140-171: causal_conv1d
- * 1.6.2.post1, mamba_ssm 2.3.2.post1).  All tensors contiguous.
+ * 1.6.2.post1, mamba_ssm 2.3.2.post1).  All tensors contiguous.  Each op
+ * is launched with programmatic dependent launch and waits for the previous
+ * kernel in the stream before its first memory access (same results as a
+ * plain launch; its start overlaps that kernel's tail), and lets the next
+ * one start early.
  *
  * sn_causal_conv1d_update (causal_conv1d_update): conv_state [B, D, W]
  * (W <= 8) shifts one step left and takes x [B, D] as its newest column, in
