@@ -482,6 +482,25 @@ int sn_layer_norm_fused(const void *x, const void *residual, int residual_f32, c
 int sn_mamba2_split_conv(const void *zxbcdt, int64_t ld, void *conv_state, const void *conv_weight,
                          const void *conv_bias, void *z, void *x, void *B, void *C, void *dt, int batch, int d_inner,
                          int ngroups, int d_state, int nheads, int headdim, int d_conv, void *stream);
+/*
+ * sn_mamba2_conv_ssu: sn_mamba2_split_conv followed by
+ * sn_selective_state_update with dt softplus, in one launch (the Mamba2
+ * step between in_proj and the gated norm: mamba_ssm Mamba2.step, as the
+ * two calls above restate it).  zxbcdt, conv_state, conv_weight,
+ * conv_bias as in sn_mamba2_split_conv; ssm_state [batch, nheads, headdim,
+ * d_state] updated in place; A fp32 [nheads], D and dt_bias bf16 [nheads]
+ * (NULL for none): the per-head values those two calls take broadcast over
+ * headdim and d_state.  Writes z [batch, d_inner] and y [batch, nheads,
+ * headdim], equal bit for bit to the two-call path.  sync: batch * ngroups
+ * unsigned counters, zero before the first call and left zero by each call
+ * (one set per stream of calls: calls that share it must not overlap).
+ * SN_ERR_UNSUPPORTED unless d_state is 128 or 256, headdim a multiple of 16
+ * and ssm_state 16-byte aligned (the two-call path serves the rest).
+ */
+int sn_mamba2_conv_ssu(const void *zxbcdt, int64_t ld, void *conv_state, const void *conv_weight,
+                       const void *conv_bias, void *ssm_state, const float *A, const void *D, const void *dt_bias,
+                       void *z, void *y, unsigned *sync, int batch, int d_inner, int ngroups, int d_state, int nheads,
+                       int headdim, int d_conv, void *stream);
 int sn_rotary_kv_append(const void *qkv, void *q, void *k_cache, void *v_cache, const float *cos, const float *sin,
                         int batch, int nheads, int nheads_kv, int head_dim, int max_seqlen, int pos, void *stream);
 int sn_swiglu(const void *h, void *y, int batch, int d, void *stream);

@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
                                            _I, ctypes.c_float, _U, _P, ctypes.c_size_t, _P], _I),
     "sn_stream_shift": ([_P, _I, _P], _I),
     "sn_mamba2_split_conv": ([_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
+    "sn_mamba2_conv_ssu": ([_P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
     "sn_rotary_kv_append": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
     "sn_swiglu": ([_P, _P, _I, _I, _P], _I),
     "sn_snake1d": ([_P, _P, _P, _I, _I, _I64, ctypes.c_float, _P], _I),

@@ -205,4 +205,25 @@ inline int sm_count() {
   return cache[dev];
 }
 
+// Release / acquire on a global counter at GPU scope (grid-wide hand-offs
+// between CTAs of one launch), and a bounded wait for a count (~1 s of
+// %globaltimer; false when it runs out).
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool wait_counter(const unsigned* c, unsigned target) {
+  if (ld_acquire_gpu(c) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_gpu(c) < target) {
+    if (globaltimer_ns() - t0 > 1000000000ull) return false;
+    __nanosleep(32);
+  }
+  return true;
+}
+
 }  // namespace sn

@@ -1842,14 +1842,6 @@ __device__ __forceinline__ ChainJob load_job(const ChainJob* jobs, int j) {
   return u.job;
 }
 
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 // Named barrier that also returns the OR of `v` over the participating threads.
 __device__ __forceinline__ bool named_bar_or(int id, int threads, bool v) {
   uint32_t r;
@@ -1862,16 +1854,6 @@ __device__ __forceinline__ bool named_bar_or(int id, int threads, bool v) {
 }
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-// Bounded wait until *c >= target (one second, as every mbarrier wait here).
-__device__ __forceinline__ bool wait_counter(const unsigned* c, unsigned target) {
-  if (ld_acquire_gpu(c) >= target) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (ld_acquire_gpu(c) < target) {
-    if (globaltimer_ns() - t0 > 1000000000ull) return false;
-    __nanosleep(32);
-  }
-  return true;
 }
 
 // Rows [r0, r1) of a job with N rows owned by CTA c of G.

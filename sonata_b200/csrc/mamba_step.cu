@@ -55,6 +55,20 @@ __device__ __forceinline__ __nv_bfloat16 conv_update_channel(__nv_bfloat16 xv, _
   return __float2bfloat16_rn(act ? silu(acc) : acc);
 }
 
+// The same output as conv_update_channel (SiLU), from the state as it is,
+// without moving it: for channels whose state another CTA moves on.
+__device__ __forceinline__ __nv_bfloat16 conv_peek_channel(__nv_bfloat16 xv, const __nv_bfloat16* st,
+                                                           const __nv_bfloat16* __restrict__ w,
+                                                           const __nv_bfloat16* __restrict__ bias, int d, int W) {
+  float acc = bias ? bf(bias, d) : 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxConvWidth; ++k) {
+    if (k + 1 < W) acc = fmaf(__bfloat162float(st[k + 1]), bf(w, static_cast<int64_t>(d) * W + k), acc);
+  }
+  acc = fmaf(__bfloat162float(xv), bf(w, static_cast<int64_t>(d) * W + W - 1), acc);
+  return __float2bfloat16_rn(silu(acc));
+}
+
 __global__ void __launch_bounds__(256) causal_conv1d_update_kernel(const __nv_bfloat16* __restrict__ x,
                                                                    __nv_bfloat16* __restrict__ state,
                                                                    const __nv_bfloat16* __restrict__ w,
@@ -490,6 +504,170 @@ __global__ void __launch_bounds__(256) mamba2_split_conv_kernel(const SplitConvP
   p.dt[static_cast<int64_t>(b) * p.nh * p.hd + i] = row[p.di + conv_dim + i / p.hd];
 }
 
+// mamba2_conv_ssu: mamba2_split_conv and selective_state_update (vector
+// form, d_state 128 or 256, dt softplus) in one launch, with A, D and
+// dt_bias per head.  A CTA is 16 rows (b, h, dd .. dd + 15) of one head, 16
+// lanes a row, as in selective_state_update_vec_kernel, with the same
+// arithmetic in the same order, so the outputs equal the two-launch path's
+// bit for bit.  x channels: lane 0 of a row runs the row's conv update (its
+// own channel).  B and C of the head's group: every CTA of the (batch,
+// group) computes them into shared memory from the conv state as it is,
+// then draws a ticket (sync[b * ngroups + g]) with release semantics; the
+// CTA that draws the last ticket, whichever it is, has seen every other
+// CTA's reads (acquire) and moves the state on at its end, then resets the
+// counter to zero.  No CTA waits for another.
+struct ConvSsuParams {
+  const __nv_bfloat16* zx;  // [b, ld]
+  int64_t ld;
+  __nv_bfloat16* conv_state;  // [b, conv_dim, W]
+  const __nv_bfloat16* w;     // [conv_dim, W]
+  const __nv_bfloat16* bias;  // [conv_dim] or null
+  __nv_bfloat16* state;       // [b, nh, hd, ds]
+  const float* A;             // [nh]
+  const __nv_bfloat16* D;     // [nh] or null
+  const __nv_bfloat16* dt_bias;  // [nh] or null
+  __nv_bfloat16 *z, *y;       // [b, di], [b, nh, hd]
+  unsigned* sync;             // [b * ng]
+  int di, gds, ds, ng, nh, hd, hpg, W;
+  int bpg;  // CTAs per (batch, group): hpg * hd / 16, the tickets drawn per call
+};
+
+// Release pattern (fence, then a relaxed atomic at GPU scope): returns the
+// count before this one.
+__device__ __forceinline__ unsigned fence_then_ticket(unsigned* c) {
+  unsigned old;
+  asm volatile("fence.acq_rel.gpu;\n\tatom.relaxed.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(c) : "memory");
+  return old;
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(256) mamba2_conv_ssu_kernel(const ConvSsuParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ __align__(16) __nv_bfloat16 sbc[2 * 128 * NCH];  // B then C of this CTA's (batch, group)
+  __shared__ int s_mover;
+  const int tid = threadIdx.x, l16 = tid & 15;
+  const int rowbase = static_cast<int>(blockIdx.x) * 16;
+  const int t = rowbase / p.hd;
+  const int b = t / p.nh;
+  const int h = t - b * p.nh;
+  const int g = h / p.hpg;
+  const int dd = rowbase - t * p.hd + (tid >> 4);
+  const int conv_dim = p.di + 2 * p.gds;
+  const int ds = 128 * NCH;
+  const __nv_bfloat16* zx = p.zx + static_cast<int64_t>(b) * p.ld;
+  __nv_bfloat16* cs = p.conv_state + static_cast<int64_t>(b) * conv_dim * p.W;
+  // every load that needs nothing computed here first: the row's SSM state,
+  // dt, A, D (selective_state_update of row (b, h, dd))
+  const int64_t row = static_cast<int64_t>(t) * p.hd + dd;
+  __nv_bfloat16* st = p.state + row * ds;
+  uint4 sv[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) sv[c] = *reinterpret_cast<const uint4*>(st + 128 * c + 8 * l16);
+  float dt = __bfloat162float(zx[p.di + conv_dim + h]);
+  if (p.dt_bias) dt += bf(p.dt_bias, h);
+  const float a = p.A[h];
+  const float dval = (p.D && l16 == 0) ? bf(p.D, h) : 0.f;
+  // B and C of (b, g), from the group's conv state as it is; each thread
+  // keeps its channels' moved-on state (the old values shifted, the new
+  // input last) for the CTA that stores it
+  __nv_bfloat16 kept[NCH][kMaxConvWidth];
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) {
+    const int k = tid + 256 * j;  // 2 * ds = 256 * NCH channels, one per thread and j
+    const int ch = p.di + (k < ds ? g * ds + k : p.gds + g * ds + (k - ds));
+    const __nv_bfloat16* cst = cs + static_cast<int64_t>(ch) * p.W;
+    const __nv_bfloat16 xin = zx[p.di + ch];
+#pragma unroll
+    for (int w = 0; w < kMaxConvWidth; ++w) kept[j][w] = (w + 1 < p.W) ? cst[w + 1] : xin;
+    sbc[k] = conv_peek_channel(xin, cst, p.w, p.bias, ch, p.W);
+  }
+  // this row's x channel (owned by this row) and z: read now, stored after
+  // the count below, so that the count's release has no global store of
+  // this CTA to wait for
+  const int ch = h * p.hd + dd;
+  __nv_bfloat16* xst = cs + static_cast<int64_t>(ch) * p.W;
+  __nv_bfloat16 xkept[kMaxConvWidth];
+  __nv_bfloat16 zv = __float2bfloat16_rn(0.f);
+  float xv = 0.f;
+  if (l16 == 0) {
+    const __nv_bfloat16 xin = zx[p.di + ch];
+#pragma unroll
+    for (int w = 0; w < kMaxConvWidth; ++w) xkept[w] = (w + 1 < p.W) ? xst[w + 1] : xin;
+    xv = __bfloat162float(conv_peek_channel(xin, xst, p.w, p.bias, ch, p.W));
+  }
+  if (l16 == 1) zv = zx[ch];
+  __syncthreads();
+  // every CTA of the group takes a ticket once all its threads have read
+  // the group's B / C state (release: fence, then the atomic; no global
+  // store of this CTA is pending yet, so the fence is cheap); the ticket
+  // comes back while the SSU below runs, and the CTA that drew the last one
+  // moves the state on at the end
+  unsigned* cnt = p.sync + b * p.ng + g;
+  unsigned ticket = 0;
+  if (tid == 0) ticket = fence_then_ticket(cnt);
+  if (l16 == 0) {
+#pragma unroll
+    for (int w = 0; w < kMaxConvWidth; ++w)
+      if (w < p.W) xst[w] = xkept[w];
+  }
+  if (l16 == 1) p.z[static_cast<int64_t>(b) * p.di + ch] = zv;
+
+  xv = __shfl_sync(0xffffffffu, xv, 0, 16);
+  dt = dt <= 20.f ? log1pf(expf(dt)) : dt;
+  const float ea = expf(dt * a);
+  const float dtx = dt * xv;
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int s = 128 * c + 8 * l16;
+    const uint4 bv = *reinterpret_cast<const uint4*>(sbc + s);
+    const uint4 cv = *reinterpret_cast<const uint4*>(sbc + ds + s);
+    const uint32_t su[4] = {sv[c].x, sv[c].y, sv[c].z, sv[c].w};
+    const uint32_t bu[4] = {bv.x, bv.y, bv.z, bv.w};
+    const uint32_t cu[4] = {cv.x, cv.y, cv.z, cv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float n0 = fmaf(bf16lo(su[k]), ea, dtx * bf16lo(bu[k]));
+      const float n1 = fmaf(bf16hi(su[k]), ea, dtx * bf16hi(bu[k]));
+      acc = fmaf(n0, bf16lo(cu[k]), acc);
+      acc = fmaf(n1, bf16hi(cu[k]), acc);
+      o[k] = pack_bf16x2(n0, n1);
+    }
+    *reinterpret_cast<uint4*>(st + s) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (l16 == 0) {
+    float out = acc;
+    if (p.D) out = fmaf(xv, dval, out);
+    p.y[row] = __float2bfloat16_rn(out);
+  }
+
+  // the CTA with the last ticket moves the B / C state on: every other CTA
+  // of the group has read it (acquire: the fence after the atomic's result)
+  if (tid == 0) {
+    s_mover = ticket == static_cast<unsigned>(p.bpg - 1);
+    if (s_mover) {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      *cnt = 0;  // the next launch starts from zero
+    }
+  }
+  __syncthreads();
+  if (s_mover) {
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      const int k = tid + 256 * j;
+      const int c2 = p.di + (k < ds ? g * ds + k : p.gds + g * ds + (k - ds));
+      __nv_bfloat16* cst = cs + static_cast<int64_t>(c2) * p.W;
+#pragma unroll
+      for (int w = 0; w < kMaxConvWidth; ++w)
+        if (w < p.W) cst[w] = kept[j][w];
+    }
+  }
+}
+
 struct RotaryParams {
   const __nv_bfloat16* qkv;  // [b, (hq + 2 hk) hd]
   __nv_bfloat16* q;          // [b, hq, hd]
@@ -666,6 +844,48 @@ int sn_mamba2_split_conv(const void* zxbcdt, int64_t ld, void* conv_state, const
   const int64_t n = static_cast<int64_t>(batch) * (2 * d_inner + 2 * gds + static_cast<int64_t>(nheads) * headdim);
   return sn::launch(sn::mamba2_split_conv_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
                     static_cast<cudaStream_t>(stream), true, p);
+}
+
+int sn_mamba2_conv_ssu(const void* zxbcdt, int64_t ld, void* conv_state, const void* conv_weight,
+                       const void* conv_bias, void* ssm_state, const float* A, const void* D, const void* dt_bias,
+                       void* z, void* y, unsigned* sync, int batch, int d_inner, int ngroups, int d_state, int nheads,
+                       int headdim, int d_conv, void* stream) {
+  if (!zxbcdt || !conv_state || !conv_weight || !ssm_state || !A || !z || !y || !sync || batch < 1 || d_inner < 1 ||
+      ngroups < 1 || d_state < 1 || nheads < 1 || headdim < 1 || d_conv < 1 || d_conv > sn::kMaxConvWidth)
+    return SN_ERR_INVALID_ARGUMENT;
+  if (static_cast<int64_t>(nheads) * headdim != d_inner || nheads % ngroups != 0) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t gds = static_cast<int64_t>(ngroups) * d_state;
+  if (ld < 2 * d_inner + 2 * gds + nheads) return SN_ERR_INVALID_ARGUMENT;
+  const int64_t rows = static_cast<int64_t>(batch) * d_inner;
+  if ((d_state != 128 && d_state != 256) || headdim % 16 != 0 || !sn::aligned16(ssm_state) ||
+      rows > INT32_MAX / 16 || 2 * d_inner + 2 * gds + nheads > INT32_MAX)
+    return SN_ERR_UNSUPPORTED;
+  sn::ConvSsuParams p;
+  p.zx = static_cast<const __nv_bfloat16*>(zxbcdt);
+  p.ld = ld;
+  p.conv_state = static_cast<__nv_bfloat16*>(conv_state);
+  p.w = static_cast<const __nv_bfloat16*>(conv_weight);
+  p.bias = static_cast<const __nv_bfloat16*>(conv_bias);
+  p.state = static_cast<__nv_bfloat16*>(ssm_state);
+  p.A = A;
+  p.D = static_cast<const __nv_bfloat16*>(D);
+  p.dt_bias = static_cast<const __nv_bfloat16*>(dt_bias);
+  p.z = static_cast<__nv_bfloat16*>(z);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.sync = sync;
+  p.di = d_inner;
+  p.gds = static_cast<int>(gds);
+  p.ds = d_state;
+  p.ng = ngroups;
+  p.nh = nheads;
+  p.hd = headdim;
+  p.hpg = nheads / ngroups;
+  p.W = d_conv;
+  p.bpg = p.hpg * headdim / 16;
+  const dim3 grid(static_cast<unsigned>(rows / 16));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return d_state == 128 ? sn::launch(sn::mamba2_conv_ssu_kernel<1>, grid, dim3(256), 0, st, true, p)
+                        : sn::launch(sn::mamba2_conv_ssu_kernel<2>, grid, dim3(256), 0, st, true, p);
 }
 
 int sn_rotary_kv_append(const void* qkv, void* q, void* k_cache, void* v_cache, const float* cos, const float* sin,

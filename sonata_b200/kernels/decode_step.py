@@ -91,12 +91,16 @@ class Mamba2Mixer(torch.nn.Module):
         self.A = (-torch.exp(self.A_log.float()))[:, None, None].expand(nh, cfg.headdim, ds).contiguous()
         self.D_e = self.D[:, None].expand(nh, cfg.headdim).contiguous()
         self.dt_bias_e = self.dt_bias[:, None].expand(nh, cfg.headdim).contiguous()
+        self.A_h = (-torch.exp(self.A_log.float())).contiguous()  # per head, for the fused conv + SSU
+        # split + conv and selective_state_update as one launch (sn_mamba2_conv_ssu) in the fused-norm step
+        self.fused_conv_ssu = ds in (128, 256) and cfg.headdim % 16 == 0
 
     def alloc_state(self, batch):
         cfg = self.cfg
         dev = self.conv_w.device
         self.conv_state = torch.zeros(batch, self.conv_dim, cfg.d_conv, device=dev, dtype=_BF16)
         self.ssm_state = torch.zeros(batch, cfg.nheads, cfg.headdim, cfg.d_state, device=dev, dtype=_BF16)
+        self.sync = torch.zeros(batch * cfg.ngroups, device=dev, dtype=torch.int32)  # the fused kernel's counters
 
     def step_fused_norms(self, h: torch.Tensor, residual, norm_w, norm_b):
         """The block's add + LayerNorm fused into in_proj and the gated RMSNorm
@@ -106,10 +110,14 @@ class Mamba2Mixer(torch.nn.Module):
         di, ds, nh = cfg.d_inner, cfg.d_state, cfg.nheads
         zxbcdt, residual = G.gemv_add_layernorm(h, residual, norm_w, norm_b, self.in_proj.weight,
                                                 cfg.norm_epsilon, link=self.in_proj)
-        z, x, Bm, Cm, dt_e = MS.mamba2_split_conv(zxbcdt, self.conv_state, self.conv_w, self.conv_b, di,
-                                                  cfg.ngroups, ds, nh)
-        y = MS.selective_state_update(self.ssm_state, x, dt_e, self.A, Bm, Cm, D=self.D_e, z=None,
-                                      dt_bias=self.dt_bias_e, dt_softplus=True)
+        if self.fused_conv_ssu:
+            z, y = MS.mamba2_conv_ssu(zxbcdt, self.conv_state, self.conv_w, self.conv_b, self.ssm_state, self.A_h,
+                                      self.D, self.dt_bias, di, cfg.ngroups, ds, nh, self.sync)
+        else:
+            z, x, Bm, Cm, dt_e = MS.mamba2_split_conv(zxbcdt, self.conv_state, self.conv_w, self.conv_b, di,
+                                                      cfg.ngroups, ds, nh)
+            y = MS.selective_state_update(self.ssm_state, x, dt_e, self.A, Bm, Cm, D=self.D_e, z=None,
+                                          dt_bias=self.dt_bias_e, dt_softplus=True)
         out = G.gemv_rmsnorm_gated(y.view(b, di), z, self.norm_w, self.out_proj.weight, cfg.norm_epsilon,
                                    link=self.out_proj)
         return out, residual
@@ -342,8 +350,10 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
     the GEMV kernel without the prefetch chain, and the unpatched nn.Linear
     (cuBLAS); and the first variant with the glue between the kernels as
     plain torch ops (slices made contiguous, rotary, SwiGLU) instead of the
-    fused glue kernels.  A replay after changing the input must change the logits
-    (the empty-graph tripwire of bench_decode.py:114-121)."""
+    fused glue kernels, and with split + conv and selective_state_update as two
+    launches instead of sn_mamba2_conv_ssu.  A replay after changing the input
+    must change the logits (the empty-graph tripwire of
+    bench_decode.py:114-121)."""
     from .patch import patch_zonos_projections, unpatch_linear
     model = SyntheticZonos(batch=batch, seed=seed)
     x = torch.randn(batch, model.cfg.d_model, device="cuda",
@@ -395,6 +405,15 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
         raise RuntimeError("decode-step graph replay did not recompute (tripwire)")
     x.mul_(-1.0)
     del g
+    mixers = [blk.mixer for blk in model.backbone.layers if not blk.is_attn]
+    fused_cs = [mx.fused_conv_ssu for mx in mixers]
+    for mx in mixers:  # split + conv and selective_state_update as two launches
+        mx.fused_conv_ssu = False
+    g, out = capture()
+    res["two_launch_conv_ssu"] = timed(g)
+    del g
+    for mx, f in zip(mixers, fused_cs):
+        mx.fused_conv_ssu = f
     for m in model.projections():
         if hasattr(m, "_gemv_next"):
             m._gemv_next = None
@@ -410,10 +429,10 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
     us = res["gemv_pdl_prefetch"]
     cfg = model.cfg
     n_attn = len(cfg.attn_layer_idx)
-    # with the fused glue and norms: per Mamba2 block split+conv and SSU; per
-    # attention block rotary+cache, SDPA and SwiGLU; then the final norm and
-    # the head's input copy
-    launches_other = (cfg.n_layer - n_attn) * 2 + n_attn * 3 + 2
+    # with the fused glue and norms: per Mamba2 block the fused conv + SSU
+    # (or split+conv and SSU); per attention block rotary+cache, SDPA and
+    # SwiGLU; then the final norm and the head's input copy
+    launches_other = sum(1 if f else 2 for f in fused_cs) + n_attn * 3 + 2
     return {
         "metric": "synthetic Zonos-hybrid decode step µs (46 layers, CUDA graph)",
         "value": round(us, 1),
@@ -424,6 +443,7 @@ def bench_decode_step(steps: int = 20, warmup: int = 3, batch: int = 1, seed: in
         "us_gemv_without_prefetch_chain": round(res["gemv_pdl"], 1),
         "us_torch_glue": round(res["torch_glue"], 1),
         "us_norms_as_kernels": round(res["gemv_unfused_norms"], 1),
+        "us_conv_ssu_two_launches": round(res["two_launch_conv_ssu"], 1),
         "us_cublas_linear": round(res["cublas"], 1),
         "patched_linears": n,
         "tokens_per_s": round(1e6 / us, 1),

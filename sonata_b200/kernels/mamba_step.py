@@ -160,6 +160,46 @@ def mamba2_split_conv(zxbcdt: torch.Tensor, conv_state: torch.Tensor, weight: to
     return z, x, Bm, Cm, dt
 
 
+def mamba2_conv_ssu(zxbcdt: torch.Tensor, conv_state: torch.Tensor, weight: torch.Tensor, bias,
+                    ssm_state: torch.Tensor, A: torch.Tensor, D, dt_bias, d_inner: int, ngroups: int,
+                    d_state: int, nheads: int, sync: torch.Tensor, stream=None):
+    """``mamba2_split_conv`` then ``selective_state_update`` (dt softplus,
+    z applied later by the gated norm) in one launch: zxbcdt [b, >= width],
+    conv_state and ssm_state [b, nheads, headdim, d_state] updated in place,
+    A fp32 [nheads], D / dt_bias bf16 [nheads] or None (per head).  Returns
+    (z [b, d_inner], y [b, nheads, headdim]), equal bit for bit to the
+    two-launch path.  ``sync``: int32 [b * ngroups] zeros (the kernel leaves
+    them zero); calls sharing it must not overlap."""
+    require_cuda("zxbcdt", zxbcdt, _BF16, 2)
+    if zxbcdt.stride(1) != 1:
+        raise ValueError("zxbcdt must be contiguous along its last dimension")
+    b = zxbcdt.shape[0]
+    hd = d_inner // nheads
+    conv_dim = d_inner + 2 * ngroups * d_state
+    _bf16("conv_state", conv_state, (b, conv_dim, conv_state.shape[-1]))
+    _bf16("weight", weight, (conv_dim, conv_state.shape[-1]))
+    if bias is not None:
+        _bf16("bias", bias, (conv_dim,))
+    _bf16("ssm_state", ssm_state, (b, nheads, hd, d_state))
+    require_cuda("A", A, torch.float32, 1)
+    if tuple(A.shape) != (nheads,) or not A.is_contiguous():
+        raise ValueError(f"A must be a contiguous fp32 [{nheads}] tensor")
+    for name, t in (("D", D), ("dt_bias", dt_bias)):
+        if t is not None:
+            _bf16(name, t, (nheads,))
+    require_cuda("sync", sync, torch.int32, 1)
+    if sync.numel() < b * ngroups or not sync.is_contiguous():
+        raise ValueError(f"sync must hold {b * ngroups} contiguous int32 counters")
+    dev = zxbcdt.device
+    z = torch.empty(b, d_inner, device=dev, dtype=_BF16)
+    y = torch.empty(b, nheads, hd, device=dev, dtype=_BF16)
+    call("sn_mamba2_conv_ssu", zxbcdt.data_ptr(), zxbcdt.stride(0) if b > 1 else zxbcdt.shape[1],
+         conv_state.data_ptr(), weight.data_ptr(), _ptr(bias), ssm_state.data_ptr(), A.data_ptr(), _ptr(D),
+         _ptr(dt_bias), z.data_ptr(), y.data_ptr(), sync.data_ptr(), b, d_inner, ngroups, d_state, nheads, hd,
+         conv_state.shape[-1], stream_handle(stream))
+    return z, y
+
+
 def rotary_kv_append(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, cos: torch.Tensor,
                      sin: torch.Tensor, nheads: int, pos: int, stream=None) -> torch.Tensor:
     """q with rotary [b, nheads, 1, head_dim]; k (rotated) and v written at

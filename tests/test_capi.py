@@ -75,6 +75,11 @@ def test_gemv_rejects_bad_arguments_on_host(L):
     assert L.sn_rmsnorm_gated(p, p, None, None, p, 2, 16384, 16384, 1e-5, 0, None) == -3
     assert L.sn_layer_norm_fused(None, None, 0, p, None, p, None, 0, 2, 64, 1e-5, 0, None) == -1
     assert L.sn_layer_norm_fused(p, None, 0, p, None, p, None, 0, 2, 9000, 1e-5, 0, None) == -3
+    # fused Mamba2 conv + SSU: the counters are required; d_state 64 is the two-launch path's
+    assert L.sn_mamba2_conv_ssu(p, 8512, p, p, None, p, p, None, None, p, p, None, 1, 4096, 1, 128, 64, 64, 4,
+                                None) == -1
+    assert L.sn_mamba2_conv_ssu(p, 8512, p, p, None, p, p, None, None, p, p, p, 1, 4096, 1, 64, 64, 64, 4,
+                                None) == -3
     assert L.sn_quantize_rows_int8(None, 8, 8, 8, p, 8, p, None) == -1
     assert L.sn_quantize_rows_fp8e4m3(p, 4, 8, 8, p, 8, p, None) == -1
 

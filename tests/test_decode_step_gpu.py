@@ -181,6 +181,42 @@ def test_glue_kernels_match_torch_glue():
     assert ((y.float() - ref.float()).abs() <= ulp).all()
 
 
+@pytest.mark.parametrize("b,di,ng,ds,nh,W", [(2, 4096, 1, 128, 64, 4), (1, 4096, 1, 128, 64, 4),
+                                               (3, 2048, 2, 256, 32, 4), (2, 1024, 4, 128, 32, 3)])
+def test_conv_ssu_equals_split_conv_then_ssu(b, di, ng, ds, nh, W):
+    """sn_mamba2_conv_ssu against mamba2_split_conv + selective_state_update
+    (per-head A / D / dt_bias broadcast for the latter): z, y and both
+    states bit for bit, over three calls in a row (its group counters must
+    come back to zero), and the counters are zero afterwards."""
+    from sonata_b200.kernels import mamba_step as MS
+    g = torch.Generator(device="cuda").manual_seed(11 + b + ng)
+    hd = di // nh
+    cd = di + 2 * ng * ds
+    r = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    w = (0.5 * r(cd, W)).to(torch.bfloat16)
+    bias = (0.1 * r(cd)).to(torch.bfloat16)
+    A_h = -torch.exp(torch.log(torch.rand(nh, device="cuda", generator=g) * 15 + 1))
+    D = (1 + 0.1 * r(nh)).to(torch.bfloat16)
+    dtb = (torch.rand(nh, device="cuda", generator=g) * 2 - 4).to(torch.bfloat16)
+    A_e = A_h[:, None, None].expand(nh, hd, ds).contiguous()
+    D_e, dtb_e = D[:, None].expand(nh, hd).contiguous(), dtb[:, None].expand(nh, hd).contiguous()
+    cs1 = r(b, cd, W).to(torch.bfloat16)
+    ss1 = (0.5 * r(b, nh, hd, ds)).to(torch.bfloat16)
+    cs2, ss2 = cs1.clone(), ss1.clone()
+    sync = torch.zeros(b * ng, device="cuda", dtype=torch.int32)
+    for _ in range(3):
+        zx = r(b, 2 * di + 2 * ng * ds + nh).to(torch.bfloat16)
+        z1, y1 = MS.mamba2_conv_ssu(zx, cs1, w, bias, ss1, A_h, D, dtb, di, ng, ds, nh, sync)
+        z2, x, Bm, Cm, dt = MS.mamba2_split_conv(zx, cs2, w, bias, di, ng, ds, nh)
+        y2 = MS.selective_state_update(ss2, x, dt, A_e, Bm, Cm, D=D_e, z=None, dt_bias=dtb_e, dt_softplus=True)
+        torch.cuda.synchronize()
+        assert torch.equal(z1, z2) and torch.equal(y1, y2)
+        assert torch.equal(cs1, cs2) and torch.equal(ss1, ss2)
+    assert int(sync.abs().sum()) == 0
+    from sonata_b200 import _lib
+    assert _lib.lib().sn_device_status(1, None) == 0
+
+
 @pytest.mark.parametrize("M", [1, 2])
 def test_norm_fused_gemv_matches_norm_then_gemv(M):
     """The norms fused into the GEMV's x staging against the standalone norm
