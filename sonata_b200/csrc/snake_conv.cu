@@ -40,6 +40,11 @@ constexpr int kScProducerWarps = 8;
 constexpr int kScEpilogueWarps = 8;  // two per TMEM lane quarter, half the columns each
 constexpr int kScThreads = (2 + kScProducerWarps + kScEpilogueWarps) * 32;  // TMA, MMA, producers, epilogue
 constexpr int kScWStages = 2;
+// x tiles by TMA (convolutions without a halo: 128 activation rows): two
+// fp32 staging buffers of [64 channels][128 rows], filled by the weight
+// producer's thread and read by the snake producers from shared memory
+constexpr int kScXStages = 2;
+constexpr uint32_t kScXBytes = 64 * 128 * 4;
 constexpr int kScPairWStages = 2;  // weight stages in the CTA-pair kernel (4 measured no faster)
 constexpr int kMaxTaps = 7;
 constexpr int kMaxRowIters = 7;  // activation rows per chunk <= 32 * 7 = 224 ((K-1)*d <= 72)
@@ -68,6 +73,7 @@ struct ScParams {
   int up_s, up_p, Cy, Ty;
   int up_sh;  // log2(up_s) when up_s is a power of two (every DAC stride), else -1
   int up_vec;          // widest vector store (1, 2 or 4 floats) the phase runs of y allow
+  int x_tma;           // 1: the x tiles arrive by TMA into shared staging (no halo, aligned x)
   // element strides of the batch and channel (row) dimensions; time is
   // contiguous.  Whole tensors: x (Cin * T, T), y and res (Cy * Ty, Ty); a
   // streaming decoder passes windows of larger per-layer buffers.
@@ -279,20 +285,24 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // that the plain convolutions carry none of its code.
 template <bool UP>
 __global__ void __launch_bounds__(kScThreads, 1)
-    snake_conv_mma_kernel(const __grid_constant__ CUtensorMap mapW, const ScParams p) {
+    snake_conv_mma_kernel(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapX,
+                          const ScParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // layout: [A0 hi][A0 lo][A1 hi][A1 lo][W0 hi][W0 lo][W1 hi][W1 lo][barriers]
+  // layout: [A0 hi][A0 lo][A1 hi][A1 lo][W0 hi][W0 lo][W1 hi][W1 lo][X0][X1 (x_tma only)][barriers]
   uint8_t* abuf = smem;
   uint8_t* wbuf = smem + 4 * p.a_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(wbuf + 2 * kScWStages * p.w_bytes);
+  uint8_t* xstage = wbuf + 2 * kScWStages * p.w_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xstage + (p.x_tma ? kScXStages * kScXBytes : 0u));
   uint64_t* a_full = bars;
   uint64_t* a_empty = bars + 2;
   uint64_t* w_full = bars + 4;
   uint64_t* w_empty = w_full + kScWStages;
   uint64_t* t_full = w_empty + kScWStages;
   uint64_t* t_empty = t_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(t_empty + 2);
+  uint64_t* x_full = t_empty + 2;           // [kScXStages]
+  uint64_t* x_empty = x_full + kScXStages;  // [kScXStages]: every producer warp has read the tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_empty + kScXStages);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nchunks = (p.Cin + 63) / 64;
@@ -311,8 +321,13 @@ __global__ void __launch_bounds__(kScThreads, 1)
       mbar_init(w_full + i, 1);
       mbar_init(w_empty + i, 1);
     }
+    for (int i = 0; i < kScXStages; ++i) {
+      mbar_init(x_full + i, 1);
+      mbar_init(x_empty + i, kScProducerWarps);
+    }
     fence_barrier_init();
     tc::prefetch_map(&mapW);
+    if (p.x_tma) tc::prefetch_map(&mapX);
   }
   if (warp == 1) tc::tmem_alloc(tmem_slot, 2 * p.tcols);
   tc::fence_before_sync();
@@ -337,8 +352,22 @@ __global__ void __launch_bounds__(kScThreads, 1)
       // (tap, chunk, tile) of stage q, kept incrementally: run-time
       // divisions here cost the single producer thread ~0.1 us each
       int q = 0, tap = 0, c = 0, j = 0, b = 0, t0 = 0, o0 = 0;
+      int gx = 0;  // x tiles issued (one per chunk, before the chunk's first weight stage)
       if (total > 0) tile_coords(0, b, t0, o0);
       for (; q < total; ++q) {
+        if (p.x_tma && tap == 0) {
+          // chunk gx's x tile: 64 channels from c * 64, rows t0 .. t0 + 127 (no
+          // halo: the time coordinate is t0, a multiple of 128); channels and
+          // times past the tensor read as zero
+          const int xs = gx & (kScXStages - 1);
+          if (gx >= kScXStages && !mbar_wait_bounded(x_empty + xs, ((gx / kScXStages) - 1) & 1)) {
+            record_status(SN_ERR_TIMEOUT);
+            break;
+          }
+          mbar_arrive_expect_tx(x_full + xs, kScXBytes);
+          tc::tma_load_3d(xstage + static_cast<size_t>(xs) * kScXBytes, &mapX, t0, c * 64, b, x_full + xs);
+          ++gx;
+        }
         const int s = q % kScWStages, k = q / kScWStages;
         if (k > 0 && !mbar_wait_bounded(w_empty + s, (k - 1) & 1)) {
           record_status(SN_ERR_TIMEOUT);
@@ -360,6 +389,10 @@ __global__ void __launch_bounds__(kScThreads, 1)
         for (int j = (q > kScWStages ? q - kScWStages : 0); j < q; ++j)
           mbar_wait_bounded(w_full + j % kScWStages, (j / kScWStages) & 1);
       }
+      // the last x tiles have landed before the CTA can exit (the producers
+      // wait for them too unless they stopped early)
+      for (int v = (gx > kScXStages ? gx - kScXStages : 0); v < gx; ++v)
+        mbar_wait_bounded(x_full + (v & (kScXStages - 1)), (v / kScXStages) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -422,40 +455,59 @@ __global__ void __launch_bounds__(kScThreads, 1)
       for (int c = 0; c < nchunks; ++c, ++g) {
         const int ab = g & 1;
         const int i0 = c * 64 + pw * 8;  // first input channel of this warp's group
-        {
-          // pull the next chunk's x lines (this warp's 8 channels x rows) into L2
-          // while this chunk's loads are outstanding: one 128-byte line per lane
-          // and (channel, 32-row step) pair
-          int nb = b, nt0 = tin0, ni0 = i0 + 64;
-          if (c + 1 == nchunks) {
-            int t1, o1;
-            if (j + 1 < my_tiles) {
-              tile_coords(j + 1, nb, t1, o1);
-              nt0 = t1 - p.pad;
-            }
-            ni0 = pw * 8;
-          }
-          const bool more = (c + 1 < nchunks) || (j + 1 < my_tiles);
-          const float* nxb = p.x + static_cast<int64_t>(nb) * p.x_bs;
-#pragma unroll
-          for (int k = lane; k < 8 * kMaxRowIters; k += 32) {
-            const int e = k & 7, it = k >> 3;
-            const int tin = max(nt0 + 32 * it, 0);
-            if (more && ni0 + e < p.Cin && 32 * it < p.rows && tin < p.T)
-              asm volatile("prefetch.global.L2 [%0];" ::"l"(nxb + static_cast<int64_t>(ni0 + e) * p.x_ld + tin));
-          }
-        }
-        // issue every x load of this chunk before the first use (memory-level
-        // parallelism: 8 channels x up to 7 rows per lane in flight)
         float v[kMaxRowIters][8];
+        if (p.x_tma) {
+          // the chunk's x tile is in staging buffer g mod kScXStages, [channel][row]
+          const int xs = g & (kScXStages - 1);
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(x_full + xs, (g / kScXStages) & 1))) {
+            record_status(SN_ERR_TIMEOUT);
+            j = my_tiles;  // unwind
+            break;
+          }
+          const float* xt = reinterpret_cast<const float*>(xstage + static_cast<size_t>(xs) * kScXBytes);
 #pragma unroll
-        for (int it = 0; it < kMaxRowIters; ++it) {
-          const int r = lane + 32 * it;
-          const int tin = tin0 + r;
-          const bool in_t = r < p.rows && tin >= 0 && tin < p.T;
+          for (int it = 0; it < kMaxRowIters; ++it) {
+            const int r = lane + 32 * it;
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.x_ld + tin) : 0.f;
+            for (int e = 0; e < 8; ++e) v[it][e] = (r < 128) ? xt[(pw * 8 + e) * 128 + r] : 0.f;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(x_empty + xs);  // this warp is done with the staging buffer
+        } else {
+          {
+            // pull the next chunk's x lines (this warp's 8 channels x rows) into L2
+            // while this chunk's loads are outstanding: one 128-byte line per lane
+            // and (channel, 32-row step) pair
+            int nb = b, nt0 = tin0, ni0 = i0 + 64;
+            if (c + 1 == nchunks) {
+              int t1, o1;
+              if (j + 1 < my_tiles) {
+                tile_coords(j + 1, nb, t1, o1);
+                nt0 = t1 - p.pad;
+              }
+              ni0 = pw * 8;
+            }
+            const bool more = (c + 1 < nchunks) || (j + 1 < my_tiles);
+            const float* nxb = p.x + static_cast<int64_t>(nb) * p.x_bs;
+  #pragma unroll
+            for (int k = lane; k < 8 * kMaxRowIters; k += 32) {
+              const int e = k & 7, it = k >> 3;
+              const int tin = max(nt0 + 32 * it, 0);
+              if (more && ni0 + e < p.Cin && 32 * it < p.rows && tin < p.T)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(nxb + static_cast<int64_t>(ni0 + e) * p.x_ld + tin));
+            }
+          }
+          // issue every x load of this chunk before the first use (memory-level
+          // parallelism: 8 channels x up to 7 rows per lane in flight)
+  #pragma unroll
+          for (int it = 0; it < kMaxRowIters; ++it) {
+            const int r = lane + 32 * it;
+            const int tin = tin0 + r;
+            const bool in_t = r < p.rows && tin >= 0 && tin < p.T;
+  #pragma unroll
+            for (int e = 0; e < 8; ++e)
+              v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.x_ld + tin) : 0.f;
+          }
         }
         float al[8], inv[8];
 #pragma unroll
@@ -543,7 +595,8 @@ __global__ void __launch_bounds__(kScThreads, 1)
 // ---------------------------------------------------------------------------
 template <bool UP>
 __global__ void __launch_bounds__(kScThreads, 1)
-    snake_conv_pair_kernel(const __grid_constant__ CUtensorMap mapW, const ScParams p) {
+    snake_conv_pair_kernel(const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapX,
+                           const ScParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // layout: [A0 hi][A0 lo][A1 hi][A1 lo][W0 hi/2][W0 lo/2][W1 hi/2][W1 lo/2][barriers]
@@ -1032,7 +1085,22 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
   p.rows = (128 + (p.K - 1) * p.dil + 7) / 8 * 8;
   p.a_bytes = static_cast<uint32_t>(p.rows) * 128;
   p.w_bytes = static_cast<uint32_t>(p.nt) * 128;
-  const size_t smem = 1024 + 4 * static_cast<size_t>(p.a_bytes) + 2 * kScWStages * static_cast<size_t>(p.w_bytes) + 256;
+  // x tiles by TMA where the tile has no halo and x's strides allow a map
+  // (the DAC residual units' k1 convolutions): one 32 KB box per chunk
+  CUtensorMap mapX = {};
+  p.x_tma = 0;
+  if (p.rows == 128 && p.pad == 0 && p.x_ld % 4 == 0 && (p.B == 1 || p.x_bs % 4 == 0) && aligned16(p.x)) {
+    const uint64_t xdims[3] = {static_cast<uint64_t>(p.T), static_cast<uint64_t>(p.Cin), static_cast<uint64_t>(p.B)};
+    const uint64_t xstr[2] = {static_cast<uint64_t>(p.x_ld) * 4,
+                              p.B == 1 ? (static_cast<uint64_t>(p.x_ld) * p.Cin * 4 + 15) / 16 * 16
+                                       : static_cast<uint64_t>(p.x_bs) * 4};
+    const uint32_t xbox[3] = {128, 64, 1};
+    p.x_tma = tc::make_map_f32_plain(&mapX, p.x, 3, xdims, xstr, xbox) ? 1 : 0;
+  }
+  const size_t smem0 = 1024 + 4 * static_cast<size_t>(p.a_bytes) + 2 * kScWStages * static_cast<size_t>(p.w_bytes) +
+                       256;
+  if (smem0 + static_cast<size_t>(kScXStages) * kScXBytes > 227 * 1024) p.x_tma = 0;  // no room for the staging
+  const size_t smem = smem0 + (p.x_tma ? static_cast<size_t>(kScXStages) * kScXBytes : 0);
   const int64_t ntiles64 = static_cast<int64_t>(p.B) * p.ntiles_t * p.ntiles_o;
   p.ntiles = static_cast<int>(std::min<int64_t>(ntiles64, INT32_MAX));
   if (!(smem <= 227 * 1024 && ntiles64 < (int64_t(1) << 31) && p.rows <= 32 * kMaxRowIters && 2 * p.tcols <= 512))
@@ -1050,6 +1118,7 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
   if (snake_pair_enabled() && p.Cout >= 128) {
     // CTA-pair kernel: 256-row time tiles, each CTA holding nt / 2 weight rows
     ScParams q = p;
+    q.x_tma = 0;  // the pair kernel reads x itself
     q.ntiles_t2 = (p.Tout + 255) / 256;
     const int npairs = std::max(1, sms / 2);
     q.nt = out_tile(p.Cout, static_cast<int64_t>(p.B) * q.ntiles_t2, npairs);
@@ -1076,7 +1145,7 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, pair_kern, mapW, q) == cudaSuccess) return SN_OK;
+      if (cudaLaunchKernelEx(&cfg, pair_kern, mapW, mapX, q) == cudaSuccess) return SN_OK;
     }
     cudaGetLastError();
   }
@@ -1085,7 +1154,7 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
     if (cudaFuncSetAttribute(mma_kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) == cudaSuccess) {
       const int grid = std::min(p.ntiles, sms);
-      return launch(mma_kern, dim3(grid), dim3(kScThreads), smem, st, false, mapW, p);
+      return launch(mma_kern, dim3(grid), dim3(kScThreads), smem, st, false, mapW, mapX, p);
     }
     cudaGetLastError();
   }

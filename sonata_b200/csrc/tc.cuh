@@ -55,6 +55,30 @@ inline bool make_map_bf16_sw128(CUtensorMap* map, const void* base, int rank, co
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tiled fp32 map without swizzle (a box lands in shared memory as a dense
+// row-major block, innermost dimension first); strides in bytes for dims
+// 1..rank-1 (multiples of 16), box innermost extent a multiple of 4
+// elements.  Out-of-range elements read as 0.
+inline bool make_map_f32_plain(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                               const uint64_t* strides_bytes, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || box[0] % 4 != 0) return false;
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    st[i] = strides_bytes[i];
+    if (st[i] % 16) return false;
+  }
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base), d, st, bx, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ---------------------------------------------------------------------------
 // device: TMA tensor loads (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------
