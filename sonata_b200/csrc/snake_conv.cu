@@ -364,8 +364,11 @@ __global__ void __launch_bounds__(kScThreads, 1)
             record_status(SN_ERR_TIMEOUT);
             break;
           }
+          // a tile wholly past T (the odd CTA of a pair at the end) reads the
+          // last 128-row block instead: its rows are computed but never stored
+          const int tx = t0 < p.T ? t0 : (p.T - 1) / 128 * 128;
           mbar_arrive_expect_tx(x_full + xs, kScXBytes);
-          tc::tma_load_3d(xstage + static_cast<size_t>(xs) * kScXBytes, &mapX, t0, c * 64, b, x_full + xs);
+          tc::tma_load_3d(xstage + static_cast<size_t>(xs) * kScXBytes, &mapX, tx, c * 64, b, x_full + xs);
           ++gx;
         }
         const int s = q % kScWStages, k = q / kScWStages;
@@ -599,18 +602,21 @@ __global__ void __launch_bounds__(kScThreads, 1)
                            const ScParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // layout: [A0 hi][A0 lo][A1 hi][A1 lo][W0 hi/2][W0 lo/2][W1 hi/2][W1 lo/2][barriers]
+  // layout: [A0 hi][A0 lo][A1 hi][A1 lo][W0 hi/2][W0 lo/2][W1 hi/2][W1 lo/2][X0][X1 (x_tma only)][barriers]
   const uint32_t wh = p.w_bytes / 2;  // this CTA's half of one weight plane
   uint8_t* abuf = smem;
   uint8_t* wbuf = smem + 4 * p.a_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(wbuf + 2 * kScPairWStages * wh);
+  uint8_t* xstage = wbuf + 2 * kScPairWStages * wh;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xstage + (p.x_tma ? kScXStages * kScXBytes : 0u));
   uint64_t* a_full = bars;        // even CTA: both CTAs' producers
   uint64_t* a_empty = bars + 2;   // both CTAs: MMA commit
   uint64_t* w_full = bars + 4;    // even CTA: both CTAs' weight bytes
   uint64_t* w_empty = w_full + kScPairWStages;  // both CTAs: MMA commit
   uint64_t* t_full = w_empty + kScPairWStages;  // both CTAs: MMA commit
   uint64_t* t_empty = t_full + 2;           // even CTA: both CTAs' epilogues
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(t_empty + 2);
+  uint64_t* x_full = t_empty + 2;           // this CTA's x staging (local barriers)
+  uint64_t* x_empty = x_full + kScXStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_empty + kScXStages);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();
@@ -629,8 +635,13 @@ __global__ void __launch_bounds__(kScThreads, 1)
       mbar_init(w_full + i, 1);
       mbar_init(w_empty + i, 1);
     }
+    for (int i = 0; i < kScXStages; ++i) {
+      mbar_init(x_full + i, 1);
+      mbar_init(x_empty + i, kScProducerWarps);
+    }
     fence_barrier_init();
     tc::prefetch_map(&mapW);
+    if (p.x_tma) tc::prefetch_map(&mapX);
   }
   if (warp == 1) tc::tmem_alloc_pair(tmem_slot, 2 * p.tcols);
   tc::fence_before_sync();
@@ -660,8 +671,23 @@ __global__ void __launch_bounds__(kScThreads, 1)
       const int total = my_tiles * nchunks * p.K;
       // (tap, chunk, tile) of stage q, kept incrementally (no divisions)
       int q = 0, tap = 0, c = 0, j = 0, b = 0, t0 = 0, o0 = 0;
+      int gx = 0;  // x tiles issued (one per chunk, before the chunk's first weight stage)
       if (total > 0) tile_coords(0, b, t0, o0);
       for (; q < total; ++q) {
+        if (p.x_tma && tap == 0) {
+          // chunk gx's x tile for this CTA's 128 rows (t0: a multiple of 128, no halo)
+          const int xs = gx & (kScXStages - 1);
+          if (gx >= kScXStages && !mbar_wait_bounded(x_empty + xs, ((gx / kScXStages) - 1) & 1)) {
+            record_status(SN_ERR_TIMEOUT);
+            break;
+          }
+          // a tile wholly past T (the odd CTA of a pair at the end) reads the
+          // last 128-row block instead: its rows are computed but never stored
+          const int tx = t0 < p.T ? t0 : (p.T - 1) / 128 * 128;
+          mbar_arrive_expect_tx(x_full + xs, kScXBytes);
+          tc::tma_load_3d(xstage + static_cast<size_t>(xs) * kScXBytes, &mapX, tx, c * 64, b, x_full + xs);
+          ++gx;
+        }
         const int s = q % kScPairWStages, k = q / kScPairWStages;
         if (k > 0 && !mbar_wait_bounded(w_empty + s, (k - 1) & 1)) {
           record_status(SN_ERR_TIMEOUT);
@@ -680,6 +706,8 @@ __global__ void __launch_bounds__(kScThreads, 1)
           }
         }
       }
+      for (int v = (gx > kScXStages ? gx - kScXStages : 0); v < gx; ++v)  // the last x tiles have landed
+        mbar_wait_bounded(x_full + (v & (kScXStages - 1)), (v / kScXStages) & 1);
       (void)q;
     }
   } else if (warp == 1) {
@@ -744,14 +772,33 @@ __global__ void __launch_bounds__(kScThreads, 1)
         const int ab = g & 1;
         const int i0 = c * 64 + pw * 8;
         float v[kMaxRowIters][8];
+        if (p.x_tma) {
+          // the chunk's x tile is in this CTA's staging buffer g mod kScXStages, [channel][row]
+          const int xs = g & (kScXStages - 1);
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(x_full + xs, (g / kScXStages) & 1))) {
+            record_status(SN_ERR_TIMEOUT);
+            j = my_tiles;
+            break;
+          }
+          const float* xt = reinterpret_cast<const float*>(xstage + static_cast<size_t>(xs) * kScXBytes);
 #pragma unroll
-        for (int it = 0; it < kMaxRowIters; ++it) {
-          const int r = lane + 32 * it;
-          const int tin = tin0 + r;
-          const bool in_t = r < p.rows && tin >= 0 && tin < p.T;
+          for (int it = 0; it < kMaxRowIters; ++it) {
+            const int r = lane + 32 * it;
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.x_ld + tin) : 0.f;
+            for (int e = 0; e < 8; ++e) v[it][e] = (r < 128) ? xt[(pw * 8 + e) * 128 + r] : 0.f;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(x_empty + xs);  // this warp is done with the staging buffer
+        } else {
+#pragma unroll
+          for (int it = 0; it < kMaxRowIters; ++it) {
+            const int r = lane + 32 * it;
+            const int tin = tin0 + r;
+            const bool in_t = r < p.rows && tin >= 0 && tin < p.T;
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              v[it][e] = (in_t && i0 + e < p.Cin) ? __ldg(xb + static_cast<int64_t>(i0 + e) * p.x_ld + tin) : 0.f;
+          }
         }
         float al[8], inv[8];
 #pragma unroll
@@ -1118,7 +1165,6 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
   if (snake_pair_enabled() && p.Cout >= 128) {
     // CTA-pair kernel: 256-row time tiles, each CTA holding nt / 2 weight rows
     ScParams q = p;
-    q.x_tma = 0;  // the pair kernel reads x itself
     q.ntiles_t2 = (p.Tout + 255) / 256;
     const int npairs = std::max(1, sms / 2);
     q.nt = out_tile(p.Cout, static_cast<int64_t>(p.B) * q.ntiles_t2, npairs);
@@ -1127,7 +1173,10 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
     q.w_bytes = static_cast<uint32_t>(q.nt) * 128;
     const int64_t nt2 = static_cast<int64_t>(p.B) * q.ntiles_t2 * q.ntiles_o;
     q.ntiles2 = static_cast<int>(std::min<int64_t>(nt2, INT32_MAX));
-    const size_t smem2 = 1024 + 4 * static_cast<size_t>(q.a_bytes) + kScPairWStages * static_cast<size_t>(q.w_bytes) + 256;
+    const size_t smem20 = 1024 + 4 * static_cast<size_t>(q.a_bytes) + kScPairWStages * static_cast<size_t>(q.w_bytes) +
+                          256;
+    if (smem20 + static_cast<size_t>(kScXStages) * kScXBytes > 227 * 1024) q.x_tma = 0;  // no room for the staging
+    const size_t smem2 = smem20 + (q.x_tma ? static_cast<size_t>(kScXStages) * kScXBytes : 0);
     const uint32_t box2[3] = {64, static_cast<uint32_t>(q.nt / 2), 1};
     if (nt2 < (int64_t(1) << 31) && 2 * q.tcols <= 512 && smem2 <= 227 * 1024 &&
         tc::make_map_bf16_sw128(&mapW, Wp, 3, dims, strides, box2) &&

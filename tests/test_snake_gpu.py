@@ -85,6 +85,31 @@ def test_odd_shapes(S, B, Cin, Cout, T, pad, d):
     check(y.cpu().numpy(), truth)
 
 
+@pytest.mark.parametrize("B,Cin,Cout,T", [
+    (1, 96, 96, 2500),     # single CTA, ragged last tile
+    (1, 48, 80, 333),      # channels past Cin read as zero by the copy engine
+    (2, 192, 192, 100),    # CTA pairs: the odd CTA's rows all past T (its tile read is clamped)
+    (1, 256, 256, 300),    # CTA pairs: a second pair tile, partly past T
+    (3, 160, 320, 700),    # CTA pairs: batch > 1, two output tiles
+])
+def test_k1_convolutions_with_residual(S, B, Cin, Cout, T):
+    """Kernel size 1 (the DAC residual units' second convolution): the x
+    tiles come by TMA into shared-memory staging; with and without the
+    residual add, against the float64 oracle."""
+    g = torch.Generator().manual_seed(T + Cin)
+    x = torch.randn(B, Cin, T, generator=g)
+    alpha = torch.rand(Cin, generator=g) + 0.5
+    W = torch.randn(Cout, Cin, 1, generator=g) / math.sqrt(Cin)
+    b = torch.randn(Cout, generator=g)
+    res = torch.randn(B, Cout, T, generator=g)
+    truth = O.snake_conv1d_ref(x.numpy(), alpha.numpy(), W.numpy(), b.numpy(), padding=0, dilation=1)
+    y = S.fused_snake_conv1d(x.cuda(), alpha.cuda(), W.cuda(), b.cuda())
+    yr = S.fused_snake_conv1d(x.cuda(), alpha.cuda(), W.cuda(), b.cuda(), residual=res.cuda())
+    torch.cuda.synchronize()
+    check(y.cpu().numpy(), truth)
+    check(yr.cpu().numpy(), truth + res.numpy().astype(np.float64))
+
+
 def test_no_bias_and_large_activations(S):
     x, alpha, W, b = rand_case(1, 64, 64, 700, seed=9, xscale=6.0)
     y = S.fused_snake_conv1d(x.cuda(), alpha.cuda(), W.cuda(), None, padding=9, dilation=3)
