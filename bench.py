@@ -915,13 +915,19 @@ def run_case(args):
         run = ch
         per = 1
     elif args.case == "snake":
+        # --shape C x T x d (a config-5 k7 unit), or C x T x 1 x 1: the residual
+        # unit's k1 convolution with its residual add (x tiles by TMA)
         from sonata_b200.kernels import fused_snake_conv as S
-        C, T, d = (shape + [384, 55168, 3][len(shape):])[:3]
+        C, T, d, K = (shape + [384, 55168, 3, 7][len(shape):])[:4]
         x, al, W, b = S.dac_stage_inputs(C, T)
         y = torch.empty_like(x)
-        run = lambda: S.fused_snake_conv1d(x, al, W, b, padding=3 * d, dilation=d, out=y)
+        if K == 1:
+            W1 = W[:, :, 3:4].contiguous()
+            run = lambda: S.fused_snake_conv1d(x, al, W1, b, out=y, residual=x)
+        else:
+            run = lambda: S.fused_snake_conv1d(x, al, W, b, padding=3 * d, dilation=d, out=y)
         per = 1
-        algo = 2 * C * C * 7 * T  # useful flops
+        algo = 2 * C * C * K * T  # useful flops
     elif args.case == "head":
         (B,) = (shape + [64])[:1]
         heads = head_set(torch.Generator(device="cuda").manual_seed(0))
