@@ -1144,6 +1144,7 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
     const uint32_t xbox[3] = {128, 64, 1};
     p.x_tma = tc::make_map_f32_plain(&mapX, p.x, 3, xdims, xstr, xbox) ? 1 : 0;
   }
+  const int x_map_ok = p.x_tma;  // each kernel below also needs room for the staging
   const size_t smem0 = 1024 + 4 * static_cast<size_t>(p.a_bytes) + 2 * kScWStages * static_cast<size_t>(p.w_bytes) +
                        256;
   if (smem0 + static_cast<size_t>(kScXStages) * kScXBytes > 227 * 1024) p.x_tma = 0;  // no room for the staging
@@ -1165,6 +1166,7 @@ int snake_fast(ScParams p, __nv_bfloat16* Wp, cudaStream_t st, Pack pack) {
   if (snake_pair_enabled() && p.Cout >= 128) {
     // CTA-pair kernel: 256-row time tiles, each CTA holding nt / 2 weight rows
     ScParams q = p;
+    q.x_tma = x_map_ok;  // the pair kernel's own room is checked below
     q.ntiles_t2 = (p.Tout + 255) / 256;
     const int npairs = std::max(1, sms / 2);
     q.nt = out_tile(p.Cout, static_cast<int64_t>(p.B) * q.ntiles_t2, npairs);
